@@ -1,0 +1,341 @@
+"""Benchmark: batched depth-limited CFR+ solves with value-network leaves.
+
+Workload: per GPU, 4096 independent subgames whose
+roots are seeded solve sites (seeded draft, 20 uniform decisions, on to the
+next MainPlay; seeds rank*4096 .. rank*4096+4095), depth 3, 512 CFR+
+iterations, the v5 value network at every iteration, Phase 2 on the live
+root belief. One step = one full batched solve of that batch: per-solve
+network pieces, init, 512 iterations, the average strategy, root values.
+
+Metric: CFR node-updates/s = sum over subgames of public nodes x iterations,
+divided by the device time of the step (CUDA events on the solver's stream,
+max over ranks). Whole-job value = all ranks' node-updates / that time.
+Weak scaling: every rank solves its own 4096 subgames; the value-net weights
+are broadcast once from rank 0 over NCCL; there is no per-iteration
+collective.
+
+--impl reference times the CPU restatement of the reference solver (the
+oracle under oracle/, the reference's own Rust cannot be built here) on a
+bounded sample of the same workload with every host thread.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "war-chest-bot-9000-_b200"))
+sys.path.insert(0, os.path.join(ROOT, "tests"))
+
+METRIC = "CFR node-updates/sec"
+UNIT = "node-updates/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--subgames", type=int, default=4096, help="subgames per GPU")
+    ap.add_argument("--depth", type=int, default=3)
+    ap.add_argument("--iters", type=int, default=512)
+    ap.add_argument("--plies", type=int, default=20)
+    ap.add_argument("--net", default="precise", choices=["precise", "fast", "none"])
+    ap.add_argument("--cpu-seconds", type=float, default=15.0, help="bounded CPU baseline sample")
+    ap.add_argument("--build-threads", type=int, default=0)
+    return ap.parse_args()
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def cfr_plus(wc):
+    return wc.Cfr.PLUS
+
+
+def build_jobs(wc, seeds, cfg, threads):
+    """Roots and flattened jobs on host threads (the C calls release the GIL)."""
+    out = [None] * len(seeds)
+    roots = [None] * len(seeds)
+
+    def work(lo, hi):
+        for i in range(lo, hi):
+            r = wc.generate_root(seeds[i], PLIES)
+            roots[i] = r
+            out[i] = wc.PackedJob.from_root(r, cfg)
+
+    n = len(seeds)
+    th = [threading.Thread(target=work, args=(n * k // threads, n * (k + 1) // threads)) for k in range(threads)]
+    for t in th:
+        t.start()
+    for t in th:
+        t.join()
+    return roots, out
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{index}.csv")
+
+    def start(self):
+        os.makedirs(os.path.dirname(self.path), exist_ok=True)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                                         stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        self.proc.terminate()
+        self.proc.wait()
+        self.f.close()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons)}
+
+
+def algorithmic_bytes(jobs):
+    """Bytes per solve each CFR kernel class must move (every value read or
+    written once; indices u32; see DESIGN.md for the per-unit figures)."""
+    c = np.sum([j.counts() for j in jobs], axis=0).astype(np.float64)
+    iters = jobs[0].cfg.iters
+    # per iteration pair each player's share runs once
+    pairs = iters / 2.0
+    rows = 24 * (c[0] + c[1]) + 8 * (c[2] + c[3])
+    vg = 12 * (c[4] + c[5]) + 8 * (c[6] + c[7])
+    reach = 24 * (c[8] + c[9]) + 16 * (c[10] + c[11]) + 8 * (c[12] + c[13])
+    return {"rows": rows * pairs, "vgather": vg * pairs, "reach": reach * pairs}
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p["hbm_gbs"], p["bf16_tflops"], "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def cpu_baseline(wc, oracle, cfg, weights, seeds, budget_s):
+    """The oracle (CPU restatement of the reference solver) on a bounded
+    sample: subgames solved on every host thread until the budget is spent."""
+    threads = os.cpu_count() or 1
+    done_nu, done_t, used = 0.0, 0.0, 0
+    chunk = max(threads, 1)
+    i = 0
+    while done_t < budget_s and i < len(seeds):
+        batch = seeds[i:i + chunk]
+        roots = [wc.generate_root(s, PLIES) for s in batch]
+        t0 = time.perf_counter()
+        nu = oracle.solve_many(roots, cfg, weights, threads)
+        done_t += time.perf_counter() - t0
+        done_nu += nu
+        used += len(batch)
+        i += chunk
+    return {"value": done_nu / done_t if done_t > 0 else 0.0, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{used} of the workload's subgames (seeds {seeds[0]}..{seeds[0] + used - 1}), "
+                      f"depth {cfg.depth}, {cfg.iters} CFR+ iterations, fp32 network, {done_t:.1f} s"}
+
+
+def main():
+    global PLIES
+    args = parse()
+    PLIES = args.plies
+    world, rank, local = dist_setup(args)
+    import oracle_lib
+    import warchest_b200 as wc
+
+    wc.set_cap_marker_value(0.0)  # the reference bench pins the horizon payoff at 0 (rebelbench.rs:35)
+    oracle_lib.lib().oracle_set_cap_marker_value(0.0)
+    cfg = wc.Cfg(depth=args.depth, iters=args.iters, snapshots=False, cfr=cfr_plus(wc), node_cap=200000)
+    seeds = list(range(rank * args.subgames, (rank + 1) * args.subgames))
+    weights = wc.seeded_weights("he", 0) if args.net != "none" else None
+    workload = {"workload": f"configs[2]: {args.subgames} subgames/GPU, depth {args.depth}, {args.iters} CFR+ iters, "
+                            f"v5 net every iteration, {args.plies}-ply seeded roots",
+                "subgames_per_gpu": args.subgames, "depth": args.depth, "iters": args.iters,
+                "net": args.net, "parallelism": f"shards{world}",
+                "l2": "working set (GBs of tree tables and state) far above the 126 MB L2"}
+
+    if args.impl == "reference":
+        if rank == 0:
+            base = cpu_baseline(wc, oracle_lib, cfg, weights, seeds, args.cpu_seconds * max(1, args.steps))
+            line = {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": UNIT, "n_gpus": world,
+                    "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+                    "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded roots)", "config": workload,
+                    "cpu_baseline": base,
+                    "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            print(json.dumps(line), flush=True)
+        return
+
+    threads = args.build_threads or max(1, (os.cpu_count() or 1))
+    t0 = time.perf_counter()
+    roots, jobs = build_jobs(wc, seeds, cfg, threads)
+    build_s = time.perf_counter() - t0
+
+    # weights: rank 0's seeded blob, broadcast once over NCCL when sharded
+    if weights is not None and world > 1:
+        import torch
+        import torch.distributed as dist
+
+        dev = torch.device("cuda", local)
+        tw = [torch.from_numpy(a).to(dev) for a in weights[1:]]
+        for t in tw:
+            dist.broadcast(t, src=0)
+        torch.cuda.synchronize()
+        client = wc.spawn(local, precise=(args.net == "precise"))
+        client.set_weights_device(0, tw[0].data_ptr(), tw[1].data_ptr(), tw[2].data_ptr())
+    elif weights is not None:
+        client = wc.spawn(local, *weights, precise=(args.net == "precise"))
+    else:
+        client = wc.spawn(local)
+
+    batch = client.upload(jobs)
+    stats = batch.stats()
+    for _ in range(args.warmup):
+        batch.solve()
+    barrier(world)
+    clocks = Clocks(local)
+    clocks.start()
+    times, profiles = [], []
+    for _ in range(args.steps):
+        prof = batch.solve_profiled()
+        times.append(prof["total"] / 1e3)
+        profiles.append(prof)
+    clocks_rec = clocks.stop()
+    barrier(world)
+    step_s = max_over_ranks(world, float(np.mean(times)))
+    total_nu = allsum(world, stats["node_updates"])
+    value = total_nu / step_s
+
+    # end to end through the public API: pinned host blobs in, results out
+    batch.free()
+    e2e_times = []
+    h2d = sum(j.info["table_bytes"] for j in jobs)
+    d2h = sum(4 * j.info["cells"] + 4 * (j.info["root_nc0"] + j.info["root_nc1"]) for j in jobs)
+    for _ in range(1):
+        barrier(world)
+        t0 = time.perf_counter()
+        res = client.solve_batch(jobs)
+        e2e_times.append(time.perf_counter() - t0)
+        del res
+    e2e_s = max_over_ranks(world, min(e2e_times))
+    e2e = {"value": total_nu / e2e_s, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+           "timing": "host wall clock around the synchronous wc_solve_batch (upload, solve, download)"}
+
+    # roofline of the dominant CFR kernel class
+    prof = {k: float(np.mean([p[k] for p in profiles])) for k in profiles[0]}
+    algo = algorithmic_bytes(jobs)
+    dom = max(("rows", "vgather", "reach"), key=lambda k: prof[k])
+    hbm, tflops, src = peaks()
+    achieved = algo[dom] / (prof[dom] / 1e3) / 1e9
+    roofline = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                "frac": achieved / hbm, "traffic": None, "peak_source": src,
+                "per_class_ms": prof, "algorithmic_bytes_per_solve": algo}
+
+    if rank == 0:
+        base = cpu_baseline(wc, oracle_lib, cfg, weights, seeds, args.cpu_seconds)
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32" if args.net != "fast" else "bf16",
+                "data": "synthetic (seeded roots, seeded He-normal weights)", "config": workload,
+                "e2e": e2e, "gpu_launches": launches_per_step(batch_levels(jobs), args.iters, args.net != "none"),
+                "roofline": roofline, "cpu_baseline": base, "clocks": clocks_rec,
+                "leaf_evals_per_sec": allsum(world, stats["leaf_evals"]) / step_s,
+                "host_build_s": build_s, "device_bytes": stats["device_bytes"]}
+        print(json.dumps(line), flush=True)
+    client.close()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+def batch_levels(jobs):
+    return max(j.info["levels"] for j in jobs)
+
+
+def launches_per_step(levels, iters, net):
+    """Kernel launches of one solve (the runtime's schedule, see runtime.cu)."""
+    per_iter = (3 if net else 2) + 2 * levels + (levels - 1)
+    setup = (3 if net else 0) + 2 + 2 * (levels - 1)
+    snaps = 1 + 1
+    phase2 = 1 + 2 * (levels - 1) + 2 * ((3 if net else 2) + 2 * levels + 1)
+    return setup + iters * per_iter + snaps + phase2
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(world, x):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def allsum(world, x):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t)
+    return float(t.item())
+
+
+PLIES = 20
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,164 @@
+/* War Chest batched CFR solver on B200 — the C ABI.
+ *
+ * This is the boundary a host engine binds (the reference engine would bind
+ * it from Rust with an `extern "C"` block). It replaces
+ * the reference's GPU solve service:
+ *
+ *   reference (fplonka/war-chest-bot-9000-)              this ABI
+ *   gpu::service::spawn      engine/src/gpu/service.rs:55-82   wc_init
+ *   GpuClient::set_weights   engine/src/gpu/client.rs:259-275  wc_publish
+ *   PackedJob::from_solver   engine/src/serialize.rs:340-360   wc_job_build
+ *   GpuClient::submit        engine/src/gpu/client.rs:212-228  wc_submit / wc_solve_batch
+ *   SolveHandle::wait        engine/src/gpu/client.rs:306-313  wc_wait
+ *   SolveResult              engine/src/gpu/client.rs:115-122  wc_result
+ *   selfplay root states     engine/src/selfplay.rs:59-81,588-905  wc_root_generate
+ *
+ * Conventions: every call returns 0 on success or a nonzero WC_E_* class;
+ * the message is in a thread-local buffer read by wc_last_error. Inputs are
+ * copied; results are owned by the library and released by wc_result_free.
+ * Submit/wait are thread-safe. Results are bit-reproducible for a fixed
+ * batch composition and device.
+ */
+#ifndef WC_B200_H
+#define WC_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    WC_OK = 0,
+    WC_E_ARG = 1,     /* bad argument or malformed input */
+    WC_E_CUDA = 2,    /* CUDA error (message has the detail) */
+    WC_E_CAPPED = 3,  /* the tree hit the node cap; the caller falls back */
+    WC_E_STATE = 4,   /* call out of order (unknown ticket, no weights, ...) */
+    WC_E_NOMEM = 5    /* the batch does not fit on the device */
+};
+
+/* search::Cfg (engine/src/search.rs:50-95) and the Cfr rule (:133-138). */
+typedef struct wc_solve_cfg {
+    int32_t depth;      /* public-tree depth in coin plays */
+    int32_t iters;      /* CFR iterations (alternating traversers) */
+    int32_t snapshots;  /* keep log-spaced average snapshots and carries */
+    int32_t reserved;
+    float alpha, beta, gamma, predict; /* discounting rule; CFR+ = (inf, -inf, 2, 0) */
+    uint64_t node_cap;  /* 0 = unlimited */
+} wc_solve_cfg;
+
+/* Weight blob of the v5 value network (engine/src/net.rs:507-528): dims must
+ * be {5}; w, b, ln are the three flat f32 arrays. A NULL w means "no network"
+ * (every non-terminal leaf is valued 0, like the reference's empty Nets). */
+typedef struct wc_weights {
+    uint32_t ndims;
+    const uint32_t* dims;
+    const float* w;
+    uint64_t nw;
+    const float* b;
+    uint64_t nb;
+    const float* ln;
+    uint64_t nln;
+} wc_weights;
+
+typedef struct wc_ctx wc_ctx;
+typedef struct wc_job wc_job;
+typedef struct wc_batch wc_batch;
+
+typedef struct wc_job_info {
+    uint64_t nodes, cells, net_rows, terminal_leaves, configs, levels;
+    uint64_t root_nc0, root_nc1, ncarried, carry_snapshots, carry_width, table_bytes;
+} wc_job_info;
+
+/* SolveResult: strategy in the reference's cell order (Solver::soff), root
+ * values per carried root as [player 0 configs | player 1 configs], carried
+ * beliefs per kept snapshot except the last as f16 over the exit nodes
+ * (network rows then terminal leaves, both players). */
+typedef struct wc_result {
+    float* strategy;
+    uint64_t ncells;
+    float* root_values;
+    uint64_t nroots;
+    uint64_t root_width;
+    uint16_t* carries;
+    uint64_t carry_snapshots;
+    uint64_t carry_width;
+    uint64_t weight_version;
+} wc_result;
+
+/* ---- service ------------------------------------------------------------ */
+/* precise != 0: fp32 network in the reference's operation order; 0: the
+ * bf16 tensor-core network. */
+int wc_init(int ndev, const int* devices, const wc_weights* w, int precise, wc_ctx** out);
+int wc_publish(wc_ctx* ctx, const wc_weights* w, uint64_t* version);
+/* Publish weights already resident on device `dev_index` (e.g. after an
+ * NCCL broadcast): pointers to w_len / b_len / ln_len f32 device arrays. */
+int wc_publish_device(wc_ctx* ctx, int dev_index, const float* w, const float* b, const float* ln,
+                      uint64_t* version);
+void wc_shutdown(wc_ctx* ctx);
+int wc_last_error(char* buf, size_t n);
+/* The v5 blob sizes: w, b, ln element counts. */
+void wc_net_layout(uint64_t* w_len, uint64_t* b_len, uint64_t* ln_len);
+/* Seeded weights: kind 0 He-normal, kind 1 the reference GPU tests' uniform
+ * +-0.05 blob. Arrays sized by wc_net_layout. */
+int wc_weights_fill(int kind, uint64_t seed, float* w, float* b, float* ln);
+/* Horizon payoff per marker of lead (engine/src/state.rs:27-43). */
+void wc_set_cap_marker_value(float v);
+
+/* ---- roots and jobs ------------------------------------------------------ */
+/* A seeded root: make_game(seed, random draft) then `plies` uniform decisions
+ * with the Bayes belief filter, then on to the next MainPlay. Serialized as
+ * the State bytes then both beliefs. */
+int wc_root_generate(uint64_t seed, int plies, int random_draft, uint8_t* buf, size_t cap, size_t* len);
+/* Build and flatten the subgame tree at a serialized root. carried holds
+ * ncarried root pairs (player 0 then player 1 over the root supports); with
+ * ncarried == 0 the live root belief is valued. */
+int wc_job_build(const uint8_t* root, size_t len, const wc_solve_cfg* cfg, const float* carried, uint32_t ncarried,
+                 wc_job** out);
+int wc_job_info_get(const wc_job* job, wc_job_info* out);
+void wc_job_free(wc_job* job);
+/* Work counts for roofline accounting, 20 slots, [p] = player 0 / 1:
+ * [0+p] regret-matching cells of p's nodes, [2+p] their rows, [4+p] value-
+ * gather entries for traverser p, [6+p] value-gather outputs, [8+p] reach
+ * entries through p's decision cells, [10+p] reach entries through p's draws,
+ * [12+p] reach outputs of mover p, [14+p] network-row configs of p, [16+p]
+ * terminal-leaf configs of p, [18] reach slots, [19] value slots. */
+int wc_job_counts(const wc_job* job, uint64_t* out, int n);
+/* The job's root belief: player 0's then player 1's weights over the root
+ * supports (root_nc0 + root_nc1 floats). */
+int wc_job_root_belief(const wc_job* job, float* out);
+/* Carry layout: nexit + 1 offsets into a carry row, and the exit nodes'
+ * reference ids (network rows then terminal leaves). Either may be NULL. */
+int wc_job_carry_offsets(const wc_job* job, uint32_t* offsets, uint32_t* exit_nodes);
+
+/* ---- batched solves ------------------------------------------------------ */
+/* Synchronous: upload, solve and download n jobs on device 0 of the
+ * context. out has n entries, filled with library-owned arrays. */
+int wc_solve_batch(wc_ctx* ctx, wc_job* const* jobs, size_t n, wc_result* out);
+void wc_result_free(wc_result* r);
+/* Device-resident form: upload once, solve any number of times, read back. */
+int wc_batch_upload(wc_ctx* ctx, int dev_index, wc_job* const* jobs, size_t n, wc_batch** out);
+int wc_batch_solve(wc_batch* b);
+/* A solve with CUDA-event timing per kernel class, in milliseconds:
+ * [0] per-solve network, [1] leaf evaluation, [2] regret-matching rows,
+ * [3] value gathers, [4] reach gathers (+ average), [5] snapshots, [6] Phase 2,
+ * [7] init, [8] whole solve. class_ms needs 9 entries. */
+int wc_batch_solve_profiled(wc_batch* b, double* class_ms, int nclass);
+int wc_batch_download(wc_batch* b, size_t job, float* strategy, float* root_values, uint16_t* carries);
+/* Totals of the batch: node-updates per solve, network-row evaluations per
+ * solve, table bytes, device bytes. */
+void wc_batch_stats(const wc_batch* b, double* node_updates, double* leaf_evals, uint64_t* table_bytes,
+                    uint64_t* device_bytes);
+void wc_batch_free(wc_batch* b);
+
+/* ---- streaming submit / wait ---------------------------------------------- */
+int wc_submit(wc_ctx* ctx, wc_job* job, uint64_t* ticket);
+int wc_wait(wc_ctx* ctx, uint64_t ticket, wc_result* out);
+/* Outstanding submitted cells, for routing (GpuClient::queued_work). */
+uint64_t wc_queued_work(wc_ctx* ctx);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* WC_B200_H */

@@ -4,6 +4,7 @@
 #include <cmath>
 #include <limits>
 
+#include "../war-chest-bot-9000-_b200/csrc/host/detmath.h"
 #include "../war-chest-bot-9000-_b200/csrc/host/pbs.h"
 
 namespace oracle {
@@ -74,10 +75,11 @@ Layout::Layout() {
 constexpr int LN_TRUNK = 2 * BLOCKS, LN_CFG = LN_TRUNK + 1, LN_JOIN = LN_CFG + 1, LN_JOUT = LN_JOIN + JBLOCKS,
               LN_H = LN_JOUT + 1;
 
-float gelu(float x) {
-    float inner = 0.79788456f * (x + 0.044715f * x * x * x);
-    return 0.5f * x * (1.0f + std::tanh(inner));
-}
+// GELU, tanh form (net.rs:126-129). tanh is the deterministic Cephes-method
+// tanh shared with the kernels (within 1 ulp of a correctly rounded tanh; the
+// reference's platform tanhf is within 2), so the fp32 device network can be
+// checked bit for bit.
+float gelu(float x) { return wc::det_gelu(x); }
 
 // net.rs:67-123, the non-Apple loop.
 void gemm(size_t m, size_t n, size_t k, const float* a, size_t lda, const float* b, size_t ldb, float beta,

@@ -1,0 +1,549 @@
+// The C ABI (include/wc_b200.h) over the host builder and the device runtime.
+#include <cmath>
+#include <condition_variable>
+#include <cstring>
+#include <deque>
+#include <map>
+#include <stdexcept>
+#include <thread>
+
+#include "../../include/wc_b200.h"
+#include "cuda/kernels.h"
+#include "host/job.h"
+#include "runtime.h"
+
+using namespace wc;
+
+struct wc_job {
+    std::unique_ptr<JobBlob> blob;
+};
+
+struct wc_batch {
+    std::unique_ptr<Batch> b;
+    wc_ctx* ctx = nullptr;
+};
+
+struct Ticket {
+    wc_job* job = nullptr;
+    bool done = false;
+    int status = 0;
+    std::string err;
+    wc_result res{};
+};
+
+struct wc_ctx {
+    std::vector<std::unique_ptr<DeviceCtx>> devs;
+    // streaming service
+    std::mutex mu;
+    std::condition_variable cv_work, cv_done;
+    std::deque<uint64_t> queue;
+    std::map<uint64_t, Ticket> tickets;
+    uint64_t next_ticket = 1;
+    uint64_t queued_cells = 0;
+    bool stop = false;
+    std::vector<std::thread> workers;
+};
+
+namespace {
+
+int fail(int code, const std::string& msg) {
+    set_error(msg);
+    return code;
+}
+
+template <class F>
+int guarded(F&& f) {
+    try {
+        return f();
+    } catch (const std::bad_alloc&) {
+        return fail(WC_E_NOMEM, "out of host memory");
+    } catch (const std::exception& e) {
+        std::string m = e.what();
+        if (m.find("out of memory") != std::string::npos) return fail(WC_E_NOMEM, m);
+        return fail(WC_E_CUDA, m);
+    }
+}
+
+int upload_weights(DeviceCtx& d, const wc_weights* w) {
+    check(cudaSetDevice(d.device), "set device");
+    if (!w || !w->w) {
+        d.have_net = false;
+        return WC_OK;
+    }
+    if (w->ndims != 1 || !w->dims || w->dims[0] != NET_MODEL_TAG)
+        return fail(WC_E_ARG, "unsupported model format; expected dims [5]");
+    if (w->nw != d.L.w_len || w->nb != d.L.b_len || w->nln != d.L.ln_len)
+        return fail(WC_E_ARG, "weight sizes do not match the v5 layout");
+    if (!d.W) {
+        check(cudaMalloc((void**)&d.W, 4ull * d.L.w_len), "weights");
+        check(cudaMalloc((void**)&d.B, 4ull * d.L.b_len), "biases");
+        check(cudaMalloc((void**)&d.LN, 4ull * d.L.ln_len), "norms");
+    }
+    check(cudaMemcpy(d.W, w->w, 4ull * d.L.w_len, cudaMemcpyHostToDevice), "upload weights");
+    check(cudaMemcpy(d.B, w->b, 4ull * d.L.b_len, cudaMemcpyHostToDevice), "upload biases");
+    check(cudaMemcpy(d.LN, w->ln, 4ull * d.L.ln_len, cudaMemcpyHostToDevice), "upload norms");
+    d.have_net = true;
+    return WC_OK;
+}
+
+void fill_result(Batch& b, size_t j, uint64_t version, wc_result* r) {
+    const JobBlob& jb = *b.jobs[j];
+    const JobImage& J = *jb.img;
+    std::memset(r, 0, sizeof *r);
+    r->ncells = J.ncells;
+    r->strategy = (float*)std::malloc(4ull * std::max<uint32_t>(J.ncells, 1));
+    r->nroots = J.ncarried;
+    r->root_width = J.root_nc[0] + J.root_nc[1];
+    r->root_values = (float*)std::malloc(4ull * std::max<uint64_t>(r->nroots * r->root_width, 1));
+    if (J.cfg.snapshots) {
+        r->carry_snapshots = jb.nsnaps_kept - 1;
+        r->carry_width = jb.carry_width;
+        r->carries = (uint16_t*)std::malloc(2ull * std::max<uint64_t>(r->carry_snapshots * r->carry_width, 1));
+    }
+    r->weight_version = version;
+    download(b, j, r->strategy, r->root_values, r->carries);
+}
+
+bool same_schedule(const SolveCfg& a, const SolveCfg& b) {
+    auto feq = [](float x, float y) { return x == y || (std::isnan(x) && std::isnan(y)); };
+    return a.iters == b.iters && a.snapshots == b.snapshots && feq(a.cfr.alpha, b.cfr.alpha) &&
+           feq(a.cfr.beta, b.cfr.beta) && feq(a.cfr.gamma, b.cfr.gamma) && feq(a.cfr.predict, b.cfr.predict);
+}
+
+// Solve jobs[lo, hi) on one device, filling results.
+void solve_on(DeviceCtx& d, wc_job* const* jobs, size_t lo, size_t hi, wc_result* out) {
+    std::lock_guard<std::mutex> lk(d.mu);
+    std::vector<const JobBlob*> v;
+    for (size_t i = lo; i < hi; ++i) v.push_back(jobs[i]->blob.get());
+    auto b = upload_batch(d, v);
+    enqueue_solve(*b);
+    for (size_t i = lo; i < hi; ++i) fill_result(*b, i - lo, d.version, out + i);
+}
+
+void worker_loop(wc_ctx* ctx, DeviceCtx* d) {
+    for (;;) {
+        std::vector<uint64_t> ids;
+        {
+            std::unique_lock<std::mutex> lk(ctx->mu);
+            ctx->cv_work.wait(lk, [&] { return ctx->stop || !ctx->queue.empty(); });
+            if (ctx->stop) return;
+            // one batch: every queued job that shares the first one's schedule
+            const SolveCfg& c0 = ctx->tickets[ctx->queue.front()].job->blob->img->cfg;
+            for (auto it = ctx->queue.begin(); it != ctx->queue.end();) {
+                if (same_schedule(ctx->tickets[*it].job->blob->img->cfg, c0)) {
+                    ids.push_back(*it);
+                    it = ctx->queue.erase(it);
+                } else {
+                    ++it;
+                }
+            }
+        }
+        std::vector<wc_job*> jobs;
+        {
+            std::lock_guard<std::mutex> lk(ctx->mu);
+            for (uint64_t id : ids) jobs.push_back(ctx->tickets[id].job);
+        }
+        std::vector<wc_result> res(jobs.size());
+        std::string err;
+        int status = WC_OK;
+        try {
+            solve_on(*d, jobs.data(), 0, jobs.size(), res.data());
+        } catch (const std::exception& e) {
+            status = WC_E_CUDA;
+            err = e.what();
+        }
+        {
+            std::lock_guard<std::mutex> lk(ctx->mu);
+            for (size_t i = 0; i < ids.size(); ++i) {
+                Ticket& t = ctx->tickets[ids[i]];
+                t.done = true;
+                t.status = status;
+                t.err = err;
+                t.res = res[i];
+                ctx->queued_cells -= std::min<uint64_t>(ctx->queued_cells, t.job->blob->img->ncells);
+            }
+        }
+        ctx->cv_done.notify_all();
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+int wc_last_error(char* buf, size_t n) {
+    const std::string& e = last_error();
+    if (buf && n) {
+        size_t k = std::min(n - 1, e.size());
+        std::memcpy(buf, e.data(), k);
+        buf[k] = 0;
+    }
+    return (int)e.size();
+}
+
+void wc_net_layout(uint64_t* w_len, uint64_t* b_len, uint64_t* ln_len) {
+    NetLayout L = NetLayout::make();
+    if (w_len) *w_len = L.w_len;
+    if (b_len) *b_len = L.b_len;
+    if (ln_len) *ln_len = L.ln_len;
+}
+
+void wc_set_cap_marker_value(float v) { set_cap_marker_value(v); }
+
+// kind 0: seeded He-normal (every Linear W ~ N(0, 2 / fan_in), the seat and
+// position embeddings ~ N(0, 2 / width)); kind 1: the reference GPU tests'
+// weights, uniform +-0.05 from Rng(seed) (engine/src/gpu/tests.rs:34-48).
+// Biases and the value bias 0, LayerNorm gamma 1 and beta 0.
+int wc_weights_fill(int kind, uint64_t seed, float* w, float* b, float* ln) {
+    if (!w || !b || !ln || kind < 0 || kind > 1) return fail(WC_E_ARG, "bad weights_fill arguments");
+    NetLayout L = NetLayout::make();
+    for (uint32_t i = 0; i < L.b_len; ++i) b[i] = 0.0f;
+    for (uint32_t i = 0; i < L.ln_len; ++i) ln[i] = 0.0f;
+    for (int k = 0; k < NetLayout::N_NORMS; ++k)
+        for (uint32_t i = 0; i < L.norm_w[k]; ++i) ln[L.norm_g[k] + i] = 1.0f;
+    Rng rng(seed);
+    if (kind == 1) {
+        for (uint32_t i = 0; i < L.w_len; ++i)
+            w[i] = ((float)rng.next_u64() / (float)UINT64_MAX - 0.5f) * 0.1f;
+        return WC_OK;
+    }
+    std::vector<float> sd(L.w_len, 0.0f);
+    auto span = [&](const NetSpan& s) {
+        float v = std::sqrt(2.0f / (float)s.i);
+        for (uint32_t q = 0; q < s.i * s.o; ++q) sd[s.w + q] = v;
+    };
+    auto embed = [&](uint32_t at, uint32_t n, uint32_t width) {
+        float v = std::sqrt(2.0f / (float)width);
+        for (uint32_t q = 0; q < n; ++q) sd[at + q] = v;
+    };
+    span(L.card[0]); span(L.card[1]); span(L.pile);
+    embed(L.seat, 2 * NET_TYPE, NET_TYPE);
+    span(L.hex_stem); span(L.tok_stem);
+    embed(L.pos, 37 * NET_C, NET_C);
+    span(L.glob_stem);
+    for (int i = 0; i < NET_BLOCKS; ++i) { span(L.mix[i]); span(L.pool[i]); span(L.out[i]); }
+    span(L.board_out); span(L.cfg1); span(L.cfg_f); span(L.cfg_g); span(L.cfg_m); span(L.join_p); span(L.join_b);
+    for (int i = 0; i < NET_JBLOCKS; ++i) span(L.join_w[i]);
+    span(L.join_out);
+    const double two_pi = 6.283185307179586;
+    for (uint32_t i = 0; i < L.w_len; ++i) {
+        double u1 = 1.0 - rng.unit_f64(), u2 = rng.unit_f64();
+        double z = std::sqrt(-2.0 * std::log(u1)) * std::cos(two_pi * u2);
+        w[i] = sd[i] * (float)z;
+    }
+    return WC_OK;
+}
+
+int wc_init(int ndev, const int* devices, const wc_weights* w, int precise, wc_ctx** out) {
+    if (ndev < 1 || !out) return fail(WC_E_ARG, "need at least one device");
+    return guarded([&] {
+        auto ctx = std::make_unique<wc_ctx>();
+        const Board& bd = board();
+        uint8_t nb[37 * 6], isloc[37];
+        for (int h = 0; h < 37; ++h) {
+            for (int d = 0; d < 6; ++d) nb[h * 6 + d] = bd.neighbors[h][d];
+            isloc[h] = bd.is_location[h] ? 1 : 0;
+        }
+        for (int i = 0; i < ndev; ++i) {
+            auto d = std::make_unique<DeviceCtx>();
+            d->device = devices ? devices[i] : i;
+            d->precise = precise != 0;
+            d->L = NetLayout::make();
+            check(cudaSetDevice(d->device), "set device");
+            check(cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking), "stream");
+            wcdev::net_set_constants(d->L, nb, isloc);
+            int rc = upload_weights(*d, w);
+            if (rc) return rc;
+            d->version = 1;
+            ctx->devs.push_back(std::move(d));
+        }
+        wc_ctx* c = ctx.release();
+        for (auto& d : c->devs) c->workers.emplace_back(worker_loop, c, d.get());
+        *out = c;
+        return (int)WC_OK;
+    });
+}
+
+int wc_publish(wc_ctx* ctx, const wc_weights* w, uint64_t* version) {
+    if (!ctx) return fail(WC_E_ARG, "null context");
+    return guarded([&] {
+        for (auto& d : ctx->devs) {
+            std::lock_guard<std::mutex> lk(d->mu);
+            int rc = upload_weights(*d, w);
+            if (rc) return rc;
+            d->version += 1;
+            if (version) *version = d->version;
+        }
+        return (int)WC_OK;
+    });
+}
+
+int wc_publish_device(wc_ctx* ctx, int dev_index, const float* w, const float* b, const float* ln,
+                      uint64_t* version) {
+    if (!ctx || dev_index < 0 || dev_index >= (int)ctx->devs.size() || !w || !b || !ln)
+        return fail(WC_E_ARG, "bad device publish arguments");
+    return guarded([&] {
+        DeviceCtx& d = *ctx->devs[dev_index];
+        std::lock_guard<std::mutex> lk(d.mu);
+        check(cudaSetDevice(d.device), "set device");
+        if (!d.W) {
+            check(cudaMalloc((void**)&d.W, 4ull * d.L.w_len), "weights");
+            check(cudaMalloc((void**)&d.B, 4ull * d.L.b_len), "biases");
+            check(cudaMalloc((void**)&d.LN, 4ull * d.L.ln_len), "norms");
+        }
+        check(cudaMemcpy(d.W, w, 4ull * d.L.w_len, cudaMemcpyDeviceToDevice), "publish weights");
+        check(cudaMemcpy(d.B, b, 4ull * d.L.b_len, cudaMemcpyDeviceToDevice), "publish biases");
+        check(cudaMemcpy(d.LN, ln, 4ull * d.L.ln_len, cudaMemcpyDeviceToDevice), "publish norms");
+        d.have_net = true;
+        d.version += 1;
+        if (version) *version = d.version;
+        return (int)WC_OK;
+    });
+}
+
+void wc_shutdown(wc_ctx* ctx) {
+    if (!ctx) return;
+    {
+        std::lock_guard<std::mutex> lk(ctx->mu);
+        ctx->stop = true;
+    }
+    ctx->cv_work.notify_all();
+    for (auto& t : ctx->workers) t.join();
+    for (auto& kv : ctx->tickets)
+        if (kv.second.done) wc_result_free(&kv.second.res);
+    for (auto& d : ctx->devs) {
+        cudaSetDevice(d->device);
+        if (d->W) cudaFree(d->W);
+        if (d->B) cudaFree(d->B);
+        if (d->LN) cudaFree(d->LN);
+        if (d->stream) cudaStreamDestroy(d->stream);
+    }
+    delete ctx;
+}
+
+int wc_root_generate(uint64_t seed, int plies, int random_draft, uint8_t* buf, size_t cap, size_t* len) {
+    return guarded([&] {
+        Root r;
+        if (!make_root(seed, plies, random_draft != 0, &r)) return fail(WC_E_ARG, "the game ended before the root");
+        std::vector<uint8_t> b = root_to_bytes(r);
+        if (len) *len = b.size();
+        if (!buf || b.size() > cap) return fail(WC_E_ARG, "root buffer too small");
+        std::memcpy(buf, b.data(), b.size());
+        return (int)WC_OK;
+    });
+}
+
+int wc_job_build(const uint8_t* root, size_t len, const wc_solve_cfg* cfg, const float* carried, uint32_t ncarried,
+                 wc_job** out) {
+    if (!root || !cfg || !out) return fail(WC_E_ARG, "null argument");
+    return guarded([&] {
+        Root r;
+        if (!root_from_bytes(root, len, &r)) return fail(WC_E_ARG, "malformed root bytes");
+        SolveCfg sc;
+        sc.depth = cfg->depth;
+        sc.iters = cfg->iters;
+        sc.snapshots = cfg->snapshots != 0;
+        sc.cfr = {cfg->alpha, cfg->beta, cfg->gamma, cfg->predict};
+        sc.node_cap = (size_t)cfg->node_cap;
+        if (sc.depth < 1 || sc.iters < 0) return fail(WC_E_ARG, "depth must be >= 1 and iters >= 0");
+        auto tree = build_tree(r.s, r.ctx, sc, r.bel);
+        if (tree->capped) return fail(WC_E_CAPPED, "the tree hit the node cap");
+        size_t w = tree->nc(0, 0) + tree->nc(0, 1);
+        std::vector<float> car;
+        if (ncarried) car.assign(carried, carried + (size_t)ncarried * w);
+        auto img = flatten(*tree, car, ncarried);
+        auto j = std::make_unique<wc_job>();
+        j->blob = make_blob(std::move(img));
+        *out = j.release();
+        return (int)WC_OK;
+    });
+}
+
+int wc_job_info_get(const wc_job* job, wc_job_info* o) {
+    if (!job || !o) return fail(WC_E_ARG, "null argument");
+    const JobImage& J = *job->blob->img;
+    o->nodes = J.nodes;
+    o->cells = J.ncells;
+    o->net_rows = J.nrows_net;
+    o->terminal_leaves = J.nterm;
+    o->configs = J.ncfg;
+    o->levels = J.nlevels;
+    o->root_nc0 = J.root_nc[0];
+    o->root_nc1 = J.root_nc[1];
+    o->ncarried = J.ncarried;
+    o->carry_snapshots = J.cfg.snapshots ? job->blob->nsnaps_kept - 1 : 0;
+    o->carry_width = job->blob->carry_width;
+    o->table_bytes = job->blob->bytes;
+    return WC_OK;
+}
+
+void wc_job_free(wc_job* job) { delete job; }
+
+int wc_job_counts(const wc_job* job, uint64_t* out, int n) {
+    if (!job || !out || n < 20) return fail(WC_E_ARG, "wc_job_counts needs 20 slots");
+    const JobImage& J = *job->blob->img;
+    for (int i = 0; i < 20; ++i) out[i] = 0;
+    for (uint32_t lv = 0; lv < J.nlevels; ++lv)
+        for (int p = 0; p < 2; ++p) {
+            const LevelRange& rr = J.rows_rng[lv * 2 + p];
+            out[0 + p] += J.row_off[rr.first + rr.count] - J.row_off[rr.first];
+            out[2 + p] += rr.count;
+            const LevelRange& vr = J.vg_rng[lv * 2 + p];
+            out[4 + p] += J.vg_start[vr.first + vr.count] - J.vg_start[vr.first];
+            out[6 + p] += vr.count;
+            if (lv == 0) continue;
+            const LevelRange& gr = J.rg_rng[lv * 2 + p];
+            for (uint32_t e = J.rg_start[gr.first]; e < J.rg_start[gr.first + gr.count]; ++e) {
+                if (J.rge_w[e] < J.ncells) out[8 + p] += 1;
+                else out[10 + p] += 1;
+            }
+            out[12 + p] += gr.count;
+        }
+    for (uint32_t r = 0; r < J.nrows_net; ++r) { out[14] += J.lr_nc[2 * r]; out[15] += J.lr_nc[2 * r + 1]; }
+    for (uint32_t k = 0; k < J.nterm; ++k) { out[16] += J.tl_nc[2 * k]; out[17] += J.tl_nc[2 * k + 1]; }
+    out[18] = J.reach_len;
+    out[19] = (uint64_t)J.val_len[0] + J.val_len[1];
+    return WC_OK;
+}
+
+int wc_job_root_belief(const wc_job* job, float* out) {
+    if (!job || !out) return fail(WC_E_ARG, "null argument");
+    const JobImage& J = *job->blob->img;
+    std::memcpy(out, J.root_belief.data(), 4 * J.root_belief.size());
+    return WC_OK;
+}
+
+int wc_job_carry_offsets(const wc_job* job, uint32_t* out, uint32_t* exit_nodes) {
+    if (!job) return fail(WC_E_ARG, "null argument");
+    const JobBlob& jb = *job->blob;
+    if (out) std::memcpy(out, jb.host + jb.off[JobBlob::CARRY_OFF], 4ull * (jb.nexit + 1));
+    if (exit_nodes) std::memcpy(exit_nodes, jb.img->exit_nodes.data(), 4ull * jb.nexit);
+    return WC_OK;
+}
+
+int wc_solve_batch(wc_ctx* ctx, wc_job* const* jobs, size_t n, wc_result* out) {
+    if (!ctx || (!jobs && n) || (!out && n)) return fail(WC_E_ARG, "null argument");
+    for (size_t i = 0; i < n; ++i)
+        if (!jobs[i] || !same_schedule(jobs[i]->blob->img->cfg, jobs[0]->blob->img->cfg))
+            return fail(WC_E_ARG, "every job of a batch needs the same iterations, snapshots and CFR rule");
+    return guarded([&] {
+        size_t nd = ctx->devs.size();
+        std::vector<std::thread> th;
+        std::vector<std::string> errs(nd);
+        for (size_t d = 0; d < nd; ++d) {
+            size_t lo = n * d / nd, hi = n * (d + 1) / nd;
+            if (lo == hi) continue;
+            th.emplace_back([&, d, lo, hi] {
+                try {
+                    solve_on(*ctx->devs[d], jobs, lo, hi, out);
+                } catch (const std::exception& e) {
+                    errs[d] = e.what();
+                }
+            });
+        }
+        for (auto& t : th) t.join();
+        for (auto& e : errs)
+            if (!e.empty()) throw std::runtime_error(e);
+        return (int)WC_OK;
+    });
+}
+
+void wc_result_free(wc_result* r) {
+    if (!r) return;
+    std::free(r->strategy);
+    std::free(r->root_values);
+    std::free(r->carries);
+    std::memset(r, 0, sizeof *r);
+}
+
+int wc_batch_upload(wc_ctx* ctx, int dev_index, wc_job* const* jobs, size_t n, wc_batch** out) {
+    if (!ctx || dev_index < 0 || dev_index >= (int)ctx->devs.size() || !out) return fail(WC_E_ARG, "bad arguments");
+    for (size_t i = 0; i < n; ++i)
+        if (!jobs[i] || !same_schedule(jobs[i]->blob->img->cfg, jobs[0]->blob->img->cfg))
+            return fail(WC_E_ARG, "every job of a batch needs the same iterations, snapshots and CFR rule");
+    return guarded([&] {
+        std::vector<const JobBlob*> v;
+        for (size_t i = 0; i < n; ++i) v.push_back(jobs[i]->blob.get());
+        auto b = std::make_unique<wc_batch>();
+        b->ctx = ctx;
+        b->b = upload_batch(*ctx->devs[dev_index], v);
+        *out = b.release();
+        return (int)WC_OK;
+    });
+}
+
+int wc_batch_solve(wc_batch* b) {
+    if (!b) return fail(WC_E_ARG, "null batch");
+    return guarded([&] {
+        std::lock_guard<std::mutex> lk(b->b->dev->mu);
+        enqueue_solve(*b->b);
+        check(cudaStreamSynchronize(b->b->dev->stream), "batch solve");
+        return (int)WC_OK;
+    });
+}
+
+int wc_batch_solve_profiled(wc_batch* b, double* class_ms, int nclass) {
+    if (!b || !class_ms || nclass < N_TC) return fail(WC_E_ARG, "bad profile arguments");
+    return guarded([&] {
+        std::lock_guard<std::mutex> lk(b->b->dev->mu);
+        b->b->profile = true;
+        enqueue_solve(*b->b);
+        read_profile(*b->b, class_ms);
+        b->b->profile = false;
+        return (int)WC_OK;
+    });
+}
+
+int wc_batch_download(wc_batch* b, size_t job, float* strategy, float* root_values, uint16_t* carries) {
+    if (!b || job >= b->b->jobs.size()) return fail(WC_E_ARG, "bad batch or job index");
+    return guarded([&] {
+        download(*b->b, job, strategy, root_values, carries);
+        return (int)WC_OK;
+    });
+}
+
+void wc_batch_stats(const wc_batch* b, double* node_updates, double* leaf_evals, uint64_t* table_bytes,
+                    uint64_t* device_bytes) {
+    if (!b) return;
+    if (node_updates) *node_updates = b->b->node_updates;
+    if (leaf_evals) *leaf_evals = b->b->leaf_evals;
+    if (table_bytes) *table_bytes = b->b->table_bytes;
+    if (device_bytes) *device_bytes = b->b->dbytes;
+}
+
+void wc_batch_free(wc_batch* b) { delete b; }
+
+int wc_submit(wc_ctx* ctx, wc_job* job, uint64_t* ticket) {
+    if (!ctx || !job || !ticket) return fail(WC_E_ARG, "null argument");
+    {
+        std::lock_guard<std::mutex> lk(ctx->mu);
+        uint64_t id = ctx->next_ticket++;
+        ctx->tickets[id].job = job;
+        ctx->queue.push_back(id);
+        ctx->queued_cells += job->blob->img->ncells;
+        *ticket = id;
+    }
+    ctx->cv_work.notify_one();
+    return WC_OK;
+}
+
+int wc_wait(wc_ctx* ctx, uint64_t ticket, wc_result* out) {
+    if (!ctx || !out) return fail(WC_E_ARG, "null argument");
+    std::unique_lock<std::mutex> lk(ctx->mu);
+    auto it = ctx->tickets.find(ticket);
+    if (it == ctx->tickets.end()) return fail(WC_E_STATE, "unknown ticket");
+    ctx->cv_done.wait(lk, [&] { return ctx->tickets[ticket].done; });
+    Ticket t = ctx->tickets[ticket];
+    ctx->tickets.erase(ticket);
+    if (t.status) return fail(t.status, t.err);
+    *out = t.res;
+    return WC_OK;
+}
+
+uint64_t wc_queued_work(wc_ctx* ctx) {
+    if (!ctx) return 0;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    return ctx->queued_cells;
+}
+
+}  // extern "C"

@@ -1,0 +1,43 @@
+// Kernel launchers, called by the runtime.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "../host/netlayout.h"
+#include "device.h"
+
+namespace wcdev {
+
+enum StratSel { STRAT_CUR = 0, STRAT_SNAP = 1 };
+enum BackMode { BACK_REGRET = 0, BACK_VALUE = 1, BACK_BEST = 2 };
+
+// cfr_kernels.cu
+void launch_init_rows(const JobDev* jobs, const WorkItem* items, uint32_t n, cudaStream_t s);
+void launch_rows(const JobDev* jobs, const WorkItem* items, uint32_t n, int p, int mode, int strat_sel, float da,
+                 float db, float predict, cudaStream_t s);
+void launch_vgather(const JobDev* jobs, const WorkItem* items, uint32_t n, int p, cudaStream_t s);
+void launch_rgather(const JobDev* jobs, const WorkItem* items, uint32_t n, int strat_sel, int which_reach,
+                    int sum_update, float dg, cudaStream_t s);
+void launch_terminal(const JobDev* jobs, const WorkItem* items, uint32_t n, int p, cudaStream_t s);
+void launch_netrows_zero(const JobDev* jobs, const WorkItem* items, uint32_t n, int p, cudaStream_t s);
+void launch_seed_root(const JobDev* jobs, uint32_t njobs, int which_reach, int carried_index, cudaStream_t s);
+void launch_snapshot(const JobDev* jobs, const WorkItem* items, uint32_t n, int t0, int t1, cudaStream_t s);
+void launch_copy_cur_to_snap(const JobDev* jobs, const WorkItem* items, uint32_t n, cudaStream_t s);
+void launch_unsort(const JobDev* jobs, const WorkItem* items, uint32_t n, cudaStream_t s);
+void launch_collect_root(const JobDev* jobs, uint32_t njobs, int root_index, int p, cudaStream_t s);
+void launch_carry(const JobDev* jobs, const WorkItem* items, uint32_t n, int snap_index, cudaStream_t s);
+
+// net_precise.cu
+void net_set_constants(const wc::NetLayout& L, const uint8_t* neighbors, const uint8_t* is_location);
+void launch_cards(const JobDev* jobs, uint32_t njobs, const float* W, const float* B, cudaStream_t s);
+void launch_trunk(const JobDev* jobs, const uint32_t* row_job, const uint32_t* row_local, uint32_t nrows,
+                  const float* W, const float* B, const float* LN, cudaStream_t s);
+void launch_configs(const JobDev* jobs, const uint32_t* cfg_job, const uint32_t* cfg_local, uint32_t ncfg,
+                    const float* W, const float* B, const float* LN, cudaStream_t s);
+void launch_pool(const JobDev* jobs, const uint32_t* row_job, const uint32_t* row_local, uint32_t nrows, int mask,
+                 cudaStream_t s);
+void launch_join_readout(const JobDev* jobs, const uint32_t* row_job, const uint32_t* row_local, uint32_t nrows,
+                         int p, const float* W, const float* B, const float* LN, cudaStream_t s);
+
+}  // namespace wcdev

@@ -1,0 +1,102 @@
+// Device runtime: per-device weight banks, job blobs, device batches and the
+// solve schedule. This replaces the reference's GPU executor
+// (engine/src/gpu/device.rs:596-754) and its wave packer (gpu/wave.rs).
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "cuda/device.h"
+#include "host/job.h"
+#include "host/netlayout.h"
+
+namespace wc {
+
+struct DeviceCtx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    float* W = nullptr;
+    float* B = nullptr;
+    float* LN = nullptr;
+    bool have_net = false;
+    bool precise = true;
+    uint64_t version = 0;
+    NetLayout L;
+    std::mutex mu;  // one batch at a time per device
+};
+
+// A job's flattened tables in one pinned host blob (device copies keep the
+// same layout).
+struct JobBlob {
+    std::unique_ptr<JobImage> img;
+    uint8_t* host = nullptr;
+    bool pinned = false;
+    size_t bytes = 0;
+    enum Arr {
+        CELL_VIDX, ROW_OFF, ROW_PLAYER, VG_START, VGE_IDX, VGE_W, RG_START, RGE_SRC, RGE_W, DRAWP, CELL_REF,
+        LR_RIDX, LR_NC, LR_VIDX, LEAF_COFF, LEAF_CIDX, TL_RIDX, TL_NC, TL_VIDX, TL_UTIL0, GPU_ROWS, CPHI,
+        CPLAYER, CARD_FEAT, ROOT_BELIEF, CARRIED, CARRY_OFF, N_ARR
+    };
+    size_t off[N_ARR] = {};
+    uint32_t nexit = 0, carry_width = 0, nsnaps_kept = 0;
+    ~JobBlob();
+};
+
+std::unique_ptr<JobBlob> make_blob(std::unique_ptr<JobImage> img);
+
+struct Batch {
+    DeviceCtx* dev = nullptr;
+    std::vector<const JobBlob*> jobs;
+    uint8_t* dmem = nullptr;
+    size_t dbytes = 0;
+    std::vector<wcdev::JobDev> hj;
+    wcdev::JobDev* d_jobs = nullptr;
+    struct Range { uint32_t off = 0, n = 0; };
+    std::vector<wcdev::WorkItem> items;  // host copy
+    wcdev::WorkItem* d_items = nullptr;
+    uint32_t nlevels = 0;
+    std::vector<Range> rows, vg, rg;  // [level * 2 + player]
+    Range rows_all, cells_all, term_all, netrows_all, exits_all;
+    uint32_t* d_row_job = nullptr;
+    uint32_t* d_row_local = nullptr;
+    uint32_t* d_cfg_job = nullptr;
+    uint32_t* d_cfg_local = nullptr;
+    uint32_t total_rows = 0, total_cfgs = 0, max_carried = 0;
+    std::vector<size_t> out_off;  // per job: strategy, roots, carry offsets in dmem
+    double node_updates = 0.0;    // sum over jobs of nodes * iters
+    double leaf_evals = 0.0;      // network-row joins per solve
+    size_t table_bytes = 0;
+    // Optional per-class device timing of a solve (CUDA events on the
+    // runtime's stream): class ids are the TimeClass values.
+    bool profile = false;
+    std::vector<cudaEvent_t> events;
+    std::vector<int> event_class;  // one entry per (start, end) pair
+    size_t events_used = 0;
+    cudaEvent_t marks[3] = {nullptr, nullptr, nullptr};  // solve start, Phase 2 start, solve end
+    ~Batch();
+};
+
+// Set the error string of the calling thread.
+void set_error(const std::string& e);
+const std::string& last_error();
+
+enum TimeClass {
+    TC_NET_SOLVE = 0, TC_LEAF = 1, TC_ROWS = 2, TC_VGATHER = 3, TC_REACH = 4, TC_SNAP = 5, TC_PHASE2 = 6,
+    TC_INIT = 7, TC_TOTAL = 8, N_TC = 9
+};
+// After a profiled solve has finished: summed milliseconds per class.
+void read_profile(Batch& b, double* ms /* N_TC */);
+
+std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobBlob*>& jobs);
+// Run the whole solve on the device (asynchronous on dev.stream).
+void enqueue_solve(Batch& b);
+// Copy one job's results to host buffers (synchronous). Any pointer may be null.
+void download(Batch& b, size_t job, float* strategy, float* roots, uint16_t* carries);
+
+void check(cudaError_t e, const char* what);
+
+}  // namespace wc

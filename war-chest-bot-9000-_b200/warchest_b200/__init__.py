@@ -1,0 +1,388 @@
+"""Python mirror of the reference's solve-service API over the C ABI.
+
+The reference drives its GPU solver from Rust (engine/src/gpu/client.rs:
+spawn / GpuClient::{submit, set_weights, queued_work} / SolveHandle::wait /
+SolveResult; engine/src/serialize.rs: PackedJob). This module exposes the same
+names and meanings over ``lib/libwcb200.so`` (include/wc_b200.h), so callers
+and tests read like the reference's own. There is no CPU fallback: every
+solve runs the CUDA kernels, and loading fails loudly if the library is
+missing.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+import os
+from dataclasses import dataclass, field
+from typing import List, Optional, Sequence
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(os.path.dirname(_HERE), "lib", "libwcb200.so")
+
+WC_E_CAPPED = 3
+
+
+class SolveError(RuntimeError):
+    """A nonzero status from the C ABI (the reference's Err(String))."""
+
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"[{code}] {msg}")
+        self.code = code
+
+
+class _SolveCfg(C.Structure):
+    _fields_ = [("depth", C.c_int32), ("iters", C.c_int32), ("snapshots", C.c_int32), ("reserved", C.c_int32),
+                ("alpha", C.c_float), ("beta", C.c_float), ("gamma", C.c_float), ("predict", C.c_float),
+                ("node_cap", C.c_uint64)]
+
+
+class _Weights(C.Structure):
+    _fields_ = [("ndims", C.c_uint32), ("dims", C.POINTER(C.c_uint32)), ("w", C.c_void_p), ("nw", C.c_uint64),
+                ("b", C.c_void_p), ("nb", C.c_uint64), ("ln", C.c_void_p), ("nln", C.c_uint64)]
+
+
+class _JobInfo(C.Structure):
+    _fields_ = [(n, C.c_uint64) for n in ("nodes", "cells", "net_rows", "terminal_leaves", "configs", "levels",
+                                          "root_nc0", "root_nc1", "ncarried", "carry_snapshots", "carry_width",
+                                          "table_bytes")]
+
+
+class _Result(C.Structure):
+    _fields_ = [("strategy", C.POINTER(C.c_float)), ("ncells", C.c_uint64),
+                ("root_values", C.POINTER(C.c_float)), ("nroots", C.c_uint64), ("root_width", C.c_uint64),
+                ("carries", C.POINTER(C.c_uint16)), ("carry_snapshots", C.c_uint64), ("carry_width", C.c_uint64),
+                ("weight_version", C.c_uint64)]
+
+
+def _load() -> C.CDLL:
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"{LIB_PATH} is not built; run __graft_entry__.build()")
+    lib = C.CDLL(LIB_PATH)
+    P, VP, U64, I = C.POINTER, C.c_void_p, C.c_uint64, C.c_int
+    sig = {
+        "wc_init": (I, [I, P(C.c_int), P(_Weights), I, P(VP)]),
+        "wc_publish": (I, [VP, P(_Weights), P(U64)]),
+        "wc_publish_device": (I, [VP, I, VP, VP, VP, P(U64)]),
+        "wc_shutdown": (None, [VP]),
+        "wc_last_error": (I, [C.c_char_p, C.c_size_t]),
+        "wc_net_layout": (None, [P(U64), P(U64), P(U64)]),
+        "wc_weights_fill": (I, [I, U64, VP, VP, VP]),
+        "wc_set_cap_marker_value": (None, [C.c_float]),
+        "wc_root_generate": (I, [U64, I, I, C.c_char_p, C.c_size_t, P(C.c_size_t)]),
+        "wc_job_build": (I, [C.c_char_p, C.c_size_t, P(_SolveCfg), VP, C.c_uint32, P(VP)]),
+        "wc_job_info_get": (I, [VP, P(_JobInfo)]),
+        "wc_job_free": (None, [VP]),
+        "wc_job_root_belief": (I, [VP, VP]),
+        "wc_job_counts": (I, [VP, P(U64), I]),
+        "wc_job_carry_offsets": (I, [VP, VP, VP]),
+        "wc_solve_batch": (I, [VP, P(VP), C.c_size_t, P(_Result)]),
+        "wc_result_free": (None, [P(_Result)]),
+        "wc_batch_upload": (I, [VP, I, P(VP), C.c_size_t, P(VP)]),
+        "wc_batch_solve": (I, [VP]),
+        "wc_batch_solve_profiled": (I, [VP, P(C.c_double), I]),
+        "wc_batch_download": (I, [VP, C.c_size_t, VP, VP, VP]),
+        "wc_batch_stats": (None, [VP, P(C.c_double), P(C.c_double), P(U64), P(U64)]),
+        "wc_batch_free": (None, [VP]),
+        "wc_submit": (I, [VP, VP, P(U64)]),
+        "wc_wait": (I, [VP, U64, P(_Result)]),
+        "wc_queued_work": (U64, [VP]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+_lib: Optional[C.CDLL] = None
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        _lib = _load()
+    return _lib
+
+
+def _check(rc: int) -> None:
+    if rc != 0:
+        buf = C.create_string_buffer(4096)
+        lib().wc_last_error(buf, 4096)
+        raise SolveError(rc, buf.value.decode(errors="replace"))
+
+
+# ----------------------------------------------------------------- config
+
+INF = float("inf")
+
+
+@dataclass(frozen=True)
+class Cfr:
+    """The discounting rule (engine/src/search.rs:133-185)."""
+    alpha: float
+    beta: float
+    gamma: float
+    predict: float
+
+
+Cfr.LINEAR = Cfr(1.0, 1.0, 1.0, 0.0)
+Cfr.PLUS = Cfr(INF, -INF, 2.0, 0.0)
+Cfr.DISCOUNTED = Cfr(1.5, 0.0, 2.0, 0.0)
+Cfr.PREDICTIVE = Cfr(INF, -INF, 2.0, 1.0)
+Cfr.SIMPLE_ASYM = Cfr(INF, -INF, 2.0, 1.0 / 3.0)
+Cfr.NAMED = {"linear": Cfr.LINEAR, "plus": Cfr.PLUS, "dcfr": Cfr.DISCOUNTED, "pcfr": Cfr.PREDICTIVE,
+             "sapcfr": Cfr.SIMPLE_ASYM}
+
+
+@dataclass(frozen=True)
+class Cfg:
+    """search::Cfg (engine/src/search.rs:50-95)."""
+    depth: int = 1
+    iters: int = 64
+    snapshots: bool = True
+    cfr: Cfr = Cfr.LINEAR
+    node_cap: int = 0
+
+    def _c(self) -> _SolveCfg:
+        return _SolveCfg(self.depth, self.iters, int(self.snapshots), 0, self.cfr.alpha, self.cfr.beta,
+                         self.cfr.gamma, self.cfr.predict, self.node_cap)
+
+
+def snapshot_iters(iters: int) -> List[int]:
+    """Kept iterations: 0, the powers of two and the final one (search.rs:102-110)."""
+    return [t for t in range(iters + 1) if t == 0 or (t & (t - 1)) == 0 or t == iters]
+
+
+def set_cap_marker_value(v: float) -> None:
+    lib().wc_set_cap_marker_value(v)
+
+
+def generate_root(seed: int, plies: int = 20, random_draft: bool = True) -> bytes:
+    """A seeded solve-site root: State bytes and both beliefs."""
+    cap = 1 << 20
+    buf = C.create_string_buffer(cap)
+    n = C.c_size_t()
+    _check(lib().wc_root_generate(seed, plies, int(random_draft), buf, cap, C.byref(n)))
+    return buf.raw[: n.value]
+
+
+# ---------------------------------------------------------------- weights
+
+def net_layout():
+    w, b, l = C.c_uint64(), C.c_uint64(), C.c_uint64()
+    lib().wc_net_layout(C.byref(w), C.byref(b), C.byref(l))
+    return w.value, b.value, l.value
+
+
+def seeded_weights(kind: str = "he", seed: int = 0):
+    """(dims, w, b, ln) for the v5 blob: "he" (seeded He-normal) or "test"
+    (the reference GPU tests' blob, engine/src/gpu/tests.rs:34-48)."""
+    nw, nb, nl = net_layout()
+    w = np.zeros(nw, np.float32)
+    b = np.zeros(nb, np.float32)
+    ln = np.zeros(nl, np.float32)
+    k = {"he": 0, "test": 1}[kind]
+    _check(lib().wc_weights_fill(k, seed, w.ctypes.data, b.ctypes.data, ln.ctypes.data))
+    return [5], w, b, ln
+
+
+def _weights_struct(dims, w, b, ln):
+    if w is None:
+        return None, None
+    d = (C.c_uint32 * len(dims))(*dims)
+    ws = _Weights(len(dims), d, w.ctypes.data, w.size, b.ctypes.data, b.size, ln.ctypes.data, ln.size)
+    return ws, (d, w, b, ln)
+
+
+# ------------------------------------------------------------------- jobs
+
+class PackedJob:
+    """One subgame solve (engine/src/serialize.rs:143-150), flattened."""
+
+    def __init__(self, handle: int, root: bytes, cfg: Cfg):
+        self._h = C.c_void_p(handle)
+        self.root = root
+        self.cfg = cfg
+        info = _JobInfo()
+        _check(lib().wc_job_info_get(self._h, C.byref(info)))
+        self.info = {n: getattr(info, n) for n, _ in _JobInfo._fields_}
+
+    @classmethod
+    def from_root(cls, root: bytes, cfg: Cfg, carried: Optional[np.ndarray] = None) -> "PackedJob":
+        h = C.c_void_p()
+        if carried is not None:
+            carried = np.ascontiguousarray(carried, np.float32)
+            n = carried.shape[0]
+            ptr = carried.ctypes.data
+        else:
+            n, ptr = 0, None
+        _check(lib().wc_job_build(root, len(root), C.byref(cfg._c()), ptr, n, C.byref(h)))
+        return cls(h.value, root, cfg)
+
+    def counts(self) -> np.ndarray:
+        """Per-player work counts (see wc_job_counts)."""
+        out = (C.c_uint64 * 20)()
+        _check(lib().wc_job_counts(self._h, out, 20))
+        return np.array(list(out), np.int64)
+
+    def root_belief(self) -> np.ndarray:
+        """Both players' root weights, player 0 first."""
+        out = np.zeros(self.info["root_nc0"] + self.info["root_nc1"], np.float32)
+        _check(lib().wc_job_root_belief(self._h, out.ctypes.data))
+        return out
+
+    def carry_layout(self):
+        """(offsets over the exit nodes, exit node ids) of a carry row."""
+        n = self.info["net_rows"] + self.info["terminal_leaves"]
+        off = np.zeros(n + 1, np.uint32)
+        ids = np.zeros(max(n, 1), np.uint32)
+        _check(lib().wc_job_carry_offsets(self._h, off.ctypes.data, ids.ctypes.data))
+        return off, ids[:n]
+
+    def __del__(self):
+        if getattr(self, "_h", None) and self._h.value and _lib is not None:
+            _lib.wc_job_free(self._h)
+            self._h = C.c_void_p()
+
+
+@dataclass
+class SolveResult:
+    """engine/src/gpu/client.rs:115-122."""
+    strategy: np.ndarray
+    root_values: List[List[np.ndarray]]
+    carries: Optional[np.ndarray]
+    weight_version: int
+
+
+def _take_result(r: _Result, job: PackedJob) -> SolveResult:
+    strat = np.ctypeslib.as_array(r.strategy, (r.ncells,)).copy() if r.ncells else np.zeros(0, np.float32)
+    n0 = job.info["root_nc0"]
+    roots = np.ctypeslib.as_array(r.root_values, (r.nroots * r.root_width,)).copy().reshape(r.nroots, r.root_width)
+    rv = [[row[:n0].copy(), row[n0:].copy()] for row in roots]
+    carries = None
+    if r.carry_snapshots:
+        carries = np.ctypeslib.as_array(r.carries, (r.carry_snapshots * r.carry_width,)).copy().view(np.float16)
+        carries = carries.reshape(r.carry_snapshots, r.carry_width)
+    out = SolveResult(strat, rv, carries, r.weight_version)
+    lib().wc_result_free(C.byref(r))
+    return out
+
+
+# ---------------------------------------------------------------- service
+
+class SolveHandle:
+    def __init__(self, client: "GpuClient", ticket: int, job: PackedJob):
+        self._client, self._ticket, self._job = client, ticket, job
+
+    def wait(self) -> SolveResult:
+        r = _Result()
+        _check(lib().wc_wait(self._client._ctx, self._ticket, C.byref(r)))
+        return _take_result(r, self._job)
+
+
+class GpuClient:
+    """engine/src/gpu/client.rs: submit / set_weights / queued_work."""
+
+    def __init__(self, ctx: int):
+        self._ctx = C.c_void_p(ctx)
+
+    def submit(self, job: PackedJob) -> SolveHandle:
+        t = C.c_uint64()
+        _check(lib().wc_submit(self._ctx, job._h, C.byref(t)))
+        return SolveHandle(self, t.value, job)
+
+    def set_weights(self, dims, w, b, ln) -> int:
+        ws, keep = _weights_struct(dims, w, b, ln)
+        v = C.c_uint64()
+        _check(lib().wc_publish(self._ctx, C.byref(ws) if ws else None, C.byref(v)))
+        return v.value
+
+    def set_weights_device(self, dev_index: int, w_ptr: int, b_ptr: int, ln_ptr: int) -> int:
+        v = C.c_uint64()
+        _check(lib().wc_publish_device(self._ctx, dev_index, w_ptr, b_ptr, ln_ptr, C.byref(v)))
+        return v.value
+
+    def queued_work(self) -> int:
+        return lib().wc_queued_work(self._ctx)
+
+    def solve_batch(self, jobs: Sequence[PackedJob]) -> List[SolveResult]:
+        n = len(jobs)
+        arr = (C.c_void_p * n)(*[j._h.value for j in jobs])
+        res = (_Result * n)()
+        _check(lib().wc_solve_batch(self._ctx, arr, n, res))
+        return [_take_result(res[i], jobs[i]) for i in range(n)]
+
+    def upload(self, jobs: Sequence[PackedJob], dev_index: int = 0) -> "DeviceBatch":
+        n = len(jobs)
+        arr = (C.c_void_p * n)(*[j._h.value for j in jobs])
+        h = C.c_void_p()
+        _check(lib().wc_batch_upload(self._ctx, dev_index, arr, n, C.byref(h)))
+        return DeviceBatch(h.value, list(jobs))
+
+    def close(self) -> None:
+        if self._ctx.value:
+            lib().wc_shutdown(self._ctx)
+            self._ctx = C.c_void_p()
+
+
+class DeviceBatch:
+    """A batch resident on one device: solve repeatedly, read back per job."""
+
+    def __init__(self, handle: int, jobs: List[PackedJob]):
+        self._h = C.c_void_p(handle)
+        self.jobs = jobs
+
+    def solve(self) -> None:
+        _check(lib().wc_batch_solve(self._h))
+
+    TIME_CLASSES = ["net_solve", "leaf", "rows", "vgather", "reach", "snapshot", "phase2", "init", "total"]
+
+    def solve_profiled(self) -> dict:
+        """One solve with per-class CUDA-event timings (ms) on the runtime's stream."""
+        ms = (C.c_double * 9)()
+        _check(lib().wc_batch_solve_profiled(self._h, ms, 9))
+        return dict(zip(self.TIME_CLASSES, list(ms)))
+
+    def stats(self):
+        nu, le = C.c_double(), C.c_double()
+        tb, db = C.c_uint64(), C.c_uint64()
+        lib().wc_batch_stats(self._h, C.byref(nu), C.byref(le), C.byref(tb), C.byref(db))
+        return {"node_updates": nu.value, "leaf_evals": le.value, "table_bytes": tb.value, "device_bytes": db.value}
+
+    def result(self, j: int) -> SolveResult:
+        job = self.jobs[j]
+        info = job.info
+        strat = np.zeros(info["cells"], np.float32)
+        width = info["root_nc0"] + info["root_nc1"]
+        roots = np.zeros(info["ncarried"] * width, np.float32)
+        carries = np.zeros(max(info["carry_snapshots"] * info["carry_width"], 1), np.uint16)
+        _check(lib().wc_batch_download(self._h, j, strat.ctypes.data, roots.ctypes.data, carries.ctypes.data))
+        roots = roots.reshape(info["ncarried"], width)
+        n0 = info["root_nc0"]
+        c = None
+        if info["carry_snapshots"]:
+            c = carries[: info["carry_snapshots"] * info["carry_width"]].view(np.float16)
+            c = c.reshape(info["carry_snapshots"], info["carry_width"])
+        return SolveResult(strat, [[r[:n0].copy(), r[n0:].copy()] for r in roots], c, 0)
+
+    def free(self) -> None:
+        if self._h.value:
+            lib().wc_batch_free(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        if getattr(self, "_h", None) is not None and self._h.value and _lib is not None:
+            self.free()
+
+
+def spawn(device, dims=None, w=None, b=None, ln=None, precise: bool = True) -> GpuClient:
+    """gpu::service::spawn (engine/src/gpu/service.rs:55-82). `device` is an
+    index or a list of indices; w=None runs without a value network."""
+    devs = [device] if isinstance(device, int) else list(device)
+    arr = (C.c_int * len(devs))(*devs)
+    ws, keep = _weights_struct(dims, w, b, ln)
+    h = C.c_void_p()
+    _check(lib().wc_init(len(devs), arr, C.byref(ws) if ws else None, int(precise), C.byref(h)))
+    return GpuClient(h.value)
