@@ -161,23 +161,16 @@ def peaks():
 
 def cpu_baseline(wc, oracle, cfg, weights, seeds, budget_s):
     """The oracle (CPU restatement of the reference solver) on a bounded
-    sample: subgames solved on every host thread until the budget is spent."""
+    sample: one workload subgame per host thread, timed through the solver
+    build and the first iterations (all the once-per-solve network work),
+    then extrapolated to the full iteration count (oracle_bench)."""
     threads = os.cpu_count() or 1
-    done_nu, done_t, used = 0.0, 0.0, 0
-    chunk = max(threads, 1)
-    i = 0
-    while done_t < budget_s and i < len(seeds):
-        batch = seeds[i:i + chunk]
-        roots = [wc.generate_root(s, PLIES) for s in batch]
-        t0 = time.perf_counter()
-        nu = oracle.solve_many(roots, cfg, weights, threads)
-        done_t += time.perf_counter() - t0
-        done_nu += nu
-        used += len(batch)
-        i += chunk
-    return {"value": done_nu / done_t if done_t > 0 else 0.0, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{used} of the workload's subgames (seeds {seeds[0]}..{seeds[0] + used - 1}), "
-                      f"depth {cfg.depth}, {cfg.iters} CFR+ iterations, fp32 network, {done_t:.1f} s"}
+    roots = [wc.generate_root(s, PLIES) for s in seeds[:threads]]
+    rate, wall, m = oracle.bench(roots, cfg, weights, threads, 2, 4)
+    return {"value": rate, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{m} subgames of the workload (seeds {seeds[0]}..{seeds[0] + m - 1}), one per thread: "
+                      f"build + 2 CFR+ iterations (incl. the per-solve network) and 4 more timed, the "
+                      f"{cfg.iters}-iteration solve extrapolated; {wall:.1f} s wall"}
 
 
 def main():

@@ -152,6 +152,12 @@ void wc_batch_stats(const wc_batch* b, double* node_updates, double* leaf_evals,
                     uint64_t* device_bytes);
 void wc_batch_free(wc_batch* b);
 
+/* ---- diagnostics --------------------------------------------------------- */
+/* D[128, n] = A[128, k] * B[n, k]^T (bf16 bit patterns, row-major) through one
+ * CTA's tcgen05 path on the current device: the descriptor and swizzle
+ * self-test of the tensor-core kernels. k % 64 == 0, n % 16 == 0, n <= 256. */
+int wc_debug_umma_gemm(const uint16_t* a, const uint16_t* b, int k, int n, float* d);
+
 /* ---- streaming submit / wait ---------------------------------------------- */
 int wc_submit(wc_ctx* ctx, wc_job* job, uint64_t* ticket);
 int wc_wait(wc_ctx* ctx, uint64_t ticket, wc_result* out);

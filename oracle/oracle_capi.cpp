@@ -3,6 +3,7 @@
 // product library.
 #include <algorithm>
 #include <atomic>
+#include <chrono>
 #include <cmath>
 #include <memory>
 #include <cstring>
@@ -330,6 +331,53 @@ int oracle_solve_many(const uint8_t* const* roots, const size_t* lens, size_t n,
     double s = 0.0;
     for (double x : upd) s += x;
     *node_updates = s;
+    return 0;
+}
+
+// Bounded CPU baseline. Each of `threads` threads takes one subgame: it
+// times the solver build plus the first k1 iterations (which includes the
+// once-per-solve network pieces), then k2 more iterations, and projects the
+// full solve as t1 + (iters - k1) * t2 / k2 plus one Phase-2 pass (about two
+// iterations). out[0] = sum over subgames of nodes * iters / projected time
+// (aggregate node-updates/s of `threads` busy threads), out[1] = measured
+// wall seconds, out[2] = subgames sampled.
+int oracle_bench(const uint8_t* const* roots, const size_t* lens, size_t n, const OracleCfg* cfg, const float* w,
+                 const float* b, const float* ln, int threads, int k1, int k2, double* out) {
+    Net net;
+    if (w) {
+        net.w.assign(w, w + net.L.w_len);
+        net.b.assign(b, b + net.L.b_len);
+        net.ln.assign(ln, ln + net.L.ln_len);
+        net.empty = false;
+    }
+    wc::SolveCfg sc = to_cfg(cfg);
+    wc::SolveCfg part = sc;
+    size_t m = std::min<size_t>(n, (size_t)threads);
+    std::vector<double> rate(m, 0.0);
+    auto wall0 = std::chrono::steady_clock::now();
+    std::vector<std::thread> pool;
+    for (size_t i = 0; i < m; ++i)
+        pool.emplace_back([&, i]() {
+            wc::Root r;
+            if (!wc::root_from_bytes(roots[i], lens[i], &r)) return;
+            auto t0 = std::chrono::steady_clock::now();
+            auto t = wc::build_tree(r.s, r.ctx, part, r.bel);
+            Solver sv(*t, &net);
+            sv.multistep(k1);
+            auto t1 = std::chrono::steady_clock::now();
+            sv.multistep(k2);
+            auto t2 = std::chrono::steady_clock::now();
+            double a = std::chrono::duration<double>(t1 - t0).count();
+            double it = std::chrono::duration<double>(t2 - t1).count() / k2;
+            double full = a + (sc.iters - k1) * it + 2.0 * it;
+            rate[i] = (double)t->nodes.size() * sc.iters / full;
+        });
+    for (auto& th : pool) th.join();
+    double sum = 0.0;
+    for (double x : rate) sum += x;
+    out[0] = sum;
+    out[1] = std::chrono::duration<double>(std::chrono::steady_clock::now() - wall0).count();
+    out[2] = (double)m;
     return 0;
 }
 

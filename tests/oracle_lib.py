@@ -45,6 +45,8 @@ def lib():
         L.oracle_set_cap_marker_value.argtypes = [C.c_float]
         L.oracle_solve_many.argtypes = [C.POINTER(C.c_char_p), C.POINTER(C.c_size_t), C.c_size_t,
                                         C.POINTER(OCfg), VP, VP, VP, C.c_int, C.POINTER(C.c_double)]
+        L.oracle_bench.argtypes = [C.POINTER(C.c_char_p), C.POINTER(C.c_size_t), C.c_size_t, C.POINTER(OCfg),
+                                   VP, VP, VP, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_double)]
         _lib = L
     return _lib
 
@@ -157,3 +159,18 @@ def solve_many(roots, cfg, weights, threads: int) -> float:
         w, b, ln = wa.ctypes.data, ba.ctypes.data, la.ctypes.data
     lib().oracle_solve_many(arr, lens, n, C.byref(ocfg(cfg)), w, b, ln, threads, C.byref(out))
     return out.value
+
+
+def bench(roots, cfg, weights, threads: int, k1: int = 2, k2: int = 4):
+    """Bounded CPU baseline (see oracle_bench): (node-updates/s, wall s, subgames)."""
+    n = len(roots)
+    arr = (C.c_char_p * n)(*roots)
+    lens = (C.c_size_t * n)(*[len(r) for r in roots])
+    out = (C.c_double * 3)()
+    if weights is None:
+        w = b = ln = None
+    else:
+        _, wa, ba, la = weights
+        w, b, ln = wa.ctypes.data, ba.ctypes.data, la.ctypes.data
+    lib().oracle_bench(arr, lens, n, C.byref(ocfg(cfg)), w, b, ln, threads, k1, k2, out)
+    return out[0], out[1], int(out[2])

@@ -5,6 +5,7 @@
 #include <deque>
 #include <map>
 #include <stdexcept>
+#include <string>
 #include <thread>
 
 #include "../../include/wc_b200.h"
@@ -378,6 +379,12 @@ int wc_job_info_get(const wc_job* job, wc_job_info* o) {
 }
 
 void wc_job_free(wc_job* job) { delete job; }
+
+int wc_debug_umma_gemm(const uint16_t* a, const uint16_t* b, int k, int n, float* d) {
+    int rc = wcdev::umma_selftest(a, b, k, n, d);
+    if (rc) return fail(WC_E_CUDA, "tcgen05 self-test failed with code " + std::to_string(rc));
+    return WC_OK;
+}
 
 int wc_job_counts(const wc_job* job, uint64_t* out, int n) {
     if (!job || !out || n < 20) return fail(WC_E_ARG, "wc_job_counts needs 20 slots");

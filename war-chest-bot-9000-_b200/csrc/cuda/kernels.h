@@ -40,4 +40,7 @@ void launch_pool(const JobDev* jobs, const uint32_t* row_job, const uint32_t* ro
 void launch_join_readout(const JobDev* jobs, const uint32_t* row_job, const uint32_t* row_local, uint32_t nrows,
                          int p, const float* W, const float* B, const float* LN, cudaStream_t s);
 
+// net_fast.cu
+int umma_selftest(const uint16_t* A, const uint16_t* B, int K, int N, float* D);
+
 }  // namespace wcdev

@@ -1,0 +1,150 @@
+// Thin sm_100a helpers for the 5th-generation tensor cores (tcgen05):
+// shared-memory matrix descriptors, the bf16 instruction descriptor, MMA
+// issue and completion through an mbarrier, TMEM allocation and loads.
+//
+// Operand layout used everywhere here: K-major, 128-byte swizzled. A tile of
+// R rows (R a multiple of 8) and K columns of bf16 is stored as K/64 "atoms";
+// atom a holds columns [64a, 64a + 64) of every row, row r at byte
+// a * R * 128 + r * 128, its 16-byte chunk c at position c ^ (r % 8). Tiles
+// start on 1024-byte boundaries. One MMA consumes K = 16 (32 bytes): the
+// descriptor start address advances by 32 bytes within an atom.
+#pragma once
+#include <cuda_bf16.h>
+
+#include <cstdint>
+
+namespace umma {
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// Byte offset of element (r, k) inside a swizzled K-major tile of R rows.
+__device__ __forceinline__ uint32_t sw128_offset(uint32_t R, uint32_t r, uint32_t k) {
+    uint32_t atom = k >> 6, kk = k & 63;
+    uint32_t chunk = (kk >> 3) ^ (r & 7);
+    return atom * R * 128u + r * 128u + chunk * 16u + (kk & 7) * 2u;
+}
+
+// Shared-memory descriptor of a swizzled K-major operand (SWIZZLE_128B:
+// layout type 2, SBO = 1024 bytes between 8-row groups, version 1).
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)1u << 16;
+    d |= (uint64_t)(1024u >> 4) << 32;
+    d |= (uint64_t)1u << 46;
+    d |= (uint64_t)2u << 61;
+    return d;
+}
+
+// Descriptor of the K-step `k0` (a multiple of 16) of a tile of R rows.
+__device__ __forceinline__ uint64_t desc_at(uint32_t tile_saddr, uint32_t R, uint32_t k0) {
+    return desc_sw128(tile_saddr + (k0 >> 6) * R * 128u + (k0 & 63) * 2u);
+}
+
+// Instruction descriptor, kind::f16: bf16 A and B (K-major), f32 D.
+__host__ __device__ constexpr uint32_t idesc_bf16(uint32_t M, uint32_t N) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((N >> 3) << 17) | ((M >> 4) << 24);
+}
+
+// D[tmem] (+)= A * B^T, one elected thread.
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n"
+        :
+        : "r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+}
+
+// Arrive on `mbar` when every MMA issued so far by this thread has completed.
+__device__ __forceinline__ void commit(uint64_t* mbar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(mbar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* mbar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(mbar)), "r"(count) : "memory");
+}
+
+// Bounded wait on phase `parity`: returns false if it gave up (the caller
+// records an error and skips its dependent work instead of hanging).
+__device__ __forceinline__ bool mbar_wait(uint64_t* mbar, uint32_t parity, uint32_t max_iter = (1u << 26)) {
+    uint32_t addr = smem_u32(mbar);
+    for (uint32_t i = 0; i < max_iter; ++i) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}\n"
+            : "=r"(done)
+            : "r"(addr), "r"(parity)
+            : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void fence_before_sync() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after_sync() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// TMEM allocation by one whole warp; the address lands in *slot.
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
+                 "r"(ncols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols));
+}
+
+// 32 consecutive f32 columns of this thread's TMEM lane (warp w reads lanes
+// 32w..32w+31): taddr already includes the lane offset (32w << 16).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Store 8 consecutive bf16 (one 16-byte chunk) of row r, columns [k, k+8).
+__device__ __forceinline__ void st_chunk(uint8_t* tile, uint32_t R, uint32_t r, uint32_t k, const float* x) {
+    __nv_bfloat162 a = __floats2bfloat162_rn(x[0], x[1]);
+    __nv_bfloat162 b = __floats2bfloat162_rn(x[2], x[3]);
+    __nv_bfloat162 c = __floats2bfloat162_rn(x[4], x[5]);
+    __nv_bfloat162 d = __floats2bfloat162_rn(x[6], x[7]);
+    uint4 v;
+    v.x = *reinterpret_cast<uint32_t*>(&a);
+    v.y = *reinterpret_cast<uint32_t*>(&b);
+    v.z = *reinterpret_cast<uint32_t*>(&c);
+    v.w = *reinterpret_cast<uint32_t*>(&d);
+    *reinterpret_cast<uint4*>(tile + sw128_offset(R, r, k)) = v;
+}
+
+__device__ __forceinline__ void st_zero_chunk(uint8_t* tile, uint32_t R, uint32_t r, uint32_t k) {
+    *reinterpret_cast<uint4*>(tile + sw128_offset(R, r, k)) = make_uint4(0, 0, 0, 0);
+}
+
+// Fast GELU for the bf16 path: tanh form with the hardware tanh.approx.
+__device__ __forceinline__ float tanh_fast(float x) {
+    float y;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float gelu_fast(float x) {
+    float inner = 0.79788456f * (x + 0.044715f * x * x * x);
+    return 0.5f * x * (1.0f + tanh_fast(inner));
+}
+
+}  // namespace umma

@@ -88,6 +88,7 @@ def _load() -> C.CDLL:
         "wc_submit": (I, [VP, VP, P(U64)]),
         "wc_wait": (I, [VP, U64, P(_Result)]),
         "wc_queued_work": (U64, [VP]),
+        "wc_debug_umma_gemm": (I, [VP, VP, I, I, VP]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -386,3 +387,13 @@ def spawn(device, dims=None, w=None, b=None, ln=None, precise: bool = True) -> G
     h = C.c_void_p()
     _check(lib().wc_init(len(devs), arr, C.byref(ws) if ws else None, int(precise), C.byref(h)))
     return GpuClient(h.value)
+
+
+def debug_umma_gemm(a_bf16: np.ndarray, b_bf16: np.ndarray) -> np.ndarray:
+    """tcgen05 self-test: A[128, K] @ B[N, K]^T with bf16 bit patterns (uint16)."""
+    a = np.ascontiguousarray(a_bf16, np.uint16)
+    b = np.ascontiguousarray(b_bf16, np.uint16)
+    k, n = a.shape[1], b.shape[0]
+    d = np.zeros((128, n), np.float32)
+    _check(lib().wc_debug_umma_gemm(a.ctypes.data, b.ctypes.data, k, n, d.ctypes.data))
+    return d
