@@ -47,7 +47,8 @@ def parse():
     ap.add_argument("--depth", type=int, default=3)
     ap.add_argument("--iters", type=int, default=512)
     ap.add_argument("--plies", type=int, default=20)
-    ap.add_argument("--net", default="precise", choices=["precise", "fast", "none"])
+    ap.add_argument("--net", default="f16", choices=["f16", "bf16", "exact", "none"],
+                    help="value network: tcgen05 with f16 / bf16 operands, fp32 exact, or none")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="bounded CPU baseline sample")
     ap.add_argument("--build-threads", type=int, default=0)
     return ap.parse_args()
@@ -139,7 +140,11 @@ class Clocks:
 
 def algorithmic_bytes(jobs):
     """Bytes per solve each CFR kernel class must move (every value read or
-    written once; indices u32; see DESIGN.md for the per-unit figures)."""
+    written once; indices u32). Per unit: a regret-matching row moves 24 B per
+    legal cell (regret, current, running sum read or written) and 8 B per row;
+    a value gather 12 B per entry (index, weight, source value) and 8 B per
+    output; a reach gather 24 B per cell entry, 16 B per draw entry and 8 B per
+    output."""
     c = np.sum([j.counts() for j in jobs], axis=0).astype(np.float64)
     iters = jobs[0].cfg.iters
     # per iteration pair each player's share runs once
@@ -218,10 +223,10 @@ def main():
         for t in tw:
             dist.broadcast(t, src=0)
         torch.cuda.synchronize()
-        client = wc.spawn(local, precise=(args.net == "precise"))
+        client = wc.spawn(local, net=args.net)
         client.set_weights_device(0, tw[0].data_ptr(), tw[1].data_ptr(), tw[2].data_ptr())
     elif weights is not None:
-        client = wc.spawn(local, *weights, precise=(args.net == "precise"))
+        client = wc.spawn(local, *weights, net=args.net)
     else:
         client = wc.spawn(local)
 
@@ -272,7 +277,7 @@ def main():
         base = cpu_baseline(wc, oracle_lib, cfg, weights, seeds, args.cpu_seconds)
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
-                "vs_baseline": None, "dtype": "f32" if args.net != "fast" else "bf16",
+                "vs_baseline": None, "dtype": DTYPES[args.net],
                 "data": "synthetic (seeded roots, seeded He-normal weights)", "config": workload,
                 "e2e": e2e, "gpu_launches": launches_per_step(batch_levels(jobs), args.iters, args.net != "none"),
                 "roofline": roofline, "cpu_baseline": base, "clocks": clocks_rec,
@@ -329,6 +334,9 @@ def allsum(world, x):
 
 
 PLIES = 20
+DTYPES = {"f16": "f32 CFR state, f16 tensor-core value net (fp32 accumulate)",
+          "bf16": "f32 CFR state, bf16 tensor-core value net (fp32 accumulate)",
+          "exact": "f32", "none": "f32"}
 
 if __name__ == "__main__":
     main()

@@ -1,7 +1,7 @@
 /* War Chest batched CFR solver on B200 — the C ABI.
  *
  * This is the boundary a host engine binds (the reference engine would bind
- * it from Rust with an `extern "C"` block). It replaces
+ * it from Rust with an `extern "C"` block over these declarations). It replaces
  * the reference's GPU solve service:
  *
  *   reference (fplonka/war-chest-bot-9000-)              this ABI
@@ -88,9 +88,17 @@ typedef struct wc_result {
 } wc_result;
 
 /* ---- service ------------------------------------------------------------ */
-/* precise != 0: fp32 network in the reference's operation order; 0: the
- * bf16 tensor-core network. */
-int wc_init(int ndev, const int* devices, const wc_weights* w, int precise, wc_ctx** out);
+/* Network arithmetic of a service (net_mode):
+ *   WC_NET_EXACT  fp32 in the reference CPU network's operation order
+ *                 (bit-identical to it);
+ *   WC_NET_F16    tcgen05 tensor cores, f16 operands, fp32 accumulation: the
+ *                 precision class of the reference GPU service's fast mode
+ *                 (cuBLAS COMPUTE_32F_FAST_16F, engine/src/gpu/device.rs:2306-2330);
+ *   WC_NET_BF16   the same kernels with bf16 operands.
+ * The values 0 / 1 keep the meaning of a `precise` flag (0 = tensor cores in
+ * bf16, 1 = exact). */
+enum { WC_NET_BF16 = 0, WC_NET_EXACT = 1, WC_NET_F16 = 2 };
+int wc_init(int ndev, const int* devices, const wc_weights* w, int net_mode, wc_ctx** out);
 int wc_publish(wc_ctx* ctx, const wc_weights* w, uint64_t* version);
 /* Publish weights already resident on device `dev_index` (e.g. after an
  * NCCL broadcast): pointers to w_len / b_len / ln_len f32 device arrays. */
@@ -146,6 +154,19 @@ int wc_batch_solve(wc_batch* b);
  * [7] init, [8] whole solve. class_ms needs 9 entries. */
 int wc_batch_solve_profiled(wc_batch* b, double* class_ms, int nclass);
 int wc_batch_download(wc_batch* b, size_t job, float* strategy, float* root_values, uint16_t* carries);
+/* Leaf evaluation alone (the per-solve network, then every network row's
+ * values for traverser p at the initial uniform-strategy reaches), and its
+ * read-back: rows in the reference's leaf_rows order, each row's p-configs
+ * in support order (counterfactual values: network value x opponent reach).
+ * class_ms, if non-NULL, receives the same 9 timing classes as
+ * wc_batch_solve_profiled (leaf evaluation alone in [1]). */
+int wc_batch_leaf_values(wc_batch* b, int p, double* class_ms);
+int wc_batch_download_leaf_values(wc_batch* b, size_t job, int p, float* out);
+/* After a solve or wc_batch_leaf_values: one job's board vectors P
+ * (net_rows x 256) and join projections jp (net_rows x 128) as the network
+ * path stores them; the bf16 path stores each row minus its mean (every
+ * consumer is a LayerNorm input, which ignores a per-row constant). */
+int wc_batch_download_board_rows(wc_batch* b, size_t job, float* pb, float* jp);
 /* Totals of the batch: node-updates per solve, network-row evaluations per
  * solve, table bytes, device bytes. */
 void wc_batch_stats(const wc_batch* b, double* node_updates, double* leaf_evals, uint64_t* table_bytes,

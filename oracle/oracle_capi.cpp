@@ -241,6 +241,18 @@ int oracle_value_under(void* p, const float* roots, size_t nroots, float* out) {
 
 void oracle_nash_conv(void* p, float* nash, float* zs) { static_cast<Handle*>(p)->sv->nash_conv(nash, zs); }
 
+// Replace the solver's latest strategy snapshot with an external average
+// strategy (reference cell layout), so nash_conv and value_under evaluate it:
+// the exploitability of another solver's output under this network.
+int oracle_set_strategy(void* p, const float* strat, size_t n) {
+    Solver& sv = *static_cast<Handle*>(p)->sv;
+    if (n != sv.cur.size()) return 1;
+    std::vector<float> s(strat, strat + n);
+    if (sv.snaps.empty()) sv.snaps.push_back(std::move(s));
+    else sv.snaps.back() = std::move(s);
+    return 0;
+}
+
 // Exit leaves in result order: network rows, then terminal leaves.
 size_t oracle_exit_leaves(void* p, uint32_t* out) {
     const wc::Tree& t = *static_cast<Handle*>(p)->tree;
@@ -274,6 +286,49 @@ int oracle_net_pieces(void* p, float* pb, float* jp, float* f, float* g) {
     if (jp) std::memcpy(jp, sv.jp.data(), sv.jp.size() * 4);
     if (f) std::memcpy(f, sv.cf.data(), sv.cf.size() * 4);
     if (g) std::memcpy(g, sv.cg.data(), sv.cg.size() * 4);
+    return 0;
+}
+
+// Leaf values for traverser p at the solver's initial reaches (search.rs:1550):
+// network rows in leaf_rows order, each row's p-configs in support order.
+// With out == NULL only the count is returned (nothing is evaluated).
+size_t oracle_leaf_values(void* h, int p, float* out) {
+    Solver& sv = *static_cast<Handle*>(h)->sv;
+    const wc::Tree& t = *static_cast<Handle*>(h)->tree;
+    if (!out) {
+        size_t n = 0;
+        for (uint32_t i : t.leaf_rows) n += t.nc(i, p);
+        return n;
+    }
+    sv.leaf_values(p);
+    size_t at = 0;
+    for (uint32_t i : t.leaf_rows) {
+        size_t n = t.nc(i, p);
+        if (out) std::memcpy(out + at, sv.vals.data() + sv.voff[i], 4 * n);
+        at += n;
+    }
+    return at;
+}
+
+// The readout's inputs behind oracle_leaf_values(p): the join output h of
+// every network row (rows x 256), the opponent's reach mass per row, and the
+// config index (into the f table of oracle_net_pieces) of every value.
+int oracle_leaf_parts(void* h, int p, float* hout, float* opp_reach, uint32_t* cidx) {
+    Solver& sv = *static_cast<Handle*>(h)->sv;
+    const wc::Tree& t = *static_cast<Handle*>(h)->tree;
+    if (!sv.net_ready()) return 1;
+    sv.leaf_values(p);
+    std::memcpy(hout, sv.h.data(), 4 * t.leaf_rows.size() * 256);
+    size_t at = 0;
+    for (size_t r = 0; r < t.leaf_rows.size(); ++r) {
+        uint32_t i = t.leaf_rows[r];
+        const float* ro = sv.reach_of(i, 1 - p);
+        float s = 0.0f;
+        for (size_t c = 0; c < t.nc(i, 1 - p); ++c) s += ro[c];
+        opp_reach[r] = s;
+        const uint32_t* idx = t.leaf_cidx.data() + t.leaf_coff[2 * r + p];
+        for (size_t c = 0; c < t.nc(i, p); ++c) cidx[at++] = idx[c];
+    }
     return 0;
 }
 

@@ -45,6 +45,8 @@ def lib():
         L.oracle_set_cap_marker_value.argtypes = [C.c_float]
         L.oracle_solve_many.argtypes = [C.POINTER(C.c_char_p), C.POINTER(C.c_size_t), C.c_size_t,
                                         C.POINTER(OCfg), VP, VP, VP, C.c_int, C.POINTER(C.c_double)]
+        L.oracle_leaf_values.restype = C.c_size_t
+        L.oracle_leaf_values.argtypes = [C.c_void_p, C.c_int, C.c_void_p]
         L.oracle_bench.argtypes = [C.POINTER(C.c_char_p), C.POINTER(C.c_size_t), C.c_size_t, C.POINTER(OCfg),
                                    VP, VP, VP, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_double)]
         _lib = L
@@ -105,6 +107,13 @@ class Oracle:
         lib().oracle_nash_conv(self.h, C.byref(n), C.byref(z))
         return n.value, z.value
 
+    def set_strategy(self, strategy: np.ndarray) -> None:
+        """Evaluate an external average strategy (reference cell layout) in
+        nash_conv / value_under from now on."""
+        s = np.ascontiguousarray(strategy, np.float32)
+        if lib().oracle_set_strategy(self.h, s.ctypes.data_as(C.c_void_p), C.c_size_t(s.size)):
+            raise ValueError("strategy length does not match the tree")
+
     def exit_leaves(self) -> np.ndarray:
         n = lib().oracle_exit_leaves(self.h, None)
         out = np.zeros(n, np.uint32)
@@ -116,6 +125,15 @@ class Oracle:
         out = np.zeros(max(n, 1) * width, np.float32)
         lib().oracle_carried_beliefs(self.h, C.c_uint32(leaf), out.ctypes.data_as(C.c_void_p))
         return out[: n * width].reshape(n, width)
+
+    def leaf_values(self, p: int) -> np.ndarray:
+        """Network-row values for traverser p at the current reaches
+        (search.rs:1550 leaf_values), rows in leaf_rows order."""
+        L = lib()
+        n = L.oracle_leaf_values(self.h, p, None)
+        out = np.zeros(max(n, 1), np.float32)
+        L.oracle_leaf_values(self.h, p, out.ctypes.data_as(C.c_void_p))
+        return out[:n]
 
     def net_pieces(self):
         s = self.shape

@@ -83,6 +83,7 @@ int upload_weights(DeviceCtx& d, const wc_weights* w) {
     check(cudaMemcpy(d.W, w->w, 4ull * d.L.w_len, cudaMemcpyHostToDevice), "upload weights");
     check(cudaMemcpy(d.B, w->b, 4ull * d.L.b_len, cudaMemcpyHostToDevice), "upload biases");
     check(cudaMemcpy(d.LN, w->ln, 4ull * d.L.ln_len, cudaMemcpyHostToDevice), "upload norms");
+    build_fast_pack(d, w->w, w->b, w->ln);
     d.have_net = true;
     return WC_OK;
 }
@@ -118,6 +119,7 @@ void solve_on(DeviceCtx& d, wc_job* const* jobs, size_t lo, size_t hi, wc_result
     for (size_t i = lo; i < hi; ++i) v.push_back(jobs[i]->blob.get());
     auto b = upload_batch(d, v);
     enqueue_solve(*b);
+    check_batch_error(*b);
     for (size_t i = lo; i < hi; ++i) fill_result(*b, i - lo, d.version, out + i);
 }
 
@@ -235,8 +237,10 @@ int wc_weights_fill(int kind, uint64_t seed, float* w, float* b, float* ln) {
     return WC_OK;
 }
 
-int wc_init(int ndev, const int* devices, const wc_weights* w, int precise, wc_ctx** out) {
+int wc_init(int ndev, const int* devices, const wc_weights* w, int net_mode, wc_ctx** out) {
     if (ndev < 1 || !out) return fail(WC_E_ARG, "need at least one device");
+    if (net_mode != WC_NET_BF16 && net_mode != WC_NET_EXACT && net_mode != WC_NET_F16)
+        return fail(WC_E_ARG, "unknown network mode");
     return guarded([&] {
         auto ctx = std::make_unique<wc_ctx>();
         const Board& bd = board();
@@ -248,11 +252,13 @@ int wc_init(int ndev, const int* devices, const wc_weights* w, int precise, wc_c
         for (int i = 0; i < ndev; ++i) {
             auto d = std::make_unique<DeviceCtx>();
             d->device = devices ? devices[i] : i;
-            d->precise = precise != 0;
+            d->precise = net_mode == WC_NET_EXACT;
+            d->half = net_mode == WC_NET_F16;
             d->L = NetLayout::make();
             check(cudaSetDevice(d->device), "set device");
             check(cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking), "stream");
             wcdev::net_set_constants(d->L, nb, isloc);
+            wcdev::trunk_set_constants(d->L, nb, isloc);
             int rc = upload_weights(*d, w);
             if (rc) return rc;
             d->version = 1;
@@ -295,6 +301,11 @@ int wc_publish_device(wc_ctx* ctx, int dev_index, const float* w, const float* b
         check(cudaMemcpy(d.W, w, 4ull * d.L.w_len, cudaMemcpyDeviceToDevice), "publish weights");
         check(cudaMemcpy(d.B, b, 4ull * d.L.b_len, cudaMemcpyDeviceToDevice), "publish biases");
         check(cudaMemcpy(d.LN, ln, 4ull * d.L.ln_len, cudaMemcpyDeviceToDevice), "publish norms");
+        std::vector<float> hw(d.L.w_len), hb(d.L.b_len), hl(d.L.ln_len);
+        check(cudaMemcpy(hw.data(), w, 4ull * d.L.w_len, cudaMemcpyDeviceToHost), "read weights");
+        check(cudaMemcpy(hb.data(), b, 4ull * d.L.b_len, cudaMemcpyDeviceToHost), "read biases");
+        check(cudaMemcpy(hl.data(), ln, 4ull * d.L.ln_len, cudaMemcpyDeviceToHost), "read norms");
+        build_fast_pack(d, hw.data(), hb.data(), hl.data());
         d.have_net = true;
         d.version += 1;
         if (version) *version = d.version;
@@ -317,6 +328,7 @@ void wc_shutdown(wc_ctx* ctx) {
         if (d->W) cudaFree(d->W);
         if (d->B) cudaFree(d->B);
         if (d->LN) cudaFree(d->LN);
+        if (d->fast_mem) cudaFree(d->fast_mem);
         if (d->stream) cudaStreamDestroy(d->stream);
     }
     delete ctx;
@@ -485,6 +497,7 @@ int wc_batch_solve(wc_batch* b) {
         std::lock_guard<std::mutex> lk(b->b->dev->mu);
         enqueue_solve(*b->b);
         check(cudaStreamSynchronize(b->b->dev->stream), "batch solve");
+        check_batch_error(*b->b);
         return (int)WC_OK;
     });
 }
@@ -497,6 +510,40 @@ int wc_batch_solve_profiled(wc_batch* b, double* class_ms, int nclass) {
         enqueue_solve(*b->b);
         read_profile(*b->b, class_ms);
         b->b->profile = false;
+        check_batch_error(*b->b);
+        return (int)WC_OK;
+    });
+}
+
+int wc_batch_leaf_values(wc_batch* b, int p, double* class_ms) {
+    if (!b || p < 0 || p > 1) return fail(WC_E_ARG, "bad leaf-values arguments");
+    return guarded([&] {
+        std::lock_guard<std::mutex> lk(b->b->dev->mu);
+        b->b->profile = class_ms != nullptr;
+        enqueue_leaf_values(*b->b, p);
+        if (class_ms) {
+            read_profile(*b->b, class_ms);
+            b->b->profile = false;
+        } else {
+            check(cudaStreamSynchronize(b->b->dev->stream), "leaf values");
+        }
+        check_batch_error(*b->b);
+        return (int)WC_OK;
+    });
+}
+
+int wc_batch_download_leaf_values(wc_batch* b, size_t job, int p, float* out) {
+    if (!b || job >= b->b->jobs.size() || p < 0 || p > 1 || !out) return fail(WC_E_ARG, "bad arguments");
+    return guarded([&] {
+        download_leaf_values(*b->b, job, p, out);
+        return (int)WC_OK;
+    });
+}
+
+int wc_batch_download_board_rows(wc_batch* b, size_t job, float* pb, float* jp) {
+    if (!b || job >= b->b->jobs.size() || !b->b->dev->have_net) return fail(WC_E_ARG, "bad arguments");
+    return guarded([&] {
+        download_board_rows(*b->b, job, pb, jp);
         return (int)WC_OK;
     });
 }

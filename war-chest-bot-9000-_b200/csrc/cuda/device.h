@@ -45,6 +45,10 @@ struct JobDev {
     const float* weights_b;
     const float* weights_ln;
     float* cardm;      // [2][NTYPE][3 * POOL]: cfg_m applied to the card tokens
+    const uint32_t* cfg_col;  // config -> index among its player's configs
+    uint16_t* f16;     // fast path: bf16 f(c) rows, player 0's configs then player 1's ([ncfg][D])
+    uint32_t ncfg_player[2];
+    uint32_t row_base; // first global network row of this job
     // ---- mutable solve state
     float* cur;
     float* regret;
@@ -69,6 +73,22 @@ struct JobDev {
     uint32_t ncells, ndraw, nrows_net, nterm, ncfg, ncarried, reach_len, nexit;
     uint32_t root_nc[2], root_rblk[2], root_vblk[2];
     uint32_t carry_width;  // sum over exit nodes of nc0 + nc1
+};
+
+// Device pointers of the bf16 tensor-core network (one per device): weight
+// matrices as swizzled K-major B tiles ([out][in], see umma.cuh), fp32 bias
+// and LayerNorm vectors.
+struct FastNetDev {
+    const uint8_t* join_tiles;  // join_b (inputs 0..127), join_w[0..2]: 4 x [128][128]
+    const uint8_t* out_tile;    // join_out: [256][128]
+    const uint8_t* trunk_tiles; // per trunk block: mix [96][192], out [96][96]
+    const float* beff[2];       // join_b bias with the seat input (-1 / +1) folded in
+    const float* bj[3];
+    const float* bout;
+    const float* ln_g[5];       // LN_JOIN + 0..2, LN_JOUT, LN_H
+    const float* ln_b[5];
+    float vbias;
+    int half;                   // operand type of every tile and stored row: 1 = f16, 0 = bf16
 };
 
 struct WorkItem {

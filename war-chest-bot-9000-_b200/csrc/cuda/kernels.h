@@ -41,6 +41,24 @@ void launch_join_readout(const JobDev* jobs, const uint32_t* row_job, const uint
                          int p, const float* W, const float* B, const float* LN, cudaStream_t s);
 
 // net_fast.cu
+// Raise a kernel's dynamic shared-memory limit on the current device, once
+// per (device, kernel); false if the driver refuses (the launch is skipped
+// and the runtime's launch check reports it).
+bool raise_smem_limit(const void* fn, size_t smem);
 int umma_selftest(const uint16_t* A, const uint16_t* B, int K, int N, float* D);
+void launch_pool_fast(const JobDev* jobs, const uint32_t* row_job, const uint32_t* row_local, uint32_t total_rows,
+                      int mask, float* pooled, cudaStream_t s);
+void launch_join_fast(const FastNetDev& fn, int p, const float* pooled, const uint16_t* jp, uint16_t* zout,
+                      uint32_t total_rows, int* err, cudaStream_t s);
+void launch_head_fast(const JobDev* jobs, const void* tiles, uint32_t ntiles, const FastNetDev& fn, int p,
+                      const uint16_t* zout, const uint16_t* pb, int* err, cudaStream_t s);
+void launch_pack_f16(const JobDev* jobs, const uint32_t* cfg_job, const uint32_t* cfg_local, uint32_t total_cfgs,
+                     bool half, cudaStream_t s);
+// trunk_fast.cu
+void trunk_set_constants(const wc::NetLayout& L, const uint8_t* neighbors, const uint8_t* is_location);
+size_t trunk_tiles_bytes();
+void launch_trunk_fast(const JobDev* jobs, const uint32_t* row_job, const uint32_t* row_local, uint32_t total_rows,
+                       const uint8_t* tiles, const float* W, const float* B, const float* LN, uint16_t* g_pb,
+                       uint16_t* g_jp, bool half, int* err, cudaStream_t s);
 
 }  // namespace wcdev

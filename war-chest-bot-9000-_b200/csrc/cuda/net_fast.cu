@@ -1,10 +1,13 @@
-// The bf16 tensor-core ("fast") value network: tcgen05 MMAs with operands in
+// The tensor-core ("fast") value network: tcgen05 MMAs with operands in
 // 128-byte-swizzled shared memory and fp32 accumulators in TMEM, epilogues on
 // the CUDA cores (bias, residual, LayerNorm, tanh-GELU).
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdint>
+#include <mutex>
+#include <set>
 
 #include "device.h"
 #include "kernels.h"
@@ -50,7 +53,7 @@ __global__ void k_umma_selftest(const __nv_bfloat16* __restrict__ A, const __nv_
     if (tid == 0) {
         const uint32_t idesc = umma::idesc_bf16(128, N);
         for (int k0 = 0; k0 < K; k0 += 16)
-            umma::mma_bf16(tmem, umma::desc_at(umma::smem_u32(sA), 128, k0), umma::desc_at(umma::smem_u32(sB), N, k0),
+            umma::mma16(tmem, umma::desc_at(umma::smem_u32(sA), 128, k0), umma::desc_at(umma::smem_u32(sB), N, k0),
                            idesc, k0 > 0);
         umma::commit(&mbar);
     }
@@ -68,6 +71,437 @@ __global__ void k_umma_selftest(const __nv_bfloat16* __restrict__ A, const __nv_
     umma::fence_before_sync();
     __syncthreads();
     if (warp == 0) umma::tmem_dealloc(tmem, ncols);
+}
+
+// ------------------------------------------------------------- fast kernels
+
+constexpr int POOL = wc::NET_POOL, JW = wc::NET_JW, D = wc::NET_D;
+constexpr uint32_t TILE_J = 128u * 128u * 2u;  // one [128][128] bf16 operand tile
+constexpr uint32_t WAIT_LIMIT = 1u << 26;
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+    return p + ((1024u - (umma::smem_u32(p) & 1023u)) & 1023u);
+}
+
+// Pooled belief embeddings, one warp per (network row, player): normalised
+// reach over the leaf's configs weighting g(c) (search.rs:1512-1547).
+__global__ void k_pool_fast(const JobDev* __restrict__ jobs, const uint32_t* __restrict__ row_job,
+                            const uint32_t* __restrict__ row_local, uint32_t total_rows, int mask,
+                            float* __restrict__ pooled) {
+    const int nq = mask == 3 ? 2 : 1;
+    const uint64_t gw = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (gw >= (uint64_t)total_rows * nq) return;
+    const uint32_t g = (uint32_t)(gw / nq);
+    const int q = mask == 3 ? (int)(gw % nq) : (mask == 1 ? 0 : 1);
+    const JobDev& J = jobs[row_job[g]];
+    const uint32_t r = row_local[g];
+    const float* w = J.reach + J.lr_ridx[2 * r + q];
+    const uint32_t n = J.lr_nc[2 * r + q];
+    const uint32_t* idx = J.leaf_cidx + J.leaf_coff[2 * r + q];
+    float tot = 0.0f;
+    for (uint32_t c = lane; c < n; c += 32) tot += w[c];
+#pragma unroll
+    for (int o = 16; o; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+    float scale, flat;
+    if (tot > 1e-30f) { scale = 1.0f / tot; flat = 0.0f; }
+    else { scale = 0.0f; flat = 1.0f / (float)(n > 0 ? n : 1); }
+    float a0 = 0.0f, a1 = 0.0f;
+    for (uint32_t c = 0; c < n; ++c) {
+        float wc = w[c] * scale + flat;
+        float2 gv = reinterpret_cast<const float2*>(J.cg + (size_t)idx[c] * POOL)[lane];
+        a0 += wc * gv.x;
+        a1 += wc * gv.y;
+    }
+    reinterpret_cast<float2*>(pooled + ((size_t)g * 2 + q) * POOL)[lane] = make_float2(a0, a1);
+}
+
+// Row statistics of a LayerNorm whose row is spread over the four column
+// groups of a 16-warp CTA (warp w: rows 32 (w % 4) .., columns group w / 4).
+__device__ __forceinline__ void row_stats4(const float* v, int n, float (*part)[4], int row, int cg, int width,
+                                           float* mean, float* inv) {
+    float s = 0.0f;
+    for (int j = 0; j < n; ++j) s += v[j];
+    part[row][cg] = s;
+    __syncthreads();
+    const float m = (part[row][0] + part[row][1] + part[row][2] + part[row][3]) / (float)width;
+    __syncthreads();
+    float q = 0.0f;
+    for (int j = 0; j < n; ++j) q += (v[j] - m) * (v[j] - m);
+    part[row][cg] = q;
+    __syncthreads();
+    *inv = rsqrtf((part[row][0] + part[row][1] + part[row][2] + part[row][3]) / (float)width + 1e-5f);
+    *mean = m;
+}
+
+// The join chain for traverser p on 128-row tiles (net.rs:801-832):
+// z = jp + [pooled_p | pooled_o] * Wb + b, three residual blocks
+// z += W_i LNGELU(z) + b_i, and out = LNGELU(z) in bf16 (the join_out input).
+// 16 warps: warp w owns TMEM lanes 32 (w % 4) .. (rows) and columns
+// 32 (w / 4) .. of the 128; z lives in registers. The four 128 x 128 weight
+// tiles stay in shared memory for the CTA's lifetime.
+template <bool H>
+__global__ void __launch_bounds__(512, 1)
+    k_join_fast(FastNetDev fn, int p, const float* __restrict__ pooled, const uint16_t* __restrict__ jp,
+                uint16_t* __restrict__ zout, uint32_t total_rows, int* __restrict__ err) {
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ uint64_t mbar;
+    __shared__ uint32_t tmem_slot;
+    __shared__ int abort_flag;
+    __shared__ float part[128][4];
+    uint8_t* smem = align1024(smem_raw);
+    uint8_t* sW = smem;
+    uint8_t* sA = smem + 4 * TILE_J;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int quad = warp & 3, cg = warp >> 2;
+    const int row = quad * 32 + lane, col0 = cg * 32;
+    {
+        const uint4* src = reinterpret_cast<const uint4*>(fn.join_tiles);
+        uint4* dst = reinterpret_cast<uint4*>(sW);
+        for (uint32_t i = tid; i < 4 * TILE_J / 16; i += blockDim.x) dst[i] = src[i];
+    }
+    if (tid == 0) {
+        umma::mbar_init(&mbar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        abort_flag = 0;
+    }
+    if (warp == 0) umma::tmem_alloc(&tmem_slot, 128);
+    umma::fence_async_smem();
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+    const uint32_t tmem = tmem_slot;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const uint32_t ntiles = (total_rows + 127) / 128;
+    const uint32_t idesc = umma::idesc16(128, 128, umma::Op16<H>::fmt);
+    const float* beff = fn.beff[p];
+    uint32_t phase = 0;
+    for (uint32_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+        const uint32_t g = tile * 128 + row;
+        const bool valid = g < total_rows;
+        float z[32];
+        if (valid) {
+            // columns 0..63 read the traverser's pooled belief, 64..127 the opponent's
+            const float* src = pooled + ((size_t)g * 2 + (cg < 2 ? p : 1 - p)) * POOL + (cg & 1) * 32;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) umma::st_chunk<H>(sA, 128, row, col0 + 8 * c, src + 8 * c);
+            const uint4* jr = reinterpret_cast<const uint4*>(jp + (size_t)g * JW + col0);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                uint4 v = jr[c];
+                const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    z[8 * c + 2 * i] = umma::Op16<H>::lo(w4[i]) + beff[col0 + 8 * c + 2 * i];
+                    z[8 * c + 2 * i + 1] = umma::Op16<H>::hi(w4[i]) + beff[col0 + 8 * c + 2 * i + 1];
+                }
+            }
+        } else {
+#pragma unroll
+            for (int c = 0; c < 4; ++c) umma::st_zero_chunk(sA, 128, row, col0 + 8 * c);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) z[j] = 0.0f;
+        }
+#pragma unroll 1
+        for (int L = 0; L < 4; ++L) {
+            umma::fence_async_smem();
+            umma::fence_before_sync();
+            __syncthreads();
+            umma::fence_after_sync();
+            if (tid == 0) {
+                const uint32_t wa = umma::smem_u32(sA), wb = umma::smem_u32(sW + L * TILE_J);
+#pragma unroll
+                for (int k0 = 0; k0 < JW; k0 += 16)
+                    umma::mma16(tmem, umma::desc_at(wa, 128, k0), umma::desc_at(wb, 128, k0), idesc, k0 > 0);
+                umma::commit(&mbar);
+            }
+            if (!umma::mbar_wait(&mbar, phase, WAIT_LIMIT)) abort_flag = 1;
+            phase ^= 1u;
+            umma::fence_after_sync();
+            {
+                float v[32];
+                umma::tmem_ld32(tmem + lane_off + col0, v);
+                if (L > 0) {
+                    const float* bias = fn.bj[L - 1] + col0;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) z[j] += v[j] + bias[j];
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) z[j] += v[j];
+                }
+            }
+            float mean, inv;
+            row_stats4(z, 32, part, row, cg, JW, &mean, &inv);
+            const float* gam = fn.ln_g[L] + col0;
+            const float* bet = fn.ln_b[L] + col0;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                float x[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) x[i] = umma::gelu_fast((z[8 * c + i] - mean) * inv * gam[8 * c + i] + bet[8 * c + i]);
+                if (L < 3)
+                    umma::st_chunk<H>(sA, 128, row, col0 + 8 * c, x);
+                else if (valid)
+                    reinterpret_cast<uint4*>(zout + (size_t)g * JW + col0)[c] = umma::pack_chunk<H>(x);
+            }
+        }
+        __syncthreads();
+        if (abort_flag) break;
+    }
+    if (tid == 0 && abort_flag) atomicExch(err, 1);
+    umma::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) umma::tmem_dealloc(tmem, 128);
+}
+
+// One tile = up to 128 network rows of one job: first local row, count.
+struct HeadTile {
+    uint32_t job, first, count, pad;
+};
+
+// The join output layer, the readout LayerNorm and the per-config readout for
+// traverser p (net.rs:833-853, search.rs:1587-1636):
+// y = P + out * Wout + bout, h = LN(y), v(c) = (<f(c), h> + bias) * opp_reach.
+// The readout is a second tensor-core product, H[128, 256] * F_p^T, against
+// the job's player-p f table (128 configs per pass). 16 warps: warp w owns
+// rows 32 (w % 4) .. and the column group w / 4 (64 of y's 256 columns, 32 of
+// each 128-config readout pass).
+template <bool H>
+__global__ void __launch_bounds__(512, 1)
+    k_head_fast(const JobDev* __restrict__ jobs, const HeadTile* __restrict__ tiles, uint32_t ntiles, FastNetDev fn,
+                int p, const uint16_t* __restrict__ zout, const uint16_t* __restrict__ pb, int* __restrict__ err) {
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ uint64_t mbar;
+    __shared__ uint32_t tmem_slot;
+    __shared__ int abort_flag;
+    __shared__ float part[128][4];
+    uint8_t* smem = align1024(smem_raw);
+    uint8_t* sW = smem;                        // [256][128]: 64 KB
+    uint8_t* sH = sW + 2 * TILE_J;             // [128][256]: 64 KB
+    uint8_t* sA = sH;                          // [128][128] operand of the first product, then H
+    uint8_t* sF = sH + 2 * TILE_J;             // [128][256]: 64 KB (after each product: the readout staging)
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int quad = warp & 3, cg = warp >> 2;
+    const int row = quad * 32 + lane;
+    {
+        const uint4* src = reinterpret_cast<const uint4*>(fn.out_tile);
+        uint4* dst = reinterpret_cast<uint4*>(sW);
+        for (uint32_t i = tid; i < 2 * TILE_J / 16; i += blockDim.x) dst[i] = src[i];
+    }
+    if (tid == 0) {
+        umma::mbar_init(&mbar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        abort_flag = 0;
+    }
+    if (warp == 0) umma::tmem_alloc(&tmem_slot, 512);
+    umma::fence_async_smem();
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+    const uint32_t tmem = tmem_slot;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    uint32_t phase = 0;
+    // [512][32] floats, element j of thread t at t * 32 + (j ^ lane): conflict-free
+    float* stage = reinterpret_cast<float*>(sF);
+    for (uint32_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
+        const HeadTile ht = tiles[t];
+        const JobDev& J = jobs[ht.job];
+        const bool valid = (uint32_t)row < ht.count;
+        const uint32_t r = ht.first + row;          // job-local network row
+        const uint32_t g = J.row_base + r;          // global network row
+        // A = out rows (bf16, 256 bytes each): this thread's 32 columns
+        if (valid) {
+            const uint4* src = reinterpret_cast<const uint4*>(zout + (size_t)g * JW + 32 * cg);
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+                *reinterpret_cast<uint4*>(sA + umma::sw128_offset(128, row, 32 * cg + 8 * c)) = src[c];
+        } else {
+#pragma unroll
+            for (int c = 0; c < 4; ++c) umma::st_zero_chunk(sA, 128, row, 32 * cg + 8 * c);
+        }
+        umma::fence_async_smem();
+        umma::fence_before_sync();
+        __syncthreads();
+        umma::fence_after_sync();
+        if (tid == 0) {
+            const uint32_t wa = umma::smem_u32(sA), wb = umma::smem_u32(sW);
+            const uint32_t idesc = umma::idesc16(128, 256, umma::Op16<H>::fmt);
+#pragma unroll
+            for (int k0 = 0; k0 < JW; k0 += 16)
+                umma::mma16(tmem, umma::desc_at(wa, 128, k0), umma::desc_at(wb, 256, k0), idesc, k0 > 0);
+            umma::commit(&mbar);
+        }
+        // meanwhile: the row's opponent reach mass and the F rows of the first pass
+        float opp_mass = 0.0f;
+        uint32_t ncfg_row = 0;
+        const uint32_t* cidx = nullptr;
+        float* out = nullptr;
+        if (valid) {
+            const float* ro = J.reach + J.lr_ridx[2 * r + 1 - p];
+            const uint32_t no = J.lr_nc[2 * r + 1 - p];
+            for (uint32_t c = 0; c < no; ++c) opp_mass += ro[c];
+            ncfg_row = J.lr_nc[2 * r + p];
+            cidx = J.leaf_cidx + J.leaf_coff[2 * r + p];
+            out = J.vals[p] + J.lr_vidx[2 * r + p];
+        }
+        const uint32_t nfp = J.ncfg_player[p];
+        const uint16_t* F = J.f16 + (size_t)(p == 1 ? J.ncfg_player[0] : 0) * D;
+        auto load_f = [&](uint32_t nb) {
+            // rows [nb, nb + 128): thread (row, cg) copies 8 of the row's 32 chunks
+            const uint32_t fr = nb + row;
+            if (fr < nfp) {
+                const uint4* src = reinterpret_cast<const uint4*>(F + (size_t)fr * D) + 8 * cg;
+#pragma unroll
+                for (int c = 0; c < 8; ++c)
+                    *reinterpret_cast<uint4*>(sF + umma::sw128_offset(128, row, 64 * cg + 8 * c)) = src[c];
+            } else {
+#pragma unroll
+                for (int c = 0; c < 8; ++c) umma::st_zero_chunk(sF, 128, row, 64 * cg + 8 * c);
+            }
+        };
+        load_f(0);
+        if (!umma::mbar_wait(&mbar, phase, WAIT_LIMIT)) abort_flag = 1;
+        phase ^= 1u;
+        umma::fence_after_sync();
+        // y = acc + P + bout on this thread's 64 columns; LayerNorm -> h -> sH
+        float y[64];
+        {
+            const uint4* pr = reinterpret_cast<const uint4*>(pb + (size_t)(valid ? g : 0) * D + 64 * cg);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                float v[32];
+                umma::tmem_ld32(tmem + lane_off + 64 * cg + 32 * h, v);
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    uint4 q = valid ? pr[4 * h + c] : make_uint4(0, 0, 0, 0);
+                    const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int j = 32 * h + 8 * c + 2 * i;
+                        y[j] = v[8 * c + 2 * i] + umma::Op16<H>::lo(w4[i]) + fn.bout[64 * cg + j];
+                        y[j + 1] = v[8 * c + 2 * i + 1] + umma::Op16<H>::hi(w4[i]) + fn.bout[64 * cg + j + 1];
+                    }
+                }
+            }
+        }
+        float mean, inv;
+        row_stats4(y, 64, part, row, cg, D, &mean, &inv);
+        {
+            const float* gam = fn.ln_g[4] + 64 * cg;
+            const float* bet = fn.ln_b[4] + 64 * cg;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                float x[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) x[i] = (y[8 * c + i] - mean) * inv * gam[8 * c + i] + bet[8 * c + i];
+                umma::st_chunk<H>(sH, 128, row, 64 * cg + 8 * c, x);
+            }
+        }
+        for (uint32_t nb = 0; nb < nfp; nb += 128) {
+            if (nb > 0) load_f(nb);
+            umma::fence_async_smem();
+            umma::fence_before_sync();
+            __syncthreads();
+            umma::fence_after_sync();
+            if (tid == 0) {
+                const uint32_t ha = umma::smem_u32(sH), fa = umma::smem_u32(sF);
+                const uint32_t idesc = umma::idesc16(128, 128, umma::Op16<H>::fmt);
+#pragma unroll
+                for (int k0 = 0; k0 < D; k0 += 16)
+                    umma::mma16(tmem + 256, umma::desc_at(ha, 128, k0), umma::desc_at(fa, 128, k0), idesc, k0 > 0);
+                umma::commit(&mbar);
+            }
+            if (!umma::mbar_wait(&mbar, phase, WAIT_LIMIT)) abort_flag = 1;
+            phase ^= 1u;
+            umma::fence_after_sync();
+            {
+                float v[32];
+                umma::tmem_ld32(tmem + lane_off + 256 + 32 * cg, v);
+                float* st = stage + tid * 32;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) st[j ^ lane] = v[j];
+                const uint32_t lo = nb + 32 * cg;
+                for (uint32_t c = 0; c < ncfg_row; ++c) {
+                    const uint32_t col = J.cfg_col[cidx[c]];
+                    if (col >= lo && col < lo + 32) out[c] = (st[(col - lo) ^ lane] + fn.vbias) * opp_mass;
+                }
+            }
+            umma::fence_before_sync();
+            __syncthreads();
+        }
+        if (abort_flag) break;
+    }
+    if (tid == 0 && abort_flag) atomicExch(err, 2);
+    umma::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) umma::tmem_dealloc(tmem, 512);
+}
+
+// f(c) rows of every config as 16-bit operands, grouped by player (player 0's first).
+template <bool H>
+__global__ void k_pack_f16(const JobDev* __restrict__ jobs, const uint32_t* __restrict__ cfg_job,
+                           const uint32_t* __restrict__ cfg_local, uint32_t total_cfgs) {
+    const uint32_t i = blockIdx.x;
+    if (i >= total_cfgs) return;
+    const JobDev& J = jobs[cfg_job[i]];
+    const uint32_t c = cfg_local[i];
+    const uint32_t row = (J.cplayer[c] == 1 ? J.ncfg_player[0] : 0) + J.cfg_col[c];
+    for (int j = threadIdx.x; j < D; j += blockDim.x)
+        J.f16[(size_t)row * D + j] = umma::Op16<H>::one(J.cf[(size_t)c * D + j]);
+}
+
+static int num_sms() {
+    int dev = 0, n = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n;
+}
+
+void launch_pool_fast(const JobDev* jobs, const uint32_t* row_job, const uint32_t* row_local, uint32_t total_rows,
+                      int mask, float* pooled, cudaStream_t s) {
+    if (!total_rows || !mask) return;
+    uint64_t warps = (uint64_t)total_rows * (mask == 3 ? 2 : 1);
+    k_pool_fast<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, s>>>(jobs, row_job, row_local, total_rows, mask, pooled);
+}
+
+bool raise_smem_limit(const void* fn, size_t smem) {
+    static std::mutex mu;
+    static std::set<std::pair<int, const void*>> done;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (done.count({dev, fn})) return true;
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return false;
+    done.insert({dev, fn});
+    return true;
+}
+
+void launch_join_fast(const FastNetDev& fn, int p, const float* pooled, const uint16_t* jp, uint16_t* zout,
+                      uint32_t total_rows, int* err, cudaStream_t s) {
+    if (!total_rows) return;
+    const size_t smem = 5 * TILE_J + 1024;
+    auto kern = fn.half ? k_join_fast<true> : k_join_fast<false>;
+    if (!raise_smem_limit((const void*)kern, smem)) return;
+    uint32_t ntiles = (total_rows + 127) / 128;
+    uint32_t grid = std::min<uint32_t>(ntiles, (uint32_t)num_sms());
+    kern<<<grid, 512, smem, s>>>(fn, p, pooled, jp, zout, total_rows, err);
+}
+
+void launch_head_fast(const JobDev* jobs, const void* tiles, uint32_t ntiles, const FastNetDev& fn, int p,
+                      const uint16_t* zout, const uint16_t* pb, int* err, cudaStream_t s) {
+    if (!ntiles) return;
+    const size_t smem = 6 * TILE_J + 1024;
+    auto kern = fn.half ? k_head_fast<true> : k_head_fast<false>;
+    if (!raise_smem_limit((const void*)kern, smem)) return;
+    uint32_t grid = std::min<uint32_t>(ntiles, (uint32_t)num_sms());
+    kern<<<grid, 512, smem, s>>>(jobs, reinterpret_cast<const HeadTile*>(tiles), ntiles, fn, p, zout, pb, err);
+}
+
+void launch_pack_f16(const JobDev* jobs, const uint32_t* cfg_job, const uint32_t* cfg_local, uint32_t total_cfgs,
+                     bool half, cudaStream_t s) {
+    if (!total_cfgs) return;
+    if (half) k_pack_f16<true><<<total_cfgs, 128, 0, s>>>(jobs, cfg_job, cfg_local, total_cfgs);
+    else k_pack_f16<false><<<total_cfgs, 128, 0, s>>>(jobs, cfg_job, cfg_local, total_cfgs);
 }
 
 int umma_selftest(const uint16_t* A, const uint16_t* B, int K, int N, float* D) {

@@ -1,0 +1,535 @@
+// The board trunk on the tensor cores (net.rs:558-731): tokens and stem,
+// eight residual blocks, the final norm, the board readout P and the join
+// projection jp, for three boards (111 hex rows, padded to M = 128) per tile.
+//
+// Each CTA keeps the residual stream x of its tile in registers: 12 warps,
+// warp w owns TMEM lanes 32 (w % 4) .. + 31 (hex rows) and columns
+// 32 (w / 4) .. + 31. Per block the two GEMMs run on tcgen05:
+//   mix: [a | sum of the six neighbours' a] (K = 192) x W_mix (N = 96)
+//   out: LNGELU(y) (K = 96) x W_out (N = 96)
+// with the block's bf16 weight tiles streamed from global memory by bulk
+// asynchronous copies into two shared-memory buffers (the next block's
+// weights land while this block computes). The per-board pooling GEMM,
+// the stem and the board readout are small and run on the CUDA cores.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+
+#include "../host/netlayout.h"
+#include "device.h"
+#include "kernels.h"
+#include "umma.cuh"
+
+namespace wcdev {
+
+using wc::NetLayout;
+
+__constant__ NetLayout c_Lt;
+__constant__ uint8_t c_nbt[37][6];
+__constant__ uint8_t c_islt[37];
+
+namespace {
+
+constexpr int NH = 37, BOARDS = 3, ROWS = BOARDS * NH;  // 111 real rows per tile
+constexpr int C = wc::NET_C, TYPE = wc::NET_TYPE, D = wc::NET_D, JW = wc::NET_JW;
+constexpr int NTYPE = 10, NSLOT = 5, HEX_FACTS = 6, LOOSE = 15, PILE = 4;
+constexpr uint32_t MIX_BYTES = 96 * 3 * 128;   // [96][192] swizzled: 3 atoms
+constexpr uint32_t OUT_BYTES = 96 * 2 * 128;   // [96][96]: 2 atoms (second half used)
+constexpr uint32_t BLOCK_BYTES = MIX_BYTES + OUT_BYTES;  // 61440
+constexpr uint32_t A1_BYTES = 128 * 3 * 128;   // [128][192]
+constexpr uint32_t A2_BYTES = 128 * 2 * 128;   // [128][96]
+constexpr uint32_t WAIT_LIMIT = 1u << 26;
+
+__device__ __forceinline__ void bulk_g2s(uint8_t* dst, const uint8_t* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            umma::smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(umma::smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(umma::smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+// One elected thread: fetch a block's weight tiles into `dst`.
+__device__ __forceinline__ void fetch_block(uint8_t* dst, const uint8_t* tiles, int blk, uint64_t* bar) {
+    expect_tx(bar, BLOCK_BYTES);
+    const uint8_t* src = tiles + (size_t)blk * BLOCK_BYTES;
+    for (uint32_t o = 0; o < BLOCK_BYTES; o += 15360) bulk_g2s(dst + o, src + o, 15360, bar);
+}
+
+template <bool H>
+__device__ __forceinline__ float op_at(const uint8_t* tile, uint32_t R, uint32_t r, uint32_t k) {
+    return umma::Op16<H>::at(*reinterpret_cast<const uint16_t*>(tile + umma::sw128_offset(R, r, k)));
+}
+
+template <bool H>
+__device__ __forceinline__ void put_x32(uint8_t* tile, uint32_t R, uint32_t r, uint32_t k0, const float* v) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) umma::st_chunk<H>(tile, R, r, k0 + 8 * c, v + 8 * c);
+}
+
+}  // namespace
+
+struct TrunkSmem {  // the non-operand scratch
+    float part_s[128][3];
+    float part_q[128][3];
+    float pooled[BOARDS][2 * C];
+    float gb[BOARDS][C];
+    uint64_t wbar[2];
+    uint64_t mbar;
+    uint32_t tmem_slot;
+    int abort_flag;
+};
+
+// Stem scratch, aliased onto the A operands before the first block.
+struct StemSmem {
+    float piles[BOARDS][NTYPE * PILE];
+    float loose[BOARDS][LOOSE];
+    float facts[ROWS][HEX_FACTS];
+    int occ[ROWS];
+    float tokens[BOARDS][NTYPE * TYPE];
+    float proj[BOARDS][NTYPE * C];
+    float glob[BOARDS][C];
+    float tpool[BOARDS][C];
+};
+
+// Readout scratch, aliased onto the A operands after the last block.
+struct HeadSmem {
+    float x[ROWS][C];
+    float input[BOARDS][2 * C + LOOSE];
+    float P[BOARDS][D];
+};
+
+template <bool H>
+__global__ void __launch_bounds__(384, 1)
+    k_trunk_fast(const JobDev* __restrict__ jobs, const uint32_t* __restrict__ row_job,
+                 const uint32_t* __restrict__ row_local, uint32_t total_rows, const uint8_t* __restrict__ tiles,
+                 const float* __restrict__ W, const float* __restrict__ B, const float* __restrict__ LN,
+                 uint16_t* __restrict__ g_pb, uint16_t* __restrict__ g_jp, int* __restrict__ err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((1024u - (umma::smem_u32(smem_raw) & 1023u)) & 1023u);
+    uint8_t* sW[2] = {smem, smem + BLOCK_BYTES};
+    uint8_t* sA1 = smem + 2 * BLOCK_BYTES;
+    uint8_t* sA2 = sA1 + A1_BYTES;
+    TrunkSmem& S = *reinterpret_cast<TrunkSmem*>(sA2 + A2_BYTES);
+    StemSmem& St = *reinterpret_cast<StemSmem*>(sA1);
+    HeadSmem& Hd = *reinterpret_cast<HeadSmem*>(sA1);
+    static_assert(sizeof(StemSmem) <= A1_BYTES + A2_BYTES, "stem scratch must fit the operand space");
+    static_assert(sizeof(HeadSmem) <= A1_BYTES + A2_BYTES, "readout scratch must fit the operand space");
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int quad = warp & 3, cg = warp >> 2;
+    const int row = quad * 32 + lane;       // hex row of the tile (TMEM lane)
+    const int board = row / NH, hex = row % NH;
+    const bool real_row = row < ROWS;
+    const int col0 = cg * 32;
+    const uint32_t ntiles = (total_rows + BOARDS - 1) / BOARDS;
+    const NetLayout& L = c_Lt;
+
+    if (tid == 0) {
+        umma::mbar_init(&S.wbar[0], 1);
+        umma::mbar_init(&S.wbar[1], 1);
+        umma::mbar_init(&S.mbar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        S.abort_flag = 0;
+    }
+    if (warp == 0) umma::tmem_alloc(&S.tmem_slot, 256);
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+    const uint32_t tmem = S.tmem_slot;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    uint32_t wphase[2] = {0, 0}, mphase = 0;
+    if (tid == 0 && blockIdx.x < ntiles) fetch_block(sW[0], tiles, 0, &S.wbar[0]);
+
+    for (uint32_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+        // ---------------------------------------------------------- stem
+        uint32_t gb_[BOARDS];
+        int nb = 0;
+        for (int i = 0; i < BOARDS; ++i) {
+            uint32_t g = tile * BOARDS + i;
+            gb_[i] = g;
+            if (g < total_rows) nb = i + 1;
+        }
+        for (int q = tid; q < ROWS; q += blockDim.x) {
+            int i = q / NH, h = q % NH;
+            float* f = St.facts[q];
+            for (int k = 0; k < HEX_FACTS; ++k) f[k] = 0.0f;
+            St.occ[q] = -1;
+            if (i >= nb) continue;
+            const JobDev& J = jobs[row_job[gb_[i]]];
+            const uint8_t* rw = J.gpu_rows + (size_t)row_local[gb_[i]] * 201;
+            uint8_t owner = rw[h], slot = rw[37 + h], marker = rw[111 + h];
+            if (owner != 255) {
+                f[owner] = 1.0f;
+                f[2] = (float)rw[74 + h] / 5.0f;
+                if (slot != 255) St.occ[q] = owner * NSLOT + slot;
+            }
+            if (marker != 255) f[3 + marker] = 1.0f;
+            f[5] = c_islt[h] ? 1.0f : 0.0f;
+        }
+        for (int q = tid; q < BOARDS * (NTYPE * PILE + LOOSE); q += blockDim.x) {
+            int i = q / (NTYPE * PILE + LOOSE), k = q % (NTYPE * PILE + LOOSE);
+            if (i >= nb) {
+                if (k < NTYPE * PILE) St.piles[i][k] = 0.0f;
+                else St.loose[i][k - NTYPE * PILE] = 0.0f;
+                continue;
+            }
+            const JobDev& J = jobs[row_job[gb_[i]]];
+            const uint8_t* rw = J.gpu_rows + (size_t)row_local[gb_[i]] * 201;
+            if (k < NTYPE * PILE) {
+                St.piles[i][k] = (float)rw[148 + k] / 5.0f;
+            } else {
+                int j = k - NTYPE * PILE;
+                float v;
+                if (j < 12) {
+                    int p = j / 6, f = j % 6;
+                    uint8_t mh = rw[188 + p];
+                    v = f == 0 ? (float)mh / 6.0f
+                      : f == 1 ? (float)(6 - mh) / 6.0f
+                      : f == 2 ? (float)rw[190 + p] / 3.0f
+                      : f == 3 ? (float)rw[192 + p] / 21.0f
+                      : f == 4 ? (float)rw[194 + p] / 21.0f
+                               : (rw[196] == p ? 1.0f : 0.0f);
+                } else if (j == 12) {
+                    v = (float)(uint16_t)(rw[199] | (rw[200] << 8)) / 256.0f;
+                } else if (j == 13) {
+                    v = rw[197] ? 1.0f : 0.0f;
+                } else {
+                    v = rw[198] == 0 ? 1.0f : 0.0f;
+                }
+                St.loose[i][j] = v;
+            }
+        }
+        __syncthreads();
+        const float* seat = W + L.seat;
+        for (int q = tid; q < BOARDS * NTYPE * TYPE; q += blockDim.x) {
+            int i = q / (NTYPE * TYPE), t = (q / TYPE) % NTYPE, j = q % TYPE;
+            float acc = 0.0f;
+            if (i < nb) {
+                const JobDev& J = jobs[row_job[gb_[i]]];
+                for (int k = 0; k < PILE; ++k) acc += St.piles[i][t * PILE + k] * W[L.pile.w + k * TYPE + j];
+                acc += J.cards[t * TYPE + j] + seat[(t / NSLOT) * TYPE + j];
+            }
+            St.tokens[i][t * TYPE + j] = acc;
+        }
+        __syncthreads();
+        for (int q = tid; q < BOARDS * NTYPE * C; q += blockDim.x) {
+            int i = q / (NTYPE * C), t = (q / C) % NTYPE, c = q % C;
+            float acc = 0.0f;
+            for (int k = 0; k < TYPE; ++k) acc += St.tokens[i][t * TYPE + k] * W[L.tok_stem.w + k * C + c];
+            St.proj[i][t * C + c] = acc;
+        }
+        for (int q = tid; q < BOARDS * C; q += blockDim.x) {
+            int i = q / C, c = q % C;
+            float acc = 0.0f;
+            for (int k = 0; k < LOOSE; ++k) acc += St.loose[i][k] * W[L.glob_stem.w + k * C + c];
+            St.glob[i][c] = acc;
+        }
+        __syncthreads();
+        for (int q = tid; q < BOARDS * C; q += blockDim.x) {
+            int i = q / C, c = q % C;
+            float acc = 0.0f;
+            for (int t = 0; t < NTYPE; ++t) acc += umma::gelu_fast(St.proj[i][t * C + c]) / (float)NTYPE;
+            St.tpool[i][c] = acc;
+        }
+        __syncthreads();
+        float x[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            const int c = col0 + j;
+            float v = 0.0f;
+            if (real_row && board < nb) {
+                for (int k = 0; k < HEX_FACTS; ++k) v += St.facts[row][k] * W[L.hex_stem.w + k * C + c];
+                v += B[L.hex_stem.b + c];
+                float occ = St.occ[row] >= 0 ? St.proj[board][St.occ[row] * C + c] : 0.0f;
+                v += occ + W[L.pos + hex * C + c] + St.glob[board][c] + St.tpool[board][c];
+            }
+            x[j] = v;
+        }
+        __syncthreads();  // stem scratch is dead from here
+
+        // ------------------------------------------------- residual blocks
+#pragma unroll 1
+        for (int blk = 0; blk < wc::NET_BLOCKS; ++blk) {
+            const int buf = blk & 1;
+            // a = LNGELU(x)
+            float a[32];
+            {
+                float s = 0.0f;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) s += x[j];
+                S.part_s[row][cg] = s;
+                __syncthreads();
+                const float mean = (S.part_s[row][0] + S.part_s[row][1] + S.part_s[row][2]) * (1.0f / C);
+                float q = 0.0f;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) q += (x[j] - mean) * (x[j] - mean);
+                S.part_q[row][cg] = q;
+                __syncthreads();
+                const float inv = rsqrtf((S.part_q[row][0] + S.part_q[row][1] + S.part_q[row][2]) * (1.0f / C) + 1e-5f);
+                const float* gam = LN + L.norm_g[NetLayout::ln_block(blk, 0)];
+                const float* bet = LN + L.norm_b[NetLayout::ln_block(blk, 0)];
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                    a[j] = real_row ? umma::gelu_fast((x[j] - mean) * inv * gam[col0 + j] + bet[col0 + j]) : 0.0f;
+            }
+            put_x32<H>(sA1, 128, row, col0, a);
+            __syncthreads();
+            // neighbour sums -> columns 96..191; board pooling (mean | max) of a
+            {
+                float nsum[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) nsum[j] = 0.0f;
+                if (real_row) {
+                    for (int d = 0; d < 6; ++d) {
+                        uint8_t nbh = c_nbt[hex][d];
+                        if (nbh == 255) continue;
+                        const int nr = board * NH + nbh;
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) nsum[j] += op_at<H>(sA1, 128, nr, col0 + j);
+                    }
+                }
+                put_x32<H>(sA1, 128, row, C + col0, nsum);
+            }
+            for (int q = tid; q < BOARDS * C; q += blockDim.x) {
+                int i = q / C, c = q % C;
+                float mean = 0.0f, mx = -INFINITY;
+                for (int h = 0; h < NH; ++h) {
+                    float v = op_at<H>(sA1, 128, i * NH + h, c);
+                    mean += v / (float)NH;
+                    mx = fmaxf(mx, v);
+                }
+                S.pooled[i][c] = mean;
+                S.pooled[i][C + c] = mx;
+            }
+            __syncthreads();
+            for (int q = tid; q < BOARDS * C; q += blockDim.x) {
+                int i = q / C, c = q % C;
+                const wc::NetSpan pl = L.pool[blk];
+                float acc = 0.0f;
+                for (int k = 0; k < 2 * C; ++k) acc += S.pooled[i][k] * W[pl.w + k * C + c];
+                S.gb[i][c] = acc + B[pl.b + c];
+            }
+            // mix product (weights of this block must have landed)
+            if (!umma::mbar_wait(&S.wbar[buf], wphase[buf], WAIT_LIMIT)) S.abort_flag = 1;
+            wphase[buf] ^= 1u;
+            umma::fence_async_smem();
+            umma::fence_before_sync();
+            __syncthreads();
+            umma::fence_after_sync();
+            if (tid == 0) {
+                const uint32_t aa = umma::smem_u32(sA1), wb = umma::smem_u32(sW[buf]);
+                const uint32_t idesc = umma::idesc16(128, 96, umma::Op16<H>::fmt);
+#pragma unroll
+                for (int k0 = 0; k0 < 2 * C; k0 += 16)
+                    umma::mma16(tmem, umma::desc_at(aa, 128, k0), umma::desc_at(wb, 96, k0), idesc, k0 > 0);
+                umma::commit(&S.mbar);
+            }
+            if (!umma::mbar_wait(&S.mbar, mphase, WAIT_LIMIT)) S.abort_flag = 1;
+            mphase ^= 1u;
+            umma::fence_after_sync();
+            // y = mix + b + pool bias; LNGELU -> A2
+            float y[32];
+            {
+                float v[32];
+                umma::tmem_ld32(tmem + lane_off + col0, v);
+                const wc::NetSpan mx = L.mix[blk];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) y[j] = v[j] + B[mx.b + col0 + j] + (real_row ? S.gb[board][col0 + j] : 0.0f);
+                float s = 0.0f;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) s += y[j];
+                S.part_s[row][cg] = s;
+                __syncthreads();
+                const float mean = (S.part_s[row][0] + S.part_s[row][1] + S.part_s[row][2]) * (1.0f / C);
+                float q = 0.0f;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) q += (y[j] - mean) * (y[j] - mean);
+                S.part_q[row][cg] = q;
+                __syncthreads();
+                const float inv = rsqrtf((S.part_q[row][0] + S.part_q[row][1] + S.part_q[row][2]) * (1.0f / C) + 1e-5f);
+                const float* gam = LN + L.norm_g[NetLayout::ln_block(blk, 1)];
+                const float* bet = LN + L.norm_b[NetLayout::ln_block(blk, 1)];
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                    y[j] = real_row ? umma::gelu_fast((y[j] - mean) * inv * gam[col0 + j] + bet[col0 + j]) : 0.0f;
+            }
+            put_x32<H>(sA2, 128, row, col0, y);
+            umma::fence_async_smem();
+            umma::fence_before_sync();
+            __syncthreads();
+            umma::fence_after_sync();
+            if (tid == 0) {
+                const uint32_t aa = umma::smem_u32(sA2), wb = umma::smem_u32(sW[buf] + MIX_BYTES);
+                const uint32_t idesc = umma::idesc16(128, 96, umma::Op16<H>::fmt);
+#pragma unroll
+                for (int k0 = 0; k0 < C; k0 += 16)
+                    umma::mma16(tmem + 128, umma::desc_at(aa, 128, k0), umma::desc_at(wb, 96, k0), idesc, k0 > 0);
+                umma::commit(&S.mbar);
+            }
+            if (!umma::mbar_wait(&S.mbar, mphase, WAIT_LIMIT)) S.abort_flag = 1;
+            mphase ^= 1u;
+            umma::fence_after_sync();
+            // the other buffer is free: fetch the next block (or the next tile's first)
+            if (tid == 0) {
+                const bool more = blk + 1 < wc::NET_BLOCKS || tile + gridDim.x < ntiles;
+                if (more) fetch_block(sW[buf ^ 1], tiles, (blk + 1) % wc::NET_BLOCKS, &S.wbar[buf ^ 1]);
+            }
+            {
+                float v[32];
+                umma::tmem_ld32(tmem + lane_off + 128 + col0, v);
+                const wc::NetSpan ou = L.out[blk];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) x[j] += v[j] + B[ou.b + col0 + j];
+            }
+            if (S.abort_flag) break;
+        }
+        // -------------------------------------- final norm and the readout
+        {
+            float s = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) s += x[j];
+            S.part_s[row][cg] = s;
+            __syncthreads();
+            const float mean = (S.part_s[row][0] + S.part_s[row][1] + S.part_s[row][2]) * (1.0f / C);
+            float q = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) q += (x[j] - mean) * (x[j] - mean);
+            S.part_q[row][cg] = q;
+            __syncthreads();
+            const float inv = rsqrtf((S.part_q[row][0] + S.part_q[row][1] + S.part_q[row][2]) * (1.0f / C) + 1e-5f);
+            const float* gam = LN + L.norm_g[NetLayout::LN_TRUNK];
+            const float* bet = LN + L.norm_b[NetLayout::LN_TRUNK];
+            if (real_row) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) Hd.x[row][col0 + j] = umma::gelu_fast((x[j] - mean) * inv * gam[col0 + j] + bet[col0 + j]);
+            }
+        }
+        __syncthreads();
+        for (int q = tid; q < BOARDS * (2 * C + LOOSE); q += blockDim.x) {
+            int i = q / (2 * C + LOOSE), k = q % (2 * C + LOOSE);
+            float v = 0.0f;
+            if (k < C) {
+                for (int h = 0; h < NH; ++h) v += Hd.x[i * NH + h][k] / (float)NH;
+            } else if (k < 2 * C) {
+                v = -INFINITY;
+                for (int h = 0; h < NH; ++h) v = fmaxf(v, Hd.x[i * NH + h][k - C]);
+            } else {
+                v = 0.0f;
+            }
+            Hd.input[i][k] = v;
+        }
+        __syncthreads();
+        // loose scalars are re-read from the rows (the stem scratch is gone)
+        for (int q = tid; q < BOARDS * LOOSE; q += blockDim.x) {
+            int i = q / LOOSE, j = q % LOOSE;
+            float v = 0.0f;
+            if (i < nb) {
+                const JobDev& J = jobs[row_job[gb_[i]]];
+                const uint8_t* rw = J.gpu_rows + (size_t)row_local[gb_[i]] * 201;
+                if (j < 12) {
+                    int p = j / 6, f = j % 6;
+                    uint8_t mh = rw[188 + p];
+                    v = f == 0 ? (float)mh / 6.0f
+                      : f == 1 ? (float)(6 - mh) / 6.0f
+                      : f == 2 ? (float)rw[190 + p] / 3.0f
+                      : f == 3 ? (float)rw[192 + p] / 21.0f
+                      : f == 4 ? (float)rw[194 + p] / 21.0f
+                               : (rw[196] == p ? 1.0f : 0.0f);
+                } else if (j == 12) {
+                    v = (float)(uint16_t)(rw[199] | (rw[200] << 8)) / 256.0f;
+                } else if (j == 13) {
+                    v = rw[197] ? 1.0f : 0.0f;
+                } else {
+                    v = rw[198] == 0 ? 1.0f : 0.0f;
+                }
+            }
+            Hd.input[i][2 * C + j] = v;
+        }
+        __syncthreads();
+        const wc::NetSpan bo = L.board_out;
+        for (int q = tid; q < BOARDS * D; q += blockDim.x) {
+            int i = q / D, c = q % D;
+            float acc = 0.0f;
+            for (int k = 0; k < 2 * C + LOOSE; ++k) acc += Hd.input[i][k] * W[bo.w + k * D + c];
+            Hd.P[i][c] = acc + B[bo.b + c];
+        }
+        __syncthreads();
+        // P and jp are stored as 16-bit operands minus their row mean: every consumer of
+        // them (the join residual stream, the readout y) goes through a
+        // LayerNorm, which ignores a per-row constant, so the shift is exact
+        // and only shrinks the rounding.
+        if (tid < BOARDS * 32) {
+            const int i = tid / 32, l = tid % 32;
+            float s = 0.0f;
+            for (int c = l; c < D; c += 32) s += Hd.P[i][c];
+#pragma unroll
+            for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+            if (l == 0) S.gb[i][0] = s / (float)D;
+        }
+        __syncthreads();
+        for (int q = tid; q < BOARDS * D; q += blockDim.x) {
+            int i = q / D, c = q % D;
+            if (i < nb)
+                g_pb[(size_t)gb_[i] * D + c] = umma::Op16<H>::one(Hd.P[i][c] - S.gb[i][0]);
+        }
+        for (int q = tid; q < BOARDS * JW; q += blockDim.x) {
+            int i = q / JW, c = q % JW;
+            float acc = 0.0f;
+            for (int k = 0; k < D; ++k) acc += Hd.P[i][k] * W[L.join_p.w + k * JW + c];
+            S.pooled[i][c] = acc;
+        }
+        __syncthreads();
+        if (tid < BOARDS * 32) {
+            const int i = tid / 32, l = tid % 32;
+            float s = 0.0f;
+            for (int c = l; c < JW; c += 32) s += S.pooled[i][c];
+#pragma unroll
+            for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+            if (l == 0) S.gb[i][1] = s / (float)JW;
+        }
+        __syncthreads();
+        for (int q = tid; q < BOARDS * JW; q += blockDim.x) {
+            int i = q / JW, c = q % JW;
+            if (i < nb)
+                g_jp[(size_t)gb_[i] * JW + c] = umma::Op16<H>::one(S.pooled[i][c] - S.gb[i][1]);
+        }
+        __syncthreads();
+        if (S.abort_flag) break;
+    }
+    if (tid == 0 && S.abort_flag) atomicExch(err, 3);
+    umma::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) umma::tmem_dealloc(tmem, 256);
+}
+
+void trunk_set_constants(const NetLayout& L, const uint8_t* neighbors, const uint8_t* is_location) {
+    cudaMemcpyToSymbol(c_Lt, &L, sizeof(NetLayout));
+    cudaMemcpyToSymbol(c_nbt, neighbors, 37 * 6);
+    cudaMemcpyToSymbol(c_islt, is_location, 37);
+}
+
+size_t trunk_tiles_bytes() { return (size_t)wc::NET_BLOCKS * BLOCK_BYTES; }
+
+void launch_trunk_fast(const JobDev* jobs, const uint32_t* row_job, const uint32_t* row_local, uint32_t total_rows,
+                       const uint8_t* tiles, const float* W, const float* B, const float* LN, uint16_t* g_pb,
+                       uint16_t* g_jp, bool half, int* err, cudaStream_t s) {
+    if (!total_rows) return;
+    const size_t smem = 2 * BLOCK_BYTES + A1_BYTES + A2_BYTES + sizeof(TrunkSmem) + 1024;
+    auto kern = half ? k_trunk_fast<true> : k_trunk_fast<false>;
+    if (!raise_smem_limit((const void*)kern, smem)) return;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    uint32_t ntiles = (total_rows + BOARDS - 1) / BOARDS;
+    uint32_t grid = std::min<uint32_t>(ntiles, (uint32_t)sms);
+    kern<<<grid, 384, smem, s>>>(jobs, row_job, row_local, total_rows, tiles, W, B, LN, g_pb, g_jp, err);
+}
+
+}  // namespace wcdev

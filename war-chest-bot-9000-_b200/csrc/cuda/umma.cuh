@@ -10,6 +10,7 @@
 // descriptor start address advances by 32 bytes within an atom.
 #pragma once
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include <cstdint>
 
@@ -43,13 +44,48 @@ __device__ __forceinline__ uint64_t desc_at(uint32_t tile_saddr, uint32_t R, uin
     return desc_sw128(tile_saddr + (k0 >> 6) * R * 128u + (k0 & 63) * 2u);
 }
 
-// Instruction descriptor, kind::f16: bf16 A and B (K-major), f32 D.
-__host__ __device__ constexpr uint32_t idesc_bf16(uint32_t M, uint32_t N) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | ((N >> 3) << 17) | ((M >> 4) << 24);
+// Instruction descriptor, kind::f16 with K-major A and B of one 16-bit type
+// (fmt: 0 = f16, 1 = bf16) and an f32 D.
+__host__ __device__ constexpr uint32_t idesc16(uint32_t M, uint32_t N, uint32_t fmt) {
+    return (1u << 4) | (fmt << 7) | (fmt << 10) | ((N >> 3) << 17) | ((M >> 4) << 24);
 }
+__host__ __device__ constexpr uint32_t idesc_bf16(uint32_t M, uint32_t N) { return idesc16(M, N, 1u); }
+
+// The 16-bit operand type of the tensor-core network: HALF = true is IEEE
+// binary16 (11 significant bits), false is bfloat16 (8 significant bits, the
+// fp32 exponent range). Both run at the same tcgen05 rate.
+template <bool HALF>
+struct Op16;
+template <>
+struct Op16<false> {
+    static constexpr uint32_t fmt = 1;
+    static __device__ __forceinline__ uint32_t pack(float a, float b) {
+        __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+        return *reinterpret_cast<uint32_t*>(&v);
+    }
+    static __device__ __forceinline__ uint16_t one(float a) {
+        __nv_bfloat16 v = __float2bfloat16_rn(a);
+        return *reinterpret_cast<uint16_t*>(&v);
+    }
+    static __device__ __forceinline__ float lo(uint32_t w) { return __uint_as_float(w << 16); }
+    static __device__ __forceinline__ float hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+    static __device__ __forceinline__ float at(uint16_t v) { return __uint_as_float((uint32_t)v << 16); }
+};
+template <>
+struct Op16<true> {
+    static constexpr uint32_t fmt = 0;
+    static __device__ __forceinline__ uint32_t pack(float a, float b) {
+        __half2 v = __floats2half2_rn(a, b);
+        return *reinterpret_cast<uint32_t*>(&v);
+    }
+    static __device__ __forceinline__ uint16_t one(float a) { return __half_as_ushort(__float2half_rn(a)); }
+    static __device__ __forceinline__ float lo(uint32_t w) { return __half2float(__ushort_as_half((uint16_t)(w & 0xffffu))); }
+    static __device__ __forceinline__ float hi(uint32_t w) { return __half2float(__ushort_as_half((uint16_t)(w >> 16))); }
+    static __device__ __forceinline__ float at(uint16_t v) { return __half2float(__ushort_as_half(v)); }
+};
 
 // D[tmem] (+)= A * B^T, one elected thread.
-__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+__device__ __forceinline__ void mma16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
@@ -118,33 +154,38 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// Store 8 consecutive bf16 (one 16-byte chunk) of row r, columns [k, k+8).
+// 8 consecutive floats as one 16-byte chunk of 16-bit operands.
+template <bool HALF = false>
+__device__ __forceinline__ uint4 pack_chunk(const float* x) {
+    return make_uint4(Op16<HALF>::pack(x[0], x[1]), Op16<HALF>::pack(x[2], x[3]), Op16<HALF>::pack(x[4], x[5]),
+                      Op16<HALF>::pack(x[6], x[7]));
+}
+
+// Store 8 consecutive operands (one 16-byte chunk) of row r, columns [k, k+8).
+template <bool HALF = false>
 __device__ __forceinline__ void st_chunk(uint8_t* tile, uint32_t R, uint32_t r, uint32_t k, const float* x) {
-    __nv_bfloat162 a = __floats2bfloat162_rn(x[0], x[1]);
-    __nv_bfloat162 b = __floats2bfloat162_rn(x[2], x[3]);
-    __nv_bfloat162 c = __floats2bfloat162_rn(x[4], x[5]);
-    __nv_bfloat162 d = __floats2bfloat162_rn(x[6], x[7]);
-    uint4 v;
-    v.x = *reinterpret_cast<uint32_t*>(&a);
-    v.y = *reinterpret_cast<uint32_t*>(&b);
-    v.z = *reinterpret_cast<uint32_t*>(&c);
-    v.w = *reinterpret_cast<uint32_t*>(&d);
-    *reinterpret_cast<uint4*>(tile + sw128_offset(R, r, k)) = v;
+    *reinterpret_cast<uint4*>(tile + sw128_offset(R, r, k)) = pack_chunk<HALF>(x);
 }
 
 __device__ __forceinline__ void st_zero_chunk(uint8_t* tile, uint32_t R, uint32_t r, uint32_t k) {
     *reinterpret_cast<uint4*>(tile + sw128_offset(R, r, k)) = make_uint4(0, 0, 0, 0);
 }
 
-// Fast GELU for the bf16 path: tanh form with the hardware tanh.approx.
-__device__ __forceinline__ float tanh_fast(float x) {
+// GELU (tanh form) for the tensor-core path, through the identity
+// 0.5 x (1 + tanh(u)) = x / (1 + exp(-2u)), u = sqrt(2/pi) (x + 0.044715 x^3),
+// with the hardware base-2 exponential (relative error about 2^-22) and a fast
+// divide: about 1e-6 relative error everywhere, well under the 16-bit operand
+// rounding, and no cancellation for negative x. The exponent is clamped at
+// 126 so the divisor stays finite (x / (1 + 2^126) is 0 to fp32 precision).
+__device__ __forceinline__ float ex2_approx(float x) {
     float y;
-    asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
 }
 __device__ __forceinline__ float gelu_fast(float x) {
-    float inner = 0.79788456f * (x + 0.044715f * x * x * x);
-    return 0.5f * x * (1.0f + tanh_fast(inner));
+    const float u = 0.79788456f * (x + 0.044715f * x * x * x);
+    const float e = ex2_approx(fminf(-2.8853900817779268f * u, 126.0f));
+    return __fdividef(x, 1.0f + e);
 }
 
 }  // namespace umma

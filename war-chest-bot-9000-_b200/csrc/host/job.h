@@ -60,6 +60,8 @@ struct JobImage {
     std::vector<uint8_t> gpu_rows;                  // nrows_net * GPU_ROW_BYTES
     std::vector<float> cphi;                        // ncfg * CFEAT
     std::vector<uint8_t> cplayer;
+    std::vector<uint32_t> cfg_col;                  // index of each config among its player's configs
+    uint32_t ncfg_player[2] = {0, 0};
     std::vector<float> card_feat;                   // 2 views * NTYPE * CARD_FEATS
     // root beliefs and the carried roots Phase 2 values
     std::vector<float> root_belief;                 // root_nc[0] + root_nc[1]

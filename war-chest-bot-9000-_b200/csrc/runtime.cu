@@ -1,11 +1,14 @@
 // Device runtime: job blobs, batch upload, the solve schedule, download.
 #include "runtime.h"
 
+#include <cuda_fp16.h>
+
 #include <algorithm>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
 #include <stdexcept>
+#include <string>
 
 #include "cuda/kernels.h"
 
@@ -47,7 +50,7 @@ std::unique_ptr<JobBlob> make_blob(std::unique_ptr<JobImage> img) {
         v(J.cell_vidx), v(J.row_off), v(J.row_player), v(J.vg_start), v(J.vge_idx), v(J.vge_w), v(J.rg_start),
         v(J.rge_src), v(J.rge_w), v(J.drawp), v(J.cell_ref), v(J.lr_ridx), v(J.lr_nc), v(J.lr_vidx),
         v(J.leaf_coff), v(J.leaf_cidx), v(J.tl_ridx), v(J.tl_nc), v(J.tl_vidx), v(J.tl_util0), v(J.gpu_rows),
-        v(J.cphi), v(J.cplayer), v(J.card_feat), v(J.root_belief), v(J.carried), v(carry_off)};
+        v(J.cphi), v(J.cplayer), v(J.card_feat), v(J.root_belief), v(J.carried), v(carry_off), v(J.cfg_col)};
     size_t at = 0;
     for (int i = 0; i < JobBlob::N_ARR; ++i) {
         b->off[i] = at;
@@ -68,6 +71,90 @@ std::unique_ptr<JobBlob> make_blob(std::unique_ptr<JobImage> img) {
         if (src[i].bytes) std::memcpy(b->host + b->off[i], src[i].p, src[i].bytes);
     b->img = std::move(img);
     return b;
+}
+
+// ---------------------------------------------------------- fast weights
+
+namespace {
+uint16_t to_bf16(float f) {
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    u += 0x7FFFu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+uint16_t to_op16(float f, bool half) { return half ? __half_as_ushort(__float2half_rn(f)) : to_bf16(f); }
+size_t sw128_offset(uint32_t R, uint32_t r, uint32_t k) {
+    uint32_t atom = k >> 6, kk = k & 63;
+    uint32_t chunk = (kk >> 3) ^ (r & 7);
+    return (size_t)atom * R * 128u + r * 128u + chunk * 16u + (kk & 7) * 2u;
+}
+// B operand tile of a [in = K][out = N] weight (rows k0 .. k0 + K): element
+// (n, k) = W[(k0 + k) * N + n], K-major and swizzled.
+void put_tile(uint8_t* dst, const float* W, uint32_t K, uint32_t N, bool half) {
+    for (uint32_t n = 0; n < N; ++n)
+        for (uint32_t k = 0; k < K; ++k) {
+            uint16_t v = to_op16(W[(size_t)k * N + n], half);
+            std::memcpy(dst + sw128_offset(N, n, k), &v, 2);
+        }
+}
+}  // namespace
+
+void build_fast_pack(DeviceCtx& d, const float* W, const float* B, const float* LN) {
+    const NetLayout& L = d.L;
+    const size_t TJ = 128 * 128 * 2;
+    // layout: 4 join tiles, out tile, trunk tiles, then f32 vectors
+    const size_t MIX = 96 * 3 * 128, BLK = MIX + 96 * 2 * 128;
+    size_t off_out = 4 * TJ, off_trunk = off_out + 2 * TJ, off_f = off_trunk + NET_BLOCKS * BLK;
+    std::vector<float> vec;
+    auto push = [&](const float* src, size_t n) {
+        size_t at = vec.size();
+        vec.insert(vec.end(), src, src + n);
+        return at;
+    };
+    std::vector<float> beff0(NET_JW), beff1(NET_JW);
+    for (int j = 0; j < NET_JW; ++j) {
+        float seat_w = W[L.join_b.w + 128 * NET_JW + j];
+        beff0[j] = B[L.join_b.b + j] - seat_w;
+        beff1[j] = B[L.join_b.b + j] + seat_w;
+    }
+    size_t o_beff0 = push(beff0.data(), NET_JW), o_beff1 = push(beff1.data(), NET_JW);
+    size_t o_bj[3];
+    for (int i = 0; i < 3; ++i) o_bj[i] = push(B + L.join_w[i].b, NET_JW);
+    size_t o_bout = push(B + L.join_out.b, NET_D);
+    size_t o_g[5], o_b[5];
+    for (int i = 0; i < 5; ++i) {
+        int norm = NetLayout::LN_JOIN + i;
+        o_g[i] = push(LN + L.norm_g[norm], L.norm_w[norm]);
+        o_b[i] = push(LN + L.norm_b[norm], L.norm_w[norm]);
+    }
+    std::vector<uint8_t> blob(off_f + 4 * vec.size(), 0);
+    const bool h = d.half;
+    put_tile(blob.data(), W + L.join_b.w, 128, NET_JW, h);
+    for (int i = 0; i < 3; ++i) put_tile(blob.data() + (1 + i) * TJ, W + L.join_w[i].w, NET_JW, NET_JW, h);
+    put_tile(blob.data() + off_out, W + L.join_out.w, NET_JW, NET_D, h);
+    for (int i = 0; i < NET_BLOCKS; ++i) {
+        put_tile(blob.data() + off_trunk + i * BLK, W + L.mix[i].w, 2 * NET_C, NET_C, h);
+        put_tile(blob.data() + off_trunk + i * BLK + MIX, W + L.out[i].w, NET_C, NET_C, h);
+    }
+    std::memcpy(blob.data() + off_f, vec.data(), 4 * vec.size());
+    check(cudaSetDevice(d.device), "set device");
+    if (d.fast_mem) cudaFree(d.fast_mem);
+    check(cudaMalloc((void**)&d.fast_mem, blob.size()), "fast weights");
+    check(cudaMemcpy(d.fast_mem, blob.data(), blob.size(), cudaMemcpyHostToDevice), "upload fast weights");
+    const float* F = reinterpret_cast<const float*>(d.fast_mem + off_f);
+    d.fast.join_tiles = d.fast_mem;
+    d.fast.out_tile = d.fast_mem + off_out;
+    d.fast.trunk_tiles = d.fast_mem + off_trunk;
+    d.fast.beff[0] = F + o_beff0;
+    d.fast.beff[1] = F + o_beff1;
+    for (int i = 0; i < 3; ++i) d.fast.bj[i] = F + o_bj[i];
+    d.fast.bout = F + o_bout;
+    for (int i = 0; i < 5; ++i) {
+        d.fast.ln_g[i] = F + o_g[i];
+        d.fast.ln_b[i] = F + o_b[i];
+    }
+    d.fast.vbias = B[L.value_bias];
+    d.fast.half = h ? 1 : 0;
 }
 
 // ---------------------------------------------------------------- batches
@@ -142,14 +229,14 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
         P.reach2 = J.cfg.snapshots ? A.take(4ull * J.reach_len) : 0;
         P.vals0 = A.take(4ull * J.val_len[0]);
         P.vals1 = A.take(4ull * J.val_len[1]);
-        bool net = dev.have_net;
+        bool net = dev.have_net, exact = net && dev.precise;
         P.cards = net ? A.take(4ull * 2 * 10 * NET_TYPE) : 0;
         P.cardm = net ? A.take(4ull * 2 * 10 * 3 * NET_POOL) : 0;
-        P.pb = net ? A.take(4ull * J.nrows_net * NET_D) : 0;
-        P.jp = net ? A.take(4ull * J.nrows_net * NET_JW) : 0;
+        P.pb = exact ? A.take(4ull * J.nrows_net * NET_D) : 0;
+        P.jp = exact ? A.take(4ull * J.nrows_net * NET_JW) : 0;
         P.cf = net ? A.take(4ull * J.ncfg * NET_D) : 0;
         P.cg = net ? A.take(4ull * J.ncfg * NET_POOL) : 0;
-        P.pooled = net ? A.take(4ull * J.nrows_net * 2 * NET_POOL) : 0;
+        P.pooled = exact ? A.take(4ull * J.nrows_net * 2 * NET_POOL) : 0;
         P.out_strategy = A.take(4ull * J.ncells);
         P.out_roots = A.take(4ull * J.ncarried * (J.root_nc[0] + J.root_nc[1]));
         P.out_carry = J.cfg.snapshots ? A.take(2ull * (jb.nsnaps_kept - 1) * jb.carry_width) : 0;
@@ -213,6 +300,24 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
     }
     b.total_rows = (uint32_t)row_job.size();
     b.total_cfgs = (uint32_t)cfg_job.size();
+    const bool fast = dev.have_net && !dev.precise;
+    std::vector<size_t> o_f16(nj, 0);
+    size_t o_gpool = 0, o_gjp = 0, o_gpb = 0, o_gz = 0, o_tiles = 0, o_err = 0;
+    struct HeadTile { uint32_t job, first, count, pad; };
+    std::vector<HeadTile> head_tiles;
+    if (fast) {
+        for (size_t j = 0; j < nj; ++j) o_f16[j] = A.take(2ull * jobs[j]->img->ncfg * NET_D);
+        size_t R = row_job.size();
+        o_gpool = A.take(4ull * R * 2 * NET_POOL);
+        o_gjp = A.take(2ull * R * NET_JW);
+        o_gpb = A.take(2ull * R * NET_D);
+        o_gz = A.take(2ull * R * NET_JW);
+        for (uint32_t j = 0; j < nj; ++j)
+            for (uint32_t f = 0; f < jobs[j]->img->nrows_net; f += 128)
+                head_tiles.push_back({j, f, std::min<uint32_t>(128, jobs[j]->img->nrows_net - f), 0});
+        o_tiles = A.take(sizeof(HeadTile) * head_tiles.size());
+        o_err = A.take(16);
+    }
     size_t o_jobs = A.take(sizeof(wcdev::JobDev) * nj);
     size_t o_items = A.take(sizeof(wcdev::WorkItem) * items.size());
     size_t o_rj = A.take(4ull * row_job.size()), o_rl = A.take(4ull * row_local.size());
@@ -222,6 +327,8 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
     uint8_t* D = b.dmem;
     // ---- descriptors
     b.hj.resize(nj);
+    std::vector<uint32_t> row_base(nj, 0);
+    for (size_t j = 1; j < nj; ++j) row_base[j] = row_base[j - 1] + jobs[j - 1]->img->nrows_net;
     b.out_off.resize(3 * nj);
     for (size_t j = 0; j < nj; ++j) {
         const JobBlob& jb = *jobs[j];
@@ -260,6 +367,11 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
         d.root_belief = tf(JobBlob::ROOT_BELIEF);
         d.carried = tf(JobBlob::CARRIED);
         d.carry_off = t32(JobBlob::CARRY_OFF);
+        d.cfg_col = t32(JobBlob::CFG_COL);
+        d.ncfg_player[0] = J.ncfg_player[0];
+        d.ncfg_player[1] = J.ncfg_player[1];
+        d.row_base = row_base[j];
+        d.f16 = fast ? reinterpret_cast<uint16_t*>(D + o_f16[j]) : nullptr;
         d.cur = reinterpret_cast<float*>(D + P.cur);
         d.regret = reinterpret_cast<float*>(D + P.regret);
         d.sum = reinterpret_cast<float*>(D + P.sum);
@@ -271,11 +383,11 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
         if (dev.have_net) {
             d.cards = reinterpret_cast<float*>(D + P.cards);
             d.cardm = reinterpret_cast<float*>(D + P.cardm);
-            d.pb = reinterpret_cast<float*>(D + P.pb);
-            d.jp = reinterpret_cast<float*>(D + P.jp);
+            d.pb = dev.precise ? reinterpret_cast<float*>(D + P.pb) : nullptr;
+            d.jp = dev.precise ? reinterpret_cast<float*>(D + P.jp) : nullptr;
             d.cf = reinterpret_cast<float*>(D + P.cf);
             d.cg = reinterpret_cast<float*>(D + P.cg);
-            d.pooled = reinterpret_cast<float*>(D + P.pooled);
+            d.pooled = dev.precise ? reinterpret_cast<float*>(D + P.pooled) : nullptr;
         }
         d.out_strategy = reinterpret_cast<float*>(D + P.out_strategy);
         d.out_roots = reinterpret_cast<float*>(D + P.out_roots);
@@ -304,6 +416,15 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
     b.d_row_local = reinterpret_cast<uint32_t*>(D + o_rl);
     b.d_cfg_job = reinterpret_cast<uint32_t*>(D + o_cj);
     b.d_cfg_local = reinterpret_cast<uint32_t*>(D + o_cl);
+    if (fast) {
+        b.g_pooled = reinterpret_cast<float*>(D + o_gpool);
+        b.g_jp = reinterpret_cast<uint16_t*>(D + o_gjp);
+        b.g_pb = reinterpret_cast<uint16_t*>(D + o_gpb);
+        b.g_zout = reinterpret_cast<uint16_t*>(D + o_gz);
+        b.d_head_tiles = D + o_tiles;
+        b.n_head_tiles = (uint32_t)head_tiles.size();
+        b.d_err = reinterpret_cast<int*>(D + o_err);
+    }
     cudaStream_t s = dev.stream;
     for (size_t j = 0; j < nj; ++j)
         check(cudaMemcpyAsync(D + plan[j].tables, jobs[j]->host, jobs[j]->bytes, cudaMemcpyHostToDevice, s), "upload job tables");
@@ -316,6 +437,12 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
     if (!cfg_job.empty()) {
         check(cudaMemcpyAsync(b.d_cfg_job, cfg_job.data(), 4 * cfg_job.size(), cudaMemcpyHostToDevice, s), "upload cfgs");
         check(cudaMemcpyAsync(b.d_cfg_local, cfg_local.data(), 4 * cfg_local.size(), cudaMemcpyHostToDevice, s), "upload cfgs");
+    }
+    if (fast) {
+        if (!head_tiles.empty())
+            check(cudaMemcpyAsync(b.d_head_tiles, head_tiles.data(), sizeof(HeadTile) * head_tiles.size(),
+                                  cudaMemcpyHostToDevice, s), "upload head tiles");
+        check(cudaMemsetAsync(b.d_err, 0, 16, s), "clear error flag");
     }
     check(cudaStreamSynchronize(s), "batch upload");
     return bp;
@@ -372,7 +499,11 @@ struct Sched {
     }
     void leaf_values_(int p, int pool_mask) {
         DeviceCtx& dv = *b.dev;
-        if (dv.have_net) {
+        if (dv.have_net && !dv.precise) {
+            wcdev::launch_pool_fast(J, b.d_row_job, b.d_row_local, b.total_rows, pool_mask, b.g_pooled, s);
+            wcdev::launch_join_fast(dv.fast, p, b.g_pooled, b.g_jp, b.g_zout, b.total_rows, b.d_err, s);
+            wcdev::launch_head_fast(J, b.d_head_tiles, b.n_head_tiles, dv.fast, p, b.g_zout, b.g_pb, b.d_err, s);
+        } else if (dv.have_net) {
             if (pool_mask) wcdev::launch_pool(J, b.d_row_job, b.d_row_local, b.total_rows, pool_mask, s);
             wcdev::launch_join_readout(J, b.d_row_job, b.d_row_local, b.total_rows, p, dv.W, dv.B, dv.LN, s);
         } else {
@@ -399,6 +530,83 @@ struct Sched {
 
 }  // namespace
 
+void enqueue_leaf_values(Batch& b, int p) {
+    if (b.jobs.empty()) return;
+    DeviceCtx& dv = *b.dev;
+    check(cudaSetDevice(dv.device), "set device");
+    Sched S(b);
+    const uint32_t nj = (uint32_t)b.jobs.size();
+    auto mark = [&](int i) {
+        if (!b.profile) return;
+        if (!b.marks[i]) check(cudaEventCreate(&b.marks[i]), "event");
+        check(cudaEventRecord(b.marks[i], S.s), "event");
+    };
+    mark(0);
+    if (dv.have_net) {
+        S.timed(TC_NET_SOLVE, [&] {
+            wcdev::launch_cards(S.J, nj, dv.W, dv.B, S.s);
+            if (dv.precise) {
+                wcdev::launch_trunk(S.J, b.d_row_job, b.d_row_local, b.total_rows, dv.W, dv.B, dv.LN, S.s);
+            } else {
+                wcdev::launch_trunk_fast(S.J, b.d_row_job, b.d_row_local, b.total_rows, dv.fast.trunk_tiles, dv.W,
+                                         dv.B, dv.LN, b.g_pb, b.g_jp, dv.half, b.d_err, S.s);
+            }
+            wcdev::launch_configs(S.J, b.d_cfg_job, b.d_cfg_local, b.total_cfgs, dv.W, dv.B, dv.LN, S.s);
+            if (!dv.precise) wcdev::launch_pack_f16(S.J, b.d_cfg_job, b.d_cfg_local, b.total_cfgs, dv.half, S.s);
+        });
+    }
+    S.timed(TC_INIT, [&] {
+        wcdev::launch_init_rows(S.J, S.it(b.rows_all), b.rows_all.n, S.s);
+        wcdev::launch_seed_root(S.J, nj, 0, -1, S.s);
+    });
+    S.propagate(wcdev::STRAT_CUR, 0, 3, 1, 1.0f);
+    mark(1);
+    S.leaf_values(p, 3);
+    mark(2);
+    check(cudaGetLastError(), "leaf values launch");
+}
+
+void download_leaf_values(Batch& b, size_t job, int p, float* out) {
+    const JobImage& J = *b.jobs[job]->img;
+    const wcdev::JobDev& d = b.hj[job];
+    cudaStream_t s = b.dev->stream;
+    std::vector<float> vals(J.val_len[p]);
+    check(cudaMemcpyAsync(vals.data(), d.vals[p], 4ull * J.val_len[p], cudaMemcpyDeviceToHost, s), "download values");
+    check(cudaStreamSynchronize(s), "download values");
+    size_t at = 0;
+    for (uint32_t r = 0; r < J.nrows_net; ++r) {
+        uint32_t v0 = J.lr_vidx[2 * r + p], n = J.lr_nc[2 * r + p];
+        for (uint32_t c = 0; c < n; ++c) out[at++] = vals[v0 + c];
+    }
+}
+
+void download_board_rows(Batch& b, size_t job, float* pb, float* jp) {
+    const JobImage& J = *b.jobs[job]->img;
+    const wcdev::JobDev& d = b.hj[job];
+    cudaStream_t s = b.dev->stream;
+    const size_t n = J.nrows_net;
+    if (b.dev->precise) {
+        if (pb) check(cudaMemcpyAsync(pb, d.pb, 4 * n * NET_D, cudaMemcpyDeviceToHost, s), "download P");
+        if (jp) check(cudaMemcpyAsync(jp, d.jp, 4 * n * NET_JW, cudaMemcpyDeviceToHost, s), "download jp");
+        check(cudaStreamSynchronize(s), "download rows");
+        return;
+    }
+    std::vector<uint16_t> hp(n * NET_D), hj(n * NET_JW);
+    check(cudaMemcpyAsync(hp.data(), b.g_pb + (size_t)d.row_base * NET_D, 2 * n * NET_D, cudaMemcpyDeviceToHost, s), "download P");
+    check(cudaMemcpyAsync(hj.data(), b.g_jp + (size_t)d.row_base * NET_JW, 2 * n * NET_JW, cudaMemcpyDeviceToHost, s), "download jp");
+    check(cudaStreamSynchronize(s), "download rows");
+    const bool half = b.dev->half;
+    auto f = [half](uint16_t v) {
+        if (half) return __half2float(__ushort_as_half(v));
+        uint32_t u = (uint32_t)v << 16;
+        float x;
+        std::memcpy(&x, &u, 4);
+        return x;
+    };
+    if (pb) for (size_t i = 0; i < hp.size(); ++i) pb[i] = f(hp[i]);
+    if (jp) for (size_t i = 0; i < hj.size(); ++i) jp[i] = f(hj[i]);
+}
+
 void enqueue_solve(Batch& b) {
     if (b.jobs.empty()) return;
     DeviceCtx& dv = *b.dev;
@@ -419,8 +627,14 @@ void enqueue_solve(Batch& b) {
     if (dv.have_net) {
         S.timed(TC_NET_SOLVE, [&] {
             wcdev::launch_cards(S.J, nj, dv.W, dv.B, S.s);
-            wcdev::launch_trunk(S.J, b.d_row_job, b.d_row_local, b.total_rows, dv.W, dv.B, dv.LN, S.s);
+            if (dv.precise) {
+                wcdev::launch_trunk(S.J, b.d_row_job, b.d_row_local, b.total_rows, dv.W, dv.B, dv.LN, S.s);
+            } else {
+                wcdev::launch_trunk_fast(S.J, b.d_row_job, b.d_row_local, b.total_rows, dv.fast.trunk_tiles, dv.W,
+                                         dv.B, dv.LN, b.g_pb, b.g_jp, dv.half, b.d_err, S.s);
+            }
             wcdev::launch_configs(S.J, b.d_cfg_job, b.d_cfg_local, b.total_cfgs, dv.W, dv.B, dv.LN, S.s);
+            if (!dv.precise) wcdev::launch_pack_f16(S.J, b.d_cfg_job, b.d_cfg_local, b.total_cfgs, dv.half, S.s);
         });
     }
     // Solver::new: uniform strategy, reaches, reach-weighted sum seed, snapshot 0
@@ -473,6 +687,14 @@ void enqueue_solve(Batch& b) {
     }
     mark(2);
     check(cudaGetLastError(), "solve launch");
+}
+
+void check_batch_error(Batch& b) {
+    if (!b.d_err) return;
+    int e[4] = {0, 0, 0, 0};
+    check(cudaMemcpyAsync(e, b.d_err, 16, cudaMemcpyDeviceToHost, b.dev->stream), "read error flag");
+    check(cudaStreamSynchronize(b.dev->stream), "read error flag");
+    if (e[0]) throw std::runtime_error("a tensor-core wait exceeded its iteration limit (code " + std::to_string(e[0]) + ")");
 }
 
 void download(Batch& b, size_t job, float* strategy, float* roots, uint16_t* carries) {

@@ -23,11 +23,18 @@ struct DeviceCtx {
     float* B = nullptr;
     float* LN = nullptr;
     bool have_net = false;
-    bool precise = true;
+    bool precise = true;  // fp32 network in the reference's operation order
+    bool half = true;     // tensor-core network operands: f16 (true) or bf16
     uint64_t version = 0;
     NetLayout L;
+    // 16-bit tensor-core copy of the network (fast path)
+    uint8_t* fast_mem = nullptr;
+    wcdev::FastNetDev fast{};
     std::mutex mu;  // one batch at a time per device
 };
+
+// Build the fast-path weight pack from the fp32 blob (host arrays) and upload it.
+void build_fast_pack(DeviceCtx& d, const float* W, const float* B, const float* LN);
 
 // A job's flattened tables in one pinned host blob (device copies keep the
 // same layout).
@@ -39,7 +46,7 @@ struct JobBlob {
     enum Arr {
         CELL_VIDX, ROW_OFF, ROW_PLAYER, VG_START, VGE_IDX, VGE_W, RG_START, RGE_SRC, RGE_W, DRAWP, CELL_REF,
         LR_RIDX, LR_NC, LR_VIDX, LEAF_COFF, LEAF_CIDX, TL_RIDX, TL_NC, TL_VIDX, TL_UTIL0, GPU_ROWS, CPHI,
-        CPLAYER, CARD_FEAT, ROOT_BELIEF, CARRIED, CARRY_OFF, N_ARR
+        CPLAYER, CARD_FEAT, ROOT_BELIEF, CARRIED, CARRY_OFF, CFG_COL, N_ARR
     };
     size_t off[N_ARR] = {};
     uint32_t nexit = 0, carry_width = 0, nsnaps_kept = 0;
@@ -66,6 +73,14 @@ struct Batch {
     uint32_t* d_cfg_job = nullptr;
     uint32_t* d_cfg_local = nullptr;
     uint32_t total_rows = 0, total_cfgs = 0, max_carried = 0;
+    // fast network path: global per-row bf16 activations and per-job tiles
+    float* g_pooled = nullptr;    // [rows][2][POOL]
+    uint16_t* g_jp = nullptr;     // [rows][JW]
+    uint16_t* g_pb = nullptr;     // [rows][D]
+    uint16_t* g_zout = nullptr;   // [rows][JW]
+    void* d_head_tiles = nullptr;
+    uint32_t n_head_tiles = 0;
+    int* d_err = nullptr;
     std::vector<size_t> out_off;  // per job: strategy, roots, carry offsets in dmem
     double node_updates = 0.0;    // sum over jobs of nodes * iters
     double leaf_evals = 0.0;      // network-row joins per solve
@@ -94,9 +109,21 @@ void read_profile(Batch& b, double* ms /* N_TC */);
 std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobBlob*>& jobs);
 // Run the whole solve on the device (asynchronous on dev.stream).
 void enqueue_solve(Batch& b);
+// Leaf evaluation alone: the per-solve network, the initial (uniform)
+// reaches, then every network row's values for traverser p.
+void enqueue_leaf_values(Batch& b, int p);
+// Values of one job's network rows for traverser p, rows in reference
+// leaf_rows order, each row's configs in support order.
+void download_leaf_values(Batch& b, size_t job, int p, float* out);
+// The per-solve board vectors P[rows][256] and join projections jp[rows][128]
+// of one job as the network path stores them (the bf16 path stores them minus
+// their row means).
+void download_board_rows(Batch& b, size_t job, float* pb, float* jp);
 // Copy one job's results to host buffers (synchronous). Any pointer may be null.
 void download(Batch& b, size_t job, float* strategy, float* roots, uint16_t* carries);
 
 void check(cudaError_t e, const char* what);
+// Throw if a kernel recorded a bounded-wait timeout during the last solve.
+void check_batch_error(Batch& b);
 
 }  // namespace wc

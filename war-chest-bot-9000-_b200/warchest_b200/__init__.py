@@ -82,6 +82,9 @@ def _load() -> C.CDLL:
         "wc_batch_upload": (I, [VP, I, P(VP), C.c_size_t, P(VP)]),
         "wc_batch_solve": (I, [VP]),
         "wc_batch_solve_profiled": (I, [VP, P(C.c_double), I]),
+        "wc_batch_leaf_values": (I, [VP, I, P(C.c_double)]),
+        "wc_batch_download_leaf_values": (I, [VP, C.c_size_t, I, VP]),
+        "wc_batch_download_board_rows": (I, [VP, C.c_size_t, VP, VP]),
         "wc_batch_download": (I, [VP, C.c_size_t, VP, VP, VP]),
         "wc_batch_stats": (None, [VP, P(C.c_double), P(C.c_double), P(U64), P(U64)]),
         "wc_batch_free": (None, [VP]),
@@ -346,6 +349,27 @@ class DeviceBatch:
         _check(lib().wc_batch_solve_profiled(self._h, ms, 9))
         return dict(zip(self.TIME_CLASSES, list(ms)))
 
+    def leaf_values(self, p: int, profile: bool = False):
+        """Run leaf evaluation alone for traverser p (initial reaches); with
+        profile=True return the per-class timings in ms."""
+        ms = (C.c_double * 9)() if profile else None
+        _check(lib().wc_batch_leaf_values(self._h, p, ms))
+        return dict(zip(self.TIME_CLASSES, list(ms))) if profile else None
+
+    def leaf_values_of(self, j: int, p: int) -> np.ndarray:
+        n = int(self.jobs[j].counts()[14 + p])
+        out = np.zeros(max(n, 1), np.float32)
+        _check(lib().wc_batch_download_leaf_values(self._h, j, p, out.ctypes.data))
+        return out[:n]
+
+    def board_rows(self, j: int):
+        """(P[rows, 256], jp[rows, 128]) of job j as the network path stores them."""
+        n = self.jobs[j].info["net_rows"]
+        pb = np.zeros((max(n, 1), 256), np.float32)
+        jp = np.zeros((max(n, 1), 128), np.float32)
+        _check(lib().wc_batch_download_board_rows(self._h, j, pb.ctypes.data, jp.ctypes.data))
+        return pb[:n], jp[:n]
+
     def stats(self):
         nu, le = C.c_double(), C.c_double()
         tb, db = C.c_uint64(), C.c_uint64()
@@ -378,14 +402,23 @@ class DeviceBatch:
             self.free()
 
 
-def spawn(device, dims=None, w=None, b=None, ln=None, precise: bool = True) -> GpuClient:
+NET_MODES = {"bf16": 0, "exact": 1, "f16": 2}
+
+
+def spawn(device, dims=None, w=None, b=None, ln=None, precise: bool = True, net: Optional[str] = None) -> GpuClient:
     """gpu::service::spawn (engine/src/gpu/service.rs:55-82). `device` is an
-    index or a list of indices; w=None runs without a value network."""
+    index or a list of indices; w=None runs without a value network.
+
+    net: "exact" (fp32, the reference CPU network's operation order), "f16"
+    or "bf16" (tcgen05 tensor cores with that operand type, fp32 accumulate).
+    Without `net`, precise=True means "exact" and False means "f16" (the
+    reference GPU service's fast mode computes with f16 operands)."""
+    mode = NET_MODES[net if net is not None else ("exact" if precise else "f16")]
     devs = [device] if isinstance(device, int) else list(device)
     arr = (C.c_int * len(devs))(*devs)
     ws, keep = _weights_struct(dims, w, b, ln)
     h = C.c_void_p()
-    _check(lib().wc_init(len(devs), arr, C.byref(ws) if ws else None, int(precise), C.byref(h)))
+    _check(lib().wc_init(len(devs), arr, C.byref(ws) if ws else None, mode, C.byref(h)))
     return GpuClient(h.value)
 
 
