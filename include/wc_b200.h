@@ -180,6 +180,8 @@ void wc_batch_free(wc_batch* b);
 int wc_debug_umma_gemm(const uint16_t* a, const uint16_t* b, int k, int n, float* d);
 
 /* ---- streaming submit / wait ---------------------------------------------- */
+/* The job stays owned by the caller and must outlive the wc_wait of its
+ * ticket; free it (wc_job_free) after that wait returns. */
 int wc_submit(wc_ctx* ctx, wc_job* job, uint64_t* ticket);
 int wc_wait(wc_ctx* ctx, uint64_t ticket, wc_result* out);
 /* Outstanding submitted cells, for routing (GpuClient::queued_work). */
