@@ -179,6 +179,21 @@ void wc_batch_free(wc_batch* b);
  * self-test of the tensor-core kernels. k % 64 == 0, n % 16 == 0, n <= 256. */
 int wc_debug_umma_gemm(const uint16_t* a, const uint16_t* b, int k, int n, float* d);
 
+/* wc_debug_umma_gemm without any device allocation; it has no counterpart in
+ * the reference. For callers that cannot call cudaMalloc: a host engine whose
+ * device memory is owned by another allocator (a caching allocator holding
+ * the free memory, or an arena fixed at start-up), or a latency-bound caller
+ * for whom cudaMalloc / cudaFree would synchronise the device. Same inputs,
+ * outputs and kernel; the device copies of a and b, the result and a status
+ * word live in one static device array of 327,936 bytes that every GPU
+ * loading this library holds until exit, so k <= 256 (n <= 256 as before);
+ * larger k is rejected with WC_E_ARG. The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress); make that first call before
+ * any stream capture. All calls share the one array: calls that overlap on
+ * the GPU (from several host threads, say) race and must be serialised by the
+ * caller. */
+int wc_debug_umma_gemm_static(const uint16_t* a, const uint16_t* b, int k, int n, float* d);
+
 /* ---- streaming submit / wait ---------------------------------------------- */
 /* The job stays owned by the caller and must outlive the wc_wait of its
  * ticket; free it (wc_job_free) after that wait returns. */

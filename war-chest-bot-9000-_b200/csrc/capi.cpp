@@ -398,6 +398,21 @@ int wc_debug_umma_gemm(const uint16_t* a, const uint16_t* b, int k, int n, float
     return WC_OK;
 }
 
+int wc_debug_umma_gemm_static(const uint16_t* a, const uint16_t* b, int k, int n, float* d) {
+    if (!a || !b || !d) return fail(WC_E_ARG, "null operand");
+    switch (wcdev::umma_selftest_static(a, b, k, n, d)) {
+        case 0: return WC_OK;
+        case 1: return fail(WC_E_ARG, "k must be a positive multiple of 64; n a multiple of 16 in [16, 256]");
+        case 4:
+            return fail(WC_E_ARG, "k = " + std::to_string(k) +
+                                      " exceeds 256, the largest problem the static scratch holds "
+                                      "(128 x 256 and 256 x 256 bf16 operands, a 128 x 256 f32 result)");
+        case 5: return fail(WC_E_CUDA, "cudaGetSymbolAddress of the static scratch failed");
+        case 3: return fail(WC_E_CUDA, "tcgen05 self-test: the MMA completion wait timed out");
+        default: return fail(WC_E_CUDA, "tcgen05 self-test: CUDA error");
+    }
+}
+
 int wc_job_counts(const wc_job* job, uint64_t* out, int n) {
     if (!job || !out || n < 20) return fail(WC_E_ARG, "wc_job_counts needs 20 slots");
     const JobImage& J = *job->blob->img;

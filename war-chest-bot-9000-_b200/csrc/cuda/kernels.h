@@ -46,6 +46,10 @@ void launch_join_readout(const JobDev* jobs, const uint32_t* row_job, const uint
 // and the runtime's launch check reports it).
 bool raise_smem_limit(const void* fn, size_t smem);
 int umma_selftest(const uint16_t* A, const uint16_t* B, int K, int N, float* D);
+// The same with device staging in a static array (no allocation): 0 ok,
+// 1 bad shape, 2 CUDA error, 3 tcgen05 wait timed out, 4 k beyond 256,
+// 5 the array's device address could not be looked up.
+int umma_selftest_static(const uint16_t* A, const uint16_t* B, int K, int N, float* D);
 void launch_pool_fast(const JobDev* jobs, const uint32_t* row_job, const uint32_t* row_local, uint32_t total_rows,
                       int mask, float* pooled, cudaStream_t s);
 void launch_join_fast(const FastNetDev& fn, int p, const float* pooled, const uint16_t* jp, uint16_t* zout,

@@ -6,6 +6,7 @@
 
 #include <algorithm>
 #include <cstdint>
+#include <map>
 #include <mutex>
 #include <set>
 
@@ -528,6 +529,67 @@ int umma_selftest(const uint16_t* A, const uint16_t* B, int K, int N, float* D) 
     cudaFree(dD);
     cudaFree(dS);
     if (e != cudaSuccess) return 2;
+    return status ? 3 : 0;
+}
+
+// ------------------------------------------ allocation-free GEMM self-test
+// The same tcgen05 self-test as umma_selftest, for callers that must not
+// allocate device memory: a host engine whose device memory belongs to another
+// allocator (a caching allocator that owns the free memory, or a fixed arena
+// sized at start-up), and callers on a latency-bound path, where cudaMalloc
+// and cudaFree would synchronise the device and stall every other stream.
+// Instead of four cudaMalloc'd buffers, the operands, the result and the
+// status word live in one file-scope device array sized for the largest
+// accepted problem (k = n = 256): 320.25 KB, held by every GPU that loads
+// this library until the process exits.
+constexpr size_t SCR_STATUS = 0, SCR_A = 256, SCR_B = SCR_A + 128 * 256 * 2, SCR_D = SCR_B + 256 * 256 * 2;
+constexpr size_t STATIC_SCRATCH_BYTES = SCR_D + 128 * 256 * 4;  // 327,936 bytes
+static __device__ __align__(256) uint8_t g_gemm_scratch[STATIC_SCRATCH_BYTES];
+
+// Device address of g_gemm_scratch on the current device. Host code cannot
+// use the array's name as a device pointer (it names a host-side stand-in),
+// so the address is looked up once per device, on that device's first call.
+static uint8_t* gemm_scratch_address(cudaError_t* e) {
+    static std::mutex mu;
+    static std::map<int, uint8_t*> addr;
+    int dev = 0;
+    *e = cudaGetDevice(&dev);
+    if (*e != cudaSuccess) return nullptr;
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = addr.find(dev);
+    if (it != addr.end()) return it->second;
+    uint8_t* ptr = nullptr;
+    *e = cudaGetSymbolAddress((void**)&ptr, g_gemm_scratch);
+    if (*e != cudaSuccess) return nullptr;
+    addr[dev] = ptr;
+    return ptr;
+}
+
+int umma_selftest_static(const uint16_t* A, const uint16_t* B, int K, int N, float* D) {
+    if (K <= 0 || K % 64 || N % 16 || N < 16 || N > 256) return 1;
+    if (K > 256) return 4;  // beyond the static scratch
+    cudaError_t e = cudaSuccess;
+    uint8_t* scr = gemm_scratch_address(&e);
+    if (!scr) return 5;
+    const size_t a_bytes = 128ull * K * 2, b_bytes = (size_t)N * K * 2, d_bytes = 128ull * N * 4;
+    auto* dA = reinterpret_cast<__nv_bfloat16*>(scr + SCR_A);
+    auto* dB = reinterpret_cast<__nv_bfloat16*>(scr + SCR_B);
+    auto* dD = reinterpret_cast<float*>(scr + SCR_D);
+    auto* dS = reinterpret_cast<int*>(scr + SCR_STATUS);
+    // The array keeps the previous call's contents: A, B and D are rewritten
+    // in full; the status word must start at zero.
+    if (cudaMemcpy(dA, A, a_bytes, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(dB, B, b_bytes, cudaMemcpyHostToDevice) != cudaSuccess || cudaMemset(dS, 0, 4) != cudaSuccess)
+        return 2;
+    size_t smem = a_bytes + b_bytes + 1024;
+    if (!raise_smem_limit((const void*)k_umma_selftest, smem)) return 2;
+    k_umma_selftest<<<1, 128, smem>>>(dA, dB, K, N, dD, dS);
+    int status = 0;
+    e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return 2;
+    if (cudaMemcpy(D, dD, d_bytes, cudaMemcpyDeviceToHost) != cudaSuccess ||
+        cudaMemcpy(&status, dS, 4, cudaMemcpyDeviceToHost) != cudaSuccess)
+        return 2;
     return status ? 3 : 0;
 }
 

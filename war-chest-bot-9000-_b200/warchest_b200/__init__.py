@@ -92,6 +92,7 @@ def _load() -> C.CDLL:
         "wc_wait": (I, [VP, U64, P(_Result)]),
         "wc_queued_work": (U64, [VP]),
         "wc_debug_umma_gemm": (I, [VP, VP, I, I, VP]),
+        "wc_debug_umma_gemm_static": (I, [VP, VP, I, I, VP]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
