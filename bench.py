@@ -189,7 +189,7 @@ def main():
     wc.set_cap_marker_value(0.0)  # the reference bench pins the horizon payoff at 0 (rebelbench.rs:35)
     oracle_lib.lib().oracle_set_cap_marker_value(0.0)
     cfg = wc.Cfg(depth=args.depth, iters=args.iters, snapshots=False, cfr=cfr_plus(wc), node_cap=200000)
-    seeds = list(range(rank * args.subgames, (rank + 1) * args.subgames))
+    seeds = seed_range(rank, args.subgames)
     weights = wc.seeded_weights("he", 0) if args.net != "none" else None
     workload = {"workload": f"configs[2]: {args.subgames} subgames/GPU, depth {args.depth}, {args.iters} CFR+ iters, "
                             f"v5 net every iteration, {args.plies}-ply seeded roots",
@@ -216,12 +216,8 @@ def main():
     # weights: rank 0's seeded blob, broadcast once over NCCL when sharded
     if weights is not None and world > 1:
         import torch
-        import torch.distributed as dist
 
-        dev = torch.device("cuda", local)
-        tw = [torch.from_numpy(a).to(dev) for a in weights[1:]]
-        for t in tw:
-            dist.broadcast(t, src=0)
+        tw = broadcast_weights(weights, torch.device("cuda", local))
         torch.cuda.synchronize()
         client = wc.spawn(local, net=args.net)
         client.set_weights_device(0, tw[0].data_ptr(), tw[1].data_ptr(), tw[2].data_ptr())
@@ -304,6 +300,30 @@ def launches_per_step(levels, iters, net):
     return setup + iters * per_iter + snaps + phase2
 
 
+def seed_range(rank, subgames):
+    """The contiguous seed block of one rank (weak scaling: every rank solves
+    its own `subgames` roots)."""
+    return list(range(rank * subgames, (rank + 1) * subgames))
+
+
+def broadcast_weights(weights, device):
+    """Rank 0's (w, b, ln) to every rank, once, as device tensors (the only
+    collective on the data path's setup; none per iteration)."""
+    import torch
+    import torch.distributed as dist
+
+    tw = [torch.from_numpy(a).to(device) for a in weights[1:]]
+    for t in tw:
+        dist.broadcast(t, src=0)
+    return tw
+
+
+def _dist_device():
+    import torch.distributed as dist
+
+    return "cuda" if dist.get_backend() == "nccl" else "cpu"
+
+
 def barrier(world):
     if world > 1:
         import torch.distributed as dist
@@ -317,7 +337,7 @@ def max_over_ranks(world, x):
     import torch
     import torch.distributed as dist
 
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    t = torch.tensor([x], dtype=torch.float64, device=_dist_device())
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 
@@ -328,7 +348,7 @@ def allsum(world, x):
     import torch
     import torch.distributed as dist
 
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    t = torch.tensor([x], dtype=torch.float64, device=_dist_device())
     dist.all_reduce(t)
     return float(t.item())
 

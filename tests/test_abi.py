@@ -1,0 +1,77 @@
+"""The C ABI without a GPU: the library loads, exports every function that
+include/wc_b200.h declares, and its device entry points fail loudly (an
+error status and message, no CPU fallback) when no CUDA device is present.
+Host-only entry points (roots, jobs, weights) work on the CPU."""
+import ctypes as C
+import os
+import re
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "wc_b200.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    names = re.findall(r"^\s*(?:const\s+)?(?:int|void|uint64_t|size_t|char)\s*\*?\s*(wc_\w+)\s*\(", text, flags=re.M)
+    return sorted(set(names))
+
+
+def test_header_declares_the_service_surface():
+    names = declared_functions()
+    for must in ["wc_init", "wc_publish", "wc_publish_device", "wc_solve_batch", "wc_submit", "wc_wait",
+                 "wc_result_free", "wc_job_build", "wc_last_error", "wc_queued_work", "wc_shutdown"]:
+        assert must in names
+
+
+def test_library_exports_every_declared_function(wc):
+    lib = wc.lib()
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_device_entry_points_fail_loudly_without_a_gpu(wc):
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("a CUDA device is present")
+    with pytest.raises(wc.SolveError) as e:
+        wc.spawn(0)
+    assert e.value.code == 2  # WC_E_CUDA
+    buf = C.create_string_buffer(4096)
+    wc.lib().wc_last_error(buf, 4096)
+    assert buf.value
+
+
+def test_root_bytes_match_the_oracle_build(wc, oracle):
+    for seed in range(4):
+        a = wc.generate_root(seed)
+        buf = C.create_string_buffer(1 << 20)
+        n = C.c_size_t()
+        assert oracle.lib().oracle_root_generate(C.c_uint64(seed), 20, 1, buf, C.c_size_t(1 << 20), C.byref(n)) == 0
+        assert a == buf.raw[: n.value]
+        assert a == wc.generate_root(seed)  # deterministic
+
+
+def test_weight_blobs(wc, oracle):
+    dims, w, b, ln = wc.seeded_weights("test", 0xD15EA5E)
+    assert dims == [5]
+    assert np.all(np.abs(w) <= 0.05) and abs(float(w.mean())) < 1e-3
+    assert np.all(b == 0)
+    L = oracle.lib()
+    n = L.oracle_norms(None, None)
+    g_off = (C.c_uint64 * n)()
+    width = (C.c_uint64 * n)()
+    L.oracle_norms(g_off, width)
+    gam = np.zeros_like(ln, dtype=bool)
+    for o, k in zip(g_off, width):
+        assert np.all(ln[o:o + k] == 1.0)  # LayerNorm gamma = 1
+        gam[o:o + k] = True
+    assert np.all(ln[~gam] == 0.0)  # beta = 0
+    _, w2, b2, _ = wc.seeded_weights("he", 0)
+    assert np.all(b2 == 0) and np.isfinite(w2).all() and 0.01 < float(w2.std()) < 1.0
+    _, w3, _, _ = wc.seeded_weights("he", 0)
+    assert np.array_equal(w2, w3)

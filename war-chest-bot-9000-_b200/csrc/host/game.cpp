@@ -6,6 +6,7 @@
 #include <cmath>
 #include <cstdio>
 #include <stdexcept>
+#include <type_traits>
 
 namespace wc {
 
@@ -194,6 +195,9 @@ void ContStack::push(const Cont& c) {
     if (n >= CONT_CAP) throw std::runtime_error("continuation stack overflow: raise CONT_CAP");
     v[n++] = c;
 }
+
+static_assert(std::has_unique_object_representations_v<State>,
+              "State has no implicit padding, so its bytes (roots, hashes) are fully defined");
 
 State State::blank(uint8_t active) {
     State s;

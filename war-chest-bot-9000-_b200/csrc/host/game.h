@@ -118,6 +118,7 @@ enum ContKind : uint8_t {
 //   WarriorPriestDraw{player=a, rg_hex=b}  WarriorPriestPlay{player=a}  _AttackPost{atk_hex=a}
 struct Cont {
     uint8_t kind = C_MAINPLAY, a = 0, b = 0;
+    uint8_t pad_[5] = {0, 0, 0, 0, 0};  // explicit, so a State's bytes are all defined
     uint64_t hexes = 0;
     static Cont make(uint8_t k, uint8_t a = 0, uint8_t b = 0, uint64_t h = 0) {
         Cont c; c.kind = k; c.a = a; c.b = b; c.hexes = h; return c;
@@ -131,6 +132,7 @@ constexpr int CONT_CAP = 16;  // state.rs:172
 
 struct ContStack {
     uint8_t n = 0;
+    uint8_t pad_[7] = {0, 0, 0, 0, 0, 0, 0};
     Cont v[CONT_CAP];
     void push(const Cont& c);
     bool pop(Cont* out) {
@@ -159,10 +161,12 @@ struct State {
     uint16_t main_plays;
     uint8_t winner;
     bool adjudicated_draw;
+    uint8_t pad0_[6];  // explicit padding (zeroed by blank()): root bytes are canonical
     Cont pending;
     ContStack conts;
     bool wp_v2_triggered;
     bool interrupt;
+    uint8_t pad1_[6];
 
     static State from_draft(const uint16_t* white4, const uint16_t* black4, uint8_t first);
     static State blank(uint8_t active);
