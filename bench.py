@@ -49,7 +49,7 @@ def parse():
     ap.add_argument("--plies", type=int, default=20)
     ap.add_argument("--net", default="f16", choices=["f16", "bf16", "exact", "none"],
                     help="value network: tcgen05 with f16 / bf16 operands, fp32 exact, or none")
-    ap.add_argument("--cpu-seconds", type=float, default=15.0, help="bounded CPU baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg (profiling runs)")
     ap.add_argument("--build-threads", type=int, default=0)
     return ap.parse_args()
 
@@ -164,25 +164,68 @@ def peaks():
         return 6650.0, 1590.0, "fallback"
 
 
-def cpu_baseline(wc, oracle, cfg, weights, seeds, budget_s):
+def cpu_sample_roots(oracle, cfg, seeds, threads):
+    """The bounded CPU sample: among the first 4 x threads workload seeds,
+    the `threads` roots whose trees have the median number of network rows
+    (one per host thread; the per-subgame rate barely depends on size, and a
+    median-sized depth-3 solve's network setup takes ~30 s on one core).
+    Tree sizes come from the oracle's own builder."""
+    import ctypes as C
+
+    cand = seeds[: 4 * threads]
+    roots = []
+    for s in cand:
+        buf = C.create_string_buffer(1 << 20)
+        n = C.c_size_t()
+        if oracle.lib().oracle_root_generate(C.c_uint64(s), PLIES, 1, buf, C.c_size_t(1 << 20), C.byref(n)) != 0:
+            raise RuntimeError("root generation failed")
+        roots.append(buf.raw[: n.value])
+    sizes = [0] * len(cand)
+
+    def size(lo, hi):
+        for i in range(lo, hi):
+            sizes[i] = oracle.Oracle(roots[i], cfg).shape["net_rows"]
+
+    th = [threading.Thread(target=size, args=(len(cand) * k // threads, len(cand) * (k + 1) // threads))
+          for k in range(threads)]
+    for t in th:
+        t.start()
+    for t in th:
+        t.join()
+    med = sorted(sizes)[len(sizes) // 2]
+    pick = sorted(range(len(cand)), key=lambda i: (abs(sizes[i] - med), i))[:threads]
+    return [roots[i] for i in pick], [cand[i] for i in pick], [sizes[i] for i in pick]
+
+
+def cpu_baseline(oracle, cfg, weights, seeds):
     """The oracle (CPU restatement of the reference solver) on a bounded
-    sample: one workload subgame per host thread, timed through the solver
-    build and the first iterations (all the once-per-solve network work),
-    then extrapolated to the full iteration count (oracle_bench)."""
+    sample of the workload, one subgame per host thread: each thread times
+    its solver build, the per-solve network and 2 CFR+ iterations, then 4
+    more iterations, and extrapolates its full solve (oracle_bench); the rate
+    is the sum of the threads' node-updates/s."""
     threads = os.cpu_count() or 1
-    roots = [wc.generate_root(s, PLIES) for s in seeds[:threads]]
+    roots, picked, sizes = cpu_sample_roots(oracle, cfg, seeds, threads)
     rate, wall, m = oracle.bench(roots, cfg, weights, threads, 2, 4)
     return {"value": rate, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{m} subgames of the workload (seeds {seeds[0]}..{seeds[0] + m - 1}), one per thread: "
-                      f"build + 2 CFR+ iterations (incl. the per-solve network) and 4 more timed, the "
-                      f"{cfg.iters}-iteration solve extrapolated; {wall:.1f} s wall"}
+            "sample": f"{m} workload subgames (seeds {min(picked)}..{max(picked)}, the median network-row count "
+                      f"{sorted(sizes)[len(sizes) // 2]} of the first {4 * threads} seeds), one per thread: build + "
+                      f"network + 2 CFR+ iterations and 4 more timed, each {cfg.iters}-iteration solve "
+                      f"extrapolated; {wall:.1f} s wall"}
 
 
 def main():
     global PLIES
     args = parse()
     PLIES = args.plies
-    world, rank, local = dist_setup(args)
+    if args.impl == "reference":
+        # the CPU reference runs on rank 0 alone; other ranks exit without work
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        if rank != 0:
+            return
+        local = 0
+    else:
+        world, rank, local = dist_setup(args)
     import oracle_lib
     import warchest_b200 as wc
 
@@ -199,7 +242,9 @@ def main():
 
     if args.impl == "reference":
         if rank == 0:
-            base = cpu_baseline(wc, oracle_lib, cfg, weights, seeds, args.cpu_seconds * max(1, args.steps))
+            samples = [cpu_baseline(oracle_lib, cfg, weights, seeds) for _ in range(max(1, args.steps))]
+            base = sorted(samples, key=lambda b: b["value"])[len(samples) // 2]
+            base["sample"] += f"; median of {len(samples)} repetitions"
             line = {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": UNIT, "n_gpus": world,
                     "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
                     "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded roots)", "config": workload,
@@ -270,7 +315,7 @@ def main():
                 "per_class_ms": prof, "algorithmic_bytes_per_solve": algo}
 
     if rank == 0:
-        base = cpu_baseline(wc, oracle_lib, cfg, weights, seeds, args.cpu_seconds)
+        base = None if args.no_cpu_baseline else cpu_baseline(oracle_lib, cfg, weights, seeds)
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": DTYPES[args.net],

@@ -46,6 +46,7 @@ struct JobDev {
     const float* weights_ln;
     float* cardm;      // [2][NTYPE][3 * POOL]: cfg_m applied to the card tokens
     const uint32_t* cfg_col;  // config -> index among its player's configs
+    const uint32_t* leaf_col; // per leaf_cidx entry: its config's cfg_col (the readout column)
     uint16_t* f16;     // fast path: bf16 f(c) rows, player 0's configs then player 1's ([ncfg][D])
     uint32_t ncfg_player[2];
     uint32_t row_base; // first global network row of this job

@@ -85,10 +85,12 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
 }
 
 // Pooled belief embeddings, one warp per (network row, player): normalised
-// reach over the leaf's configs weighting g(c) (search.rs:1512-1547).
+// reach over the leaf's configs weighting g(c) (search.rs:1512-1547). The
+// reach mass (the normaliser) is kept: it is the opponent mass the readout
+// of the other player's query scales by.
 __global__ void k_pool_fast(const JobDev* __restrict__ jobs, const uint32_t* __restrict__ row_job,
                             const uint32_t* __restrict__ row_local, uint32_t total_rows, int mask,
-                            float* __restrict__ pooled) {
+                            float* __restrict__ pooled, float* __restrict__ mass) {
     const int nq = mask == 3 ? 2 : 1;
     const uint64_t gw = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
@@ -107,7 +109,9 @@ __global__ void k_pool_fast(const JobDev* __restrict__ jobs, const uint32_t* __r
     float scale, flat;
     if (tot > 1e-30f) { scale = 1.0f / tot; flat = 0.0f; }
     else { scale = 0.0f; flat = 1.0f / (float)(n > 0 ? n : 1); }
+    if (lane == 0) mass[(size_t)g * 2 + q] = tot;
     float a0 = 0.0f, a1 = 0.0f;
+#pragma unroll 4
     for (uint32_t c = 0; c < n; ++c) {
         float wc = w[c] * scale + flat;
         float2 gv = reinterpret_cast<const float2*>(J.cg + (size_t)idx[c] * POOL)[lane];
@@ -153,6 +157,9 @@ __global__ void __launch_bounds__(512, 1)
     uint8_t* smem = align1024(smem_raw);
     uint8_t* sW = smem;
     uint8_t* sA = smem + 4 * TILE_J;
+    // per-layer vectors: [0] join_b bias (seat folded in), [1..3] block biases,
+    // [4..7] LayerNorm gammas, [8..11] betas
+    float (*vec)[JW] = reinterpret_cast<float (*)[JW]>(sA + TILE_J);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int quad = warp & 3, cg = warp >> 2;
     const int row = quad * 32 + lane, col0 = cg * 32;
@@ -160,6 +167,10 @@ __global__ void __launch_bounds__(512, 1)
         const uint4* src = reinterpret_cast<const uint4*>(fn.join_tiles);
         uint4* dst = reinterpret_cast<uint4*>(sW);
         for (uint32_t i = tid; i < 4 * TILE_J / 16; i += blockDim.x) dst[i] = src[i];
+        for (int i = tid; i < 12 * JW; i += blockDim.x) {
+            const int v = i / JW, c = i % JW;
+            vec[v][c] = v == 0 ? fn.beff[p][c] : v < 4 ? fn.bj[v - 1][c] : v < 8 ? fn.ln_g[v - 4][c] : fn.ln_b[v - 8][c];
+        }
     }
     if (tid == 0) {
         umma::mbar_init(&mbar, 1);
@@ -175,7 +186,7 @@ __global__ void __launch_bounds__(512, 1)
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const uint32_t ntiles = (total_rows + 127) / 128;
     const uint32_t idesc = umma::idesc16(128, 128, umma::Op16<H>::fmt);
-    const float* beff = fn.beff[p];
+    const float* beff = vec[0];
     uint32_t phase = 0;
     for (uint32_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
         const uint32_t g = tile * 128 + row;
@@ -223,7 +234,7 @@ __global__ void __launch_bounds__(512, 1)
                 float v[32];
                 umma::tmem_ld32(tmem + lane_off + col0, v);
                 if (L > 0) {
-                    const float* bias = fn.bj[L - 1] + col0;
+                    const float* bias = vec[L] + col0;
 #pragma unroll
                     for (int j = 0; j < 32; ++j) z[j] += v[j] + bias[j];
                 } else {
@@ -233,17 +244,18 @@ __global__ void __launch_bounds__(512, 1)
             }
             float mean, inv;
             row_stats4(z, 32, part, row, cg, JW, &mean, &inv);
-            const float* gam = fn.ln_g[L] + col0;
-            const float* bet = fn.ln_b[L] + col0;
+            const float* gam = vec[4 + L] + col0;
+            const float* bet = vec[8 + L] + col0;
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
                 float x[8];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) x[i] = umma::gelu_fast((z[8 * c + i] - mean) * inv * gam[8 * c + i] + bet[8 * c + i]);
+                for (int i = 0; i < 8; ++i) x[i] = (z[8 * c + i] - mean) * inv * gam[8 * c + i] + bet[8 * c + i];
+                const uint4 o = umma::gelu_chunk<H>(x);
                 if (L < 3)
-                    umma::st_chunk<H>(sA, 128, row, col0 + 8 * c, x);
+                    *reinterpret_cast<uint4*>(sA + umma::sw128_offset(128, row, col0 + 8 * c)) = o;
                 else if (valid)
-                    reinterpret_cast<uint4*>(zout + (size_t)g * JW + col0)[c] = umma::pack_chunk<H>(x);
+                    reinterpret_cast<uint4*>(zout + (size_t)g * JW + col0)[c] = o;
             }
         }
         __syncthreads();
@@ -270,7 +282,8 @@ struct HeadTile {
 template <bool H>
 __global__ void __launch_bounds__(512, 1)
     k_head_fast(const JobDev* __restrict__ jobs, const HeadTile* __restrict__ tiles, uint32_t ntiles, FastNetDev fn,
-                int p, const uint16_t* __restrict__ zout, const uint16_t* __restrict__ pb, int* __restrict__ err) {
+                int p, const uint16_t* __restrict__ zout, const uint16_t* __restrict__ pb, const float* __restrict__ mass,
+                int* __restrict__ err) {
     extern __shared__ uint8_t smem_raw[];
     __shared__ uint64_t mbar;
     __shared__ uint32_t tmem_slot;
@@ -281,6 +294,7 @@ __global__ void __launch_bounds__(512, 1)
     uint8_t* sH = sW + 2 * TILE_J;             // [128][256]: 64 KB
     uint8_t* sA = sH;                          // [128][128] operand of the first product, then H
     uint8_t* sF = sH + 2 * TILE_J;             // [128][256]: 64 KB (after each product: the readout staging)
+    float (*vec)[D] = reinterpret_cast<float (*)[D]>(sF + 2 * TILE_J);  // join_out bias, LN_H gamma, beta
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int quad = warp & 3, cg = warp >> 2;
     const int row = quad * 32 + lane;
@@ -288,6 +302,10 @@ __global__ void __launch_bounds__(512, 1)
         const uint4* src = reinterpret_cast<const uint4*>(fn.out_tile);
         uint4* dst = reinterpret_cast<uint4*>(sW);
         for (uint32_t i = tid; i < 2 * TILE_J / 16; i += blockDim.x) dst[i] = src[i];
+        for (int i = tid; i < 3 * D; i += blockDim.x) {
+            const int v = i / D, c = i % D;
+            vec[v][c] = v == 0 ? fn.bout[c] : v == 1 ? fn.ln_g[4][c] : fn.ln_b[4][c];
+        }
     }
     if (tid == 0) {
         umma::mbar_init(&mbar, 1);
@@ -302,7 +320,9 @@ __global__ void __launch_bounds__(512, 1)
     const uint32_t tmem = tmem_slot;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     uint32_t phase = 0;
-    // [512][32] floats, element j of thread t at t * 32 + (j ^ lane): conflict-free
+    // readout staging, row-major [128 rows][128 columns] with the low five
+    // column bits XORed by the row's: conflict-free for both the writes (one
+    // row per lane) and the per-row reads
     float* stage = reinterpret_cast<float*>(sF);
     for (uint32_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
         const HeadTile ht = tiles[t];
@@ -332,17 +352,16 @@ __global__ void __launch_bounds__(512, 1)
                 umma::mma16(tmem, umma::desc_at(wa, 128, k0), umma::desc_at(wb, 256, k0), idesc, k0 > 0);
             umma::commit(&mbar);
         }
-        // meanwhile: the row's opponent reach mass and the F rows of the first pass
+        // meanwhile: the row's opponent reach mass (kept by the pooling
+        // kernel), its readout columns, and the F rows of the first pass
         float opp_mass = 0.0f;
         uint32_t ncfg_row = 0;
-        const uint32_t* cidx = nullptr;
+        const uint32_t* lcol = nullptr;
         float* out = nullptr;
         if (valid) {
-            const float* ro = J.reach + J.lr_ridx[2 * r + 1 - p];
-            const uint32_t no = J.lr_nc[2 * r + 1 - p];
-            for (uint32_t c = 0; c < no; ++c) opp_mass += ro[c];
+            opp_mass = mass[(size_t)g * 2 + 1 - p];
             ncfg_row = J.lr_nc[2 * r + p];
-            cidx = J.leaf_cidx + J.leaf_coff[2 * r + p];
+            lcol = J.leaf_col + J.leaf_coff[2 * r + p];
             out = J.vals[p] + J.lr_vidx[2 * r + p];
         }
         const uint32_t nfp = J.ncfg_player[p];
@@ -379,8 +398,8 @@ __global__ void __launch_bounds__(512, 1)
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
                         const int j = 32 * h + 8 * c + 2 * i;
-                        y[j] = v[8 * c + 2 * i] + umma::Op16<H>::lo(w4[i]) + fn.bout[64 * cg + j];
-                        y[j + 1] = v[8 * c + 2 * i + 1] + umma::Op16<H>::hi(w4[i]) + fn.bout[64 * cg + j + 1];
+                        y[j] = v[8 * c + 2 * i] + umma::Op16<H>::lo(w4[i]) + vec[0][64 * cg + j];
+                        y[j + 1] = v[8 * c + 2 * i + 1] + umma::Op16<H>::hi(w4[i]) + vec[0][64 * cg + j + 1];
                     }
                 }
             }
@@ -388,8 +407,8 @@ __global__ void __launch_bounds__(512, 1)
         float mean, inv;
         row_stats4(y, 64, part, row, cg, D, &mean, &inv);
         {
-            const float* gam = fn.ln_g[4] + 64 * cg;
-            const float* bet = fn.ln_b[4] + 64 * cg;
+            const float* gam = vec[1] + 64 * cg;
+            const float* bet = vec[2] + 64 * cg;
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
                 float x[8];
@@ -418,13 +437,17 @@ __global__ void __launch_bounds__(512, 1)
             {
                 float v[32];
                 umma::tmem_ld32(tmem + lane_off + 256 + 32 * cg, v);
-                float* st = stage + tid * 32;
+                float* st = stage + row * 128 + 32 * cg;
 #pragma unroll
                 for (int j = 0; j < 32; ++j) st[j ^ lane] = v[j];
-                const uint32_t lo = nb + 32 * cg;
-                for (uint32_t c = 0; c < ncfg_row; ++c) {
-                    const uint32_t col = J.cfg_col[cidx[c]];
-                    if (col >= lo && col < lo + 32) out[c] = (st[(col - lo) ^ lane] + fn.vbias) * opp_mass;
+            }
+            __syncthreads();
+            {
+                // thread (row, cg) writes every fourth of the row's values
+                const float* st = stage + row * 128;
+                for (uint32_t c = cg; c < ncfg_row; c += 4) {
+                    const uint32_t col = lcol[c] - nb;
+                    if (col < 128) out[c] = (st[(col & ~31u) | ((col & 31u) ^ (uint32_t)lane)] + fn.vbias) * opp_mass;
                 }
             }
             umma::fence_before_sync();
@@ -459,10 +482,11 @@ static int num_sms() {
 }
 
 void launch_pool_fast(const JobDev* jobs, const uint32_t* row_job, const uint32_t* row_local, uint32_t total_rows,
-                      int mask, float* pooled, cudaStream_t s) {
+                      int mask, float* pooled, float* mass, cudaStream_t s) {
     if (!total_rows || !mask) return;
     uint64_t warps = (uint64_t)total_rows * (mask == 3 ? 2 : 1);
-    k_pool_fast<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, s>>>(jobs, row_job, row_local, total_rows, mask, pooled);
+    k_pool_fast<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, s>>>(jobs, row_job, row_local, total_rows, mask, pooled,
+                                                                      mass);
 }
 
 bool raise_smem_limit(const void* fn, size_t smem) {
@@ -480,7 +504,7 @@ bool raise_smem_limit(const void* fn, size_t smem) {
 void launch_join_fast(const FastNetDev& fn, int p, const float* pooled, const uint16_t* jp, uint16_t* zout,
                       uint32_t total_rows, int* err, cudaStream_t s) {
     if (!total_rows) return;
-    const size_t smem = 5 * TILE_J + 1024;
+    const size_t smem = 5 * TILE_J + 12 * JW * 4 + 1024;
     auto kern = fn.half ? k_join_fast<true> : k_join_fast<false>;
     if (!raise_smem_limit((const void*)kern, smem)) return;
     uint32_t ntiles = (total_rows + 127) / 128;
@@ -489,13 +513,13 @@ void launch_join_fast(const FastNetDev& fn, int p, const float* pooled, const ui
 }
 
 void launch_head_fast(const JobDev* jobs, const void* tiles, uint32_t ntiles, const FastNetDev& fn, int p,
-                      const uint16_t* zout, const uint16_t* pb, int* err, cudaStream_t s) {
+                      const uint16_t* zout, const uint16_t* pb, const float* mass, int* err, cudaStream_t s) {
     if (!ntiles) return;
-    const size_t smem = 6 * TILE_J + 1024;
+    const size_t smem = 6 * TILE_J + 3 * D * 4 + 1024;
     auto kern = fn.half ? k_head_fast<true> : k_head_fast<false>;
     if (!raise_smem_limit((const void*)kern, smem)) return;
     uint32_t grid = std::min<uint32_t>(ntiles, (uint32_t)num_sms());
-    kern<<<grid, 512, smem, s>>>(jobs, reinterpret_cast<const HeadTile*>(tiles), ntiles, fn, p, zout, pb, err);
+    kern<<<grid, 512, smem, s>>>(jobs, reinterpret_cast<const HeadTile*>(tiles), ntiles, fn, p, zout, pb, mass, err);
 }
 
 void launch_pack_f16(const JobDev* jobs, const uint32_t* cfg_job, const uint32_t* cfg_local, uint32_t total_cfgs,

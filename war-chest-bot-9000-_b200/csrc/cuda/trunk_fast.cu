@@ -63,14 +63,62 @@ __device__ __forceinline__ void fetch_block(uint8_t* dst, const uint8_t* tiles, 
 }
 
 template <bool H>
-__device__ __forceinline__ float op_at(const uint8_t* tile, uint32_t R, uint32_t r, uint32_t k) {
-    return umma::Op16<H>::at(*reinterpret_cast<const uint16_t*>(tile + umma::sw128_offset(R, r, k)));
-}
-
-template <bool H>
 __device__ __forceinline__ void put_x32(uint8_t* tile, uint32_t R, uint32_t r, uint32_t k0, const float* v) {
 #pragma unroll
     for (int c = 0; c < 4; ++c) umma::st_chunk<H>(tile, R, r, k0 + 8 * c, v + 8 * c);
+}
+
+// out[i][n] = bias[n] + sum_k in[i][k] * W[k][n] for the NB rows of a tile, on
+// the CUDA cores: one thread per (column n, K slice), the NB rows in
+// registers so every weight load feeds NB FMAs, and the loads unrolled so
+// several are in flight (the weights come from L2). With KS > 1 the K slices
+// meet in `part` (KS * NB * N floats). `in` has row stride ldi, `out` ldo.
+template <int NB, int K, int N, int KS>
+__device__ __forceinline__ void rows_gemm(const float* in, int ldi, const float* __restrict__ W,
+                                          const float* __restrict__ bias, float* out, int ldo, float* part) {
+    constexpr int KC = (K + KS - 1) / KS;
+    for (int it = threadIdx.x; it < N * KS; it += blockDim.x) {
+        const int n = it % N, ks = it / N;
+        const int k0 = ks * KC, k1 = k0 + KC < K ? k0 + KC : K;
+        float acc[NB];
+#pragma unroll
+        for (int i = 0; i < NB; ++i) acc[i] = 0.0f;
+#pragma unroll 8
+        for (int k = k0; k < k1; ++k) {
+            const float w = __ldg(W + (size_t)k * N + n);
+#pragma unroll
+            for (int i = 0; i < NB; ++i) acc[i] += in[i * ldi + k] * w;
+        }
+        if (KS == 1) {
+#pragma unroll
+            for (int i = 0; i < NB; ++i) out[i * ldo + n] = acc[i] + (bias ? bias[n] : 0.0f);
+        } else {
+#pragma unroll
+            for (int i = 0; i < NB; ++i) part[(ks * NB + i) * N + n] = acc[i];
+        }
+    }
+    if (KS > 1) {
+        __syncthreads();
+        for (int it = threadIdx.x; it < NB * N; it += blockDim.x) {
+            const int i = it / N, n = it % N;
+            float v = bias ? bias[n] : 0.0f;
+#pragma unroll
+            for (int ks = 0; ks < KS; ++ks) v += part[(ks * NB + i) * N + n];
+            out[i * ldo + n] = v;
+        }
+    }
+}
+
+// Eight consecutive 16-bit operands of row r, columns [k, k + 8), as floats.
+template <bool H>
+__device__ __forceinline__ void ld_chunk(const uint8_t* tile, uint32_t R, uint32_t r, uint32_t k, float* v) {
+    const uint4 q = *reinterpret_cast<const uint4*>(tile + umma::sw128_offset(R, r, k));
+    const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        v[2 * i] = umma::Op16<H>::lo(w4[i]);
+        v[2 * i + 1] = umma::Op16<H>::hi(w4[i]);
+    }
 }
 
 }  // namespace
@@ -80,6 +128,7 @@ struct TrunkSmem {  // the non-operand scratch
     float part_q[128][3];
     float pooled[BOARDS][2 * C];
     float gb[BOARDS][C];
+    float part[4 * BOARDS * C];  // K-slice partial sums of the pooling GEMM
     uint64_t wbar[2];
     uint64_t mbar;
     uint32_t tmem_slot;
@@ -103,6 +152,8 @@ struct HeadSmem {
     float x[ROWS][C];
     float input[BOARDS][2 * C + LOOSE];
     float P[BOARDS][D];
+    float jp[BOARDS][JW];
+    float part[3 * BOARDS * JW];
 };
 
 template <bool H>
@@ -219,18 +270,10 @@ __global__ void __launch_bounds__(384, 1)
             St.tokens[i][t * TYPE + j] = acc;
         }
         __syncthreads();
-        for (int q = tid; q < BOARDS * NTYPE * C; q += blockDim.x) {
-            int i = q / (NTYPE * C), t = (q / C) % NTYPE, c = q % C;
-            float acc = 0.0f;
-            for (int k = 0; k < TYPE; ++k) acc += St.tokens[i][t * TYPE + k] * W[L.tok_stem.w + k * C + c];
-            St.proj[i][t * C + c] = acc;
-        }
-        for (int q = tid; q < BOARDS * C; q += blockDim.x) {
-            int i = q / C, c = q % C;
-            float acc = 0.0f;
-            for (int k = 0; k < LOOSE; ++k) acc += St.loose[i][k] * W[L.glob_stem.w + k * C + c];
-            St.glob[i][c] = acc;
-        }
+        // proj[i][t] = tokens[i][t] * W_tok: 30 token rows; glob = loose * W_glob
+        rows_gemm<BOARDS * NTYPE, TYPE, C, 1>(&St.tokens[0][0], TYPE, W + L.tok_stem.w, nullptr, &St.proj[0][0], C,
+                                              nullptr);
+        rows_gemm<BOARDS, LOOSE, C, 1>(&St.loose[0][0], LOOSE, W + L.glob_stem.w, nullptr, &St.glob[0][0], C, nullptr);
         __syncthreads();
         for (int q = tid; q < BOARDS * C; q += blockDim.x) {
             int i = q / C, c = q % C;
@@ -276,10 +319,11 @@ __global__ void __launch_bounds__(384, 1)
                 const float* gam = LN + L.norm_g[NetLayout::ln_block(blk, 0)];
                 const float* bet = LN + L.norm_b[NetLayout::ln_block(blk, 0)];
 #pragma unroll
-                for (int j = 0; j < 32; ++j)
-                    a[j] = real_row ? umma::gelu_fast((x[j] - mean) * inv * gam[col0 + j] + bet[col0 + j]) : 0.0f;
+                for (int j = 0; j < 32; ++j) a[j] = real_row ? (x[j] - mean) * inv * gam[col0 + j] + bet[col0 + j] : 0.0f;
             }
-            put_x32<H>(sA1, 128, row, col0, a);
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+                *reinterpret_cast<uint4*>(sA1 + umma::sw128_offset(128, row, col0 + 8 * c)) = umma::gelu_chunk<H>(a + 8 * c);
             __syncthreads();
             // neighbour sums -> columns 96..191; board pooling (mean | max) of a
             {
@@ -292,30 +336,36 @@ __global__ void __launch_bounds__(384, 1)
                         if (nbh == 255) continue;
                         const int nr = board * NH + nbh;
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) nsum[j] += op_at<H>(sA1, 128, nr, col0 + j);
+                        for (int c = 0; c < 4; ++c) {
+                            float v[8];
+                            ld_chunk<H>(sA1, 128, nr, col0 + 8 * c, v);
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) nsum[8 * c + j] += v[j];
+                        }
                     }
                 }
                 put_x32<H>(sA1, 128, row, C + col0, nsum);
             }
-            for (int q = tid; q < BOARDS * C; q += blockDim.x) {
-                int i = q / C, c = q % C;
-                float mean = 0.0f, mx = -INFINITY;
+            if (tid < BOARDS * (C / 8)) {  // (board, 8-column chunk): mean | max over the hexes
+                const int i = tid / (C / 8), c0 = (tid % (C / 8)) * 8;
+                float sum[8], mx[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) { sum[j] = 0.0f; mx[j] = -INFINITY; }
                 for (int h = 0; h < NH; ++h) {
-                    float v = op_at<H>(sA1, 128, i * NH + h, c);
-                    mean += v / (float)NH;
-                    mx = fmaxf(mx, v);
+                    float v[8];
+                    ld_chunk<H>(sA1, 128, i * NH + h, c0, v);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) { sum[j] += v[j]; mx[j] = fmaxf(mx[j], v[j]); }
                 }
-                S.pooled[i][c] = mean;
-                S.pooled[i][C + c] = mx;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    S.pooled[i][c0 + j] = sum[j] * (1.0f / NH);
+                    S.pooled[i][C + c0 + j] = mx[j];
+                }
             }
             __syncthreads();
-            for (int q = tid; q < BOARDS * C; q += blockDim.x) {
-                int i = q / C, c = q % C;
-                const wc::NetSpan pl = L.pool[blk];
-                float acc = 0.0f;
-                for (int k = 0; k < 2 * C; ++k) acc += S.pooled[i][k] * W[pl.w + k * C + c];
-                S.gb[i][c] = acc + B[pl.b + c];
-            }
+            rows_gemm<BOARDS, 2 * C, C, 4>(&S.pooled[0][0], 2 * C, W + L.pool[blk].w, B + L.pool[blk].b, &S.gb[0][0], C,
+                                           S.part);
             // mix product (weights of this block must have landed)
             if (!umma::mbar_wait(&S.wbar[buf], wphase[buf], WAIT_LIMIT)) S.abort_flag = 1;
             wphase[buf] ^= 1u;
@@ -357,10 +407,11 @@ __global__ void __launch_bounds__(384, 1)
                 const float* gam = LN + L.norm_g[NetLayout::ln_block(blk, 1)];
                 const float* bet = LN + L.norm_b[NetLayout::ln_block(blk, 1)];
 #pragma unroll
-                for (int j = 0; j < 32; ++j)
-                    y[j] = real_row ? umma::gelu_fast((y[j] - mean) * inv * gam[col0 + j] + bet[col0 + j]) : 0.0f;
+                for (int j = 0; j < 32; ++j) y[j] = real_row ? (y[j] - mean) * inv * gam[col0 + j] + bet[col0 + j] : 0.0f;
             }
-            put_x32<H>(sA2, 128, row, col0, y);
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+                *reinterpret_cast<uint4*>(sA2 + umma::sw128_offset(128, row, col0 + 8 * c)) = umma::gelu_chunk<H>(y + 8 * c);
             umma::fence_async_smem();
             umma::fence_before_sync();
             __syncthreads();
@@ -453,13 +504,8 @@ __global__ void __launch_bounds__(384, 1)
             Hd.input[i][2 * C + j] = v;
         }
         __syncthreads();
-        const wc::NetSpan bo = L.board_out;
-        for (int q = tid; q < BOARDS * D; q += blockDim.x) {
-            int i = q / D, c = q % D;
-            float acc = 0.0f;
-            for (int k = 0; k < 2 * C + LOOSE; ++k) acc += Hd.input[i][k] * W[bo.w + k * D + c];
-            Hd.P[i][c] = acc + B[bo.b + c];
-        }
+        rows_gemm<BOARDS, 2 * C + LOOSE, D, 1>(&Hd.input[0][0], 2 * C + LOOSE, W + L.board_out.w, B + L.board_out.b,
+                                               &Hd.P[0][0], D, nullptr);
         __syncthreads();
         // P and jp are stored as 16-bit operands minus their row mean: every consumer of
         // them (the join residual stream, the readout y) goes through a
@@ -479,17 +525,12 @@ __global__ void __launch_bounds__(384, 1)
             if (i < nb)
                 g_pb[(size_t)gb_[i] * D + c] = umma::Op16<H>::one(Hd.P[i][c] - S.gb[i][0]);
         }
-        for (int q = tid; q < BOARDS * JW; q += blockDim.x) {
-            int i = q / JW, c = q % JW;
-            float acc = 0.0f;
-            for (int k = 0; k < D; ++k) acc += Hd.P[i][k] * W[L.join_p.w + k * JW + c];
-            S.pooled[i][c] = acc;
-        }
+        rows_gemm<BOARDS, D, JW, 3>(&Hd.P[0][0], D, W + L.join_p.w, nullptr, &Hd.jp[0][0], JW, Hd.part);
         __syncthreads();
         if (tid < BOARDS * 32) {
             const int i = tid / 32, l = tid % 32;
             float s = 0.0f;
-            for (int c = l; c < JW; c += 32) s += S.pooled[i][c];
+            for (int c = l; c < JW; c += 32) s += Hd.jp[i][c];
 #pragma unroll
             for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
             if (l == 0) S.gb[i][1] = s / (float)JW;
@@ -498,7 +539,7 @@ __global__ void __launch_bounds__(384, 1)
         for (int q = tid; q < BOARDS * JW; q += blockDim.x) {
             int i = q / JW, c = q % JW;
             if (i < nb)
-                g_jp[(size_t)gb_[i] * JW + c] = umma::Op16<H>::one(S.pooled[i][c] - S.gb[i][1]);
+                g_jp[(size_t)gb_[i] * JW + c] = umma::Op16<H>::one(Hd.jp[i][c] - S.gb[i][1]);
         }
         __syncthreads();
         if (S.abort_flag) break;

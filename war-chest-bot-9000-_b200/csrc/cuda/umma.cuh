@@ -188,4 +188,38 @@ __device__ __forceinline__ float gelu_fast(float x) {
     return __fdividef(x, 1.0f + e);
 }
 
+// GELU (tanh form) of two floats, returned as a packed pair of 16-bit
+// operands. f16: computed in f16x2 arithmetic with the hardware f16x2 tanh
+// (two elements per instruction; its error is of the order of the f16
+// rounding the result gets anyway); the tanh argument uses the input clamped
+// to +-16, where tanh(u) is +-1 to f16 precision, so x^2 cannot overflow.
+// bf16: the fp32 gelu_fast, then rounded.
+template <bool HALF>
+__device__ __forceinline__ uint32_t gelu_pack2(float a, float b);
+template <>
+__device__ __forceinline__ uint32_t gelu_pack2<true>(float a, float b) {
+    const __half2 x = __floats2half2_rn(a, b);
+    const __half2 lim = __float2half2_rn(16.0f);
+    const __half2 xc = __hmax2(__hmin2(x, lim), __hneg2(lim));
+    const __half2 inner = __hfma2(__hmul2(xc, xc), __float2half2_rn(0.035677408f), __float2half2_rn(0.79788456f));
+    const __half2 u = __hmul2(xc, inner);
+    uint32_t ub = *reinterpret_cast<const uint32_t*>(&u), tb;
+    asm("tanh.approx.f16x2 %0, %1;" : "=r"(tb) : "r"(ub));
+    const __half2 t = *reinterpret_cast<const __half2*>(&tb);
+    const __half2 hx = __hmul2(x, __float2half2_rn(0.5f));
+    const __half2 g = __hfma2(hx, t, hx);
+    return *reinterpret_cast<const uint32_t*>(&g);
+}
+template <>
+__device__ __forceinline__ uint32_t gelu_pack2<false>(float a, float b) {
+    return Op16<false>::pack(gelu_fast(a), gelu_fast(b));
+}
+
+// GELU of 8 consecutive floats as one 16-byte chunk of 16-bit operands.
+template <bool HALF>
+__device__ __forceinline__ uint4 gelu_chunk(const float* x) {
+    return make_uint4(gelu_pack2<HALF>(x[0], x[1]), gelu_pack2<HALF>(x[2], x[3]), gelu_pack2<HALF>(x[4], x[5]),
+                      gelu_pack2<HALF>(x[6], x[7]));
+}
+
 }  // namespace umma

@@ -12,7 +12,7 @@ size_t JobImage::table_bytes() const {
               vge_w.size() + rg_start.size() + rge_src.size() + rge_w.size() + drawp.size() + lr_ridx.size() +
               lr_nc.size() + lr_vidx.size() + leaf_coff.size() + leaf_cidx.size() + tl_ridx.size() +
               tl_nc.size() + tl_vidx.size() + tl_util0.size() + cphi.size() + card_feat.size() + cfg_col.size() +
-              root_belief.size() + carried.size());
+              leaf_col.size() + root_belief.size() + carried.size());
     b += row_player.size() + gpu_rows.size() + cplayer.size();
     return b;
 }
@@ -232,6 +232,8 @@ std::unique_ptr<JobImage> flatten(const Tree& t, const std::vector<float>& carri
     J.cphi = t.cphi;
     J.cplayer = t.cplayer;
     for (uint8_t q : J.cplayer) J.cfg_col.push_back(J.ncfg_player[q]++);
+    J.leaf_col.reserve(J.leaf_cidx.size());
+    for (uint32_t c : J.leaf_cidx) J.leaf_col.push_back(J.cfg_col[c]);
     J.nterm = (uint32_t)t.term_leaves.size();
     for (uint32_t i : t.term_leaves) {
         for (int q = 0; q < 2; ++q) {

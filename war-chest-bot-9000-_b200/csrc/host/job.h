@@ -61,6 +61,7 @@ struct JobImage {
     std::vector<float> cphi;                        // ncfg * CFEAT
     std::vector<uint8_t> cplayer;
     std::vector<uint32_t> cfg_col;                  // index of each config among its player's configs
+    std::vector<uint32_t> leaf_col;                 // cfg_col of every leaf_cidx entry (readout column)
     uint32_t ncfg_player[2] = {0, 0};
     std::vector<float> card_feat;                   // 2 views * NTYPE * CARD_FEATS
     // root beliefs and the carried roots Phase 2 values

@@ -50,7 +50,8 @@ std::unique_ptr<JobBlob> make_blob(std::unique_ptr<JobImage> img) {
         v(J.cell_vidx), v(J.row_off), v(J.row_player), v(J.vg_start), v(J.vge_idx), v(J.vge_w), v(J.rg_start),
         v(J.rge_src), v(J.rge_w), v(J.drawp), v(J.cell_ref), v(J.lr_ridx), v(J.lr_nc), v(J.lr_vidx),
         v(J.leaf_coff), v(J.leaf_cidx), v(J.tl_ridx), v(J.tl_nc), v(J.tl_vidx), v(J.tl_util0), v(J.gpu_rows),
-        v(J.cphi), v(J.cplayer), v(J.card_feat), v(J.root_belief), v(J.carried), v(carry_off), v(J.cfg_col)};
+        v(J.cphi), v(J.cplayer), v(J.card_feat), v(J.root_belief), v(J.carried), v(carry_off), v(J.cfg_col),
+        v(J.leaf_col)};
     size_t at = 0;
     for (int i = 0; i < JobBlob::N_ARR; ++i) {
         b->off[i] = at;
@@ -302,7 +303,7 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
     b.total_cfgs = (uint32_t)cfg_job.size();
     const bool fast = dev.have_net && !dev.precise;
     std::vector<size_t> o_f16(nj, 0);
-    size_t o_gpool = 0, o_gjp = 0, o_gpb = 0, o_gz = 0, o_tiles = 0, o_err = 0;
+    size_t o_gpool = 0, o_gjp = 0, o_gmass = 0, o_gpb = 0, o_gz = 0, o_tiles = 0, o_err = 0;
     struct HeadTile { uint32_t job, first, count, pad; };
     std::vector<HeadTile> head_tiles;
     if (fast) {
@@ -310,6 +311,7 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
         size_t R = row_job.size();
         o_gpool = A.take(4ull * R * 2 * NET_POOL);
         o_gjp = A.take(2ull * R * NET_JW);
+        o_gmass = A.take(8ull * R);
         o_gpb = A.take(2ull * R * NET_D);
         o_gz = A.take(2ull * R * NET_JW);
         for (uint32_t j = 0; j < nj; ++j)
@@ -368,6 +370,7 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
         d.carried = tf(JobBlob::CARRIED);
         d.carry_off = t32(JobBlob::CARRY_OFF);
         d.cfg_col = t32(JobBlob::CFG_COL);
+        d.leaf_col = t32(JobBlob::LEAF_COL);
         d.ncfg_player[0] = J.ncfg_player[0];
         d.ncfg_player[1] = J.ncfg_player[1];
         d.row_base = row_base[j];
@@ -419,6 +422,7 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
     if (fast) {
         b.g_pooled = reinterpret_cast<float*>(D + o_gpool);
         b.g_jp = reinterpret_cast<uint16_t*>(D + o_gjp);
+        b.g_mass = reinterpret_cast<float*>(D + o_gmass);
         b.g_pb = reinterpret_cast<uint16_t*>(D + o_gpb);
         b.g_zout = reinterpret_cast<uint16_t*>(D + o_gz);
         b.d_head_tiles = D + o_tiles;
@@ -500,9 +504,10 @@ struct Sched {
     void leaf_values_(int p, int pool_mask) {
         DeviceCtx& dv = *b.dev;
         if (dv.have_net && !dv.precise) {
-            wcdev::launch_pool_fast(J, b.d_row_job, b.d_row_local, b.total_rows, pool_mask, b.g_pooled, s);
+            wcdev::launch_pool_fast(J, b.d_row_job, b.d_row_local, b.total_rows, pool_mask, b.g_pooled, b.g_mass, s);
             wcdev::launch_join_fast(dv.fast, p, b.g_pooled, b.g_jp, b.g_zout, b.total_rows, b.d_err, s);
-            wcdev::launch_head_fast(J, b.d_head_tiles, b.n_head_tiles, dv.fast, p, b.g_zout, b.g_pb, b.d_err, s);
+            wcdev::launch_head_fast(J, b.d_head_tiles, b.n_head_tiles, dv.fast, p, b.g_zout, b.g_pb, b.g_mass, b.d_err,
+                                    s);
         } else if (dv.have_net) {
             if (pool_mask) wcdev::launch_pool(J, b.d_row_job, b.d_row_local, b.total_rows, pool_mask, s);
             wcdev::launch_join_readout(J, b.d_row_job, b.d_row_local, b.total_rows, p, dv.W, dv.B, dv.LN, s);

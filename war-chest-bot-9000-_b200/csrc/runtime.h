@@ -46,7 +46,7 @@ struct JobBlob {
     enum Arr {
         CELL_VIDX, ROW_OFF, ROW_PLAYER, VG_START, VGE_IDX, VGE_W, RG_START, RGE_SRC, RGE_W, DRAWP, CELL_REF,
         LR_RIDX, LR_NC, LR_VIDX, LEAF_COFF, LEAF_CIDX, TL_RIDX, TL_NC, TL_VIDX, TL_UTIL0, GPU_ROWS, CPHI,
-        CPLAYER, CARD_FEAT, ROOT_BELIEF, CARRIED, CARRY_OFF, CFG_COL, N_ARR
+        CPLAYER, CARD_FEAT, ROOT_BELIEF, CARRIED, CARRY_OFF, CFG_COL, LEAF_COL, N_ARR
     };
     size_t off[N_ARR] = {};
     uint32_t nexit = 0, carry_width = 0, nsnaps_kept = 0;
@@ -78,6 +78,7 @@ struct Batch {
     uint16_t* g_jp = nullptr;     // [rows][JW]
     uint16_t* g_pb = nullptr;     // [rows][D]
     uint16_t* g_zout = nullptr;   // [rows][JW]
+    float* g_mass = nullptr;      // [rows][2]: each player's reach mass at the row (pooling's normaliser)
     void* d_head_tiles = nullptr;
     uint32_t n_head_tiles = 0;
     int* d_err = nullptr;
