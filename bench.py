@@ -75,7 +75,9 @@ def cfr_plus(wc):
 
 
 def build_jobs(wc, seeds, cfg, threads):
-    """Roots and flattened jobs on host threads (the C calls release the GIL)."""
+    """Roots and flattened jobs on host threads (the C calls release the GIL).
+    Roots whose tree hits the node cap are counted and skipped, as the
+    reference's tape builder does (wave_tape.rs:51-56)."""
     out = [None] * len(seeds)
     roots = [None] * len(seeds)
 
@@ -83,7 +85,11 @@ def build_jobs(wc, seeds, cfg, threads):
         for i in range(lo, hi):
             r = wc.generate_root(seeds[i], PLIES)
             roots[i] = r
-            out[i] = wc.PackedJob.from_root(r, cfg)
+            try:
+                out[i] = wc.PackedJob.from_root(r, cfg)
+            except wc.SolveError as e:
+                if e.code != 3:  # WC_E_CAPPED
+                    raise
 
     n = len(seeds)
     th = [threading.Thread(target=work, args=(n * k // threads, n * (k + 1) // threads)) for k in range(threads)]
@@ -91,7 +97,8 @@ def build_jobs(wc, seeds, cfg, threads):
         t.start()
     for t in th:
         t.join()
-    return roots, out
+    keep = [i for i in range(len(seeds)) if out[i] is not None]
+    return [roots[i] for i in keep], [out[i] for i in keep]
 
 
 class Clocks:
@@ -184,7 +191,10 @@ def cpu_sample_roots(oracle, cfg, seeds, threads):
 
     def size(lo, hi):
         for i in range(lo, hi):
-            sizes[i] = oracle.Oracle(roots[i], cfg).shape["net_rows"]
+            try:
+                sizes[i] = oracle.Oracle(roots[i], cfg).shape["net_rows"]
+            except RuntimeError:  # node cap: skipped like the GPU workload
+                sizes[i] = -1
 
     th = [threading.Thread(target=size, args=(len(cand) * k // threads, len(cand) * (k + 1) // threads))
           for k in range(threads)]
@@ -192,8 +202,9 @@ def cpu_sample_roots(oracle, cfg, seeds, threads):
         t.start()
     for t in th:
         t.join()
-    med = sorted(sizes)[len(sizes) // 2]
-    pick = sorted(range(len(cand)), key=lambda i: (abs(sizes[i] - med), i))[:threads]
+    ok = [i for i in range(len(cand)) if sizes[i] >= 0]
+    med = sorted(sizes[i] for i in ok)[len(ok) // 2]
+    pick = sorted(ok, key=lambda i: (abs(sizes[i] - med), i))[:threads]
     return [roots[i] for i in pick], [cand[i] for i in pick], [sizes[i] for i in pick]
 
 
@@ -257,6 +268,8 @@ def main():
     t0 = time.perf_counter()
     roots, jobs = build_jobs(wc, seeds, cfg, threads)
     build_s = time.perf_counter() - t0
+    workload["capped_skipped"] = len(seeds) - len(jobs)
+    workload["subgames_solved_per_gpu"] = len(jobs)
 
     # weights: rank 0's seeded blob, broadcast once over NCCL when sharded
     if weights is not None and world > 1:

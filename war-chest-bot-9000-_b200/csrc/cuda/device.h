@@ -47,9 +47,11 @@ struct JobDev {
     float* cardm;      // [2][NTYPE][3 * POOL]: cfg_m applied to the card tokens
     const uint32_t* cfg_col;  // config -> index among its player's configs
     const uint32_t* leaf_col; // per leaf_cidx entry: its config's cfg_col (the readout column)
-    uint16_t* f16;     // fast path: bf16 f(c) rows, player 0's configs then player 1's ([ncfg][D])
+    uint16_t* f16;     // fast path: f(c) as readout operand images, 128 configs x D each (64 KB),
+                       // player 0's ceil(n0 / 128) passes then player 1's
     uint32_t ncfg_player[2];
     uint32_t row_base; // first global network row of this job
+    uint32_t tile_base; // first 128-row leaf tile of this job (tensor-core path)
     // ---- mutable solve state
     float* cur;
     float* regret;

@@ -51,9 +51,9 @@ int umma_selftest(const uint16_t* A, const uint16_t* B, int K, int N, float* D);
 // 5 the array's device address could not be looked up.
 int umma_selftest_static(const uint16_t* A, const uint16_t* B, int K, int N, float* D);
 void launch_pool_fast(const JobDev* jobs, const uint32_t* row_job, const uint32_t* row_local, uint32_t total_rows,
-                      int mask, float* pooled, float* mass, cudaStream_t s);
-void launch_join_fast(const FastNetDev& fn, int p, const float* pooled, const uint16_t* jp, uint16_t* zout,
-                      uint32_t total_rows, int* err, cudaStream_t s);
+                      int mask, uint16_t* pool_img, float* mass, bool half, cudaStream_t s);
+void launch_join_fast(const JobDev* jobs, const void* tiles, uint32_t ntiles, const FastNetDev& fn, int p,
+                      const uint16_t* pool_img, const uint16_t* jp, uint16_t* zout_img, int* err, cudaStream_t s);
 void launch_head_fast(const JobDev* jobs, const void* tiles, uint32_t ntiles, const FastNetDev& fn, int p,
                       const uint16_t* zout, const uint16_t* pb, const float* mass, int* err, cudaStream_t s);
 void launch_pack_f16(const JobDev* jobs, const uint32_t* cfg_job, const uint32_t* cfg_local, uint32_t total_cfgs,

@@ -77,7 +77,8 @@ __global__ void k_umma_selftest(const __nv_bfloat16* __restrict__ A, const __nv_
 // ------------------------------------------------------------- fast kernels
 
 constexpr int POOL = wc::NET_POOL, JW = wc::NET_JW, D = wc::NET_D;
-constexpr uint32_t TILE_J = 128u * 128u * 2u;  // one [128][128] bf16 operand tile
+constexpr uint32_t TILE_J = 128u * 128u * 2u;  // one [128][128] 16-bit operand tile
+constexpr uint32_t ATOM = 128u * 128u;         // one 128-row x 64-column atom of 16-bit operands
 constexpr uint32_t WAIT_LIMIT = 1u << 26;
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
@@ -86,11 +87,16 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
 
 // Pooled belief embeddings, one warp per (network row, player): normalised
 // reach over the leaf's configs weighting g(c) (search.rs:1512-1547). The
-// reach mass (the normaliser) is kept: it is the opponent mass the readout
-// of the other player's query scales by.
+// warp loads 32 (weight, config) pairs at a time and broadcasts them by
+// shuffle, so the g-row loads (a lane per column pair) do not wait on the
+// index loads one by one. The result goes to the player's 64-column atom of
+// the row's tile image, the join's A operand as it sits in shared memory.
+// The reach mass (the normaliser) is kept: it is the opponent mass the
+// readout of the other player's query scales by.
+template <bool H>
 __global__ void k_pool_fast(const JobDev* __restrict__ jobs, const uint32_t* __restrict__ row_job,
                             const uint32_t* __restrict__ row_local, uint32_t total_rows, int mask,
-                            float* __restrict__ pooled, float* __restrict__ mass) {
+                            uint16_t* __restrict__ pool_img, float* __restrict__ mass) {
     const int nq = mask == 3 ? 2 : 1;
     const uint64_t gw = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
@@ -111,14 +117,28 @@ __global__ void k_pool_fast(const JobDev* __restrict__ jobs, const uint32_t* __r
     else { scale = 0.0f; flat = 1.0f / (float)(n > 0 ? n : 1); }
     if (lane == 0) mass[(size_t)g * 2 + q] = tot;
     float a0 = 0.0f, a1 = 0.0f;
+    for (uint32_t c0 = 0; c0 < n; c0 += 32) {
+        const uint32_t c = c0 + lane;
+        float wl = 0.0f;
+        uint32_t il = 0;
+        if (c < n) {
+            wl = w[c] * scale + flat;
+            il = idx[c];
+        }
+        const uint32_t m = n - c0 < 32 ? n - c0 : 32;
 #pragma unroll 4
-    for (uint32_t c = 0; c < n; ++c) {
-        float wc = w[c] * scale + flat;
-        float2 gv = reinterpret_cast<const float2*>(J.cg + (size_t)idx[c] * POOL)[lane];
-        a0 += wc * gv.x;
-        a1 += wc * gv.y;
+        for (uint32_t k = 0; k < m; ++k) {
+            const float wk = __shfl_sync(0xffffffffu, wl, k);
+            const uint32_t ik = __shfl_sync(0xffffffffu, il, k);
+            const float2 gv = reinterpret_cast<const float2*>(J.cg + (size_t)ik * POOL)[lane];
+            a0 += wk * gv.x;
+            a1 += wk * gv.y;
+        }
     }
-    reinterpret_cast<float2*>(pooled + ((size_t)g * 2 + q) * POOL)[lane] = make_float2(a0, a1);
+    const uint32_t i = r & 127, col = 2 * lane;
+    uint8_t* img = reinterpret_cast<uint8_t*>(pool_img) + (size_t)(J.tile_base + (r >> 7)) * (2 * ATOM) + q * ATOM;
+    *reinterpret_cast<uint32_t*>(img + i * 128 + (((col >> 3) ^ (i & 7)) << 4) + (col & 7) * 2) =
+        umma::Op16<H>::pack(a0, a1);
 }
 
 // Row statistics of a LayerNorm whose row is spread over the four column
@@ -139,138 +159,203 @@ __device__ __forceinline__ void row_stats4(const float* v, int n, float (*part)[
     *mean = m;
 }
 
-// The join chain for traverser p on 128-row tiles (net.rs:801-832):
-// z = jp + [pooled_p | pooled_o] * Wb + b, three residual blocks
-// z += W_i LNGELU(z) + b_i, and out = LNGELU(z) in bf16 (the join_out input).
-// 16 warps: warp w owns TMEM lanes 32 (w % 4) .. (rows) and columns
-// 32 (w / 4) .. of the 128; z lives in registers. The four 128 x 128 weight
-// tiles stay in shared memory for the CTA's lifetime.
+// One tile = up to 128 network rows of one job: first local row, count.
+struct HeadTile {
+    uint32_t job, first, count, pad;
+};
+
+// The join chain for traverser p (net.rs:801-832), one 128-row tile of one
+// job at a time: z = jp + [pooled_p | pooled_o] Wb + b, three residual
+// blocks z += W_i LNGELU(z) + b_i, and out = LNGELU(z), written as the head's
+// A-operand image. One thread per row (TMEM lane), so a row's LayerNorm
+// needs no exchange between threads. The residual stream z lives in TMEM:
+// initialised with jp + b by tcgen05.st, each layer's MMA accumulates onto it,
+// and the epilogue adds the running sum of the block biases. The four weight
+// tiles stream through two 32 KB slots by bulk copy (the next weight lands
+// while a layer computes) and the next tile's pooled images land during the
+// last layer, so a CTA needs ~100 KB of shared memory and two run per SM,
+// each one's MMAs and copies overlapping the other's epilogues.
 template <bool H>
-__global__ void __launch_bounds__(512, 1)
-    k_join_fast(FastNetDev fn, int p, const float* __restrict__ pooled, const uint16_t* __restrict__ jp,
-                uint16_t* __restrict__ zout, uint32_t total_rows, int* __restrict__ err) {
+__global__ void __launch_bounds__(128, 2)
+    k_join_fast(const JobDev* __restrict__ jobs, const HeadTile* __restrict__ tiles, uint32_t ntiles, FastNetDev fn,
+                int p, const uint16_t* __restrict__ pool_img, const uint16_t* __restrict__ jp,
+                uint16_t* __restrict__ zout_img, int* __restrict__ err) {
     extern __shared__ uint8_t smem_raw[];
-    __shared__ uint64_t mbar;
+    __shared__ uint64_t bar_in, bar_w[2], bar_mma;
     __shared__ uint32_t tmem_slot;
     __shared__ int abort_flag;
-    __shared__ float part[128][4];
     uint8_t* smem = align1024(smem_raw);
-    uint8_t* sW = smem;
-    uint8_t* sA = smem + 4 * TILE_J;
-    // per-layer vectors: [0] join_b bias (seat folded in), [1..3] block biases,
+    uint8_t* ring[2] = {smem, smem + TILE_J};
+    uint8_t* sA = smem + 2 * TILE_J;
+    // [0] b with the seat folded in, [1..3] running sums of the block biases,
     // [4..7] LayerNorm gammas, [8..11] betas
     float (*vec)[JW] = reinterpret_cast<float (*)[JW]>(sA + TILE_J);
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int quad = warp & 3, cg = warp >> 2;
-    const int row = quad * 32 + lane, col0 = cg * 32;
-    {
-        const uint4* src = reinterpret_cast<const uint4*>(fn.join_tiles);
-        uint4* dst = reinterpret_cast<uint4*>(sW);
-        for (uint32_t i = tid; i < 4 * TILE_J / 16; i += blockDim.x) dst[i] = src[i];
-        for (int i = tid; i < 12 * JW; i += blockDim.x) {
-            const int v = i / JW, c = i % JW;
-            vec[v][c] = v == 0 ? fn.beff[p][c] : v < 4 ? fn.bj[v - 1][c] : v < 8 ? fn.ln_g[v - 4][c] : fn.ln_b[v - 8][c];
+    const int tid = threadIdx.x, warp = tid >> 5;
+    for (int i = tid; i < 12 * JW; i += blockDim.x) {
+        const int v = i / JW, c = i % JW;
+        float x;
+        if (v == 0) {
+            x = fn.beff[p][c];
+        } else if (v < 4) {
+            x = 0.0f;
+            for (int u = 0; u < v; ++u) x += fn.bj[u][c];
+        } else {
+            x = v < 8 ? fn.ln_g[v - 4][c] : fn.ln_b[v - 8][c];
         }
+        vec[v][c] = x;
     }
     if (tid == 0) {
-        umma::mbar_init(&mbar, 1);
+        umma::mbar_init(&bar_in, 1);
+        umma::mbar_init(&bar_w[0], 1);
+        umma::mbar_init(&bar_w[1], 1);
+        umma::mbar_init(&bar_mma, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         abort_flag = 0;
     }
     if (warp == 0) umma::tmem_alloc(&tmem_slot, 128);
-    umma::fence_async_smem();
     umma::fence_before_sync();
     __syncthreads();
     umma::fence_after_sync();
     const uint32_t tmem = tmem_slot;
-    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    const uint32_t ntiles = (total_rows + 127) / 128;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const uint32_t my_tiles = blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const uint64_t uses = (uint64_t)my_tiles * 4;  // weight-slot uses: Wb, W1, W2, W3 per tile
+    bool pend_in = false, pend_w[2] = {false, false};
+    auto load_weight = [&](uint64_t k) {
+        const uint32_t slot = (uint32_t)(k & 1);
+        const uint8_t* src = fn.join_tiles + (size_t)(k & 3) * TILE_J;
+        umma::expect_tx(&bar_w[slot], TILE_J);
+        for (uint32_t o = 0; o < TILE_J; o += ATOM) umma::bulk_g2s(ring[slot] + o, src + o, ATOM, &bar_w[slot]);
+        pend_w[slot] = true;
+    };
+    auto load_pooled = [&](uint32_t t) {
+        const uint8_t* base = reinterpret_cast<const uint8_t*>(pool_img) + (size_t)t * (2 * ATOM);
+        umma::expect_tx(&bar_in, 2 * ATOM);
+        umma::bulk_g2s(sA, base + p * ATOM, ATOM, &bar_in);
+        umma::bulk_g2s(sA + ATOM, base + (1 - p) * ATOM, ATOM, &bar_in);
+        pend_in = true;
+    };
+    if (tid == 0 && my_tiles) {
+        load_pooled(blockIdx.x);
+        load_weight(0);
+        if (uses > 1) load_weight(1);
+    }
+    uint32_t ph_in = 0, ph_w[2] = {0, 0}, ph_mma = 0;
+    uint64_t k = 0;
     const uint32_t idesc = umma::idesc16(128, 128, umma::Op16<H>::fmt);
-    const float* beff = vec[0];
-    uint32_t phase = 0;
-    for (uint32_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-        const uint32_t g = tile * 128 + row;
-        const bool valid = g < total_rows;
-        float z[32];
-        if (valid) {
-            // columns 0..63 read the traverser's pooled belief, 64..127 the opponent's
-            const float* src = pooled + ((size_t)g * 2 + (cg < 2 ? p : 1 - p)) * POOL + (cg & 1) * 32;
-#pragma unroll
-            for (int c = 0; c < 4; ++c) umma::st_chunk<H>(sA, 128, row, col0 + 8 * c, src + 8 * c);
-            const uint4* jr = reinterpret_cast<const uint4*>(jp + (size_t)g * JW + col0);
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                uint4 v = jr[c];
-                const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+    for (uint32_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
+        const HeadTile ht = tiles[t];
+        const JobDev& J = jobs[ht.job];
+        const bool valid = (uint32_t)tid < ht.count;
+        const uint32_t g = J.row_base + ht.first + tid;
+        {  // z = jp + b
+            const uint4* jr = reinterpret_cast<const uint4*>(jp + (size_t)(valid ? g : 0) * JW);
+#pragma unroll 1
+            for (int c4 = 0; c4 < 4; ++c4) {
+                float v[32];
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
-                    z[8 * c + 2 * i] = umma::Op16<H>::lo(w4[i]) + beff[col0 + 8 * c + 2 * i];
-                    z[8 * c + 2 * i + 1] = umma::Op16<H>::hi(w4[i]) + beff[col0 + 8 * c + 2 * i + 1];
+                    const uint4 q = valid ? jr[4 * c4 + i] : make_uint4(0, 0, 0, 0);
+                    const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        v[8 * i + 2 * e] = umma::Op16<H>::lo(w4[e]) + vec[0][32 * c4 + 8 * i + 2 * e];
+                        v[8 * i + 2 * e + 1] = umma::Op16<H>::hi(w4[e]) + vec[0][32 * c4 + 8 * i + 2 * e + 1];
+                    }
                 }
+                umma::tmem_st32(tmem + lane_off + 32 * c4, v);
             }
-        } else {
-#pragma unroll
-            for (int c = 0; c < 4; ++c) umma::st_zero_chunk(sA, 128, row, col0 + 8 * c);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) z[j] = 0.0f;
         }
+        umma::fence_before_sync();
+        __syncthreads();
+        umma::fence_after_sync();
 #pragma unroll 1
-        for (int L = 0; L < 4; ++L) {
-            umma::fence_async_smem();
-            umma::fence_before_sync();
-            __syncthreads();
-            umma::fence_after_sync();
+        for (int L = 0; L < 4; ++L, ++k) {
+            const uint32_t slot = (uint32_t)(k & 1);
             if (tid == 0) {
-                const uint32_t wa = umma::smem_u32(sA), wb = umma::smem_u32(sW + L * TILE_J);
+                bool ok = true;
+                if (L == 0) {
+                    ok = umma::mbar_wait(&bar_in, ph_in, WAIT_LIMIT) && ok;
+                    pend_in = false;
+                }
+                ok = umma::mbar_wait(&bar_w[slot], ph_w[slot], WAIT_LIMIT) && ok;
+                pend_w[slot] = false;
+                if (!ok) abort_flag = 1;
+                umma::fence_after_sync();
+                const uint32_t a = umma::smem_u32(sA), b = umma::smem_u32(ring[slot]);
 #pragma unroll
                 for (int k0 = 0; k0 < JW; k0 += 16)
-                    umma::mma16(tmem, umma::desc_at(wa, 128, k0), umma::desc_at(wb, 128, k0), idesc, k0 > 0);
-                umma::commit(&mbar);
+                    umma::mma16(tmem, umma::desc_at(a, 128, k0), umma::desc_at(b, 128, k0), idesc, 1u);
+                umma::commit(&bar_mma);
             }
-            if (!umma::mbar_wait(&mbar, phase, WAIT_LIMIT)) abort_flag = 1;
-            phase ^= 1u;
+            if (L == 0) ph_in ^= 1u;
+            ph_w[slot] ^= 1u;
+            if (!umma::mbar_wait(&bar_mma, ph_mma, WAIT_LIMIT)) abort_flag = 1;
+            ph_mma ^= 1u;
             umma::fence_after_sync();
-            {
+            if (tid == 0) {  // the slot and (after the last layer) sA are free again
+                if (k + 2 < uses) load_weight(k + 2);
+                if (L == 3 && t + gridDim.x < ntiles) load_pooled(t + gridDim.x);
+            }
+            // epilogue: LayerNorm over the row (two passes over TMEM), GELU
+            const float* cb = vec[L];  // running bias sum (unused at L = 0)
+            float s = 0.0f, sq = 0.0f;
+#pragma unroll 1
+            for (int c4 = 0; c4 < 4; ++c4) {
                 float v[32];
-                umma::tmem_ld32(tmem + lane_off + col0, v);
-                if (L > 0) {
-                    const float* bias = vec[L] + col0;
+                umma::tmem_ld32(tmem + lane_off + 32 * c4, v);
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) z[j] += v[j] + bias[j];
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) z[j] += v[j];
+                for (int j = 0; j < 32; ++j) {
+                    const float x = L ? v[j] + cb[32 * c4 + j] : v[j];
+                    s += x;
+                    sq += x * x;
                 }
             }
-            float mean, inv;
-            row_stats4(z, 32, part, row, cg, JW, &mean, &inv);
-            const float* gam = vec[4 + L] + col0;
-            const float* bet = vec[8 + L] + col0;
+            const float mean = s * (1.0f / JW);
+            const float inv = rsqrtf(fmaxf(sq * (1.0f / JW) - mean * mean, 0.0f) + 1e-5f);
+            const float* gam = vec[4 + L];
+            const float* bet = vec[8 + L];
+#pragma unroll 1
+            for (int c4 = 0; c4 < 4; ++c4) {
+                float v[32];
+                umma::tmem_ld32(tmem + lane_off + 32 * c4, v);
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                float x[8];
+                for (int j = 0; j < 32; ++j) {
+                    const int c = 32 * c4 + j;
+                    v[j] = ((L ? v[j] + cb[c] : v[j]) - mean) * inv * gam[c] + bet[c];
+                }
 #pragma unroll
-                for (int i = 0; i < 8; ++i) x[i] = (z[8 * c + i] - mean) * inv * gam[8 * c + i] + bet[8 * c + i];
-                const uint4 o = umma::gelu_chunk<H>(x);
-                if (L < 3)
-                    *reinterpret_cast<uint4*>(sA + umma::sw128_offset(128, row, col0 + 8 * c)) = o;
-                else if (valid)
-                    reinterpret_cast<uint4*>(zout + (size_t)g * JW + col0)[c] = o;
+                for (int c8 = 0; c8 < 4; ++c8) {
+                    const uint4 o = umma::gelu_chunk<H>(v + 8 * c8);
+                    const uint32_t off = umma::sw128_offset(128, tid, 32 * c4 + 8 * c8);
+                    if (L < 3)
+                        *reinterpret_cast<uint4*>(sA + off) = o;
+                    else
+                        *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(zout_img) + (size_t)t * TILE_J + off) = o;
+                }
+            }
+            if (L < 3) {
+                umma::fence_async_smem();
+                umma::fence_before_sync();
+                __syncthreads();
+                umma::fence_after_sync();
             }
         }
         __syncthreads();
         if (abort_flag) break;
     }
-    if (tid == 0 && abort_flag) atomicExch(err, 1);
+    if (tid == 0) {
+        if (abort_flag) atomicExch(err, 1);
+        // copies still in flight after an early exit must land before the
+        // shared memory goes away
+        if (pend_in) umma::mbar_wait(&bar_in, ph_in, WAIT_LIMIT);
+        for (int sl = 0; sl < 2; ++sl)
+            if (pend_w[sl]) umma::mbar_wait(&bar_w[sl], ph_w[sl], WAIT_LIMIT);
+    }
     umma::fence_before_sync();
     __syncthreads();
     if (warp == 0) umma::tmem_dealloc(tmem, 128);
 }
-
-// One tile = up to 128 network rows of one job: first local row, count.
-struct HeadTile {
-    uint32_t job, first, count, pad;
-};
 
 // The join output layer, the readout LayerNorm and the per-config readout for
 // traverser p (net.rs:833-853, search.rs:1587-1636):
@@ -285,7 +370,7 @@ __global__ void __launch_bounds__(512, 1)
                 int p, const uint16_t* __restrict__ zout, const uint16_t* __restrict__ pb, const float* __restrict__ mass,
                 int* __restrict__ err) {
     extern __shared__ uint8_t smem_raw[];
-    __shared__ uint64_t mbar;
+    __shared__ uint64_t mbar, bar_a, bar_f;
     __shared__ uint32_t tmem_slot;
     __shared__ int abort_flag;
     __shared__ float part[128][4];
@@ -309,6 +394,8 @@ __global__ void __launch_bounds__(512, 1)
     }
     if (tid == 0) {
         umma::mbar_init(&mbar, 1);
+        umma::mbar_init(&bar_a, 1);
+        umma::mbar_init(&bar_f, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         abort_flag = 0;
     }
@@ -319,7 +406,16 @@ __global__ void __launch_bounds__(512, 1)
     umma::fence_after_sync();
     const uint32_t tmem = tmem_slot;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    uint32_t phase = 0;
+    uint32_t phase = 0, ph_a = 0, ph_f = 0;
+    bool pend_a = false, pend_f = false;
+    // the f(c) operand image of readout pass `pass` (128 configs of player p)
+    auto load_f = [&](const JobDev& J, uint32_t pass) {
+        const uint8_t* src = reinterpret_cast<const uint8_t*>(J.f16) +
+                             ((p == 1 ? (J.ncfg_player[0] + 127) / 128 : 0) + pass) * (size_t)(2 * TILE_J);
+        umma::expect_tx(&bar_f, 2 * TILE_J);
+        for (uint32_t o = 0; o < 2 * TILE_J; o += ATOM) umma::bulk_g2s(sF + o, src + o, ATOM, &bar_f);
+        pend_f = true;
+    };
     // readout staging, row-major [128 rows][128 columns] with the low five
     // column bits XORed by the row's: conflict-free for both the writes (one
     // row per lane) and the per-row reads
@@ -330,21 +426,18 @@ __global__ void __launch_bounds__(512, 1)
         const bool valid = (uint32_t)row < ht.count;
         const uint32_t r = ht.first + row;          // job-local network row
         const uint32_t g = J.row_base + r;          // global network row
-        // A = out rows (bf16, 256 bytes each): this thread's 32 columns
-        if (valid) {
-            const uint4* src = reinterpret_cast<const uint4*>(zout + (size_t)g * JW + 32 * cg);
-#pragma unroll
-            for (int c = 0; c < 4; ++c)
-                *reinterpret_cast<uint4*>(sA + umma::sw128_offset(128, row, 32 * cg + 8 * c)) = src[c];
-        } else {
-#pragma unroll
-            for (int c = 0; c < 4; ++c) umma::st_zero_chunk(sA, 128, row, 32 * cg + 8 * c);
-        }
-        umma::fence_async_smem();
-        umma::fence_before_sync();
-        __syncthreads();
-        umma::fence_after_sync();
+        // A = the join output image of this tile, and the first f(c) image,
+        // by bulk copy
         if (tid == 0) {
+            const uint8_t* src = reinterpret_cast<const uint8_t*>(zout) + (size_t)t * TILE_J;
+            umma::expect_tx(&bar_a, TILE_J);
+            umma::bulk_g2s(sA, src, ATOM, &bar_a);
+            umma::bulk_g2s(sA + ATOM, src + ATOM, ATOM, &bar_a);
+            pend_a = true;
+            if (J.ncfg_player[p]) load_f(J, 0);
+            if (!umma::mbar_wait(&bar_a, ph_a, WAIT_LIMIT)) abort_flag = 1;
+            pend_a = false;
+            umma::fence_after_sync();
             const uint32_t wa = umma::smem_u32(sA), wb = umma::smem_u32(sW);
             const uint32_t idesc = umma::idesc16(128, 256, umma::Op16<H>::fmt);
 #pragma unroll
@@ -352,8 +445,9 @@ __global__ void __launch_bounds__(512, 1)
                 umma::mma16(tmem, umma::desc_at(wa, 128, k0), umma::desc_at(wb, 256, k0), idesc, k0 > 0);
             umma::commit(&mbar);
         }
+        ph_a ^= 1u;
         // meanwhile: the row's opponent reach mass (kept by the pooling
-        // kernel), its readout columns, and the F rows of the first pass
+        // kernel) and its readout columns
         float opp_mass = 0.0f;
         uint32_t ncfg_row = 0;
         const uint32_t* lcol = nullptr;
@@ -365,21 +459,6 @@ __global__ void __launch_bounds__(512, 1)
             out = J.vals[p] + J.lr_vidx[2 * r + p];
         }
         const uint32_t nfp = J.ncfg_player[p];
-        const uint16_t* F = J.f16 + (size_t)(p == 1 ? J.ncfg_player[0] : 0) * D;
-        auto load_f = [&](uint32_t nb) {
-            // rows [nb, nb + 128): thread (row, cg) copies 8 of the row's 32 chunks
-            const uint32_t fr = nb + row;
-            if (fr < nfp) {
-                const uint4* src = reinterpret_cast<const uint4*>(F + (size_t)fr * D) + 8 * cg;
-#pragma unroll
-                for (int c = 0; c < 8; ++c)
-                    *reinterpret_cast<uint4*>(sF + umma::sw128_offset(128, row, 64 * cg + 8 * c)) = src[c];
-            } else {
-#pragma unroll
-                for (int c = 0; c < 8; ++c) umma::st_zero_chunk(sF, 128, row, 64 * cg + 8 * c);
-            }
-        };
-        load_f(0);
         if (!umma::mbar_wait(&mbar, phase, WAIT_LIMIT)) abort_flag = 1;
         phase ^= 1u;
         umma::fence_after_sync();
@@ -418,12 +497,15 @@ __global__ void __launch_bounds__(512, 1)
             }
         }
         for (uint32_t nb = 0; nb < nfp; nb += 128) {
-            if (nb > 0) load_f(nb);
+            if (nb > 0 && tid == 0) load_f(J, nb / 128);
             umma::fence_async_smem();
             umma::fence_before_sync();
             __syncthreads();
             umma::fence_after_sync();
             if (tid == 0) {
+                if (!umma::mbar_wait(&bar_f, ph_f, WAIT_LIMIT)) abort_flag = 1;
+                pend_f = false;
+                umma::fence_after_sync();
                 const uint32_t ha = umma::smem_u32(sH), fa = umma::smem_u32(sF);
                 const uint32_t idesc = umma::idesc16(128, 128, umma::Op16<H>::fmt);
 #pragma unroll
@@ -431,6 +513,7 @@ __global__ void __launch_bounds__(512, 1)
                     umma::mma16(tmem + 256, umma::desc_at(ha, 128, k0), umma::desc_at(fa, 128, k0), idesc, k0 > 0);
                 umma::commit(&mbar);
             }
+            ph_f ^= 1u;
             if (!umma::mbar_wait(&mbar, phase, WAIT_LIMIT)) abort_flag = 1;
             phase ^= 1u;
             umma::fence_after_sync();
@@ -450,28 +533,37 @@ __global__ void __launch_bounds__(512, 1)
                     if (col < 128) out[c] = (st[(col & ~31u) | ((col & 31u) ^ (uint32_t)lane)] + fn.vbias) * opp_mass;
                 }
             }
+            umma::fence_async_smem();  // the staging writes precede the next bulk copy into sF
             umma::fence_before_sync();
             __syncthreads();
         }
         if (abort_flag) break;
     }
-    if (tid == 0 && abort_flag) atomicExch(err, 2);
+    if (tid == 0) {
+        if (abort_flag) atomicExch(err, 2);
+        if (pend_a) umma::mbar_wait(&bar_a, ph_a, WAIT_LIMIT);
+        if (pend_f) umma::mbar_wait(&bar_f, ph_f, WAIT_LIMIT);
+    }
     umma::fence_before_sync();
     __syncthreads();
     if (warp == 0) umma::tmem_dealloc(tmem, 512);
 }
 
-// f(c) rows of every config as 16-bit operands, grouped by player (player 0's first).
+// f(c) of every config as the readout's B-operand images: for each player,
+// passes of 128 configs (by index among the player's configs) x 256, K-major
+// and 128-byte swizzled; player 0's passes first.
 template <bool H>
 __global__ void k_pack_f16(const JobDev* __restrict__ jobs, const uint32_t* __restrict__ cfg_job,
                            const uint32_t* __restrict__ cfg_local, uint32_t total_cfgs) {
-    const uint32_t i = blockIdx.x;
-    if (i >= total_cfgs) return;
-    const JobDev& J = jobs[cfg_job[i]];
-    const uint32_t c = cfg_local[i];
-    const uint32_t row = (J.cplayer[c] == 1 ? J.ncfg_player[0] : 0) + J.cfg_col[c];
+    const uint32_t e = blockIdx.x;
+    if (e >= total_cfgs) return;
+    const JobDev& J = jobs[cfg_job[e]];
+    const uint32_t c = cfg_local[e];
+    const uint32_t col = J.cfg_col[c], i = col & 127;
+    uint8_t* img = reinterpret_cast<uint8_t*>(J.f16) +
+                   ((J.cplayer[c] == 1 ? (J.ncfg_player[0] + 127) / 128 : 0) + (col >> 7)) * (size_t)(2 * TILE_J);
     for (int j = threadIdx.x; j < D; j += blockDim.x)
-        J.f16[(size_t)row * D + j] = umma::Op16<H>::one(J.cf[(size_t)c * D + j]);
+        *reinterpret_cast<uint16_t*>(img + umma::sw128_offset(128, i, j)) = umma::Op16<H>::one(J.cf[(size_t)c * D + j]);
 }
 
 static int num_sms() {
@@ -482,11 +574,12 @@ static int num_sms() {
 }
 
 void launch_pool_fast(const JobDev* jobs, const uint32_t* row_job, const uint32_t* row_local, uint32_t total_rows,
-                      int mask, float* pooled, float* mass, cudaStream_t s) {
+                      int mask, uint16_t* pool_img, float* mass, bool half, cudaStream_t s) {
     if (!total_rows || !mask) return;
     uint64_t warps = (uint64_t)total_rows * (mask == 3 ? 2 : 1);
-    k_pool_fast<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, s>>>(jobs, row_job, row_local, total_rows, mask, pooled,
-                                                                      mass);
+    const unsigned grid = (unsigned)((warps * 32 + 255) / 256);
+    if (half) k_pool_fast<true><<<grid, 256, 0, s>>>(jobs, row_job, row_local, total_rows, mask, pool_img, mass);
+    else k_pool_fast<false><<<grid, 256, 0, s>>>(jobs, row_job, row_local, total_rows, mask, pool_img, mass);
 }
 
 bool raise_smem_limit(const void* fn, size_t smem) {
@@ -501,15 +594,15 @@ bool raise_smem_limit(const void* fn, size_t smem) {
     return true;
 }
 
-void launch_join_fast(const FastNetDev& fn, int p, const float* pooled, const uint16_t* jp, uint16_t* zout,
-                      uint32_t total_rows, int* err, cudaStream_t s) {
-    if (!total_rows) return;
-    const size_t smem = 5 * TILE_J + 12 * JW * 4 + 1024;
+void launch_join_fast(const JobDev* jobs, const void* tiles, uint32_t ntiles, const FastNetDev& fn, int p,
+                      const uint16_t* pool_img, const uint16_t* jp, uint16_t* zout_img, int* err, cudaStream_t s) {
+    if (!ntiles) return;
+    const size_t smem = 3 * TILE_J + 12 * JW * 4 + 1024;  // two weight slots, the A operand, the vectors
     auto kern = fn.half ? k_join_fast<true> : k_join_fast<false>;
     if (!raise_smem_limit((const void*)kern, smem)) return;
-    uint32_t ntiles = (total_rows + 127) / 128;
-    uint32_t grid = std::min<uint32_t>(ntiles, (uint32_t)num_sms());
-    kern<<<grid, 512, smem, s>>>(fn, p, pooled, jp, zout, total_rows, err);
+    uint32_t grid = std::min<uint32_t>(ntiles, 2u * (uint32_t)num_sms());
+    kern<<<grid, 128, smem, s>>>(jobs, reinterpret_cast<const HeadTile*>(tiles), ntiles, fn, p, pool_img, jp, zout_img,
+                                 err);
 }
 
 void launch_head_fast(const JobDev* jobs, const void* tiles, uint32_t ntiles, const FastNetDev& fn, int p,

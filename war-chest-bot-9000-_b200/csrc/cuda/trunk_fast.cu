@@ -42,24 +42,11 @@ constexpr uint32_t A1_BYTES = 128 * 3 * 128;   // [128][192]
 constexpr uint32_t A2_BYTES = 128 * 2 * 128;   // [128][96]
 constexpr uint32_t WAIT_LIMIT = 1u << 26;
 
-__device__ __forceinline__ void bulk_g2s(uint8_t* dst, const uint8_t* src, uint32_t bytes, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-            umma::smem_u32(dst)),
-        "l"(src), "r"(bytes), "r"(umma::smem_u32(bar))
-        : "memory");
-}
-
-__device__ __forceinline__ void expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(umma::smem_u32(bar)), "r"(bytes)
-                 : "memory");
-}
-
 // One elected thread: fetch a block's weight tiles into `dst`.
 __device__ __forceinline__ void fetch_block(uint8_t* dst, const uint8_t* tiles, int blk, uint64_t* bar) {
-    expect_tx(bar, BLOCK_BYTES);
+    umma::expect_tx(bar, BLOCK_BYTES);
     const uint8_t* src = tiles + (size_t)blk * BLOCK_BYTES;
-    for (uint32_t o = 0; o < BLOCK_BYTES; o += 15360) bulk_g2s(dst + o, src + o, 15360, bar);
+    for (uint32_t o = 0; o < BLOCK_BYTES; o += 15360) umma::bulk_g2s(dst + o, src + o, 15360, bar);
 }
 
 template <bool H>

@@ -306,17 +306,29 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
     size_t o_gpool = 0, o_gjp = 0, o_gmass = 0, o_gpb = 0, o_gz = 0, o_tiles = 0, o_err = 0;
     struct HeadTile { uint32_t job, first, count, pad; };
     std::vector<HeadTile> head_tiles;
+    std::vector<uint32_t> tile_base(nj, 0);
+    std::vector<size_t> f16_bytes(nj, 0);
     if (fast) {
-        for (size_t j = 0; j < nj; ++j) o_f16[j] = A.take(2ull * jobs[j]->img->ncfg * NET_D);
+        // per-job tiles of 128 network rows; the pooled beliefs and the join
+        // output live as per-tile operand images (128-byte swizzled, K-major)
+        for (uint32_t j = 0; j < nj; ++j) {
+            tile_base[j] = (uint32_t)head_tiles.size();
+            for (uint32_t f = 0; f < jobs[j]->img->nrows_net; f += 128)
+                head_tiles.push_back({j, f, std::min<uint32_t>(128, jobs[j]->img->nrows_net - f), 0});
+        }
+        const size_t NT = head_tiles.size();
+        for (size_t j = 0; j < nj; ++j) {
+            const JobImage& J = *jobs[j]->img;
+            // f(c) as readout operand images: 128 configs x 256 per pass, per player
+            f16_bytes[j] = 65536ull * ((J.ncfg_player[0] + 127) / 128 + (J.ncfg_player[1] + 127) / 128);
+            o_f16[j] = A.take(f16_bytes[j]);
+        }
         size_t R = row_job.size();
-        o_gpool = A.take(4ull * R * 2 * NET_POOL);
+        o_gpool = A.take(32768ull * NT);  // [tile][player 0 | player 1] 128 x 64 images
         o_gjp = A.take(2ull * R * NET_JW);
         o_gmass = A.take(8ull * R);
         o_gpb = A.take(2ull * R * NET_D);
-        o_gz = A.take(2ull * R * NET_JW);
-        for (uint32_t j = 0; j < nj; ++j)
-            for (uint32_t f = 0; f < jobs[j]->img->nrows_net; f += 128)
-                head_tiles.push_back({j, f, std::min<uint32_t>(128, jobs[j]->img->nrows_net - f), 0});
+        o_gz = A.take(32768ull * NT);     // [tile] 128 x 128 image
         o_tiles = A.take(sizeof(HeadTile) * head_tiles.size());
         o_err = A.take(16);
     }
@@ -374,6 +386,7 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
         d.ncfg_player[0] = J.ncfg_player[0];
         d.ncfg_player[1] = J.ncfg_player[1];
         d.row_base = row_base[j];
+        d.tile_base = tile_base[j];
         d.f16 = fast ? reinterpret_cast<uint16_t*>(D + o_f16[j]) : nullptr;
         d.cur = reinterpret_cast<float*>(D + P.cur);
         d.regret = reinterpret_cast<float*>(D + P.regret);
@@ -420,11 +433,11 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
     b.d_cfg_job = reinterpret_cast<uint32_t*>(D + o_cj);
     b.d_cfg_local = reinterpret_cast<uint32_t*>(D + o_cl);
     if (fast) {
-        b.g_pooled = reinterpret_cast<float*>(D + o_gpool);
+        b.g_pool_img = reinterpret_cast<uint16_t*>(D + o_gpool);
         b.g_jp = reinterpret_cast<uint16_t*>(D + o_gjp);
         b.g_mass = reinterpret_cast<float*>(D + o_gmass);
         b.g_pb = reinterpret_cast<uint16_t*>(D + o_gpb);
-        b.g_zout = reinterpret_cast<uint16_t*>(D + o_gz);
+        b.g_zout_img = reinterpret_cast<uint16_t*>(D + o_gz);
         b.d_head_tiles = D + o_tiles;
         b.n_head_tiles = (uint32_t)head_tiles.size();
         b.d_err = reinterpret_cast<int*>(D + o_err);
@@ -447,6 +460,10 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
             check(cudaMemcpyAsync(b.d_head_tiles, head_tiles.data(), sizeof(HeadTile) * head_tiles.size(),
                                   cudaMemcpyHostToDevice, s), "upload head tiles");
         check(cudaMemsetAsync(b.d_err, 0, 16, s), "clear error flag");
+        // padding rows and configs of the operand images stay zero
+        check(cudaMemsetAsync(b.g_pool_img, 0, 32768ull * head_tiles.size(), s), "clear pooled images");
+        for (size_t j = 0; j < nj; ++j)
+            check(cudaMemsetAsync(D + o_f16[j], 0, f16_bytes[j], s), "clear readout images");
     }
     check(cudaStreamSynchronize(s), "batch upload");
     return bp;
@@ -504,10 +521,12 @@ struct Sched {
     void leaf_values_(int p, int pool_mask) {
         DeviceCtx& dv = *b.dev;
         if (dv.have_net && !dv.precise) {
-            wcdev::launch_pool_fast(J, b.d_row_job, b.d_row_local, b.total_rows, pool_mask, b.g_pooled, b.g_mass, s);
-            wcdev::launch_join_fast(dv.fast, p, b.g_pooled, b.g_jp, b.g_zout, b.total_rows, b.d_err, s);
-            wcdev::launch_head_fast(J, b.d_head_tiles, b.n_head_tiles, dv.fast, p, b.g_zout, b.g_pb, b.g_mass, b.d_err,
-                                    s);
+            wcdev::launch_pool_fast(J, b.d_row_job, b.d_row_local, b.total_rows, pool_mask, b.g_pool_img, b.g_mass,
+                                    dv.half, s);
+            wcdev::launch_join_fast(J, b.d_head_tiles, b.n_head_tiles, dv.fast, p, b.g_pool_img, b.g_jp, b.g_zout_img,
+                                    b.d_err, s);
+            wcdev::launch_head_fast(J, b.d_head_tiles, b.n_head_tiles, dv.fast, p, b.g_zout_img, b.g_pb, b.g_mass,
+                                    b.d_err, s);
         } else if (dv.have_net) {
             if (pool_mask) wcdev::launch_pool(J, b.d_row_job, b.d_row_local, b.total_rows, pool_mask, s);
             wcdev::launch_join_readout(J, b.d_row_job, b.d_row_local, b.total_rows, p, dv.W, dv.B, dv.LN, s);

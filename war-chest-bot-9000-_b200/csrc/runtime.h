@@ -74,10 +74,10 @@ struct Batch {
     uint32_t* d_cfg_local = nullptr;
     uint32_t total_rows = 0, total_cfgs = 0, max_carried = 0;
     // fast network path: global per-row bf16 activations and per-job tiles
-    float* g_pooled = nullptr;    // [rows][2][POOL]
+    uint16_t* g_pool_img = nullptr; // [tile][player][128 x POOL operand image]
     uint16_t* g_jp = nullptr;     // [rows][JW]
     uint16_t* g_pb = nullptr;     // [rows][D]
-    uint16_t* g_zout = nullptr;   // [rows][JW]
+    uint16_t* g_zout_img = nullptr; // [tile][128 x JW operand image]: the join output
     float* g_mass = nullptr;      // [rows][2]: each player's reach mass at the row (pooling's normaliser)
     void* d_head_tiles = nullptr;
     uint32_t n_head_tiles = 0;
