@@ -40,7 +40,7 @@ UNIT = "node-updates/s"
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--steps", type=int, default=2)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--subgames", type=int, default=4096, help="subgames per GPU")
@@ -145,30 +145,66 @@ class Clocks:
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons)}
 
 
-def algorithmic_bytes(jobs):
-    """Bytes per solve each CFR kernel class must move (every value read or
-    written once; indices u32). Per unit: a regret-matching row moves 24 B per
-    legal cell (regret, current, running sum read or written) and 8 B per row;
-    a value gather 12 B per entry (index, weight, source value) and 8 B per
-    output; a reach gather 24 B per cell entry, 16 B per draw entry and 8 B per
-    output."""
+def algorithmic_work(jobs):
+    """Per kernel class, the work one solve must do (every value read or
+    written once; indices u32): HBM bytes for the CFR and pooling kernels,
+    tensor FLOPs for the network kernels. Per unit:
+      rows     24 B per legal cell (regret R/W, current W, child value, index) + 8 B per row
+      vgather  12 B per entry (index, weight, source value) + 8 B per output
+      reach    24 B per cell entry, 16 B per draw entry, 8 B per output
+      pool     8 B per leaf-config entry (reach, column) + 128 B per row (the f16 pooled atom)
+      join     4 x 2*128*128 FLOP per network row
+      head     2*128*256 FLOP per network row + 2*256 per leaf-config entry of the traverser
+      trunk    17.0 MFLOP per network row (once per solve)
+    CFR classes run once per iteration for one player, so a solve does each
+    player's share iters/2 times; the leaf classes run once per iteration and
+    twice per carried root in Phase 2."""
     c = np.sum([j.counts() for j in jobs], axis=0).astype(np.float64)
     iters = jobs[0].cfg.iters
-    # per iteration pair each player's share runs once
     pairs = iters / 2.0
-    rows = 24 * (c[0] + c[1]) + 8 * (c[2] + c[3])
-    vg = 12 * (c[4] + c[5]) + 8 * (c[6] + c[7])
-    reach = 24 * (c[8] + c[9]) + 16 * (c[10] + c[11]) + 8 * (c[12] + c[13])
-    return {"rows": rows * pairs, "vgather": vg * pairs, "reach": reach * pairs}
+    rows = sum(j.info["net_rows"] for j in jobs)
+    carried = max(max(j.info["ncarried"], 1) for j in jobs)
+    calls = iters + 2 * carried
+    entries = (c[14] + c[15]) / 2.0  # leaf-config entries per call (players alternate)
+    return {
+        "rows": ("hbm", (24 * (c[0] + c[1]) + 8 * (c[2] + c[3])) * pairs),
+        "vgather": ("hbm", (12 * (c[4] + c[5]) + 8 * (c[6] + c[7])) * pairs),
+        "reach": ("hbm", (24 * (c[8] + c[9]) + 16 * (c[10] + c[11]) + 8 * (c[12] + c[13])) * pairs),
+        "pool": ("hbm", (8 * entries + 128 * rows) * calls),
+        "join": ("tensor", 4 * 2 * 128 * 128 * rows * calls),
+        "head": ("tensor", (2 * 128 * 256 * rows + 2 * 256 * entries) * calls),
+        "trunk": ("tensor", 17.0e6 * rows),
+    }
 
 
 def peaks():
+    """Measured HBM GB/s and bf16 TFLOP/s of this pool's B200s: the burst
+    figure for a kernel timed alone, the sustained one for kernels timed
+    inside a long step (the classes here are timed inside whole solves)."""
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             p = json.load(f)
-        return p["hbm_gbs"], p["bf16_tflops"], "measured"
+        return p["hbm_gbs"], p.get("bf16_tflops_sustained", p["bf16_tflops"]), "measured (tensor: sustained)"
     except Exception:
-        return 6650.0, 1590.0, "fallback"
+        return 6650.0, 1400.0, "fallback"
+
+
+def rooflines(prof, work):
+    """Achieved rate and fraction of peak per kernel class, from the
+    per-class CUDA-event times of the timed solves."""
+    hbm, tflops, src = peaks()
+    out = {}
+    for k, (bound, amount) in work.items():
+        ms = prof.get(k, 0.0)
+        if ms <= 0:
+            continue
+        if bound == "hbm":
+            a = amount / (ms / 1e3) / 1e9
+            out[k] = {"bound": "hbm", "achieved": a, "peak": hbm, "unit": "GB/s", "frac": a / hbm, "ms": ms}
+        else:
+            a = amount / (ms / 1e3) / 1e12
+            out[k] = {"bound": "tensor", "achieved": a, "peak": tflops, "unit": "TFLOP/s", "frac": a / tflops, "ms": ms}
+    return out, src
 
 
 def cpu_sample_roots(oracle, cfg, seeds, threads):
@@ -317,15 +353,13 @@ def main():
     e2e = {"value": total_nu / e2e_s, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
            "timing": "host wall clock around the synchronous wc_solve_batch (upload, solve, download)"}
 
-    # roofline of the dominant CFR kernel class
+    # rooflines per kernel class; the headline object is the dominant one
     prof = {k: float(np.mean([p[k] for p in profiles])) for k in profiles[0]}
-    algo = algorithmic_bytes(jobs)
-    dom = max(("rows", "vgather", "reach"), key=lambda k: prof[k])
-    hbm, tflops, src = peaks()
-    achieved = algo[dom] / (prof[dom] / 1e3) / 1e9
-    roofline = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                "frac": achieved / hbm, "traffic": None, "peak_source": src,
-                "per_class_ms": prof, "algorithmic_bytes_per_solve": algo}
+    per_class, src = rooflines(prof, algorithmic_work(jobs))
+    dom = max(per_class, key=lambda k: per_class[k]["ms"])
+    roofline = dict(per_class[dom])
+    roofline.update({"kernel": KERNELS.get(dom, dom), "traffic": TRAFFIC.get(dom), "peak_source": src,
+                     "per_class": per_class, "per_class_ms": prof})
 
     if rank == 0:
         base = None if args.no_cpu_baseline else cpu_baseline(oracle_lib, cfg, weights, seeds)
@@ -333,7 +367,8 @@ def main():
                 "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": DTYPES[args.net],
                 "data": "synthetic (seeded roots, seeded He-normal weights)", "config": workload,
-                "e2e": e2e, "gpu_launches": launches_per_step(batch_levels(jobs), args.iters, args.net != "none"),
+                "e2e": e2e, "gpu_launches": launches_per_step(batch_levels(jobs), args.iters, args.net,
+                                                  max(max(j.info["ncarried"], 1) for j in jobs)),
                 "roofline": roofline, "cpu_baseline": base, "clocks": clocks_rec,
                 "leaf_evals_per_sec": allsum(world, stats["leaf_evals"]) / step_s,
                 "host_build_s": build_s, "device_bytes": stats["device_bytes"]}
@@ -349,12 +384,17 @@ def batch_levels(jobs):
     return max(j.info["levels"] for j in jobs)
 
 
-def launches_per_step(levels, iters, net):
-    """Kernel launches of one solve (the runtime's schedule, see runtime.cu)."""
-    per_iter = (3 if net else 2) + 2 * levels + (levels - 1)
-    setup = (3 if net else 0) + 2 + 2 * (levels - 1)
-    snaps = 1 + 1
-    phase2 = 1 + 2 * (levels - 1) + 2 * ((3 if net else 2) + 2 * levels + 1)
+def launches_per_step(levels, iters, net, carried=1):
+    """Kernel launches of one solve, following the runtime's schedule: per
+    leaf call pooling (when a reach changed), join, head and terminal leaves
+    on the tensor path; pooling, join+readout and terminals on the exact
+    path; per level a rows and a value-gather launch and, per moved player, a
+    reach gather."""
+    leaf = {"f16": 4, "bf16": 4, "exact": 3, "none": 2}[net]
+    setup = {"f16": 4, "bf16": 4, "exact": 3, "none": 0}[net] + 2 + 2 * (levels - 1)
+    per_iter = leaf + 2 * levels + (levels - 1)
+    snaps = 2
+    phase2 = carried * (1 + 2 * (levels - 1) + 2 * (leaf + 2 * levels + 1) - 1)
     return setup + iters * per_iter + snaps + phase2
 
 
@@ -412,6 +452,12 @@ def allsum(world, x):
 
 
 PLIES = 20
+KERNELS = {"rows": "k_rows", "vgather": "k_vgather", "reach": "k_rgather", "pool": "k_pool_fast",
+           "join": "k_join_fast", "head": "k_head_fast", "trunk": "k_trunk_fast"}
+# DRAM bytes per launch from ncu (dram__bytes_read.sum + dram__bytes_write.sum)
+# of the kernel on a smaller case, scaled to the full launch by network rows;
+# None until a capture exists for the current build.
+TRAFFIC = {}
 DTYPES = {"f16": "f32 CFR state, f16 tensor-core value net (fp32 accumulate)",
           "bf16": "f32 CFR state, bf16 tensor-core value net (fp32 accumulate)",
           "exact": "f32", "none": "f32"}

@@ -151,14 +151,16 @@ int wc_batch_solve(wc_batch* b);
 /* A solve with CUDA-event timing per kernel class, in milliseconds:
  * [0] per-solve network, [1] leaf evaluation, [2] regret-matching rows,
  * [3] value gathers, [4] reach gathers (+ average), [5] snapshots, [6] Phase 2,
- * [7] init, [8] whole solve. class_ms needs 9 entries. */
+ * [7] init, [8] whole solve; on the tensor-core path also the parts
+ * [9] pooling, [10] join, [11] head (of [1]) and [12] trunk (of [0]).
+ * class_ms needs 13 entries. */
 int wc_batch_solve_profiled(wc_batch* b, double* class_ms, int nclass);
 int wc_batch_download(wc_batch* b, size_t job, float* strategy, float* root_values, uint16_t* carries);
 /* Leaf evaluation alone (the per-solve network, then every network row's
  * values for traverser p at the initial uniform-strategy reaches), and its
  * read-back: rows in the reference's leaf_rows order, each row's p-configs
  * in support order (counterfactual values: network value x opponent reach).
- * class_ms, if non-NULL, receives the same 9 timing classes as
+ * class_ms, if non-NULL, receives the same 13 timing classes as
  * wc_batch_solve_profiled (leaf evaluation alone in [1]). */
 int wc_batch_leaf_values(wc_batch* b, int p, double* class_ms);
 int wc_batch_download_leaf_values(wc_batch* b, size_t job, int p, float* out);

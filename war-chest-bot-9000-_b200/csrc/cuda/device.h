@@ -49,6 +49,7 @@ struct JobDev {
     const uint32_t* leaf_col; // per leaf_cidx entry: its config's cfg_col (the readout column)
     uint16_t* f16;     // fast path: f(c) as readout operand images, 128 configs x D each (64 KB),
                        // player 0's ceil(n0 / 128) passes then player 1's
+    uint16_t* g16;     // fast path: g(c) as pooling operand images, 64 x 128 configs each (16 KB), same order
     uint32_t ncfg_player[2];
     uint32_t row_base; // first global network row of this job
     uint32_t tile_base; // first 128-row leaf tile of this job (tensor-core path)

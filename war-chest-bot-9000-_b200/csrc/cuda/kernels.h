@@ -50,8 +50,8 @@ int umma_selftest(const uint16_t* A, const uint16_t* B, int K, int N, float* D);
 // 1 bad shape, 2 CUDA error, 3 tcgen05 wait timed out, 4 k beyond 256,
 // 5 the array's device address could not be looked up.
 int umma_selftest_static(const uint16_t* A, const uint16_t* B, int K, int N, float* D);
-void launch_pool_fast(const JobDev* jobs, const uint32_t* row_job, const uint32_t* row_local, uint32_t total_rows,
-                      int mask, uint16_t* pool_img, float* mass, bool half, cudaStream_t s);
+void launch_pool_fast(const JobDev* jobs, const void* tiles, uint32_t ntiles, int mask, uint16_t* pool_img, float* mass,
+                      bool half, int* err, cudaStream_t s);
 void launch_join_fast(const JobDev* jobs, const void* tiles, uint32_t ntiles, const FastNetDev& fn, int p,
                       const uint16_t* pool_img, const uint16_t* jp, uint16_t* zout_img, int* err, cudaStream_t s);
 void launch_head_fast(const JobDev* jobs, const void* tiles, uint32_t ntiles, const FastNetDev& fn, int p,

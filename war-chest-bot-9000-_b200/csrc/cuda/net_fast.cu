@@ -85,62 +85,6 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
     return p + ((1024u - (umma::smem_u32(p) & 1023u)) & 1023u);
 }
 
-// Pooled belief embeddings, one warp per (network row, player): normalised
-// reach over the leaf's configs weighting g(c) (search.rs:1512-1547). The
-// warp loads 32 (weight, config) pairs at a time and broadcasts them by
-// shuffle, so the g-row loads (a lane per column pair) do not wait on the
-// index loads one by one. The result goes to the player's 64-column atom of
-// the row's tile image, the join's A operand as it sits in shared memory.
-// The reach mass (the normaliser) is kept: it is the opponent mass the
-// readout of the other player's query scales by.
-template <bool H>
-__global__ void k_pool_fast(const JobDev* __restrict__ jobs, const uint32_t* __restrict__ row_job,
-                            const uint32_t* __restrict__ row_local, uint32_t total_rows, int mask,
-                            uint16_t* __restrict__ pool_img, float* __restrict__ mass) {
-    const int nq = mask == 3 ? 2 : 1;
-    const uint64_t gw = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
-    if (gw >= (uint64_t)total_rows * nq) return;
-    const uint32_t g = (uint32_t)(gw / nq);
-    const int q = mask == 3 ? (int)(gw % nq) : (mask == 1 ? 0 : 1);
-    const JobDev& J = jobs[row_job[g]];
-    const uint32_t r = row_local[g];
-    const float* w = J.reach + J.lr_ridx[2 * r + q];
-    const uint32_t n = J.lr_nc[2 * r + q];
-    const uint32_t* idx = J.leaf_cidx + J.leaf_coff[2 * r + q];
-    float tot = 0.0f;
-    for (uint32_t c = lane; c < n; c += 32) tot += w[c];
-#pragma unroll
-    for (int o = 16; o; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
-    float scale, flat;
-    if (tot > 1e-30f) { scale = 1.0f / tot; flat = 0.0f; }
-    else { scale = 0.0f; flat = 1.0f / (float)(n > 0 ? n : 1); }
-    if (lane == 0) mass[(size_t)g * 2 + q] = tot;
-    float a0 = 0.0f, a1 = 0.0f;
-    for (uint32_t c0 = 0; c0 < n; c0 += 32) {
-        const uint32_t c = c0 + lane;
-        float wl = 0.0f;
-        uint32_t il = 0;
-        if (c < n) {
-            wl = w[c] * scale + flat;
-            il = idx[c];
-        }
-        const uint32_t m = n - c0 < 32 ? n - c0 : 32;
-#pragma unroll 4
-        for (uint32_t k = 0; k < m; ++k) {
-            const float wk = __shfl_sync(0xffffffffu, wl, k);
-            const uint32_t ik = __shfl_sync(0xffffffffu, il, k);
-            const float2 gv = reinterpret_cast<const float2*>(J.cg + (size_t)ik * POOL)[lane];
-            a0 += wk * gv.x;
-            a1 += wk * gv.y;
-        }
-    }
-    const uint32_t i = r & 127, col = 2 * lane;
-    uint8_t* img = reinterpret_cast<uint8_t*>(pool_img) + (size_t)(J.tile_base + (r >> 7)) * (2 * ATOM) + q * ATOM;
-    *reinterpret_cast<uint32_t*>(img + i * 128 + (((col >> 3) ^ (i & 7)) << 4) + (col & 7) * 2) =
-        umma::Op16<H>::pack(a0, a1);
-}
-
 // Row statistics of a LayerNorm whose row is spread over the four column
 // groups of a 16-warp CTA (warp w: rows 32 (w % 4) .., columns group w / 4).
 __device__ __forceinline__ void row_stats4(const float* v, int n, float (*part)[4], int row, int cg, int width,
@@ -357,6 +301,127 @@ __global__ void __launch_bounds__(128, 2)
     if (warp == 0) umma::tmem_dealloc(tmem, 128);
 }
 
+// Pooled belief embeddings (search.rs:1512-1547) of one 128-row tile on the
+// tensor cores: pooled_q = beta_q G_q, where beta_q[row][c] is the row's
+// normalised reach on config c (player q's configs, by index; about 20 of
+// ~110 nonzero per row) and G_q[c] = g(c). One thread per row computes its
+// reach mass (kept: it is the opponent mass of the other player's readout)
+// and scatters its normalised weights into a zeroed 128 x 128 A tile in
+// shared memory; the job's g table arrives as a 64 x 128 B image by bulk
+// copy; one MMA per 128 configs accumulates D = beta G (64 columns of TMEM),
+// which becomes the player's 64-column atom of the tile's pooled image.
+template <bool H>
+__global__ void __launch_bounds__(128, 4)
+    k_pool_fast(const JobDev* __restrict__ jobs, const HeadTile* __restrict__ tiles, uint32_t ntiles, int mask,
+                uint16_t* __restrict__ pool_img, float* __restrict__ mass, int* __restrict__ err) {
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ uint64_t bar_g, bar_mma;
+    __shared__ uint32_t tmem_slot;
+    __shared__ int abort_flag;
+    uint8_t* smem = align1024(smem_raw);
+    uint8_t* sBeta = smem;           // [128 rows][128 configs]: 32 KB
+    uint8_t* sG = smem + TILE_J;     // [64 features][128 configs]: 16 KB
+    const int tid = threadIdx.x, warp = tid >> 5;
+    if (tid == 0) {
+        umma::mbar_init(&bar_g, 1);
+        umma::mbar_init(&bar_mma, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        abort_flag = 0;
+    }
+    if (warp == 0) umma::tmem_alloc(&tmem_slot, 64);
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+    const uint32_t tmem = tmem_slot;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const uint32_t idesc = umma::idesc16(128, 64, umma::Op16<H>::fmt);
+    uint32_t ph_g = 0, ph_mma = 0;
+    for (uint32_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
+        const HeadTile ht = tiles[t];
+        const JobDev& J = jobs[ht.job];
+        const bool valid = (uint32_t)tid < ht.count;
+        const uint32_t r = ht.first + tid;
+        for (int q = 0; q < 2; ++q) {
+            if (!(mask & (1 << q))) continue;
+            const uint32_t ncq = J.ncfg_player[q], nchunk = (ncq + 127) / 128;
+            const float* w = nullptr;
+            const uint32_t* lc = nullptr;
+            uint32_t n = 0;
+            float scale = 0.0f, flat = 0.0f;
+            if (valid) {  // one thread per row: its reach mass and normaliser
+                w = J.reach + J.lr_ridx[2 * r + q];
+                n = J.lr_nc[2 * r + q];
+                lc = J.leaf_col + J.leaf_coff[2 * r + q];
+                float tot = 0.0f;
+#pragma unroll 4
+                for (uint32_t e = 0; e < n; ++e) tot += w[e];
+                mass[(size_t)(J.row_base + r) * 2 + q] = tot;
+                if (tot > 1e-30f) scale = 1.0f / tot;
+                else flat = 1.0f / (float)(n > 0 ? n : 1);
+            }
+            const uint8_t* gsrc = reinterpret_cast<const uint8_t*>(J.g16) +
+                                  (q == 1 ? (J.ncfg_player[0] + 127) / 128 : 0) * (size_t)ATOM;
+            for (uint32_t c = 0; c < nchunk; ++c) {
+                if (tid == 0) {
+                    umma::expect_tx(&bar_g, ATOM);
+                    umma::bulk_g2s(sG, gsrc + (size_t)c * ATOM, ATOM, &bar_g);
+                }
+#pragma unroll
+                for (int k = 0; k < 128; k += 8)
+                    *reinterpret_cast<uint4*>(sBeta + umma::sw128_offset(128, tid, k)) = make_uint4(0, 0, 0, 0);
+#pragma unroll 4
+                for (uint32_t e = 0; e < n; ++e) {
+                    const uint32_t col = lc[e] - 128 * c;
+                    if (col < 128)
+                        *reinterpret_cast<uint16_t*>(sBeta + umma::sw128_offset(128, tid, col)) =
+                            umma::Op16<H>::one(w[e] * scale + flat);
+                }
+                umma::fence_async_smem();
+                umma::fence_before_sync();
+                __syncthreads();
+                umma::fence_after_sync();
+                if (tid == 0) {
+                    if (!umma::mbar_wait(&bar_g, ph_g, WAIT_LIMIT)) abort_flag = 1;
+                    umma::fence_after_sync();
+                    const uint32_t a = umma::smem_u32(sBeta), b = umma::smem_u32(sG);
+#pragma unroll
+                    for (int k0 = 0; k0 < 128; k0 += 16)
+                        umma::mma16(tmem, umma::desc_at(a, 128, k0), umma::desc_at(b, 64, k0), idesc,
+                                    (c > 0 || k0 > 0) ? 1u : 0u);
+                    umma::commit(&bar_mma);
+                }
+                ph_g ^= 1u;
+                if (!umma::mbar_wait(&bar_mma, ph_mma, WAIT_LIMIT)) abort_flag = 1;
+                ph_mma ^= 1u;
+                umma::fence_after_sync();
+            }
+            // the row of the player's pooled atom in the tile image
+            uint8_t* img = reinterpret_cast<uint8_t*>(pool_img) + (size_t)t * (2 * ATOM) + q * ATOM + tid * 128;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                float v[32];
+                if (nchunk) umma::tmem_ld32(tmem + lane_off + 32 * h, v);
+                else
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] = 0.0f;
+#pragma unroll
+                for (int c8 = 0; c8 < 4; ++c8) {
+                    const uint32_t chunk = 4 * h + c8;
+                    *reinterpret_cast<uint4*>(img + ((chunk ^ (tid & 7)) << 4)) = umma::pack_chunk<H>(v + 8 * c8);
+                }
+            }
+            umma::fence_before_sync();
+            __syncthreads();  // TMEM and sBeta are reused by the next player or tile
+            umma::fence_after_sync();
+        }
+        if (abort_flag) break;
+    }
+    if (tid == 0 && abort_flag) atomicExch(err, 4);
+    umma::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) umma::tmem_dealloc(tmem, 64);
+}
+
 // The join output layer, the readout LayerNorm and the per-config readout for
 // traverser p (net.rs:833-853, search.rs:1587-1636):
 // y = P + out * Wout + bout, h = LN(y), v(c) = (<f(c), h> + bias) * opp_reach.
@@ -551,7 +616,8 @@ __global__ void __launch_bounds__(512, 1)
 
 // f(c) of every config as the readout's B-operand images: for each player,
 // passes of 128 configs (by index among the player's configs) x 256, K-major
-// and 128-byte swizzled; player 0's passes first.
+// and 128-byte swizzled; player 0's passes first. Likewise g(c) as the
+// pooling's B images (64 features x 128 configs).
 template <bool H>
 __global__ void k_pack_f16(const JobDev* __restrict__ jobs, const uint32_t* __restrict__ cfg_job,
                            const uint32_t* __restrict__ cfg_local, uint32_t total_cfgs) {
@@ -564,6 +630,11 @@ __global__ void k_pack_f16(const JobDev* __restrict__ jobs, const uint32_t* __re
                    ((J.cplayer[c] == 1 ? (J.ncfg_player[0] + 127) / 128 : 0) + (col >> 7)) * (size_t)(2 * TILE_J);
     for (int j = threadIdx.x; j < D; j += blockDim.x)
         *reinterpret_cast<uint16_t*>(img + umma::sw128_offset(128, i, j)) = umma::Op16<H>::one(J.cf[(size_t)c * D + j]);
+    // g(c) into the pooling B image: row = feature, K = config index
+    uint8_t* gimg = reinterpret_cast<uint8_t*>(J.g16) +
+                    ((J.cplayer[c] == 1 ? (J.ncfg_player[0] + 127) / 128 : 0) + (col >> 7)) * (size_t)ATOM;
+    for (int j = threadIdx.x; j < POOL; j += blockDim.x)
+        *reinterpret_cast<uint16_t*>(gimg + umma::sw128_offset(64, j, i)) = umma::Op16<H>::one(J.cg[(size_t)c * POOL + j]);
 }
 
 static int num_sms() {
@@ -573,13 +644,14 @@ static int num_sms() {
     return n;
 }
 
-void launch_pool_fast(const JobDev* jobs, const uint32_t* row_job, const uint32_t* row_local, uint32_t total_rows,
-                      int mask, uint16_t* pool_img, float* mass, bool half, cudaStream_t s) {
-    if (!total_rows || !mask) return;
-    uint64_t warps = (uint64_t)total_rows * (mask == 3 ? 2 : 1);
-    const unsigned grid = (unsigned)((warps * 32 + 255) / 256);
-    if (half) k_pool_fast<true><<<grid, 256, 0, s>>>(jobs, row_job, row_local, total_rows, mask, pool_img, mass);
-    else k_pool_fast<false><<<grid, 256, 0, s>>>(jobs, row_job, row_local, total_rows, mask, pool_img, mass);
+void launch_pool_fast(const JobDev* jobs, const void* tiles, uint32_t ntiles, int mask, uint16_t* pool_img, float* mass,
+                      bool half, int* err, cudaStream_t s) {
+    if (!ntiles || !mask) return;
+    const size_t smem = TILE_J + ATOM + 1024;
+    auto kern = half ? k_pool_fast<true> : k_pool_fast<false>;
+    if (!raise_smem_limit((const void*)kern, smem)) return;
+    const uint32_t grid = std::min<uint32_t>(ntiles, 4u * (uint32_t)num_sms());
+    kern<<<grid, 128, smem, s>>>(jobs, reinterpret_cast<const HeadTile*>(tiles), ntiles, mask, pool_img, mass, err);
 }
 
 bool raise_smem_limit(const void* fn, size_t smem) {

@@ -170,9 +170,9 @@ Batch::~Batch() {
 void read_profile(Batch& b, double* ms) {
     for (int c = 0; c < N_TC; ++c) ms[c] = 0.0;
     check(cudaStreamSynchronize(b.dev->stream), "profile sync");
-    for (size_t i = 0; i < b.events_used / 2; ++i) {
+    for (size_t i = 0; i + 2 < b.event_class.size(); i += 3) {
         float t = 0.0f;
-        check(cudaEventElapsedTime(&t, b.events[2 * i], b.events[2 * i + 1]), "event time");
+        check(cudaEventElapsedTime(&t, b.events[b.event_class[i + 1]], b.events[b.event_class[i + 2]]), "event time");
         ms[b.event_class[i]] += t;
     }
     float t = 0.0f;
@@ -320,7 +320,9 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
         for (size_t j = 0; j < nj; ++j) {
             const JobImage& J = *jobs[j]->img;
             // f(c) as readout operand images: 128 configs x 256 per pass, per player
-            f16_bytes[j] = 65536ull * ((J.ncfg_player[0] + 127) / 128 + (J.ncfg_player[1] + 127) / 128);
+            // g(c) as pooling operand images: 64 x 128 configs per chunk, per player
+            const size_t npass = (J.ncfg_player[0] + 127) / 128 + (J.ncfg_player[1] + 127) / 128;
+            f16_bytes[j] = (65536ull + 16384ull) * npass;
             o_f16[j] = A.take(f16_bytes[j]);
         }
         size_t R = row_job.size();
@@ -388,6 +390,9 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
         d.row_base = row_base[j];
         d.tile_base = tile_base[j];
         d.f16 = fast ? reinterpret_cast<uint16_t*>(D + o_f16[j]) : nullptr;
+        d.g16 = fast ? reinterpret_cast<uint16_t*>(D + o_f16[j] + 65536ull * ((J.ncfg_player[0] + 127) / 128 +
+                                                                             (J.ncfg_player[1] + 127) / 128))
+                     : nullptr;
         d.cur = reinterpret_cast<float*>(D + P.cur);
         d.regret = reinterpret_cast<float*>(D + P.regret);
         d.sum = reinterpret_cast<float*>(D + P.sum);
@@ -498,10 +503,14 @@ struct Sched {
     template <class F>
     void timed(int cls, F&& f) {
         if (!b.profile) { f(); return; }
+        const int e0 = (int)b.events_used;
         check(cudaEventRecord(next_event(), s), "event");
         f();
+        const int e1 = (int)b.events_used;
         check(cudaEventRecord(next_event(), s), "event");
         b.event_class.push_back(cls);
+        b.event_class.push_back(e0);
+        b.event_class.push_back(e1);
     }
     const wcdev::WorkItem* it(const Batch::Range& r) const { return I + r.off; }
 
@@ -521,12 +530,18 @@ struct Sched {
     void leaf_values_(int p, int pool_mask) {
         DeviceCtx& dv = *b.dev;
         if (dv.have_net && !dv.precise) {
-            wcdev::launch_pool_fast(J, b.d_row_job, b.d_row_local, b.total_rows, pool_mask, b.g_pool_img, b.g_mass,
-                                    dv.half, s);
-            wcdev::launch_join_fast(J, b.d_head_tiles, b.n_head_tiles, dv.fast, p, b.g_pool_img, b.g_jp, b.g_zout_img,
-                                    b.d_err, s);
-            wcdev::launch_head_fast(J, b.d_head_tiles, b.n_head_tiles, dv.fast, p, b.g_zout_img, b.g_pb, b.g_mass,
-                                    b.d_err, s);
+            timed(TC_POOL, [&] {
+                wcdev::launch_pool_fast(J, b.d_head_tiles, b.n_head_tiles, pool_mask, b.g_pool_img, b.g_mass, dv.half,
+                                        b.d_err, s);
+            });
+            timed(TC_JOIN, [&] {
+                wcdev::launch_join_fast(J, b.d_head_tiles, b.n_head_tiles, dv.fast, p, b.g_pool_img, b.g_jp,
+                                        b.g_zout_img, b.d_err, s);
+            });
+            timed(TC_HEAD, [&] {
+                wcdev::launch_head_fast(J, b.d_head_tiles, b.n_head_tiles, dv.fast, p, b.g_zout_img, b.g_pb, b.g_mass,
+                                        b.d_err, s);
+            });
         } else if (dv.have_net) {
             if (pool_mask) wcdev::launch_pool(J, b.d_row_job, b.d_row_local, b.total_rows, pool_mask, s);
             wcdev::launch_join_readout(J, b.d_row_job, b.d_row_local, b.total_rows, p, dv.W, dv.B, dv.LN, s);
@@ -572,8 +587,10 @@ void enqueue_leaf_values(Batch& b, int p) {
             if (dv.precise) {
                 wcdev::launch_trunk(S.J, b.d_row_job, b.d_row_local, b.total_rows, dv.W, dv.B, dv.LN, S.s);
             } else {
-                wcdev::launch_trunk_fast(S.J, b.d_row_job, b.d_row_local, b.total_rows, dv.fast.trunk_tiles, dv.W,
-                                         dv.B, dv.LN, b.g_pb, b.g_jp, dv.half, b.d_err, S.s);
+                S.timed(TC_TRUNK, [&] {
+                    wcdev::launch_trunk_fast(S.J, b.d_row_job, b.d_row_local, b.total_rows, dv.fast.trunk_tiles, dv.W,
+                                             dv.B, dv.LN, b.g_pb, b.g_jp, dv.half, b.d_err, S.s);
+                });
             }
             wcdev::launch_configs(S.J, b.d_cfg_job, b.d_cfg_local, b.total_cfgs, dv.W, dv.B, dv.LN, S.s);
             if (!dv.precise) wcdev::launch_pack_f16(S.J, b.d_cfg_job, b.d_cfg_local, b.total_cfgs, dv.half, S.s);
@@ -654,8 +671,10 @@ void enqueue_solve(Batch& b) {
             if (dv.precise) {
                 wcdev::launch_trunk(S.J, b.d_row_job, b.d_row_local, b.total_rows, dv.W, dv.B, dv.LN, S.s);
             } else {
-                wcdev::launch_trunk_fast(S.J, b.d_row_job, b.d_row_local, b.total_rows, dv.fast.trunk_tiles, dv.W,
-                                         dv.B, dv.LN, b.g_pb, b.g_jp, dv.half, b.d_err, S.s);
+                S.timed(TC_TRUNK, [&] {
+                    wcdev::launch_trunk_fast(S.J, b.d_row_job, b.d_row_local, b.total_rows, dv.fast.trunk_tiles, dv.W,
+                                             dv.B, dv.LN, b.g_pb, b.g_jp, dv.half, b.d_err, S.s);
+                });
             }
             wcdev::launch_configs(S.J, b.d_cfg_job, b.d_cfg_local, b.total_cfgs, dv.W, dv.B, dv.LN, S.s);
             if (!dv.precise) wcdev::launch_pack_f16(S.J, b.d_cfg_job, b.d_cfg_local, b.total_cfgs, dv.half, S.s);

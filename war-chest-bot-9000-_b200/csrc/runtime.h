@@ -90,7 +90,7 @@ struct Batch {
     // runtime's stream): class ids are the TimeClass values.
     bool profile = false;
     std::vector<cudaEvent_t> events;
-    std::vector<int> event_class;  // one entry per (start, end) pair
+    std::vector<int> event_class;  // per timed region: class, start event, end event
     size_t events_used = 0;
     cudaEvent_t marks[3] = {nullptr, nullptr, nullptr};  // solve start, Phase 2 start, solve end
     ~Batch();
@@ -102,7 +102,9 @@ const std::string& last_error();
 
 enum TimeClass {
     TC_NET_SOLVE = 0, TC_LEAF = 1, TC_ROWS = 2, TC_VGATHER = 3, TC_REACH = 4, TC_SNAP = 5, TC_PHASE2 = 6,
-    TC_INIT = 7, TC_TOTAL = 8, N_TC = 9
+    TC_INIT = 7, TC_TOTAL = 8,
+    // parts of TC_LEAF / TC_NET_SOLVE on the tensor-core path (not in the total twice)
+    TC_POOL = 9, TC_JOIN = 10, TC_HEAD = 11, TC_TRUNK = 12, N_TC = 13
 };
 // After a profiled solve has finished: summed milliseconds per class.
 void read_profile(Batch& b, double* ms /* N_TC */);

@@ -342,18 +342,19 @@ class DeviceBatch:
     def solve(self) -> None:
         _check(lib().wc_batch_solve(self._h))
 
-    TIME_CLASSES = ["net_solve", "leaf", "rows", "vgather", "reach", "snapshot", "phase2", "init", "total"]
+    TIME_CLASSES = ["net_solve", "leaf", "rows", "vgather", "reach", "snapshot", "phase2", "init", "total",
+                    "pool", "join", "head", "trunk"]
 
     def solve_profiled(self) -> dict:
         """One solve with per-class CUDA-event timings (ms) on the runtime's stream."""
-        ms = (C.c_double * 9)()
-        _check(lib().wc_batch_solve_profiled(self._h, ms, 9))
+        ms = (C.c_double * 13)()
+        _check(lib().wc_batch_solve_profiled(self._h, ms, len(ms)))
         return dict(zip(self.TIME_CLASSES, list(ms)))
 
     def leaf_values(self, p: int, profile: bool = False):
         """Run leaf evaluation alone for traverser p (initial reaches); with
         profile=True return the per-class timings in ms."""
-        ms = (C.c_double * 9)() if profile else None
+        ms = (C.c_double * 13)() if profile else None
         _check(lib().wc_batch_leaf_values(self._h, p, ms))
         return dict(zip(self.TIME_CLASSES, list(ms))) if profile else None
 
