@@ -332,6 +332,7 @@ def main():
         prof = batch.solve_profiled()
         times.append(prof["total"] / 1e3)
         profiles.append(prof)
+    launches = batch.launches()  # counted by the runtime as it launches
     clocks_rec = clocks.stop()
     barrier(world)
     step_s = max_over_ranks(world, float(np.mean(times)))
@@ -367,8 +368,7 @@ def main():
                 "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": DTYPES[args.net],
                 "data": "synthetic (seeded roots, seeded He-normal weights)", "config": workload,
-                "e2e": e2e, "gpu_launches": launches_per_step(batch_levels(jobs), args.iters, args.net,
-                                                  max(max(j.info["ncarried"], 1) for j in jobs)),
+                "e2e": e2e, "gpu_launches": launches,
                 "roofline": roofline, "cpu_baseline": base, "clocks": clocks_rec,
                 "leaf_evals_per_sec": allsum(world, stats["leaf_evals"]) / step_s,
                 "host_build_s": build_s, "device_bytes": stats["device_bytes"]}
@@ -382,20 +382,6 @@ def main():
 
 def batch_levels(jobs):
     return max(j.info["levels"] for j in jobs)
-
-
-def launches_per_step(levels, iters, net, carried=1):
-    """Kernel launches of one solve, following the runtime's schedule: per
-    leaf call pooling (when a reach changed), join, head and terminal leaves
-    on the tensor path; pooling, join+readout and terminals on the exact
-    path; per level a rows and a value-gather launch and, per moved player, a
-    reach gather."""
-    leaf = {"f16": 4, "bf16": 4, "exact": 3, "none": 2}[net]
-    setup = {"f16": 4, "bf16": 4, "exact": 3, "none": 0}[net] + 2 + 2 * (levels - 1)
-    per_iter = leaf + 2 * levels + (levels - 1)
-    snaps = 2
-    phase2 = carried * (1 + 2 * (levels - 1) + 2 * (leaf + 2 * levels + 1) - 1)
-    return setup + iters * per_iter + snaps + phase2
 
 
 def seed_range(rank, subgames):

@@ -174,6 +174,8 @@ int wc_batch_download_board_rows(wc_batch* b, size_t job, float* pb, float* jp);
 void wc_batch_stats(const wc_batch* b, double* node_updates, double* leaf_evals, uint64_t* table_bytes,
                     uint64_t* device_bytes);
 void wc_batch_free(wc_batch* b);
+/* Kernel launches of the batch's last solve or leaf evaluation. */
+uint64_t wc_batch_launches(const wc_batch* b);
 
 /* ---- diagnostics --------------------------------------------------------- */
 /* D[128, n] = A[128, k] * B[n, k]^T (bf16 bit patterns, row-major) through one

@@ -392,6 +392,8 @@ int wc_job_info_get(const wc_job* job, wc_job_info* o) {
 
 void wc_job_free(wc_job* job) { delete job; }
 
+uint64_t wc_batch_launches(const wc_batch* b) { return b ? b->b->launches : 0; }
+
 int wc_debug_umma_gemm(const uint16_t* a, const uint16_t* b, int k, int n, float* d) {
     int rc = wcdev::umma_selftest(a, b, k, n, d);
     if (rc) return fail(WC_E_CUDA, "tcgen05 self-test failed with code " + std::to_string(rc));

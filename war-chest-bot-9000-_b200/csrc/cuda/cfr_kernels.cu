@@ -44,11 +44,59 @@ __global__ void k_init_rows(const JobDev* __restrict__ jobs, const WorkItem* __r
 
 // Traverser decision rows: node value under the strategy, then (regret mode)
 // the fused regret update and regret matching with the 1e-6 floor.
+// In regret mode an item's cells (at most ROW_CELL_CAP) are staged in shared
+// memory: child values (gathered), strategy and regrets come in, and the new
+// regrets and strategy go out, by coalesced cell-parallel loops; each row's
+// arithmetic is the same sequence as below, on the staged copies.
 __global__ void k_rows(const JobDev* __restrict__ jobs, const WorkItem* __restrict__ items, int p, int mode,
                        int strat_sel, float da, float db, float predict) {
+    __shared__ float s_val[ROW_CELL_CAP], s_str[ROW_CELL_CAP], s_reg[ROW_CELL_CAP];
     const WorkItem wi = items[blockIdx.x];
-    if (threadIdx.x >= wi.count) return;
     const JobDev& J = jobs[wi.job];
+    if (mode == BACK_REGRET) {
+        const uint32_t c0 = J.row_off[wi.first], nc = J.row_off[wi.first + wi.count] - c0;
+        if (nc <= (uint32_t)ROW_CELL_CAP) {
+            float* vals = J.vals[p];
+            const float* strat = pick_strat(J, strat_sel);
+            for (uint32_t i = threadIdx.x; i < nc; i += blockDim.x) {
+                s_val[i] = vals[J.cell_vidx[c0 + i]];
+                s_str[i] = strat[c0 + i];
+                s_reg[i] = J.regret[c0 + i];
+            }
+            __syncthreads();
+            if (threadIdx.x < wi.count) {
+                const uint32_t row = wi.first + threadIdx.x;
+                const uint32_t lo = J.row_off[row] - c0, hi = J.row_off[row + 1] - c0;
+                float base = 0.0f;
+                for (uint32_t c = lo; c < hi; ++c) base += s_val[c] * s_str[c];
+                const float EPS = 1e-6f;
+                float s = 0.0f;
+                for (uint32_t c = lo; c < hi; ++c) {
+                    float delta = 0.0f;
+                    delta += s_val[c];
+                    delta -= base;
+                    float old = s_reg[c];
+                    float r = old * (old > 0.0f ? da : db) + delta;
+                    s_reg[c] = r;
+                    float v = fmaxf(r + predict * delta, EPS);
+                    s_str[c] = v;
+                    s += v;
+                }
+                if (s > 0.0f) {
+                    float inv = 1.0f / s;
+                    for (uint32_t c = lo; c < hi; ++c) s_str[c] *= inv;
+                }
+                vals[wi.out_first + threadIdx.x] = base;
+            }
+            __syncthreads();
+            for (uint32_t i = threadIdx.x; i < nc; i += blockDim.x) {
+                J.regret[c0 + i] = s_reg[i];
+                J.cur[c0 + i] = s_str[i];
+            }
+            return;
+        }
+    }
+    if (threadIdx.x >= wi.count) return;
     uint32_t row = wi.first + threadIdx.x;
     uint32_t lo = J.row_off[row], hi = J.row_off[row + 1];
     float* vals = J.vals[p];

@@ -11,6 +11,7 @@
 namespace wcdev {
 
 constexpr int WI_TASKS = 256;  // tasks per work item == threads per CTA
+constexpr int ROW_CELL_CAP = 2048;  // cells of a regret-matching work item staged in shared memory
 
 struct JobDev {
     // ---- immutable tables

@@ -241,42 +241,39 @@ __global__ void __launch_bounds__(128, 2)
                 if (k + 2 < uses) load_weight(k + 2);
                 if (L == 3 && t + gridDim.x < ntiles) load_pooled(t + gridDim.x);
             }
-            // epilogue: LayerNorm over the row (two passes over TMEM), GELU
+            // epilogue: the row's 128 values in one go (four loads, one
+            // wait), LayerNorm, GELU
             const float* cb = vec[L];  // running bias sum (unused at L = 0)
-            float s = 0.0f, sq = 0.0f;
-#pragma unroll 1
-            for (int c4 = 0; c4 < 4; ++c4) {
-                float v[32];
-                umma::tmem_ld32(tmem + lane_off + 32 * c4, v);
+            uint32_t zr[JW];
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const float x = L ? v[j] + cb[32 * c4 + j] : v[j];
-                    s += x;
-                    sq += x * x;
-                }
+            for (int c4 = 0; c4 < 4; ++c4) umma::tmem_ld32_nowait(tmem + lane_off + 32 * c4, zr + 32 * c4);
+            umma::tmem_wait_ld();
+            float s = 0.0f, sq = 0.0f;
+#pragma unroll
+            for (int c = 0; c < JW; ++c) {
+                const float x = L ? __uint_as_float(zr[c]) + cb[c] : __uint_as_float(zr[c]);
+                zr[c] = __float_as_uint(x);
+                s += x;
+                sq += x * x;
             }
             const float mean = s * (1.0f / JW);
             const float inv = rsqrtf(fmaxf(sq * (1.0f / JW) - mean * mean, 0.0f) + 1e-5f);
             const float* gam = vec[4 + L];
             const float* bet = vec[8 + L];
-#pragma unroll 1
-            for (int c4 = 0; c4 < 4; ++c4) {
-                float v[32];
-                umma::tmem_ld32(tmem + lane_off + 32 * c4, v);
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int c = 32 * c4 + j;
-                    v[j] = ((L ? v[j] + cb[c] : v[j]) - mean) * inv * gam[c] + bet[c];
-                }
+            for (int c8 = 0; c8 < JW / 8; ++c8) {
+                float v[8];
 #pragma unroll
-                for (int c8 = 0; c8 < 4; ++c8) {
-                    const uint4 o = umma::gelu_chunk<H>(v + 8 * c8);
-                    const uint32_t off = umma::sw128_offset(128, tid, 32 * c4 + 8 * c8);
-                    if (L < 3)
-                        *reinterpret_cast<uint4*>(sA + off) = o;
-                    else
-                        *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(zout_img) + (size_t)t * TILE_J + off) = o;
+                for (int j = 0; j < 8; ++j) {
+                    const int c = 8 * c8 + j;
+                    v[j] = (__uint_as_float(zr[c]) - mean) * inv * gam[c] + bet[c];
                 }
+                const uint4 o = umma::gelu_chunk<H>(v);
+                const uint32_t off = umma::sw128_offset(128, tid, 8 * c8);
+                if (L < 3)
+                    *reinterpret_cast<uint4*>(sA + off) = o;
+                else
+                    *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(zout_img) + (size_t)t * TILE_J + off) = o;
             }
             if (L < 3) {
                 umma::fence_async_smem();

@@ -91,10 +91,11 @@ size_t sw128_offset(uint32_t R, uint32_t r, uint32_t k) {
 }
 // B operand tile of a [in = K][out = N] weight (rows k0 .. k0 + K): element
 // (n, k) = W[(k0 + k) * N + n], K-major and swizzled.
-void put_tile(uint8_t* dst, const float* W, uint32_t K, uint32_t N, bool half) {
+void put_tile(uint8_t* dst, const float* W, uint32_t K, uint32_t N, bool half, uint32_t ldw = 0) {
+    if (!ldw) ldw = N;
     for (uint32_t n = 0; n < N; ++n)
         for (uint32_t k = 0; k < K; ++k) {
-            uint16_t v = to_op16(W[(size_t)k * N + n], half);
+            uint16_t v = to_op16(W[(size_t)k * ldw + n], half);
             std::memcpy(dst + sw128_offset(N, n, k), &v, 2);
         }
 }
@@ -193,6 +194,22 @@ struct Alloc {
     }
 };
 
+// Regret-matching rows: at most WI_TASKS rows and ROW_CELL_CAP cells per
+// item (a longer single row gets an item of its own), so the kernel can stage
+// an item's cells in shared memory.
+void add_row_items(std::vector<wcdev::WorkItem>& items, uint32_t job, uint32_t first, uint32_t count,
+                   uint32_t out_first, const std::vector<uint32_t>& row_off) {
+    uint32_t k = 0;
+    while (k < count) {
+        uint32_t n = 1;
+        while (n < (uint32_t)wcdev::WI_TASKS && k + n < count &&
+               row_off[first + k + n + 1] - row_off[first + k] <= (uint32_t)wcdev::ROW_CELL_CAP)
+            ++n;
+        items.push_back({job, first + k, n, out_first + k});
+        k += n;
+    }
+}
+
 void add_items(std::vector<wcdev::WorkItem>& items, uint32_t job, uint32_t first, uint32_t count,
                uint32_t out_first) {
     for (uint32_t k = 0; k < count; k += wcdev::WI_TASKS) {
@@ -265,7 +282,7 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
                     const JobImage& J = *jobs[j]->img;
                     if (lv >= J.nlevels) continue;
                     const LevelRange& r = J.rows_rng[lv * 2 + p];
-                    add_items(items, j, r.first, r.count, r.out_first);
+                    add_row_items(items, j, r.first, r.count, r.out_first, J.row_off);
                 }
             });
             b.vg[lv * 2 + p] = range_of([&] {
@@ -520,7 +537,7 @@ struct Sched {
             for (int q = 0; q < 2; ++q) {
                 if (!(mover_mask & (1 << q))) continue;
                 const Batch::Range& r = b.rg[lv * 2 + q];
-                timed(TC_REACH, [&] { wcdev::launch_rgather(J, it(r), r.n, strat_sel, which_reach, sum_update, dg, s); });
+                timed(TC_REACH, [&] { b.count_launch(r.n), wcdev::launch_rgather(J, it(r), r.n, strat_sel, which_reach, sum_update, dg, s); });
             }
     }
 
@@ -531,39 +548,39 @@ struct Sched {
         DeviceCtx& dv = *b.dev;
         if (dv.have_net && !dv.precise) {
             timed(TC_POOL, [&] {
-                wcdev::launch_pool_fast(J, b.d_head_tiles, b.n_head_tiles, pool_mask, b.g_pool_img, b.g_mass, dv.half,
+                b.count_launch((pool_mask ? b.n_head_tiles : 0)), wcdev::launch_pool_fast(J, b.d_head_tiles, b.n_head_tiles, pool_mask, b.g_pool_img, b.g_mass, dv.half,
                                         b.d_err, s);
             });
             timed(TC_JOIN, [&] {
-                wcdev::launch_join_fast(J, b.d_head_tiles, b.n_head_tiles, dv.fast, p, b.g_pool_img, b.g_jp,
+                b.count_launch(b.n_head_tiles), wcdev::launch_join_fast(J, b.d_head_tiles, b.n_head_tiles, dv.fast, p, b.g_pool_img, b.g_jp,
                                         b.g_zout_img, b.d_err, s);
             });
             timed(TC_HEAD, [&] {
-                wcdev::launch_head_fast(J, b.d_head_tiles, b.n_head_tiles, dv.fast, p, b.g_zout_img, b.g_pb, b.g_mass,
+                b.count_launch(b.n_head_tiles), wcdev::launch_head_fast(J, b.d_head_tiles, b.n_head_tiles, dv.fast, p, b.g_zout_img, b.g_pb, b.g_mass,
                                         b.d_err, s);
             });
         } else if (dv.have_net) {
-            if (pool_mask) wcdev::launch_pool(J, b.d_row_job, b.d_row_local, b.total_rows, pool_mask, s);
-            wcdev::launch_join_readout(J, b.d_row_job, b.d_row_local, b.total_rows, p, dv.W, dv.B, dv.LN, s);
+            if (pool_mask) b.count_launch((pool_mask ? b.total_rows : 0)), wcdev::launch_pool(J, b.d_row_job, b.d_row_local, b.total_rows, pool_mask, s);
+            b.count_launch(b.total_rows), wcdev::launch_join_readout(J, b.d_row_job, b.d_row_local, b.total_rows, p, dv.W, dv.B, dv.LN, s);
         } else {
-            wcdev::launch_netrows_zero(J, it(b.netrows_all), b.netrows_all.n, p, s);
+            b.count_launch(b.netrows_all.n), wcdev::launch_netrows_zero(J, it(b.netrows_all), b.netrows_all.n, p, s);
         }
-        wcdev::launch_terminal(J, it(b.term_all), b.term_all.n, p, s);
+        b.count_launch(b.term_all.n), wcdev::launch_terminal(J, it(b.term_all), b.term_all.n, p, s);
     }
 
     void backprop(int p, int mode, int strat_sel, float da, float db, float predict) {
         for (int lv = (int)b.nlevels - 1; lv >= 0; --lv) {
             const Batch::Range& rr = b.rows[lv * 2 + p];
             const Batch::Range& vr = b.vg[lv * 2 + p];
-            timed(TC_ROWS, [&] { wcdev::launch_rows(J, it(rr), rr.n, p, mode, strat_sel, da, db, predict, s); });
-            timed(TC_VGATHER, [&] { wcdev::launch_vgather(J, it(vr), vr.n, p, s); });
+            timed(TC_ROWS, [&] { b.count_launch(rr.n), wcdev::launch_rows(J, it(rr), rr.n, p, mode, strat_sel, da, db, predict, s); });
+            timed(TC_VGATHER, [&] { b.count_launch(vr.n), wcdev::launch_vgather(J, it(vr), vr.n, p, s); });
         }
     }
 
     void carries(int snap_index) {
-        wcdev::launch_seed_root(J, (uint32_t)b.jobs.size(), 1, -1, s);
+        b.count_launch(b.jobs.size()), wcdev::launch_seed_root(J, (uint32_t)b.jobs.size(), 1, -1, s);
         propagate(wcdev::STRAT_SNAP, 1, 3, 0, 1.0f);
-        wcdev::launch_carry(J, it(b.exits_all), b.exits_all.n, snap_index, s);
+        b.count_launch(b.exits_all.n), wcdev::launch_carry(J, it(b.exits_all), b.exits_all.n, snap_index, s);
     }
 };
 
@@ -571,6 +588,7 @@ struct Sched {
 
 void enqueue_leaf_values(Batch& b, int p) {
     if (b.jobs.empty()) return;
+    b.launches = 0;
     DeviceCtx& dv = *b.dev;
     check(cudaSetDevice(dv.device), "set device");
     Sched S(b);
@@ -583,22 +601,22 @@ void enqueue_leaf_values(Batch& b, int p) {
     mark(0);
     if (dv.have_net) {
         S.timed(TC_NET_SOLVE, [&] {
-            wcdev::launch_cards(S.J, nj, dv.W, dv.B, S.s);
+            b.count_launch(nj), wcdev::launch_cards(S.J, nj, dv.W, dv.B, S.s);
             if (dv.precise) {
-                wcdev::launch_trunk(S.J, b.d_row_job, b.d_row_local, b.total_rows, dv.W, dv.B, dv.LN, S.s);
+                b.count_launch(b.total_rows), wcdev::launch_trunk(S.J, b.d_row_job, b.d_row_local, b.total_rows, dv.W, dv.B, dv.LN, S.s);
             } else {
                 S.timed(TC_TRUNK, [&] {
-                    wcdev::launch_trunk_fast(S.J, b.d_row_job, b.d_row_local, b.total_rows, dv.fast.trunk_tiles, dv.W,
+                    b.count_launch(b.total_rows), wcdev::launch_trunk_fast(S.J, b.d_row_job, b.d_row_local, b.total_rows, dv.fast.trunk_tiles, dv.W,
                                              dv.B, dv.LN, b.g_pb, b.g_jp, dv.half, b.d_err, S.s);
                 });
             }
-            wcdev::launch_configs(S.J, b.d_cfg_job, b.d_cfg_local, b.total_cfgs, dv.W, dv.B, dv.LN, S.s);
-            if (!dv.precise) wcdev::launch_pack_f16(S.J, b.d_cfg_job, b.d_cfg_local, b.total_cfgs, dv.half, S.s);
+            b.count_launch(b.total_cfgs), wcdev::launch_configs(S.J, b.d_cfg_job, b.d_cfg_local, b.total_cfgs, dv.W, dv.B, dv.LN, S.s);
+            if (!dv.precise) b.count_launch(b.total_cfgs), wcdev::launch_pack_f16(S.J, b.d_cfg_job, b.d_cfg_local, b.total_cfgs, dv.half, S.s);
         });
     }
     S.timed(TC_INIT, [&] {
-        wcdev::launch_init_rows(S.J, S.it(b.rows_all), b.rows_all.n, S.s);
-        wcdev::launch_seed_root(S.J, nj, 0, -1, S.s);
+        b.count_launch(b.rows_all.n), wcdev::launch_init_rows(S.J, S.it(b.rows_all), b.rows_all.n, S.s);
+        b.count_launch(b.jobs.size()), wcdev::launch_seed_root(S.J, nj, 0, -1, S.s);
     });
     S.propagate(wcdev::STRAT_CUR, 0, 3, 1, 1.0f);
     mark(1);
@@ -650,6 +668,7 @@ void download_board_rows(Batch& b, size_t job, float* pb, float* jp) {
 
 void enqueue_solve(Batch& b) {
     if (b.jobs.empty()) return;
+    b.launches = 0;
     DeviceCtx& dv = *b.dev;
     check(cudaSetDevice(dv.device), "set device");
     Sched S(b);
@@ -667,28 +686,28 @@ void enqueue_solve(Batch& b) {
     // per-solve network pieces (search.rs:1464-1499)
     if (dv.have_net) {
         S.timed(TC_NET_SOLVE, [&] {
-            wcdev::launch_cards(S.J, nj, dv.W, dv.B, S.s);
+            b.count_launch(nj), wcdev::launch_cards(S.J, nj, dv.W, dv.B, S.s);
             if (dv.precise) {
-                wcdev::launch_trunk(S.J, b.d_row_job, b.d_row_local, b.total_rows, dv.W, dv.B, dv.LN, S.s);
+                b.count_launch(b.total_rows), wcdev::launch_trunk(S.J, b.d_row_job, b.d_row_local, b.total_rows, dv.W, dv.B, dv.LN, S.s);
             } else {
                 S.timed(TC_TRUNK, [&] {
-                    wcdev::launch_trunk_fast(S.J, b.d_row_job, b.d_row_local, b.total_rows, dv.fast.trunk_tiles, dv.W,
+                    b.count_launch(b.total_rows), wcdev::launch_trunk_fast(S.J, b.d_row_job, b.d_row_local, b.total_rows, dv.fast.trunk_tiles, dv.W,
                                              dv.B, dv.LN, b.g_pb, b.g_jp, dv.half, b.d_err, S.s);
                 });
             }
-            wcdev::launch_configs(S.J, b.d_cfg_job, b.d_cfg_local, b.total_cfgs, dv.W, dv.B, dv.LN, S.s);
-            if (!dv.precise) wcdev::launch_pack_f16(S.J, b.d_cfg_job, b.d_cfg_local, b.total_cfgs, dv.half, S.s);
+            b.count_launch(b.total_cfgs), wcdev::launch_configs(S.J, b.d_cfg_job, b.d_cfg_local, b.total_cfgs, dv.W, dv.B, dv.LN, S.s);
+            if (!dv.precise) b.count_launch(b.total_cfgs), wcdev::launch_pack_f16(S.J, b.d_cfg_job, b.d_cfg_local, b.total_cfgs, dv.half, S.s);
         });
     }
     // Solver::new: uniform strategy, reaches, reach-weighted sum seed, snapshot 0
     S.timed(TC_INIT, [&] {
-        wcdev::launch_init_rows(S.J, S.it(b.rows_all), b.rows_all.n, S.s);
-        wcdev::launch_seed_root(S.J, nj, 0, -1, S.s);
+        b.count_launch(b.rows_all.n), wcdev::launch_init_rows(S.J, S.it(b.rows_all), b.rows_all.n, S.s);
+        b.count_launch(b.jobs.size()), wcdev::launch_seed_root(S.J, nj, 0, -1, S.s);
     });
     S.propagate(wcdev::STRAT_CUR, 0, 3, 1, 1.0f);
     int snap_index = 0;
     if (cfg.snapshots || cfg.iters == 0) {
-        wcdev::launch_copy_cur_to_snap(S.J, S.it(b.rows_all), b.rows_all.n, S.s);
+        b.count_launch(b.rows_all.n), wcdev::launch_copy_cur_to_snap(S.J, S.it(b.rows_all), b.rows_all.n, S.s);
         if (cfg.snapshots && snap_list.size() > 1) S.carries(snap_index);
         ++snap_index;
     }
@@ -709,23 +728,23 @@ void enqueue_solve(Batch& b) {
                                   : done == cfg.iters;
         if (keep) {
             S.timed(TC_SNAP, [&] {
-                wcdev::launch_snapshot(S.J, S.it(b.rows_all), b.rows_all.n, touched[0], touched[1], S.s);
+                b.count_launch(b.rows_all.n), wcdev::launch_snapshot(S.J, S.it(b.rows_all), b.rows_all.n, touched[0], touched[1], S.s);
             });
             if (cfg.snapshots && done != cfg.iters) S.carries(snap_index);
             ++snap_index;
         }
         steps[p] += 1;
     }
-    S.timed(TC_SNAP, [&] { wcdev::launch_unsort(S.J, S.it(b.cells_all), b.cells_all.n, S.s); });
+    S.timed(TC_SNAP, [&] { b.count_launch(b.cells_all.n), wcdev::launch_unsort(S.J, S.it(b.cells_all), b.cells_all.n, S.s); });
     // Phase 2: one fixed-policy pass per carried root (search.rs:1851-1871)
     mark(1);
     for (uint32_t r = 0; r < b.max_carried; ++r) {
-        wcdev::launch_seed_root(S.J, nj, 0, (int)r, S.s);
+        b.count_launch(b.jobs.size()), wcdev::launch_seed_root(S.J, nj, 0, (int)r, S.s);
         S.propagate(wcdev::STRAT_SNAP, 0, 3, 0, 1.0f);
         for (int p = 0; p < 2; ++p) {
             S.leaf_values(p, p == 0 ? 3 : 0);
             S.backprop(p, wcdev::BACK_VALUE, wcdev::STRAT_SNAP, 0.0f, 0.0f, 0.0f);
-            wcdev::launch_collect_root(S.J, nj, (int)r, p, S.s);
+            b.count_launch(nj), wcdev::launch_collect_root(S.J, nj, (int)r, p, S.s);
         }
     }
     mark(2);

@@ -91,6 +91,10 @@ struct Batch {
     bool profile = false;
     std::vector<cudaEvent_t> events;
     std::vector<int> event_class;  // per timed region: class, start event, end event
+    uint64_t launches = 0;         // kernel launches of the last enqueued solve or leaf evaluation
+    void count_launch(uint64_t n) {
+        if (n) ++launches;  // the launchers launch nothing for an empty range
+    }
     size_t events_used = 0;
     cudaEvent_t marks[3] = {nullptr, nullptr, nullptr};  // solve start, Phase 2 start, solve end
     ~Batch();

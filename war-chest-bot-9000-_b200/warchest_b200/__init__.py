@@ -88,6 +88,7 @@ def _load() -> C.CDLL:
         "wc_batch_download": (I, [VP, C.c_size_t, VP, VP, VP]),
         "wc_batch_stats": (None, [VP, P(C.c_double), P(C.c_double), P(U64), P(U64)]),
         "wc_batch_free": (None, [VP]),
+        "wc_batch_launches": (U64, [VP]),
         "wc_submit": (I, [VP, VP, P(U64)]),
         "wc_wait": (I, [VP, U64, P(_Result)]),
         "wc_queued_work": (U64, [VP]),
@@ -371,6 +372,10 @@ class DeviceBatch:
         jp = np.zeros((max(n, 1), 128), np.float32)
         _check(lib().wc_batch_download_board_rows(self._h, j, pb.ctypes.data, jp.ctypes.data))
         return pb[:n], jp[:n]
+
+    def launches(self) -> int:
+        """Kernel launches of the last solve or leaf evaluation."""
+        return int(lib().wc_batch_launches(self._h))
 
     def stats(self):
         nu, le = C.c_double(), C.c_double()
