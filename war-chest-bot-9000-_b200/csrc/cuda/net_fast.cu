@@ -132,9 +132,15 @@ __global__ void __launch_bounds__(128, 2)
     uint8_t* ring[2] = {smem, smem + TILE_J};
     uint8_t* sA = smem + 2 * TILE_J;
     // [0] b with the seat folded in, [1..3] running sums of the block biases,
-    // [4..7] LayerNorm gammas, [8..11] betas
+    // [4..7] LayerNorm gammas, [8..11] betas; then per layer the (gamma, beta)
+    // column pairs packed for ln_gelu2
     float (*vec)[JW] = reinterpret_cast<float (*)[JW]>(sA + TILE_J);
+    uint32_t (*gb2)[JW] = reinterpret_cast<uint32_t (*)[JW]>(sA + TILE_J + 12 * JW * 4);
     const int tid = threadIdx.x, warp = tid >> 5;
+    for (int i = tid; i < 4 * (JW / 2); i += blockDim.x) {
+        const int L = i / (JW / 2), c = 2 * (i % (JW / 2));
+        umma::pack_gb2(fn.ln_g[L], fn.ln_b[L], c, &gb2[L][c]);
+    }
     for (int i = tid; i < 12 * JW; i += blockDim.x) {
         const int v = i / JW, c = i % JW;
         float x;
@@ -258,17 +264,19 @@ __global__ void __launch_bounds__(128, 2)
             }
             const float mean = s * (1.0f / JW);
             const float inv = rsqrtf(fmaxf(sq * (1.0f / JW) - mean * mean, 0.0f) + 1e-5f);
+            const float nm = -mean * inv;
             const float* gam = vec[4 + L];
             const float* bet = vec[8 + L];
 #pragma unroll
             for (int c8 = 0; c8 < JW / 8; ++c8) {
-                float v[8];
+                uint32_t w4[4];
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const int c = 8 * c8 + j;
-                    v[j] = (__uint_as_float(zr[c]) - mean) * inv * gam[c] + bet[c];
+                for (int j = 0; j < 4; ++j) {
+                    const int c = 8 * c8 + 2 * j;
+                    w4[j] = umma::ln_gelu2<H>(__uint_as_float(zr[c]) * inv + nm, __uint_as_float(zr[c + 1]) * inv + nm, c,
+                                              gam, bet, gb2[L]);
                 }
-                const uint4 o = umma::gelu_chunk<H>(v);
+                const uint4 o = make_uint4(w4[0], w4[1], w4[2], w4[3]);
                 const uint32_t off = umma::sw128_offset(128, tid, 8 * c8);
                 if (L < 3)
                     *reinterpret_cast<uint4*>(sA + off) = o;
@@ -666,7 +674,7 @@ bool raise_smem_limit(const void* fn, size_t smem) {
 void launch_join_fast(const JobDev* jobs, const void* tiles, uint32_t ntiles, const FastNetDev& fn, int p,
                       const uint16_t* pool_img, const uint16_t* jp, uint16_t* zout_img, int* err, cudaStream_t s) {
     if (!ntiles) return;
-    const size_t smem = 3 * TILE_J + 12 * JW * 4 + 1024;  // two weight slots, the A operand, the vectors
+    const size_t smem = 3 * TILE_J + 16 * JW * 4 + 1024;  // two weight slots, the A operand, the vectors
     auto kern = fn.half ? k_join_fast<true> : k_join_fast<false>;
     if (!raise_smem_limit((const void*)kern, smem)) return;
     uint32_t grid = std::min<uint32_t>(ntiles, 2u * (uint32_t)num_sms());

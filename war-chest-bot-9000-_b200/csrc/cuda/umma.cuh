@@ -240,28 +240,62 @@ __device__ __forceinline__ float gelu_fast(float x) {
 // GELU (tanh form) of two floats, returned as a packed pair of 16-bit
 // operands. f16: computed in f16x2 arithmetic with the hardware f16x2 tanh
 // (two elements per instruction; its error is of the order of the f16
-// rounding the result gets anyway); the tanh argument uses the input clamped
-// to +-16, where tanh(u) is +-1 to f16 precision, so x^2 cannot overflow.
+// rounding the result gets anyway), as x (1 + tanh(u)) / 2 with x^2 capped at
+// 1024 inside u (|x| >= 32: tanh has long saturated, and u stays finite).
 // bf16: the fp32 gelu_fast, then rounded.
 template <bool HALF>
 __device__ __forceinline__ uint32_t gelu_pack2(float a, float b);
 template <>
 __device__ __forceinline__ uint32_t gelu_pack2<true>(float a, float b) {
     const __half2 x = __floats2half2_rn(a, b);
-    const __half2 lim = __float2half2_rn(16.0f);
-    const __half2 xc = __hmax2(__hmin2(x, lim), __hneg2(lim));
-    const __half2 inner = __hfma2(__hmul2(xc, xc), __float2half2_rn(0.035677408f), __float2half2_rn(0.79788456f));
-    const __half2 u = __hmul2(xc, inner);
+    const __half2 x2 = __hmin2(__hmul2(x, x), __float2half2_rn(1024.0f));
+    const __half2 u = __hmul2(x, __hfma2(x2, __float2half2_rn(0.035677408f), __float2half2_rn(0.79788456f)));
     uint32_t ub = *reinterpret_cast<const uint32_t*>(&u), tb;
     asm("tanh.approx.f16x2 %0, %1;" : "=r"(tb) : "r"(ub));
     const __half2 t = *reinterpret_cast<const __half2*>(&tb);
-    const __half2 hx = __hmul2(x, __float2half2_rn(0.5f));
-    const __half2 g = __hfma2(hx, t, hx);
+    const __half2 g = __hmul2(x, __hfma2(t, __float2half2_rn(0.5f), __float2half2_rn(0.5f)));
     return *reinterpret_cast<const uint32_t*>(&g);
 }
 template <>
 __device__ __forceinline__ uint32_t gelu_pack2<false>(float a, float b) {
     return Op16<false>::pack(gelu_fast(a), gelu_fast(b));
+}
+
+// LayerNorm affine + GELU of two already-normalised values n = (x - mean) / sd
+// at columns c, c + 1, packed as two 16-bit operands. gb2 holds the
+// (gamma, beta) pairs of the columns as packed f16x2 words: [2 * (c / 2)] the
+// gammas, [2 * (c / 2) + 1] the betas. f16: affine and GELU in f16x2 (one
+// conversion, one FMA for gamma / beta, the tanh form with x^2 capped at
+// 1024, where tanh has long saturated; 7 packed ops and one tanh per pair).
+// bf16: fp32 affine and gelu_fast.
+template <bool HALF>
+__device__ __forceinline__ uint32_t ln_gelu2(float n0, float n1, int c, const float* gam, const float* bet,
+                                             const uint32_t* gb2);
+template <>
+__device__ __forceinline__ uint32_t ln_gelu2<true>(float n0, float n1, int c, const float*, const float*,
+                                                   const uint32_t* gb2) {
+    const uint2 gb = *reinterpret_cast<const uint2*>(gb2 + 2 * (c >> 1));
+    const __half2 n = __floats2half2_rn(n0, n1);
+    const __half2 x = __hfma2(n, *reinterpret_cast<const __half2*>(&gb.x), *reinterpret_cast<const __half2*>(&gb.y));
+    const __half2 x2 = __hmin2(__hmul2(x, x), __float2half2_rn(1024.0f));
+    const __half2 u = __hmul2(x, __hfma2(x2, __float2half2_rn(0.035677408f), __float2half2_rn(0.79788456f)));
+    uint32_t ub = *reinterpret_cast<const uint32_t*>(&u), tb;
+    asm("tanh.approx.f16x2 %0, %1;" : "=r"(tb) : "r"(ub));
+    const __half2 t = *reinterpret_cast<const __half2*>(&tb);
+    const __half2 g = __hmul2(x, __hfma2(t, __float2half2_rn(0.5f), __float2half2_rn(0.5f)));
+    return *reinterpret_cast<const uint32_t*>(&g);
+}
+template <>
+__device__ __forceinline__ uint32_t ln_gelu2<false>(float n0, float n1, int c, const float* gam, const float* bet,
+                                                    const uint32_t*) {
+    return Op16<false>::pack(gelu_fast(n0 * gam[c] + bet[c]), gelu_fast(n1 * gam[c + 1] + bet[c + 1]));
+}
+
+// (gamma, beta) of columns c, c + 1 as the packed words ln_gelu2 reads.
+__device__ __forceinline__ void pack_gb2(const float* gam, const float* bet, int c, uint32_t* out2) {
+    const __half2 g = __floats2half2_rn(gam[c], gam[c + 1]), b = __floats2half2_rn(bet[c], bet[c + 1]);
+    out2[0] = *reinterpret_cast<const uint32_t*>(&g);
+    out2[1] = *reinterpret_cast<const uint32_t*>(&b);
 }
 
 // GELU of 8 consecutive floats as one 16-byte chunk of 16-bit operands.
