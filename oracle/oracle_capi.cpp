@@ -332,6 +332,23 @@ int oracle_leaf_parts(void* h, int p, float* hout, float* opp_reach, uint32_t* c
     return 0;
 }
 
+// Fraction of network leaf rows whose player-q reach mass is exactly zero at
+// the solver's current reaches (the rows whose values for the other player
+// are all zero).
+double oracle_zero_mass_fraction(void* h, int q) {
+    Solver& sv = *static_cast<Handle*>(h)->sv;
+    const wc::Tree& t = *static_cast<Handle*>(h)->tree;
+    if (t.leaf_rows.empty()) return 0.0;
+    size_t zero = 0;
+    for (uint32_t i : t.leaf_rows) {
+        const float* ro = sv.reach_of(i, q);
+        float s = 0.0f;
+        for (size_t c = 0; c < t.nc(i, q); ++c) s += ro[c];
+        zero += s == 0.0f;
+    }
+    return (double)zero / (double)t.leaf_rows.size();
+}
+
 void oracle_layout(uint64_t* out3) {
     Layout L;
     out3[0] = L.w_len;

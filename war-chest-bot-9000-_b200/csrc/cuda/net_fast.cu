@@ -529,20 +529,26 @@ __global__ void __launch_bounds__(512, 1)
             out = J.vals[p] + J.lr_vidx[2 * r + p];
         }
         const uint32_t nfp = J.ncfg_player[p];
+        // this thread's 64 P values, loaded while the product runs
+        uint4 pq[8];
+        {
+            const uint4* pr = reinterpret_cast<const uint4*>(pb + (size_t)(valid ? g : 0) * D + 64 * cg);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) pq[i] = valid ? pr[i] : make_uint4(0, 0, 0, 0);
+        }
         if (!umma::mbar_wait(&mbar, phase, WAIT_LIMIT)) abort_flag = 1;
         phase ^= 1u;
         umma::fence_after_sync();
         // y = acc + P + bout on this thread's 64 columns; LayerNorm -> h -> sH
         float y[64];
         {
-            const uint4* pr = reinterpret_cast<const uint4*>(pb + (size_t)(valid ? g : 0) * D + 64 * cg);
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 float v[32];
                 umma::tmem_ld32(tmem + lane_off + 64 * cg + 32 * h, v);
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
-                    uint4 q = valid ? pr[4 * h + c] : make_uint4(0, 0, 0, 0);
+                    const uint4 q = pq[4 * h + c];
                     const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
@@ -565,6 +571,13 @@ __global__ void __launch_bounds__(512, 1)
                 for (int i = 0; i < 8; ++i) x[i] = (y[8 * c + i] - mean) * inv * gam[8 * c + i] + bet[8 * c + i];
                 umma::st_chunk<H>(sH, 128, row, 64 * cg + 8 * c, x);
             }
+        }
+        // this thread's first eight readout columns (entries cg, cg + 4, ...)
+        uint32_t lc8[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const uint32_t e = (uint32_t)cg + 4u * k;
+            lc8[k] = e < ncfg_row ? lcol[e] : 0xffffffffu;
         }
         for (uint32_t nb = 0; nb < nfp; nb += 128) {
             if (nb > 0 && tid == 0) load_f(J, nb / 128);
@@ -598,7 +611,13 @@ __global__ void __launch_bounds__(512, 1)
             {
                 // thread (row, cg) writes every fourth of the row's values
                 const float* st = stage + row * 128;
-                for (uint32_t c = cg; c < ncfg_row; c += 4) {
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const uint32_t col = lc8[k] - nb;
+                    if (col < 128)
+                        out[cg + 4 * k] = (st[(col & ~31u) | ((col & 31u) ^ (uint32_t)lane)] + fn.vbias) * opp_mass;
+                }
+                for (uint32_t c = cg + 32; c < ncfg_row; c += 4) {
                     const uint32_t col = lcol[c] - nb;
                     if (col < 128) out[c] = (st[(col & ~31u) | ((col & 31u) ^ (uint32_t)lane)] + fn.vbias) * opp_mass;
                 }

@@ -12,6 +12,7 @@
 // weights land while this block computes). The per-board pooling GEMM,
 // the stem and the board readout are small and run on the CUDA cores.
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -60,25 +61,32 @@ __device__ __forceinline__ void put_x32(uint8_t* tile, uint32_t R, uint32_t r, u
 // registers so every weight load feeds NB FMAs, and the loads unrolled so
 // several are in flight (the weights come from L2). With KS > 1 the K slices
 // meet in `part` (KS * NB * N floats). `in` has row stride ldi, `out` ldo.
-template <int NB, int K, int N, int KS>
+// With RS > 1 (and KS == 1) the rows are split into RS groups as well, so
+// N * RS threads share the work.
+template <int NB, int K, int N, int KS, int RS = 1>
 __device__ __forceinline__ void rows_gemm(const float* in, int ldi, const float* __restrict__ W,
                                           const float* __restrict__ bias, float* out, int ldo, float* part) {
+    static_assert(RS == 1 || KS == 1, "split rows or K, not both");
     constexpr int KC = (K + KS - 1) / KS;
-    for (int it = threadIdx.x; it < N * KS; it += blockDim.x) {
-        const int n = it % N, ks = it / N;
+    constexpr int NR = (NB + RS - 1) / RS;
+    for (int it = threadIdx.x; it < N * KS * RS; it += blockDim.x) {
+        const int n = it % N, ks = (it / N) % KS, rs = it / (N * KS);
         const int k0 = ks * KC, k1 = k0 + KC < K ? k0 + KC : K;
-        float acc[NB];
+        const int r0 = rs * NR;
+        float acc[NR];
 #pragma unroll
-        for (int i = 0; i < NB; ++i) acc[i] = 0.0f;
+        for (int i = 0; i < NR; ++i) acc[i] = 0.0f;
 #pragma unroll 8
         for (int k = k0; k < k1; ++k) {
             const float w = __ldg(W + (size_t)k * N + n);
 #pragma unroll
-            for (int i = 0; i < NB; ++i) acc[i] += in[i * ldi + k] * w;
+            for (int i = 0; i < NR; ++i)
+                if (r0 + i < NB) acc[i] += in[(r0 + i) * ldi + k] * w;
         }
         if (KS == 1) {
 #pragma unroll
-            for (int i = 0; i < NB; ++i) out[i * ldo + n] = acc[i] + (bias ? bias[n] : 0.0f);
+            for (int i = 0; i < NR; ++i)
+                if (r0 + i < NB) out[(r0 + i) * ldo + n] = acc[i] + (bias ? bias[n] : 0.0f);
         } else {
 #pragma unroll
             for (int i = 0; i < NB; ++i) part[(ks * NB + i) * N + n] = acc[i];
@@ -258,8 +266,8 @@ __global__ void __launch_bounds__(384, 1)
         }
         __syncthreads();
         // proj[i][t] = tokens[i][t] * W_tok: 30 token rows; glob = loose * W_glob
-        rows_gemm<BOARDS * NTYPE, TYPE, C, 1>(&St.tokens[0][0], TYPE, W + L.tok_stem.w, nullptr, &St.proj[0][0], C,
-                                              nullptr);
+        rows_gemm<BOARDS * NTYPE, TYPE, C, 1, 4>(&St.tokens[0][0], TYPE, W + L.tok_stem.w, nullptr, &St.proj[0][0], C,
+                                                 nullptr);
         rows_gemm<BOARDS, LOOSE, C, 1>(&St.loose[0][0], LOOSE, W + L.glob_stem.w, nullptr, &St.glob[0][0], C, nullptr);
         __syncthreads();
         for (int q = tid; q < BOARDS * C; q += blockDim.x) {
@@ -317,37 +325,87 @@ __global__ void __launch_bounds__(384, 1)
                 float nsum[32];
 #pragma unroll
                 for (int j = 0; j < 32; ++j) nsum[j] = 0.0f;
-                if (real_row) {
-                    for (int d = 0; d < 6; ++d) {
-                        uint8_t nbh = c_nbt[hex][d];
-                        if (nbh == 255) continue;
-                        const int nr = board * NH + nbh;
+                if (H) {
+                    // f16: packed adds (the sum is stored as f16 anyway)
+                    __half2 acc[16];
 #pragma unroll
-                        for (int c = 0; c < 4; ++c) {
-                            float v[8];
-                            ld_chunk<H>(sA1, 128, nr, col0 + 8 * c, v);
+                    for (int j = 0; j < 16; ++j) acc[j] = __float2half2_rn(0.0f);
+                    if (real_row) {
+                        for (int d = 0; d < 6; ++d) {
+                            uint8_t nbh = c_nbt[hex][d];
+                            if (nbh == 255) continue;
+                            const int nr = board * NH + nbh;
 #pragma unroll
-                            for (int j = 0; j < 8; ++j) nsum[8 * c + j] += v[j];
+                            for (int c = 0; c < 4; ++c) {
+                                const uint4 q = *reinterpret_cast<const uint4*>(sA1 + umma::sw128_offset(128, nr, col0 + 8 * c));
+                                const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                                for (int e = 0; e < 4; ++e)
+                                    acc[4 * c + e] = __hadd2(acc[4 * c + e], *reinterpret_cast<const __half2*>(&w4[e]));
+                            }
                         }
                     }
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        uint4 o;
+                        o.x = *reinterpret_cast<const uint32_t*>(&acc[4 * c]);
+                        o.y = *reinterpret_cast<const uint32_t*>(&acc[4 * c + 1]);
+                        o.z = *reinterpret_cast<const uint32_t*>(&acc[4 * c + 2]);
+                        o.w = *reinterpret_cast<const uint32_t*>(&acc[4 * c + 3]);
+                        *reinterpret_cast<uint4*>(sA1 + umma::sw128_offset(128, row, C + col0 + 8 * c)) = o;
+                    }
+                } else {
+                    if (real_row) {
+                        for (int d = 0; d < 6; ++d) {
+                            uint8_t nbh = c_nbt[hex][d];
+                            if (nbh == 255) continue;
+                            const int nr = board * NH + nbh;
+#pragma unroll
+                            for (int c = 0; c < 4; ++c) {
+                                float v[8];
+                                ld_chunk<H>(sA1, 128, nr, col0 + 8 * c, v);
+#pragma unroll
+                                for (int j = 0; j < 8; ++j) nsum[8 * c + j] += v[j];
+                            }
+                        }
+                    }
+                    put_x32<H>(sA1, 128, row, C + col0, nsum);
                 }
-                put_x32<H>(sA1, 128, row, C + col0, nsum);
             }
-            if (tid < BOARDS * (C / 8)) {  // (board, 8-column chunk): mean | max over the hexes
-                const int i = tid / (C / 8), c0 = (tid % (C / 8)) * 8;
-                float sum[8], mx[8];
+            // mean | max over each board's hexes: (board, 8-column chunk, hex group)
+            // partials in the free A2 space, then one thread per (board, column)
+            {
+                constexpr int HG = 10;  // hex groups: hexes h = g, g + HG, ...
+                float* psum = reinterpret_cast<float*>(sA2);                 // [BOARDS][C][HG]
+                float* pmax = psum + BOARDS * C * HG;
+                if (tid < BOARDS * (C / 8) * HG) {
+                    const int gidx = tid % HG, c0 = ((tid / HG) % (C / 8)) * 8, i = tid / (HG * (C / 8));
+                    float sum[8], mx[8];
 #pragma unroll
-                for (int j = 0; j < 8; ++j) { sum[j] = 0.0f; mx[j] = -INFINITY; }
-                for (int h = 0; h < NH; ++h) {
-                    float v[8];
-                    ld_chunk<H>(sA1, 128, i * NH + h, c0, v);
+                    for (int j = 0; j < 8; ++j) { sum[j] = 0.0f; mx[j] = -INFINITY; }
+                    for (int h = gidx; h < NH; h += HG) {
+                        float v[8];
+                        ld_chunk<H>(sA1, 128, i * NH + h, c0, v);
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) { sum[j] += v[j]; mx[j] = fmaxf(mx[j], v[j]); }
+                        for (int j = 0; j < 8; ++j) { sum[j] += v[j]; mx[j] = fmaxf(mx[j], v[j]); }
+                    }
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        psum[(i * C + c0 + j) * HG + gidx] = sum[j];
+                        pmax[(i * C + c0 + j) * HG + gidx] = mx[j];
+                    }
                 }
+                __syncthreads();
+                if (tid < BOARDS * C) {
+                    const int i = tid / C, c = tid % C;
+                    float sm = 0.0f, m = -INFINITY;
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    S.pooled[i][c0 + j] = sum[j] * (1.0f / NH);
-                    S.pooled[i][C + c0 + j] = mx[j];
+                    for (int gg = 0; gg < HG; ++gg) {
+                        sm += psum[(i * C + c) * HG + gg];
+                        m = fmaxf(m, pmax[(i * C + c) * HG + gg]);
+                    }
+                    S.pooled[i][c] = sm * (1.0f / NH);
+                    S.pooled[i][C + c] = m;
                 }
             }
             __syncthreads();
