@@ -65,7 +65,9 @@ def dist_setup(args):
         import torch.distributed as dist
 
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+        # short: ranks that wait on a missing peer end with an error; the longest
+        # legitimate gap between collectives is the warm-up solves (~2 min)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
     return world, rank, local
 
@@ -337,6 +339,7 @@ def main():
     barrier(world)
     step_s = max_over_ranks(world, float(np.mean(times)))
     total_nu = allsum(world, stats["node_updates"])
+    total_leaf = allsum(world, stats["leaf_evals"])  # every collective runs on every rank, in the same order
     value = total_nu / step_s
 
     # end to end through the public API: pinned host blobs in, results out
@@ -370,13 +373,14 @@ def main():
                 "data": "synthetic (seeded roots, seeded He-normal weights)", "config": workload,
                 "e2e": e2e, "gpu_launches": launches,
                 "roofline": roofline, "cpu_baseline": base, "clocks": clocks_rec,
-                "leaf_evals_per_sec": allsum(world, stats["leaf_evals"]) / step_s,
+                "leaf_evals_per_sec": total_leaf / step_s,
                 "host_build_s": build_s, "device_bytes": stats["device_bytes"]}
         print(json.dumps(line), flush=True)
     client.close()
     if world > 1:
         import torch.distributed as dist
 
+        barrier(world)  # the other ranks wait here while rank 0 timed the CPU baseline
         dist.destroy_process_group()
 
 
