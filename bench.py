@@ -362,7 +362,10 @@ def main():
     per_class, src = rooflines(prof, algorithmic_work(jobs))
     dom = max(per_class, key=lambda k: per_class[k]["ms"])
     roofline = dict(per_class[dom])
-    roofline.update({"kernel": KERNELS.get(dom, dom), "traffic": TRAFFIC.get(dom), "peak_source": src,
+    net_rows = sum(j.info["net_rows"] for j in jobs)
+    traffic = TRAFFIC_PER_ROW[dom] * net_rows if dom in TRAFFIC_PER_ROW else None
+    roofline.update({"kernel": KERNELS.get(dom, dom), "traffic": traffic, "peak_source": src,
+                     "traffic_basis": "ncu DRAM bytes per network row (64-subgame capture) x this workload's rows",
                      "per_class": per_class, "per_class_ms": prof})
 
     if rank == 0:
@@ -444,10 +447,12 @@ def allsum(world, x):
 PLIES = 20
 KERNELS = {"rows": "k_rows", "vgather": "k_vgather", "reach": "k_rgather", "pool": "k_pool_fast",
            "join": "k_join_fast", "head": "k_head_fast", "trunk": "k_trunk_fast"}
-# DRAM bytes per launch from ncu (dram__bytes_read.sum + dram__bytes_write.sum)
-# of the kernel on a smaller case, scaled to the full launch by network rows;
-# None until a capture exists for the current build.
-TRAFFIC = {}
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per network row
+# per launch, from one ncu capture of the kernel on 64 subgames (372,818
+# rows, seeds 0..63, depth 3); a launch's traffic grows with
+# its rows, so the full launch's traffic is this times the workload's rows.
+# The pooling figure is of a launch that pooled both players.
+TRAFFIC_PER_ROW = {"head": 1029.6, "join": 683.4, "pool": 353.3, "trunk": 886.7}
 DTYPES = {"f16": "f32 CFR state, f16 tensor-core value net (fp32 accumulate)",
           "bf16": "f32 CFR state, bf16 tensor-core value net (fp32 accumulate)",
           "exact": "f32", "none": "f32"}
