@@ -64,6 +64,7 @@ struct JobDev {
     float* vals[2];    // per-traverser value arenas
     // ---- network state (per solve)
     float* cards;      // [2][NTYPE][TYPE]
+    float* tokproj;    // fast path: [NTYPE][C] = (cards + seat) W_tok, the per-job part of the token projection
     float* pb;         // [rows][D]
     float* jp;         // [rows][JW]
     float* cf;         // [ncfg][D]
@@ -93,6 +94,7 @@ struct FastNetDev {
     const float* ln_g[5];       // LN_JOIN + 0..2, LN_JOUT, LN_H
     const float* ln_b[5];
     float vbias;
+    const float* pile_tok;      // [4][96] = W_pile W_tok: pile counts straight to the token projection
     int half;                   // operand type of every tile and stored row: 1 = f16, 0 = bf16
 };
 

@@ -353,13 +353,30 @@ __global__ void __launch_bounds__(128, 4)
             const uint32_t* lc = nullptr;
             uint32_t n = 0;
             float scale = 0.0f, flat = 0.0f;
+            // the row's first EC entries, all loads issued at once (a typical
+            // row has ~20), kept in registers for the scatter
+            constexpr int EC = 24;
+            float wr[EC];
+            uint32_t cr[EC];
+#pragma unroll
+            for (int k = 0; k < EC; ++k) {
+                wr[k] = 0.0f;
+                cr[k] = 0xffffffffu;
+            }
             if (valid) {  // one thread per row: its reach mass and normaliser
                 w = J.reach + J.lr_ridx[2 * r + q];
                 n = J.lr_nc[2 * r + q];
                 lc = J.leaf_col + J.leaf_coff[2 * r + q];
+#pragma unroll
+                for (int k = 0; k < EC; ++k)
+                    if ((uint32_t)k < n) {
+                        wr[k] = w[k];
+                        cr[k] = lc[k];
+                    }
                 float tot = 0.0f;
-#pragma unroll 4
-                for (uint32_t e = 0; e < n; ++e) tot += w[e];
+#pragma unroll
+                for (int k = 0; k < EC; ++k) tot += wr[k];
+                for (uint32_t e = EC; e < n; ++e) tot += w[e];
                 mass[(size_t)(J.row_base + r) * 2 + q] = tot;
                 if (tot > 1e-30f) scale = 1.0f / tot;
                 else flat = 1.0f / (float)(n > 0 ? n : 1);
@@ -374,8 +391,14 @@ __global__ void __launch_bounds__(128, 4)
 #pragma unroll
                 for (int k = 0; k < 128; k += 8)
                     *reinterpret_cast<uint4*>(sBeta + umma::sw128_offset(128, tid, k)) = make_uint4(0, 0, 0, 0);
-#pragma unroll 4
-                for (uint32_t e = 0; e < n; ++e) {
+#pragma unroll
+                for (int k = 0; k < EC; ++k) {
+                    const uint32_t col = cr[k] - 128 * c;
+                    if (col < 128)
+                        *reinterpret_cast<uint16_t*>(sBeta + umma::sw128_offset(128, tid, col)) =
+                            umma::Op16<H>::one(wr[k] * scale + flat);
+                }
+                for (uint32_t e = EC; e < n; ++e) {
                     const uint32_t col = lc[e] - 128 * c;
                     if (col < 128)
                         *reinterpret_cast<uint16_t*>(sBeta + umma::sw128_offset(128, tid, col)) =

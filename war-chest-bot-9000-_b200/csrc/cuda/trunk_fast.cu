@@ -136,7 +136,6 @@ struct StemSmem {
     float loose[BOARDS][LOOSE];
     float facts[ROWS][HEX_FACTS];
     int occ[ROWS];
-    float tokens[BOARDS][NTYPE * TYPE];
     float proj[BOARDS][NTYPE * C];
     float glob[BOARDS][C];
     float tpool[BOARDS][C];
@@ -156,7 +155,8 @@ __global__ void __launch_bounds__(384, 1)
     k_trunk_fast(const JobDev* __restrict__ jobs, const uint32_t* __restrict__ row_job,
                  const uint32_t* __restrict__ row_local, uint32_t total_rows, const uint8_t* __restrict__ tiles,
                  const float* __restrict__ W, const float* __restrict__ B, const float* __restrict__ LN,
-                 uint16_t* __restrict__ g_pb, uint16_t* __restrict__ g_jp, int* __restrict__ err) {
+                 const float* __restrict__ pile_tok, uint16_t* __restrict__ g_pb, uint16_t* __restrict__ g_jp,
+                 int* __restrict__ err) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (umma::smem_u32(smem_raw) & 1023u)) & 1023u);
     uint8_t* sW[2] = {smem, smem + BLOCK_BYTES};
@@ -253,21 +253,19 @@ __global__ void __launch_bounds__(384, 1)
             }
         }
         __syncthreads();
-        const float* seat = W + L.seat;
-        for (int q = tid; q < BOARDS * NTYPE * TYPE; q += blockDim.x) {
-            int i = q / (NTYPE * TYPE), t = (q / TYPE) % NTYPE, j = q % TYPE;
+        // proj[i][t] = tokens[i][t] W_tok with tokens = piles W_pile + cards + seat,
+        // by linearity piles (W_pile W_tok) + the job's (cards + seat) W_tok
+        for (int q = tid; q < BOARDS * NTYPE * C; q += blockDim.x) {
+            const int i = q / (NTYPE * C), t = (q / C) % NTYPE, c = q % C;
             float acc = 0.0f;
             if (i < nb) {
                 const JobDev& J = jobs[row_job[gb_[i]]];
-                for (int k = 0; k < PILE; ++k) acc += St.piles[i][t * PILE + k] * W[L.pile.w + k * TYPE + j];
-                acc += J.cards[t * TYPE + j] + seat[(t / NSLOT) * TYPE + j];
+                acc = J.tokproj[t * C + c];
+#pragma unroll
+                for (int k = 0; k < PILE; ++k) acc += St.piles[i][t * PILE + k] * pile_tok[k * C + c];
             }
-            St.tokens[i][t * TYPE + j] = acc;
+            St.proj[i][t * C + c] = acc;
         }
-        __syncthreads();
-        // proj[i][t] = tokens[i][t] * W_tok: 30 token rows; glob = loose * W_glob
-        rows_gemm<BOARDS * NTYPE, TYPE, C, 1, 4>(&St.tokens[0][0], TYPE, W + L.tok_stem.w, nullptr, &St.proj[0][0], C,
-                                                 nullptr);
         rows_gemm<BOARDS, LOOSE, C, 1>(&St.loose[0][0], LOOSE, W + L.glob_stem.w, nullptr, &St.glob[0][0], C, nullptr);
         __syncthreads();
         for (int q = tid; q < BOARDS * C; q += blockDim.x) {
@@ -603,9 +601,27 @@ void trunk_set_constants(const NetLayout& L, const uint8_t* neighbors, const uin
 
 size_t trunk_tiles_bytes() { return (size_t)wc::NET_BLOCKS * BLOCK_BYTES; }
 
+// The per-job part of the stem's token projection: (cards + seat) W_tok per
+// card type (the trunk adds the pile counts times W_pile W_tok).
+__global__ void k_tokproj(const JobDev* __restrict__ jobs, const float* __restrict__ W) {
+    const JobDev& J = jobs[blockIdx.x];
+    const NetLayout& L = c_Lt;
+    for (int i = threadIdx.x; i < NTYPE * C; i += blockDim.x) {
+        const int t = i / C, c = i % C;
+        float acc = 0.0f;
+        for (int j = 0; j < TYPE; ++j)
+            acc += (J.cards[t * TYPE + j] + W[L.seat + (t / NSLOT) * TYPE + j]) * W[L.tok_stem.w + j * C + c];
+        J.tokproj[i] = acc;
+    }
+}
+
+void launch_tokproj(const JobDev* jobs, uint32_t njobs, const float* W, cudaStream_t s) {
+    if (njobs) k_tokproj<<<njobs, 256, 0, s>>>(jobs, W);
+}
+
 void launch_trunk_fast(const JobDev* jobs, const uint32_t* row_job, const uint32_t* row_local, uint32_t total_rows,
-                       const uint8_t* tiles, const float* W, const float* B, const float* LN, uint16_t* g_pb,
-                       uint16_t* g_jp, bool half, int* err, cudaStream_t s) {
+                       const uint8_t* tiles, const float* W, const float* B, const float* LN, const float* pile_tok,
+                       uint16_t* g_pb, uint16_t* g_jp, bool half, int* err, cudaStream_t s) {
     if (!total_rows) return;
     const size_t smem = 2 * BLOCK_BYTES + A1_BYTES + A2_BYTES + sizeof(TrunkSmem) + 1024;
     auto kern = half ? k_trunk_fast<true> : k_trunk_fast<false>;
@@ -615,7 +631,7 @@ void launch_trunk_fast(const JobDev* jobs, const uint32_t* row_job, const uint32
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     uint32_t ntiles = (total_rows + BOARDS - 1) / BOARDS;
     uint32_t grid = std::min<uint32_t>(ntiles, (uint32_t)sms);
-    kern<<<grid, 384, smem, s>>>(jobs, row_job, row_local, total_rows, tiles, W, B, LN, g_pb, g_jp, err);
+    kern<<<grid, 384, smem, s>>>(jobs, row_job, row_local, total_rows, tiles, W, B, LN, pile_tok, g_pb, g_jp, err);
 }
 
 }  // namespace wcdev

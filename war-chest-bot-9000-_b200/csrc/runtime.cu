@@ -123,6 +123,17 @@ void build_fast_pack(DeviceCtx& d, const float* W, const float* B, const float* 
     size_t o_bj[3];
     for (int i = 0; i < 3; ++i) o_bj[i] = push(B + L.join_w[i].b, NET_JW);
     size_t o_bout = push(B + L.join_out.b, NET_D);
+    // the stem's token projection is linear in the pile counts:
+    // (piles W_pile + cards + seat) W_tok = piles (W_pile W_tok) + (cards + seat) W_tok
+    std::vector<float> pile_tok(4 * NET_C);
+    for (int k = 0; k < 4; ++k)
+        for (int c = 0; c < NET_C; ++c) {
+            double acc = 0.0;
+            for (int j = 0; j < NET_TYPE; ++j)
+                acc += (double)W[L.pile.w + k * NET_TYPE + j] * (double)W[L.tok_stem.w + j * NET_C + c];
+            pile_tok[k * NET_C + c] = (float)acc;
+        }
+    size_t o_ptok = push(pile_tok.data(), pile_tok.size());
     size_t o_g[5], o_b[5];
     for (int i = 0; i < 5; ++i) {
         int norm = NetLayout::LN_JOIN + i;
@@ -156,6 +167,7 @@ void build_fast_pack(DeviceCtx& d, const float* W, const float* B, const float* 
         d.fast.ln_b[i] = F + o_b[i];
     }
     d.fast.vbias = B[L.value_bias];
+    d.fast.pile_tok = F + o_ptok;
     d.fast.half = h ? 1 : 0;
 }
 
@@ -230,7 +242,7 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
     // ---- device memory plan: per job, table blob then state then outputs
     Alloc A;
     struct Plan {
-        size_t tables, cur, regret, sum, snap, reach, reach2, vals0, vals1, cards, cardm, pb, jp, cf, cg, pooled,
+        size_t tables, cur, regret, sum, snap, reach, reach2, vals0, vals1, cards, cardm, tokproj, pb, jp, cf, cg, pooled,
             out_strategy, out_roots, out_carry;
     };
     std::vector<Plan> plan(nj);
@@ -250,6 +262,7 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
         bool net = dev.have_net, exact = net && dev.precise;
         P.cards = net ? A.take(4ull * 2 * 10 * NET_TYPE) : 0;
         P.cardm = net ? A.take(4ull * 2 * 10 * 3 * NET_POOL) : 0;
+        P.tokproj = (net && !exact) ? A.take(4ull * 10 * NET_C) : 0;
         P.pb = exact ? A.take(4ull * J.nrows_net * NET_D) : 0;
         P.jp = exact ? A.take(4ull * J.nrows_net * NET_JW) : 0;
         P.cf = net ? A.take(4ull * J.ncfg * NET_D) : 0;
@@ -421,6 +434,7 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
         if (dev.have_net) {
             d.cards = reinterpret_cast<float*>(D + P.cards);
             d.cardm = reinterpret_cast<float*>(D + P.cardm);
+            d.tokproj = dev.precise ? nullptr : reinterpret_cast<float*>(D + P.tokproj);
             d.pb = dev.precise ? reinterpret_cast<float*>(D + P.pb) : nullptr;
             d.jp = dev.precise ? reinterpret_cast<float*>(D + P.jp) : nullptr;
             d.cf = reinterpret_cast<float*>(D + P.cf);
@@ -606,8 +620,9 @@ void enqueue_leaf_values(Batch& b, int p) {
                 b.count_launch(b.total_rows), wcdev::launch_trunk(S.J, b.d_row_job, b.d_row_local, b.total_rows, dv.W, dv.B, dv.LN, S.s);
             } else {
                 S.timed(TC_TRUNK, [&] {
+                    b.count_launch(nj), wcdev::launch_tokproj(S.J, nj, dv.W, S.s);
                     b.count_launch(b.total_rows), wcdev::launch_trunk_fast(S.J, b.d_row_job, b.d_row_local, b.total_rows, dv.fast.trunk_tiles, dv.W,
-                                             dv.B, dv.LN, b.g_pb, b.g_jp, dv.half, b.d_err, S.s);
+                                             dv.B, dv.LN, dv.fast.pile_tok, b.g_pb, b.g_jp, dv.half, b.d_err, S.s);
                 });
             }
             b.count_launch(b.total_cfgs), wcdev::launch_configs(S.J, b.d_cfg_job, b.d_cfg_local, b.total_cfgs, dv.W, dv.B, dv.LN, S.s);
@@ -691,8 +706,9 @@ void enqueue_solve(Batch& b) {
                 b.count_launch(b.total_rows), wcdev::launch_trunk(S.J, b.d_row_job, b.d_row_local, b.total_rows, dv.W, dv.B, dv.LN, S.s);
             } else {
                 S.timed(TC_TRUNK, [&] {
+                    b.count_launch(nj), wcdev::launch_tokproj(S.J, nj, dv.W, S.s);
                     b.count_launch(b.total_rows), wcdev::launch_trunk_fast(S.J, b.d_row_job, b.d_row_local, b.total_rows, dv.fast.trunk_tiles, dv.W,
-                                             dv.B, dv.LN, b.g_pb, b.g_jp, dv.half, b.d_err, S.s);
+                                             dv.B, dv.LN, dv.fast.pile_tok, b.g_pb, b.g_jp, dv.half, b.d_err, S.s);
                 });
             }
             b.count_launch(b.total_cfgs), wcdev::launch_configs(S.J, b.d_cfg_job, b.d_cfg_local, b.total_cfgs, dv.W, dv.B, dv.LN, S.s);
