@@ -166,8 +166,9 @@ int wc_batch_leaf_values(wc_batch* b, int p, double* class_ms);
 int wc_batch_download_leaf_values(wc_batch* b, size_t job, int p, float* out);
 /* After a solve or wc_batch_leaf_values: one job's board vectors P
  * (net_rows x 256) and join projections jp (net_rows x 128) as the network
- * path stores them; the bf16 path stores each row minus its mean (every
- * consumer is a LayerNorm input, which ignores a per-row constant). */
+ * path stores them; the 16-bit paths store P plus the join output bias, and
+ * each row of both minus its mean (every consumer is a LayerNorm input, which
+ * ignores a per-row constant). */
 int wc_batch_download_board_rows(wc_batch* b, size_t job, float* pb, float* jp);
 /* Totals of the batch: node-updates per solve, network-row evaluations per
  * solve, table bytes, device bytes. */

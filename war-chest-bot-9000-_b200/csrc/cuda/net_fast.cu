@@ -103,6 +103,15 @@ __device__ __forceinline__ void row_stats4(const float* v, int n, float (*part)[
     *mean = m;
 }
 
+// A read-only 16-byte load the compiler keeps where it is written (a
+// loop-invariant load hoisted out of a loop would hold its registers
+// throughout).
+__device__ __forceinline__ float4 ldg4_inplace(const float4* p) {
+    float4 v;
+    asm volatile("ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+    return v;
+}
+
 // One tile = up to 128 network rows of one job: first local row, count.
 struct HeadTile {
     uint32_t job, first, count, pad;
@@ -453,212 +462,381 @@ __global__ void __launch_bounds__(128, 4)
 // The join output layer, the readout LayerNorm and the per-config readout for
 // traverser p (net.rs:833-853, search.rs:1587-1636):
 // y = P + out * Wout + bout, h = LN(y), v(c) = (<f(c), h> + bias) * opp_reach.
-// The readout is a second tensor-core product, H[128, 256] * F_p^T, against
-// the job's player-p f table (128 configs per pass). 16 warps: warp w owns
-// rows 32 (w % 4) .. and the column group w / 4 (64 of y's 256 columns, 32 of
-// each 128-config readout pass).
+// Two tensor-core products per 128-row tile: Y = out * Wout (A = the join
+// output image in shared memory) and the readout V = H * F_p^T against the
+// job's player-p f table (128 configs per pass), with H = LN(y) written by
+// the epilogue into tensor memory as that product's A operand. The P rows
+// (which already include bout) arrive per tile by bulk copy, stored by the
+// trunk as 64 KB tile images: row r at r * 512 bytes, its 16-byte chunk k at
+// chunk k ^ (r & 7), so the epilogue's row-per-lane reads are conflict-free.
+//
+// Warp roles. Warps 0..15 run the epilogue: warp w owns rows 32 (w % 4) ..
+// and the column group w / 4 (64 of y's 256 columns, 32 of each pass's
+// configs). Warp 16 issues every bulk copy and product (issuing a product
+// holds the issuing thread for most of its duration, so no epilogue warp
+// waits on it). Handoffs: the products and copies arrive on mbarriers the
+// epilogue waits for; the epilogue warps arrive on `h_ready` (H written, Y
+// and P read) and `s_done` (a pass's staging read and scattered). While the
+// epilogue scatters tile t, the next tile's Y product runs and its P image
+// lands; its join-output image landed during tile t's epilogue; the row
+// tables of the tile after next are prefetched into L2.
+// TMEM: Y in columns 0..255, V in 256..383, H in 384..511; during the
+// epilogue, V's first columns carry the LayerNorm partials.
 template <bool H>
-__global__ void __launch_bounds__(512, 1)
+__global__ void __launch_bounds__(544, 1)
     k_head_fast(const JobDev* __restrict__ jobs, const HeadTile* __restrict__ tiles, uint32_t ntiles, FastNetDev fn,
-                int p, const uint16_t* __restrict__ zout, const uint16_t* __restrict__ pb, const float* __restrict__ mass,
-                int* __restrict__ err) {
+                int p, const uint16_t* __restrict__ zout, const uint16_t* __restrict__ pimg,
+                const float* __restrict__ mass, int* __restrict__ err) {
+    constexpr uint32_t TY = 0, TV = 256, TH = 384;
+    constexpr uint32_t NWORK = 512;  // epilogue threads
     extern __shared__ uint8_t smem_raw[];
-    __shared__ uint64_t mbar, bar_a, bar_f;
+    __shared__ uint64_t bar_y, bar_v, bar_a, bar_f, bar_p, h_ready, s_done;
     __shared__ uint32_t tmem_slot;
     __shared__ int abort_flag;
-    __shared__ float part[128][4];
     uint8_t* smem = align1024(smem_raw);
-    uint8_t* sW = smem;                        // [256][128]: 64 KB
-    uint8_t* sH = sW + 2 * TILE_J;             // [128][256]: 64 KB
-    uint8_t* sA = sH;                          // [128][128] operand of the first product, then H
-    uint8_t* sF = sH + 2 * TILE_J;             // [128][256]: 64 KB (after each product: the readout staging)
-    float (*vec)[D] = reinterpret_cast<float (*)[D]>(sF + 2 * TILE_J);  // join_out bias, LN_H gamma, beta
+    uint8_t* sW = smem;                  // [256][128] Wout: 64 KB
+    uint8_t* sF = sW + 2 * TILE_J;       // [128][256] f image of a pass, then its staging: 64 KB
+    uint8_t* sP = sF + 2 * TILE_J;       // [128][256] P tile image: 64 KB
+    uint8_t* sA = sP + 2 * TILE_J;       // [128][128] join-output image: 32 KB
+    float* stage = reinterpret_cast<float*>(sF);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int quad = warp & 3, cg = warp >> 2;
-    const int row = quad * 32 + lane;
     {
         const uint4* src = reinterpret_cast<const uint4*>(fn.out_tile);
         uint4* dst = reinterpret_cast<uint4*>(sW);
         for (uint32_t i = tid; i < 2 * TILE_J / 16; i += blockDim.x) dst[i] = src[i];
-        for (int i = tid; i < 3 * D; i += blockDim.x) {
-            const int v = i / D, c = i % D;
-            vec[v][c] = v == 0 ? fn.bout[c] : v == 1 ? fn.ln_g[4][c] : fn.ln_b[4][c];
-        }
     }
     if (tid == 0) {
-        umma::mbar_init(&mbar, 1);
+        umma::mbar_init(&bar_y, 1);
+        umma::mbar_init(&bar_v, 1);
         umma::mbar_init(&bar_a, 1);
         umma::mbar_init(&bar_f, 1);
+        umma::mbar_init(&bar_p, 1);
+        umma::mbar_init(&h_ready, NWORK / 32);
+        umma::mbar_init(&s_done, NWORK / 32);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         abort_flag = 0;
     }
-    if (warp == 0) umma::tmem_alloc(&tmem_slot, 512);
+    if (warp == 16) umma::tmem_alloc(&tmem_slot, 512);
     umma::fence_async_smem();
     umma::fence_before_sync();
     __syncthreads();
     umma::fence_after_sync();
     const uint32_t tmem = tmem_slot;
-    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    uint32_t phase = 0, ph_a = 0, ph_f = 0;
-    bool pend_a = false, pend_f = false;
-    // the f(c) operand image of readout pass `pass` (128 configs of player p)
-    auto load_f = [&](const JobDev& J, uint32_t pass) {
-        const uint8_t* src = reinterpret_cast<const uint8_t*>(J.f16) +
-                             ((p == 1 ? (J.ncfg_player[0] + 127) / 128 : 0) + pass) * (size_t)(2 * TILE_J);
-        umma::expect_tx(&bar_f, 2 * TILE_J);
-        for (uint32_t o = 0; o < 2 * TILE_J; o += ATOM) umma::bulk_g2s(sF + o, src + o, ATOM, &bar_f);
-        pend_f = true;
+    volatile int* abort_v = &abort_flag;
+    // a bounded wait that also gives up as soon as another thread has
+    // recorded an abort (so no role waits out its limit on a dead partner)
+    auto wait = [&](uint64_t* bar, uint32_t parity) {
+        const uint32_t addr = umma::smem_u32(bar);
+        for (uint32_t i = 0; i < WAIT_LIMIT; ++i) {
+            uint32_t done;
+            asm volatile(
+                "{\n\t.reg .pred q;\n\t"
+                "mbarrier.try_wait.parity.shared::cta.b64 q, [%1], %2;\n\t"
+                "selp.u32 %0, 1, 0, q;\n\t}\n"
+                : "=r"(done)
+                : "r"(addr), "r"(parity)
+                : "memory");
+            if (done) return true;
+            if ((i & 15u) == 15u && *abort_v) return false;
+        }
+        *abort_v = 1;
+        return false;
     };
-    // readout staging, row-major [128 rows][128 columns] with the low five
-    // column bits XORed by the row's: conflict-free for both the writes (one
-    // row per lane) and the per-row reads
-    float* stage = reinterpret_cast<float*>(sF);
-    for (uint32_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
-        const HeadTile ht = tiles[t];
-        const JobDev& J = jobs[ht.job];
-        const bool valid = (uint32_t)row < ht.count;
-        const uint32_t r = ht.first + row;          // job-local network row
-        const uint32_t g = J.row_base + r;          // global network row
-        // A = the join output image of this tile, and the first f(c) image,
-        // by bulk copy
-        if (tid == 0) {
-            const uint8_t* src = reinterpret_cast<const uint8_t*>(zout) + (size_t)t * TILE_J;
-            umma::expect_tx(&bar_a, TILE_J);
-            umma::bulk_g2s(sA, src, ATOM, &bar_a);
-            umma::bulk_g2s(sA + ATOM, src + ATOM, ATOM, &bar_a);
-            pend_a = true;
-            if (J.ncfg_player[p]) load_f(J, 0);
-            if (!umma::mbar_wait(&bar_a, ph_a, WAIT_LIMIT)) abort_flag = 1;
-            pend_a = false;
-            umma::fence_after_sync();
-            const uint32_t wa = umma::smem_u32(sA), wb = umma::smem_u32(sW);
-            const uint32_t idesc = umma::idesc16(128, 256, umma::Op16<H>::fmt);
+
+    if (warp == 16) {
+        // ------------------------------------------------------ the issuer
+        if (lane == 0) {
+            uint32_t ph_y = 0, ph_a = 0, ph_f = 0, ph_h = 0, ph_s = 0;
+            bool pend_a = false, pend_f = false, pend_p = false, pend_y = false, pend_v = false;
+            uint32_t ph_v = 0, ph_p = 0;
+            auto load_a = [&](uint32_t t) {
+                const uint8_t* src = reinterpret_cast<const uint8_t*>(zout) + (size_t)t * TILE_J;
+                umma::expect_tx(&bar_a, TILE_J);
+                umma::bulk_g2s(sA, src, ATOM, &bar_a);
+                umma::bulk_g2s(sA + ATOM, src + ATOM, ATOM, &bar_a);
+                pend_a = true;
+            };
+            auto load_p = [&](uint32_t t) {
+                const uint32_t bytes = tiles[t].count * 512u;
+                const uint8_t* src = reinterpret_cast<const uint8_t*>(pimg) + (size_t)t * 2 * TILE_J;
+                umma::expect_tx(&bar_p, bytes);
+                for (uint32_t o = 0; o < bytes; o += ATOM)
+                    umma::bulk_g2s(sP + o, src + o, bytes - o < ATOM ? bytes - o : ATOM, &bar_p);
+                pend_p = true;
+                ph_p ^= 1u;   // the epilogue waits for it; tracked here for the exit
+            };
+            auto load_f = [&](uint32_t job, uint32_t pass) {
+                const JobDev& J = jobs[job];
+                const uint8_t* src = reinterpret_cast<const uint8_t*>(J.f16) +
+                                     ((p == 1 ? (J.ncfg_player[0] + 127) / 128 : 0) + pass) * (size_t)(2 * TILE_J);
+                umma::expect_tx(&bar_f, 2 * TILE_J);
+                for (uint32_t o = 0; o < 2 * TILE_J; o += ATOM) umma::bulk_g2s(sF + o, src + o, ATOM, &bar_f);
+                pend_f = true;
+            };
+            auto prefetch_rows = [&](uint32_t t) {
+                const HeadTile ht = tiles[t];
+                const JobDev& J = jobs[ht.job];
+                umma::bulk_prefetch_l2(mass + ((size_t)J.row_base + ht.first) * 2, (size_t)ht.count * 8);
+                umma::bulk_prefetch_l2(J.lr_nc + 2 * (size_t)ht.first, (size_t)ht.count * 8);
+                umma::bulk_prefetch_l2(J.leaf_coff + 2 * (size_t)ht.first, (size_t)ht.count * 8);
+                umma::bulk_prefetch_l2(J.lr_vidx + 2 * (size_t)ht.first, (size_t)ht.count * 8);
+            };
+            auto issue_y = [&]() -> bool {
+                if (!wait(&bar_a, ph_a)) return false;
+                ph_a ^= 1u;
+                pend_a = false;
+                umma::fence_after_sync();
+                const uint32_t wa = umma::smem_u32(sA), wb = umma::smem_u32(sW);
+                const uint32_t idesc = umma::idesc16(128, 256, umma::Op16<H>::fmt);
 #pragma unroll
-            for (int k0 = 0; k0 < JW; k0 += 16)
-                umma::mma16(tmem, umma::desc_at(wa, 128, k0), umma::desc_at(wb, 256, k0), idesc, k0 > 0);
-            umma::commit(&mbar);
-        }
-        ph_a ^= 1u;
-        // meanwhile: the row's opponent reach mass (kept by the pooling
-        // kernel) and its readout columns
-        float opp_mass = 0.0f;
-        uint32_t ncfg_row = 0;
-        const uint32_t* lcol = nullptr;
-        float* out = nullptr;
-        if (valid) {
-            opp_mass = mass[(size_t)g * 2 + 1 - p];
-            ncfg_row = J.lr_nc[2 * r + p];
-            lcol = J.leaf_col + J.leaf_coff[2 * r + p];
-            out = J.vals[p] + J.lr_vidx[2 * r + p];
-        }
-        const uint32_t nfp = J.ncfg_player[p];
-        // this thread's 64 P values, loaded while the product runs
-        uint4 pq[8];
-        {
-            const uint4* pr = reinterpret_cast<const uint4*>(pb + (size_t)(valid ? g : 0) * D + 64 * cg);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) pq[i] = valid ? pr[i] : make_uint4(0, 0, 0, 0);
-        }
-        if (!umma::mbar_wait(&mbar, phase, WAIT_LIMIT)) abort_flag = 1;
-        phase ^= 1u;
-        umma::fence_after_sync();
-        // y = acc + P + bout on this thread's 64 columns; LayerNorm -> h -> sH
-        float y[64];
-        {
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                float v[32];
-                umma::tmem_ld32(tmem + lane_off + 64 * cg + 32 * h, v);
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    const uint4 q = pq[4 * h + c];
-                    const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const int j = 32 * h + 8 * c + 2 * i;
-                        y[j] = v[8 * c + 2 * i] + umma::Op16<H>::lo(w4[i]) + vec[0][64 * cg + j];
-                        y[j + 1] = v[8 * c + 2 * i + 1] + umma::Op16<H>::hi(w4[i]) + vec[0][64 * cg + j + 1];
-                    }
-                }
-            }
-        }
-        float mean, inv;
-        row_stats4(y, 64, part, row, cg, D, &mean, &inv);
-        {
-            const float* gam = vec[1] + 64 * cg;
-            const float* bet = vec[2] + 64 * cg;
-#pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                float x[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) x[i] = (y[8 * c + i] - mean) * inv * gam[8 * c + i] + bet[8 * c + i];
-                umma::st_chunk<H>(sH, 128, row, 64 * cg + 8 * c, x);
-            }
-        }
-        // this thread's first eight readout columns (entries cg, cg + 4, ...)
-        uint32_t lc8[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            const uint32_t e = (uint32_t)cg + 4u * k;
-            lc8[k] = e < ncfg_row ? lcol[e] : 0xffffffffu;
-        }
-        for (uint32_t nb = 0; nb < nfp; nb += 128) {
-            if (nb > 0 && tid == 0) load_f(J, nb / 128);
-            umma::fence_async_smem();
-            umma::fence_before_sync();
-            __syncthreads();
-            umma::fence_after_sync();
-            if (tid == 0) {
-                if (!umma::mbar_wait(&bar_f, ph_f, WAIT_LIMIT)) abort_flag = 1;
+                for (int k0 = 0; k0 < JW; k0 += 16)
+                    umma::mma16(tmem + TY, umma::desc_at(wa, 128, k0), umma::desc_at(wb, 256, k0), idesc, k0 > 0);
+                umma::commit(&bar_y);
+                pend_y = true;
+                return true;
+            };
+            auto issue_v = [&]() -> bool {
+                if (!wait(&bar_f, ph_f)) return false;
+                ph_f ^= 1u;
                 pend_f = false;
                 umma::fence_after_sync();
-                const uint32_t ha = umma::smem_u32(sH), fa = umma::smem_u32(sF);
+                const uint32_t fa = umma::smem_u32(sF);
                 const uint32_t idesc = umma::idesc16(128, 128, umma::Op16<H>::fmt);
 #pragma unroll
                 for (int k0 = 0; k0 < D; k0 += 16)
-                    umma::mma16(tmem + 256, umma::desc_at(ha, 128, k0), umma::desc_at(fa, 128, k0), idesc, k0 > 0);
-                umma::commit(&mbar);
+                    umma::mma16_ts(tmem + TV, tmem + TH + k0 / 2, umma::desc_at(fa, 128, k0), idesc, k0 > 0);
+                umma::commit(&bar_v);
+                pend_v = true;
+                ph_v ^= 1u;
+                return true;
+            };
+            const uint32_t G = gridDim.x;
+            uint32_t t = blockIdx.x;
+            bool ok = true;
+            if (t < ntiles) {
+                load_a(t);
+                load_p(t);
+                const uint32_t j0 = tiles[t].job;
+                if (jobs[j0].ncfg_player[p]) load_f(j0, 0);
+                if (t + G < ntiles) prefetch_rows(t + G);
+                ok = issue_y();
             }
-            ph_f ^= 1u;
-            if (!umma::mbar_wait(&mbar, phase, WAIT_LIMIT)) abort_flag = 1;
-            phase ^= 1u;
-            umma::fence_after_sync();
-            {
-                float v[32];
-                umma::tmem_ld32(tmem + lane_off + 256 + 32 * cg, v);
-                float* st = stage + row * 128 + 32 * cg;
-#pragma unroll
-                for (int j = 0; j < 32; ++j) st[j ^ lane] = v[j];
-            }
-            __syncthreads();
-            {
-                // thread (row, cg) writes every fourth of the row's values
-                const float* st = stage + row * 128;
-#pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    const uint32_t col = lc8[k] - nb;
-                    if (col < 128)
-                        out[cg + 4 * k] = (st[(col & ~31u) | ((col & 31u) ^ (uint32_t)lane)] + fn.vbias) * opp_mass;
+            for (; ok && t < ntiles; t += G) {
+                const uint32_t tn = t + G;
+                const HeadTile ht = tiles[t];
+                const uint32_t npass = (jobs[ht.job].ncfg_player[p] + 127) / 128;
+                // Y(t) done: its join-output image has been read
+                if (!(ok = wait(&bar_y, ph_y))) break;
+                ph_y ^= 1u;
+                pend_y = false;
+                if (tn < ntiles) load_a(tn);
+                if (tn + G < ntiles) prefetch_rows(tn + G);
+                // the epilogue has read Y(t) and P(t) and written H(t)
+                if (!(ok = wait(&h_ready, ph_h))) break;
+                ph_h ^= 1u;
+                pend_p = false;
+                umma::fence_after_sync();
+                if (tn < ntiles) load_p(tn);
+                if (npass && !(ok = issue_v())) break;
+                if (tn < ntiles && !(ok = issue_y())) break;
+                for (uint32_t k = 0; k < npass; ++k) {
+                    // pass k's staging has been read and V consumed: sF is free
+                    if (!(ok = wait(&s_done, ph_s))) break;
+                    ph_s ^= 1u;
+                    pend_v = false;
+                    umma::fence_after_sync();
+                    if (k + 1 < npass) {
+                        load_f(ht.job, k + 1);
+                        if (!(ok = issue_v())) break;
+                    }
                 }
-                for (uint32_t c = cg + 32; c < ncfg_row; c += 4) {
-                    const uint32_t col = lcol[c] - nb;
-                    if (col < 128) out[c] = (st[(col & ~31u) | ((col & 31u) ^ (uint32_t)lane)] + fn.vbias) * opp_mass;
+                if (!ok) break;
+                if (tn < ntiles) {
+                    const uint32_t jn = tiles[tn].job;
+                    if (jobs[jn].ncfg_player[p]) load_f(jn, 0);
                 }
             }
-            umma::fence_async_smem();  // the staging writes precede the next bulk copy into sF
-            umma::fence_before_sync();
-            __syncthreads();
+            if (!ok) atomicExch(err, 2);
+            // nothing may be in flight when the tensor memory is released
+            if (pend_y) umma::mbar_wait(&bar_y, ph_y, WAIT_LIMIT);
+            if (pend_v) umma::mbar_wait(&bar_v, ph_v ^ 1u, WAIT_LIMIT);
+            if (pend_a) umma::mbar_wait(&bar_a, ph_a, WAIT_LIMIT);
+            if (pend_f) umma::mbar_wait(&bar_f, ph_f, WAIT_LIMIT);
+            if (pend_p) umma::mbar_wait(&bar_p, ph_p ^ 1u, WAIT_LIMIT);
         }
-        if (abort_flag) break;
-    }
-    if (tid == 0) {
-        if (abort_flag) atomicExch(err, 2);
-        if (pend_a) umma::mbar_wait(&bar_a, ph_a, WAIT_LIMIT);
-        if (pend_f) umma::mbar_wait(&bar_f, ph_f, WAIT_LIMIT);
+        __syncwarp();
+    } else {
+        // ---------------------------------------------------- the epilogue
+        const int quad = warp & 3, cg = warp >> 2;
+        const int row = quad * 32 + lane;
+        const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+        uint32_t ph_y = 0, ph_v = 0, ph_p = 0;
+        bool bad = false;
+        auto bar_or = [&](bool v) {   // named barrier over the epilogue threads, OR of v
+            uint32_t r;
+            asm volatile(
+                "{\n\t.reg .pred p, q;\n\t"
+                "setp.ne.u32 p, %1, 0;\n\t"
+                "barrier.red.or.pred q, 1, 512, p;\n\t"
+                "selp.u32 %0, 1, 0, q;\n\t}\n"
+                : "=r"(r)
+                : "r"((uint32_t)v)
+                : "memory");
+            return r != 0;
+        };
+        const float4* gam4 = reinterpret_cast<const float4*>(fn.ln_g[4] + 64 * cg);
+        const float4* bet4 = reinterpret_cast<const float4*>(fn.ln_b[4] + 64 * cg);
+        for (uint32_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
+            const HeadTile ht = tiles[t];
+            const JobDev& J = jobs[ht.job];
+            const uint32_t npass = (J.ncfg_player[p] + 127) / 128;
+            if (!wait(&bar_y, ph_y)) bad = true;
+            ph_y ^= 1u;
+            if (!wait(&bar_p, ph_p)) bad = true;
+            ph_p ^= 1u;
+            umma::fence_after_sync();
+            // y = Y + P, in two 32-column halves: each half's mean and sum
+            // of squared deviations, and y written back over Y
+            float m2h[2], mh[2];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                float v[32];
+                umma::tmem_ld32(tmem + lane_off + TY + 64 * cg + 32 * h, v);
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const uint32_t k = (uint32_t)(8 * cg + 4 * h + c);
+                    const uint4 q = *reinterpret_cast<const uint4*>(sP + row * 512 + 16 * (k ^ (uint32_t)(row & 7)));
+                    const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        v[8 * c + 2 * i] += umma::Op16<H>::lo(w4[i]);
+                        v[8 * c + 2 * i + 1] += umma::Op16<H>::hi(w4[i]);
+                    }
+                }
+                float s = 0.0f;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) s += v[j];
+                const float m = s * (1.0f / 32);
+                float q2 = 0.0f;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) q2 += (v[j] - m) * (v[j] - m);
+                mh[h] = m;
+                m2h[h] = q2;
+                umma::tmem_st32(tmem + lane_off + TY + 64 * cg + 32 * h, v);
+            }
+            // the row's four column groups meet through V's first columns
+            {
+                const float m = 0.5f * (mh[0] + mh[1]);
+                const float m2 = m2h[0] + m2h[1] + 16.0f * (mh[0] - mh[1]) * (mh[0] - mh[1]);
+                uint32_t w2[2] = {__float_as_uint(m), __float_as_uint(m2)};
+                asm volatile("tcgen05.st.sync.aligned.32x32b.x2.b32 [%0], {%1, %2};" ::"r"(tmem + lane_off + TV + 2 * cg),
+                             "r"(w2[0]), "r"(w2[1])
+                             : "memory");
+                umma::tmem_wait_st();
+            }
+            umma::fence_before_sync();
+            if (bar_or(bad)) break;
+            umma::fence_after_sync();
+            float mean, inv;
+            {
+                uint32_t r8[8];
+                asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                             : "=r"(r8[0]), "=r"(r8[1]), "=r"(r8[2]), "=r"(r8[3]), "=r"(r8[4]), "=r"(r8[5]),
+                               "=r"(r8[6]), "=r"(r8[7])
+                             : "r"(tmem + lane_off + TV));
+                umma::tmem_wait_ld();
+                float mc[4], m2 = 0.0f;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) mc[c] = __uint_as_float(r8[2 * c]);
+                mean = 0.25f * (mc[0] + mc[1] + mc[2] + mc[3]);
+#pragma unroll
+                for (int c = 0; c < 4; ++c) m2 += __uint_as_float(r8[2 * c + 1]) + 64.0f * (mc[c] - mean) * (mc[c] - mean);
+                inv = rsqrtf(m2 * (1.0f / D) + 1e-5f);
+            }
+            // h = LN(y) as 16-bit pairs into H's TMEM columns (K = 64 cg ..)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                float v[32];
+                umma::tmem_ld32(tmem + lane_off + TY + 64 * cg + 32 * h, v);
+                uint32_t hw[16];
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    const float4 g = ldg4_inplace(gam4 + 8 * h + c), b = ldg4_inplace(bet4 + 8 * h + c);
+                    hw[2 * c] = umma::Op16<H>::pack((v[4 * c] - mean) * inv * g.x + b.x, (v[4 * c + 1] - mean) * inv * g.y + b.y);
+                    hw[2 * c + 1] =
+                        umma::Op16<H>::pack((v[4 * c + 2] - mean) * inv * g.z + b.z, (v[4 * c + 3] - mean) * inv * g.w + b.w);
+                }
+                asm volatile(
+                    "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+                    "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(tmem + lane_off + TH + 32 * cg + 16 * h),
+                    "r"(hw[0]), "r"(hw[1]), "r"(hw[2]), "r"(hw[3]), "r"(hw[4]), "r"(hw[5]), "r"(hw[6]), "r"(hw[7]),
+                    "r"(hw[8]), "r"(hw[9]), "r"(hw[10]), "r"(hw[11]), "r"(hw[12]), "r"(hw[13]), "r"(hw[14]), "r"(hw[15])
+                    : "memory");
+            }
+            umma::tmem_wait_st();
+            umma::fence_async_smem();     // the P reads precede the next P image's bulk copy
+            umma::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(umma::smem_u32(&h_ready)) : "memory");
+            // the row's opponent reach mass (kept by the pooling kernel), its
+            // readout columns and value slots (prefetched into L2)
+            const bool valid = (uint32_t)row < ht.count;
+            const uint32_t r = ht.first + row;          // job-local network row
+            float opp_mass = 0.0f;
+            uint32_t ncfg_row = 0;
+            const uint32_t* lcol = nullptr;
+            float* out = nullptr;
+            if (valid) {
+                opp_mass = mass[(size_t)(J.row_base + r) * 2 + 1 - p];
+                ncfg_row = J.lr_nc[2 * r + p];
+                lcol = J.leaf_col + J.leaf_coff[2 * r + p];
+                out = J.vals[p] + J.lr_vidx[2 * r + p];
+            }
+            // this thread's first eight readout columns (entries cg, cg + 4, ...)
+            uint32_t lc8[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const uint32_t e = (uint32_t)cg + 4u * k;
+                lc8[k] = e < ncfg_row ? lcol[e] : 0xffffffffu;
+            }
+            for (uint32_t k = 0; k < npass; ++k) {
+                const uint32_t nb = 128 * k;
+                if (!wait(&bar_v, ph_v)) bad = true;
+                ph_v ^= 1u;
+                umma::fence_after_sync();
+                {
+                    float v[32];
+                    umma::tmem_ld32(tmem + lane_off + TV + 32 * cg, v);
+                    float* st = stage + row * 128 + 32 * cg;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) st[j ^ lane] = v[j];
+                }
+                umma::fence_before_sync();
+                if (bar_or(bad)) { bad = true; break; }
+                {
+                    // thread (row, cg) writes every fourth of the row's values
+                    const float* st = stage + row * 128;
+#pragma unroll
+                    for (int k8 = 0; k8 < 8; ++k8) {
+                        const uint32_t col = lc8[k8] - nb;
+                        if (col < 128)
+                            out[cg + 4 * k8] = (st[(col & ~31u) | ((col & 31u) ^ (uint32_t)lane)] + fn.vbias) * opp_mass;
+                    }
+                    for (uint32_t c = cg + 32; c < ncfg_row; c += 4) {
+                        const uint32_t col = lcol[c] - nb;
+                        if (col < 128) out[c] = (st[(col & ~31u) | ((col & 31u) ^ (uint32_t)lane)] + fn.vbias) * opp_mass;
+                    }
+                }
+                umma::fence_async_smem();  // the staging reads precede the next bulk copy into sF
+                __syncwarp();
+                if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(umma::smem_u32(&s_done)) : "memory");
+            }
+            if (bad) break;
+        }
     }
     umma::fence_before_sync();
     __syncthreads();
-    if (warp == 0) umma::tmem_dealloc(tmem, 512);
+    if (warp == 16) umma::tmem_dealloc(tmem, 512);
 }
 
 // f(c) of every config as the readout's B-operand images: for each player,
@@ -727,11 +905,11 @@ void launch_join_fast(const JobDev* jobs, const void* tiles, uint32_t ntiles, co
 void launch_head_fast(const JobDev* jobs, const void* tiles, uint32_t ntiles, const FastNetDev& fn, int p,
                       const uint16_t* zout, const uint16_t* pb, const float* mass, int* err, cudaStream_t s) {
     if (!ntiles) return;
-    const size_t smem = 6 * TILE_J + 3 * D * 4 + 1024;
+    const size_t smem = 7 * TILE_J + 1024;
     auto kern = fn.half ? k_head_fast<true> : k_head_fast<false>;
     if (!raise_smem_limit((const void*)kern, smem)) return;
     uint32_t grid = std::min<uint32_t>(ntiles, (uint32_t)num_sms());
-    kern<<<grid, 512, smem, s>>>(jobs, reinterpret_cast<const HeadTile*>(tiles), ntiles, fn, p, zout, pb, mass, err);
+    kern<<<grid, 544, smem, s>>>(jobs, reinterpret_cast<const HeadTile*>(tiles), ntiles, fn, p, zout, pb, mass, err);
 }
 
 void launch_pack_f16(const JobDev* jobs, const uint32_t* cfg_job, const uint32_t* cfg_local, uint32_t total_cfgs,

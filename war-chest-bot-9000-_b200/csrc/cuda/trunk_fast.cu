@@ -550,23 +550,32 @@ __global__ void __launch_bounds__(384, 1)
         rows_gemm<BOARDS, 2 * C + LOOSE, D, 1>(&Hd.input[0][0], 2 * C + LOOSE, W + L.board_out.w, B + L.board_out.b,
                                                &Hd.P[0][0], D, nullptr);
         __syncthreads();
-        // P and jp are stored as 16-bit operands minus their row mean: every consumer of
-        // them (the join residual stream, the readout y) goes through a
-        // LayerNorm, which ignores a per-row constant, so the shift is exact
-        // and only shrinks the rounding.
+        // P + bout (the join output bias, which the readout adds to every row)
+        // and jp are stored as 16-bit operands minus their row mean: every
+        // consumer of them (the join residual stream, the readout y) goes
+        // through a LayerNorm, which ignores a per-row constant, so the shift
+        // is exact and only shrinks the rounding.
+        const float* bout = B + L.join_out.b;
         if (tid < BOARDS * 32) {
             const int i = tid / 32, l = tid % 32;
             float s = 0.0f;
-            for (int c = l; c < D; c += 32) s += Hd.P[i][c];
+            for (int c = l; c < D; c += 32) s += Hd.P[i][c] + bout[c];
 #pragma unroll
             for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
             if (l == 0) S.gb[i][0] = s / (float)D;
         }
         __syncthreads();
+        // P goes to the readout's per-tile images: the row's 128-row tile of
+        // its job (64 KB), row r at r * 512 bytes, its 16-byte chunk k at k ^ (r & 7)
         for (int q = tid; q < BOARDS * D; q += blockDim.x) {
             int i = q / D, c = q % D;
-            if (i < nb)
-                g_pb[(size_t)gb_[i] * D + c] = umma::Op16<H>::one(Hd.P[i][c] - S.gb[i][0]);
+            if (i < nb) {
+                const uint32_t lr = row_local[gb_[i]];
+                const size_t slot = jobs[row_job[gb_[i]]].tile_base + lr / 128;
+                const uint32_t rt = lr % 128;
+                g_pb[slot * 32768 + rt * 256 + ((uint32_t)(c >> 3) ^ (rt & 7)) * 8 + (c & 7)] =
+                    umma::Op16<H>::one(Hd.P[i][c] + bout[c] - S.gb[i][0]);
+            }
         }
         rows_gemm<BOARDS, D, JW, 3>(&Hd.P[0][0], D, W + L.join_p.w, nullptr, &Hd.jp[0][0], JW, Hd.part);
         __syncthreads();

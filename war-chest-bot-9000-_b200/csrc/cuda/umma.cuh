@@ -94,6 +94,18 @@ __device__ __forceinline__ void mma16(uint32_t tmem_d, uint64_t a, uint64_t b, u
         : "r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
 }
 
+// The same product with A read from tensor memory: tmem_a is A's first
+// column (lane field 0), one row per lane, two 16-bit K elements per 32-bit
+// column (low half the even element), so each K step of 16 is 8 columns.
+__device__ __forceinline__ void mma16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}\n"
+        :
+        : "r"(tmem_d), "r"(tmem_a), "l"(b), "r"(idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+}
+
 // Arrive on `mbar` when every MMA issued so far by this thread has completed.
 __device__ __forceinline__ void commit(uint64_t* mbar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(mbar))
@@ -186,6 +198,33 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
           "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
         : "memory");
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// 32 raw 32-bit words into consecutive columns of this thread's TMEM lane,
+// without the wait (follow with tmem_wait_st before the data is consumed).
+__device__ __forceinline__ void tmem_st32_nowait(uint32_t taddr, const uint32_t* r) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+        :
+        : "r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+          "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+          "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+          "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Prefetch [p, p + bytes) into L2 without waiting (the bulk copy engine
+// fetches it). The copy wants 16-byte boundaries: the start is rounded down
+// (still inside the 16-byte aligned allocation that holds p) and the end is
+// rounded down too, so nothing past the range's end is touched.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* p, size_t bytes) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p) & ~uintptr_t(15);
+    const uintptr_t e = (reinterpret_cast<uintptr_t>(p) + bytes) & ~uintptr_t(15);
+    if (e > a)
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a), "r"((uint32_t)(e - a)) : "memory");
 }
 
 // Bulk asynchronous copy global -> shared (16-byte aligned, size a multiple

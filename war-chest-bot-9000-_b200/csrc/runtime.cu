@@ -108,7 +108,8 @@ void build_fast_pack(DeviceCtx& d, const float* W, const float* B, const float* 
     const size_t MIX = 96 * 3 * 128, BLK = MIX + 96 * 2 * 128;
     size_t off_out = 4 * TJ, off_trunk = off_out + 2 * TJ, off_f = off_trunk + NET_BLOCKS * BLK;
     std::vector<float> vec;
-    auto push = [&](const float* src, size_t n) {
+    auto push = [&](const float* src, size_t n) {  // each vector 16-byte aligned (vector loads)
+        while (vec.size() % 4) vec.push_back(0.0f);
         size_t at = vec.size();
         vec.insert(vec.end(), src, src + n);
         return at;
@@ -359,7 +360,7 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
         o_gpool = A.take(32768ull * NT);  // [tile][player 0 | player 1] 128 x 64 images
         o_gjp = A.take(2ull * R * NET_JW);
         o_gmass = A.take(8ull * R);
-        o_gpb = A.take(2ull * R * NET_D);
+        o_gpb = A.take(65536ull * NT);    // [tile] 128 x 256 P image (row-swizzled 16-byte chunks)
         o_gz = A.take(32768ull * NT);     // [tile] 128 x 128 image
         o_tiles = A.take(sizeof(HeadTile) * head_tiles.size());
         o_err = A.take(16);
@@ -665,10 +666,16 @@ void download_board_rows(Batch& b, size_t job, float* pb, float* jp) {
         check(cudaStreamSynchronize(s), "download rows");
         return;
     }
-    std::vector<uint16_t> hp(n * NET_D), hj(n * NET_JW);
-    check(cudaMemcpyAsync(hp.data(), b.g_pb + (size_t)d.row_base * NET_D, 2 * n * NET_D, cudaMemcpyDeviceToHost, s), "download P");
+    const size_t ntile = (n + 127) / 128;
+    std::vector<uint16_t> hpt(ntile * 32768), hp(n * NET_D), hj(n * NET_JW);
+    check(cudaMemcpyAsync(hpt.data(), b.g_pb + (size_t)d.tile_base * 32768, 2 * hpt.size(), cudaMemcpyDeviceToHost, s),
+          "download P");
     check(cudaMemcpyAsync(hj.data(), b.g_jp + (size_t)d.row_base * NET_JW, 2 * n * NET_JW, cudaMemcpyDeviceToHost, s), "download jp");
     check(cudaStreamSynchronize(s), "download rows");
+    for (size_t r = 0; r < n; ++r) {  // undo the per-tile layout of P
+        const size_t rt = r % 128, base = (r / 128) * 32768 + rt * 256;
+        for (size_t c = 0; c < NET_D; ++c) hp[r * NET_D + c] = hpt[base + (((c >> 3) ^ (rt & 7)) << 3) + (c & 7)];
+    }
     const bool half = b.dev->half;
     auto f = [half](uint16_t v) {
         if (half) return __half2float(__ushort_as_half(v));
