@@ -124,22 +124,24 @@ struct HeadTile {
 // needs no exchange between threads. The residual stream z lives in TMEM:
 // initialised with jp + b by tcgen05.st, each layer's MMA accumulates onto it,
 // and the epilogue adds the running sum of the block biases. The four weight
-// tiles stream through two 32 KB slots by bulk copy (the next weight lands
-// while a layer computes) and the next tile's pooled images land during the
-// last layer, so a CTA needs ~100 KB of shared memory and two run per SM,
-// each one's MMAs and copies overlapping the other's epilogues.
+// tiles stream through one 32 KB slot by bulk copy (the next layer's weight
+// lands during this layer's epilogue) and the next tile's pooled images
+// land during the last layer, so a CTA needs ~73 KB of shared memory and
+// three run per SM, each one's MMAs and copies overlapping the others'
+// epilogues. The epilogue takes the row's 128 values in two halves (read
+// twice from TMEM: once for the statistics, once for LayerNorm and GELU).
 template <bool H>
-__global__ void __launch_bounds__(128, 2)
+__global__ void __launch_bounds__(128, 3)
     k_join_fast(const JobDev* __restrict__ jobs, const HeadTile* __restrict__ tiles, uint32_t ntiles, FastNetDev fn,
                 int p, const uint16_t* __restrict__ pool_img, const uint16_t* __restrict__ jp,
                 uint16_t* __restrict__ zout_img, int* __restrict__ err) {
     extern __shared__ uint8_t smem_raw[];
-    __shared__ uint64_t bar_in, bar_w[2], bar_mma;
+    __shared__ uint64_t bar_in, bar_w, bar_mma;
     __shared__ uint32_t tmem_slot;
     __shared__ int abort_flag;
     uint8_t* smem = align1024(smem_raw);
-    uint8_t* ring[2] = {smem, smem + TILE_J};
-    uint8_t* sA = smem + 2 * TILE_J;
+    uint8_t* sWt = smem;               // the current layer's weight tile
+    uint8_t* sA = smem + TILE_J;
     // [0] b with the seat folded in, [1..3] running sums of the block biases,
     // [4..7] LayerNorm gammas, [8..11] betas; then per layer the (gamma, beta)
     // column pairs packed for ln_gelu2
@@ -165,8 +167,7 @@ __global__ void __launch_bounds__(128, 2)
     }
     if (tid == 0) {
         umma::mbar_init(&bar_in, 1);
-        umma::mbar_init(&bar_w[0], 1);
-        umma::mbar_init(&bar_w[1], 1);
+        umma::mbar_init(&bar_w, 1);
         umma::mbar_init(&bar_mma, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         abort_flag = 0;
@@ -179,13 +180,12 @@ __global__ void __launch_bounds__(128, 2)
     const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
     const uint32_t my_tiles = blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
     const uint64_t uses = (uint64_t)my_tiles * 4;  // weight-slot uses: Wb, W1, W2, W3 per tile
-    bool pend_in = false, pend_w[2] = {false, false};
+    bool pend_in = false, pend_w = false;
     auto load_weight = [&](uint64_t k) {
-        const uint32_t slot = (uint32_t)(k & 1);
         const uint8_t* src = fn.join_tiles + (size_t)(k & 3) * TILE_J;
-        umma::expect_tx(&bar_w[slot], TILE_J);
-        for (uint32_t o = 0; o < TILE_J; o += ATOM) umma::bulk_g2s(ring[slot] + o, src + o, ATOM, &bar_w[slot]);
-        pend_w[slot] = true;
+        umma::expect_tx(&bar_w, TILE_J);
+        for (uint32_t o = 0; o < TILE_J; o += ATOM) umma::bulk_g2s(sWt + o, src + o, ATOM, &bar_w);
+        pend_w = true;
     };
     auto load_pooled = [&](uint32_t t) {
         const uint8_t* base = reinterpret_cast<const uint8_t*>(pool_img) + (size_t)t * (2 * ATOM);
@@ -194,12 +194,17 @@ __global__ void __launch_bounds__(128, 2)
         umma::bulk_g2s(sA + ATOM, base + (1 - p) * ATOM, ATOM, &bar_in);
         pend_in = true;
     };
+    // the jp rows of tile t into L2 (they are read at the tile's start)
+    auto prefetch_jp = [&](uint32_t t) {
+        const HeadTile ht = tiles[t];
+        umma::bulk_prefetch_l2(jp + ((size_t)jobs[ht.job].row_base + ht.first) * JW, (size_t)ht.count * JW * 2);
+    };
     if (tid == 0 && my_tiles) {
         load_pooled(blockIdx.x);
         load_weight(0);
-        if (uses > 1) load_weight(1);
+        if (blockIdx.x + gridDim.x < ntiles) prefetch_jp(blockIdx.x + gridDim.x);
     }
-    uint32_t ph_in = 0, ph_w[2] = {0, 0}, ph_mma = 0;
+    uint32_t ph_in = 0, ph_w = 0, ph_mma = 0;
     uint64_t k = 0;
     const uint32_t idesc = umma::idesc16(128, 128, umma::Op16<H>::fmt);
     for (uint32_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
@@ -207,6 +212,7 @@ __global__ void __launch_bounds__(128, 2)
         const JobDev& J = jobs[ht.job];
         const bool valid = (uint32_t)tid < ht.count;
         const uint32_t g = J.row_base + ht.first + tid;
+        if (tid == 32 && t + 2 * gridDim.x < ntiles) prefetch_jp(t + 2 * gridDim.x);
         {  // z = jp + b
             const uint4* jr = reinterpret_cast<const uint4*>(jp + (size_t)(valid ? g : 0) * JW);
 #pragma unroll 1
@@ -230,67 +236,81 @@ __global__ void __launch_bounds__(128, 2)
         umma::fence_after_sync();
 #pragma unroll 1
         for (int L = 0; L < 4; ++L, ++k) {
-            const uint32_t slot = (uint32_t)(k & 1);
             if (tid == 0) {
                 bool ok = true;
                 if (L == 0) {
                     ok = umma::mbar_wait(&bar_in, ph_in, WAIT_LIMIT) && ok;
                     pend_in = false;
                 }
-                ok = umma::mbar_wait(&bar_w[slot], ph_w[slot], WAIT_LIMIT) && ok;
-                pend_w[slot] = false;
+                ok = umma::mbar_wait(&bar_w, ph_w, WAIT_LIMIT) && ok;
+                pend_w = false;
                 if (!ok) abort_flag = 1;
                 umma::fence_after_sync();
-                const uint32_t a = umma::smem_u32(sA), b = umma::smem_u32(ring[slot]);
+                const uint32_t a = umma::smem_u32(sA), b = umma::smem_u32(sWt);
 #pragma unroll
                 for (int k0 = 0; k0 < JW; k0 += 16)
                     umma::mma16(tmem, umma::desc_at(a, 128, k0), umma::desc_at(b, 128, k0), idesc, 1u);
                 umma::commit(&bar_mma);
             }
             if (L == 0) ph_in ^= 1u;
-            ph_w[slot] ^= 1u;
+            ph_w ^= 1u;
             if (!umma::mbar_wait(&bar_mma, ph_mma, WAIT_LIMIT)) abort_flag = 1;
             ph_mma ^= 1u;
             umma::fence_after_sync();
             if (tid == 0) {  // the slot and (after the last layer) sA are free again
-                if (k + 2 < uses) load_weight(k + 2);
+                if (k + 1 < uses) load_weight(k + 1);
                 if (L == 3 && t + gridDim.x < ntiles) load_pooled(t + gridDim.x);
             }
-            // epilogue: the row's 128 values in one go (four loads, one
-            // wait), LayerNorm, GELU
+            // epilogue: the row's statistics over two 64-column halves, then
+            // LayerNorm and GELU over the halves read again
             const float* cb = vec[L];  // running bias sum (unused at L = 0)
-            uint32_t zr[JW];
+            float s4[4] = {0.0f, 0.0f, 0.0f, 0.0f}, q4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-            for (int c4 = 0; c4 < 4; ++c4) umma::tmem_ld32_nowait(tmem + lane_off + 32 * c4, zr + 32 * c4);
-            umma::tmem_wait_ld();
-            float s = 0.0f, sq = 0.0f;
+            for (int hf = 0; hf < 2; ++hf) {
+                uint32_t zr[64];
+                umma::tmem_ld32_nowait(tmem + lane_off + 64 * hf, zr);
+                umma::tmem_ld32_nowait(tmem + lane_off + 64 * hf + 32, zr + 32);
+                umma::tmem_wait_ld();
 #pragma unroll
-            for (int c = 0; c < JW; ++c) {
-                const float x = L ? __uint_as_float(zr[c]) + cb[c] : __uint_as_float(zr[c]);
-                zr[c] = __float_as_uint(x);
-                s += x;
-                sq += x * x;
+                for (int c = 0; c < 64; ++c) asm volatile("" : "+r"(zr[c]));  // the values exist after the wait
+#pragma unroll
+                for (int c = 0; c < 64; ++c) {
+                    const float x = L ? __uint_as_float(zr[c]) + cb[64 * hf + c] : __uint_as_float(zr[c]);
+                    s4[c & 3] += x;
+                    q4[c & 3] += x * x;
+                }
             }
+            const float s = (s4[0] + s4[1]) + (s4[2] + s4[3]), sq = (q4[0] + q4[1]) + (q4[2] + q4[3]);
             const float mean = s * (1.0f / JW);
             const float inv = rsqrtf(fmaxf(sq * (1.0f / JW) - mean * mean, 0.0f) + 1e-5f);
             const float nm = -mean * inv;
             const float* gam = vec[4 + L];
             const float* bet = vec[8 + L];
 #pragma unroll
-            for (int c8 = 0; c8 < JW / 8; ++c8) {
-                uint32_t w4[4];
+            for (int hf = 0; hf < 2; ++hf) {
+                uint32_t zr[64];
+                umma::tmem_ld32_nowait(tmem + lane_off + 64 * hf, zr);
+                umma::tmem_ld32_nowait(tmem + lane_off + 64 * hf + 32, zr + 32);
+                umma::tmem_wait_ld();
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const int c = 8 * c8 + 2 * j;
-                    w4[j] = umma::ln_gelu2<H>(__uint_as_float(zr[c]) * inv + nm, __uint_as_float(zr[c + 1]) * inv + nm, c,
-                                              gam, bet, gb2[L]);
+                for (int c = 0; c < 64; ++c) asm volatile("" : "+r"(zr[c]));
+#pragma unroll
+                for (int c8 = 0; c8 < 8; ++c8) {
+                    uint32_t w4[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int c = 8 * c8 + 2 * j, cc = 64 * hf + c;
+                        const float x0 = L ? __uint_as_float(zr[c]) + cb[cc] : __uint_as_float(zr[c]);
+                        const float x1 = L ? __uint_as_float(zr[c + 1]) + cb[cc + 1] : __uint_as_float(zr[c + 1]);
+                        w4[j] = umma::ln_gelu2<H>(x0 * inv + nm, x1 * inv + nm, cc, gam, bet, gb2[L]);
+                    }
+                    const uint4 o = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+                    const uint32_t off = umma::sw128_offset(128, tid, 64 * hf + 8 * c8);
+                    if (L < 3)
+                        *reinterpret_cast<uint4*>(sA + off) = o;
+                    else
+                        *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(zout_img) + (size_t)t * TILE_J + off) = o;
                 }
-                const uint4 o = make_uint4(w4[0], w4[1], w4[2], w4[3]);
-                const uint32_t off = umma::sw128_offset(128, tid, 8 * c8);
-                if (L < 3)
-                    *reinterpret_cast<uint4*>(sA + off) = o;
-                else
-                    *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(zout_img) + (size_t)t * TILE_J + off) = o;
             }
             if (L < 3) {
                 umma::fence_async_smem();
@@ -307,8 +327,7 @@ __global__ void __launch_bounds__(128, 2)
         // copies still in flight after an early exit must land before the
         // shared memory goes away
         if (pend_in) umma::mbar_wait(&bar_in, ph_in, WAIT_LIMIT);
-        for (int sl = 0; sl < 2; ++sl)
-            if (pend_w[sl]) umma::mbar_wait(&bar_w[sl], ph_w[sl], WAIT_LIMIT);
+        if (pend_w) umma::mbar_wait(&bar_w, ph_w, WAIT_LIMIT);
     }
     umma::fence_before_sync();
     __syncthreads();
@@ -493,6 +512,7 @@ __global__ void __launch_bounds__(544, 1)
     __shared__ uint64_t bar_y, bar_v, bar_a, bar_f, bar_p, h_ready, s_done;
     __shared__ uint32_t tmem_slot;
     __shared__ int abort_flag;
+    __shared__ uint32_t gb2[D];   // f16: the LayerNorm's (gamma, beta) per column pair, packed
     uint8_t* smem = align1024(smem_raw);
     uint8_t* sW = smem;                  // [256][128] Wout: 64 KB
     uint8_t* sF = sW + 2 * TILE_J;       // [128][256] f image of a pass, then its staging: 64 KB
@@ -504,6 +524,7 @@ __global__ void __launch_bounds__(544, 1)
         const uint4* src = reinterpret_cast<const uint4*>(fn.out_tile);
         uint4* dst = reinterpret_cast<uint4*>(sW);
         for (uint32_t i = tid; i < 2 * TILE_J / 16; i += blockDim.x) dst[i] = src[i];
+        for (int c = 2 * tid; c < D; c += 2 * blockDim.x) umma::pack_gb2(fn.ln_g[4], fn.ln_b[4], c, &gb2[c]);
     }
     if (tid == 0) {
         umma::mbar_init(&bar_y, 1);
@@ -759,12 +780,27 @@ __global__ void __launch_bounds__(544, 1)
                 float v[32];
                 umma::tmem_ld32(tmem + lane_off + TY + 64 * cg + 32 * h, v);
                 uint32_t hw[16];
+                if constexpr (H) {
+                    // f16: the affine in f16x2 on the normalised pair (the
+                    // result is an f16 operand either way)
+                    const float nm = -mean * inv;
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    const float4 g = ldg4_inplace(gam4 + 8 * h + c), b = ldg4_inplace(bet4 + 8 * h + c);
-                    hw[2 * c] = umma::Op16<H>::pack((v[4 * c] - mean) * inv * g.x + b.x, (v[4 * c + 1] - mean) * inv * g.y + b.y);
-                    hw[2 * c + 1] =
-                        umma::Op16<H>::pack((v[4 * c + 2] - mean) * inv * g.z + b.z, (v[4 * c + 3] - mean) * inv * g.w + b.w);
+                    for (int c = 0; c < 16; ++c) {
+                        const uint2 gb = *reinterpret_cast<const uint2*>(&gb2[64 * cg + 32 * h + 2 * c]);
+                        const __half2 n = __floats2half2_rn(fmaf(v[2 * c], inv, nm), fmaf(v[2 * c + 1], inv, nm));
+                        const __half2 x = __hfma2(n, *reinterpret_cast<const __half2*>(&gb.x),
+                                                  *reinterpret_cast<const __half2*>(&gb.y));
+                        hw[c] = *reinterpret_cast<const uint32_t*>(&x);
+                    }
+                } else {
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        const float4 g = ldg4_inplace(gam4 + 8 * h + c), b = ldg4_inplace(bet4 + 8 * h + c);
+                        hw[2 * c] = umma::Op16<H>::pack((v[4 * c] - mean) * inv * g.x + b.x,
+                                                        (v[4 * c + 1] - mean) * inv * g.y + b.y);
+                        hw[2 * c + 1] = umma::Op16<H>::pack((v[4 * c + 2] - mean) * inv * g.z + b.z,
+                                                            (v[4 * c + 3] - mean) * inv * g.w + b.w);
+                    }
                 }
                 asm volatile(
                     "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
@@ -894,10 +930,10 @@ bool raise_smem_limit(const void* fn, size_t smem) {
 void launch_join_fast(const JobDev* jobs, const void* tiles, uint32_t ntiles, const FastNetDev& fn, int p,
                       const uint16_t* pool_img, const uint16_t* jp, uint16_t* zout_img, int* err, cudaStream_t s) {
     if (!ntiles) return;
-    const size_t smem = 3 * TILE_J + 16 * JW * 4 + 1024;  // two weight slots, the A operand, the vectors
+    const size_t smem = 2 * TILE_J + 16 * JW * 4 + 1024;  // the weight slot, the A operand, the vectors
     auto kern = fn.half ? k_join_fast<true> : k_join_fast<false>;
     if (!raise_smem_limit((const void*)kern, smem)) return;
-    uint32_t grid = std::min<uint32_t>(ntiles, 2u * (uint32_t)num_sms());
+    uint32_t grid = std::min<uint32_t>(ntiles, 3u * (uint32_t)num_sms());
     kern<<<grid, 128, smem, s>>>(jobs, reinterpret_cast<const HeadTile*>(tiles), ntiles, fn, p, pool_img, jp, zout_img,
                                  err);
 }
