@@ -95,6 +95,8 @@ struct FastNetDev {
     const float* ln_b[5];
     float vbias;
     const float* pile_tok;      // [4][96] = W_pile W_tok: pile counts straight to the token projection
+    const float* trunk_pb;      // per trunk block [96]: the pooling bias plus the mix bias (both add to y)
+    const float* trunk_ob;      // per trunk block [96]: the out bias
     int half;                   // operand type of every tile and stored row: 1 = f16, 0 = bf16
 };
 

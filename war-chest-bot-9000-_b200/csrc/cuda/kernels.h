@@ -63,7 +63,7 @@ void trunk_set_constants(const wc::NetLayout& L, const uint8_t* neighbors, const
 size_t trunk_tiles_bytes();
 void launch_tokproj(const JobDev* jobs, uint32_t njobs, const float* W, cudaStream_t s);
 void launch_trunk_fast(const JobDev* jobs, const uint32_t* row_job, const uint32_t* row_local, uint32_t total_rows,
-                       const uint8_t* tiles, const float* W, const float* B, const float* LN, const float* pile_tok,
-                       uint16_t* g_pb, uint16_t* g_jp, bool half, int* err, cudaStream_t s);
+                       const uint8_t* tiles, const float* W, const float* B, const float* LN, const FastNetDev& fn,
+                       uint16_t* g_pb, uint16_t* g_jp, int* err, cudaStream_t s);
 
 }  // namespace wcdev

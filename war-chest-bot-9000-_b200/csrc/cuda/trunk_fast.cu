@@ -124,6 +124,7 @@ struct TrunkSmem {  // the non-operand scratch
     float pooled[BOARDS][2 * C];
     float gb[BOARDS][C];
     float part[4 * BOARDS * C];  // K-slice partial sums of the pooling GEMM
+    uint32_t gb2[wc::NET_BLOCKS][2][C];  // per block and LayerNorm: (gamma, beta) column pairs for ln_gelu2
     uint64_t wbar[2];
     uint64_t mbar;
     uint32_t tmem_slot;
@@ -155,8 +156,7 @@ __global__ void __launch_bounds__(384, 1)
     k_trunk_fast(const JobDev* __restrict__ jobs, const uint32_t* __restrict__ row_job,
                  const uint32_t* __restrict__ row_local, uint32_t total_rows, const uint8_t* __restrict__ tiles,
                  const float* __restrict__ W, const float* __restrict__ B, const float* __restrict__ LN,
-                 const float* __restrict__ pile_tok, uint16_t* __restrict__ g_pb, uint16_t* __restrict__ g_jp,
-                 int* __restrict__ err) {
+                 const FastNetDev fn, uint16_t* __restrict__ g_pb, uint16_t* __restrict__ g_jp, int* __restrict__ err) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (umma::smem_u32(smem_raw) & 1023u)) & 1023u);
     uint8_t* sW[2] = {smem, smem + BLOCK_BYTES};
@@ -177,6 +177,11 @@ __global__ void __launch_bounds__(384, 1)
     const uint32_t ntiles = (total_rows + BOARDS - 1) / BOARDS;
     const NetLayout& L = c_Lt;
 
+    for (int i = tid; i < wc::NET_BLOCKS * 2 * (C / 2); i += blockDim.x) {
+        const int blk = i / C, which = (i / (C / 2)) % 2, c = 2 * (i % (C / 2));
+        const int ln = NetLayout::ln_block(blk, which);
+        umma::pack_gb2(LN + L.norm_g[ln], LN + L.norm_b[ln], c, &S.gb2[blk][which][c]);
+    }
     if (tid == 0) {
         umma::mbar_init(&S.wbar[0], 1);
         umma::mbar_init(&S.wbar[1], 1);
@@ -262,7 +267,7 @@ __global__ void __launch_bounds__(384, 1)
                 const JobDev& J = jobs[row_job[gb_[i]]];
                 acc = J.tokproj[t * C + c];
 #pragma unroll
-                for (int k = 0; k < PILE; ++k) acc += St.piles[i][t * PILE + k] * pile_tok[k * C + c];
+                for (int k = 0; k < PILE; ++k) acc += St.piles[i][t * PILE + k] * fn.pile_tok[k * C + c];
             }
             St.proj[i][t * C + c] = acc;
         }
@@ -294,8 +299,7 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll 1
         for (int blk = 0; blk < wc::NET_BLOCKS; ++blk) {
             const int buf = blk & 1;
-            // a = LNGELU(x)
-            float a[32];
+            // LNGELU(x) -> A1 columns 0..95
             {
                 float s = 0.0f;
 #pragma unroll
@@ -309,14 +313,23 @@ __global__ void __launch_bounds__(384, 1)
                 S.part_q[row][cg] = q;
                 __syncthreads();
                 const float inv = rsqrtf((S.part_q[row][0] + S.part_q[row][1] + S.part_q[row][2]) * (1.0f / C) + 1e-5f);
+                const float nm = -mean * inv;
                 const float* gam = LN + L.norm_g[NetLayout::ln_block(blk, 0)];
                 const float* bet = LN + L.norm_b[NetLayout::ln_block(blk, 0)];
 #pragma unroll
-                for (int j = 0; j < 32; ++j) a[j] = real_row ? (x[j] - mean) * inv * gam[col0 + j] + bet[col0 + j] : 0.0f;
-            }
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t w4[4];
 #pragma unroll
-            for (int c = 0; c < 4; ++c)
-                *reinterpret_cast<uint4*>(sA1 + umma::sw128_offset(128, row, col0 + 8 * c)) = umma::gelu_chunk<H>(a + 8 * c);
+                    for (int j = 0; j < 4; ++j) {
+                        const int k = 8 * c + 2 * j;
+                        w4[j] = real_row ? umma::ln_gelu2<H>(x[k] * inv + nm, x[k + 1] * inv + nm, col0 + k, gam, bet,
+                                                             S.gb2[blk][0])
+                                         : 0u;
+                    }
+                    *reinterpret_cast<uint4*>(sA1 + umma::sw128_offset(128, row, col0 + 8 * c)) =
+                        make_uint4(w4[0], w4[1], w4[2], w4[3]);
+                }
+            }
             __syncthreads();
             // neighbour sums -> columns 96..191; board pooling (mean | max) of a
             {
@@ -407,8 +420,8 @@ __global__ void __launch_bounds__(384, 1)
                 }
             }
             __syncthreads();
-            rows_gemm<BOARDS, 2 * C, C, 4>(&S.pooled[0][0], 2 * C, W + L.pool[blk].w, B + L.pool[blk].b, &S.gb[0][0], C,
-                                           S.part);
+            rows_gemm<BOARDS, 2 * C, C, 4>(&S.pooled[0][0], 2 * C, W + L.pool[blk].w, fn.trunk_pb + blk * C, &S.gb[0][0],
+                                           C, S.part);
             // mix product (weights of this block must have landed)
             if (!umma::mbar_wait(&S.wbar[buf], wphase[buf], WAIT_LIMIT)) S.abort_flag = 1;
             wphase[buf] ^= 1u;
@@ -427,14 +440,14 @@ __global__ void __launch_bounds__(384, 1)
             if (!umma::mbar_wait(&S.mbar, mphase, WAIT_LIMIT)) S.abort_flag = 1;
             mphase ^= 1u;
             umma::fence_after_sync();
-            // y = mix + b + pool bias; LNGELU -> A2
+            // y = mix + (b_mix + pooled W_pool + b_pool); LNGELU -> A2
             float y[32];
             {
                 float v[32];
                 umma::tmem_ld32(tmem + lane_off + col0, v);
-                const wc::NetSpan mx = L.mix[blk];
+                const float* gbr = &S.gb[real_row ? board : 0][col0];
 #pragma unroll
-                for (int j = 0; j < 32; ++j) y[j] = v[j] + B[mx.b + col0 + j] + (real_row ? S.gb[board][col0 + j] : 0.0f);
+                for (int j = 0; j < 32; ++j) y[j] = v[j] + gbr[j];
                 float s = 0.0f;
 #pragma unroll
                 for (int j = 0; j < 32; ++j) s += y[j];
@@ -447,14 +460,23 @@ __global__ void __launch_bounds__(384, 1)
                 S.part_q[row][cg] = q;
                 __syncthreads();
                 const float inv = rsqrtf((S.part_q[row][0] + S.part_q[row][1] + S.part_q[row][2]) * (1.0f / C) + 1e-5f);
+                const float nm = -mean * inv;
                 const float* gam = LN + L.norm_g[NetLayout::ln_block(blk, 1)];
                 const float* bet = LN + L.norm_b[NetLayout::ln_block(blk, 1)];
 #pragma unroll
-                for (int j = 0; j < 32; ++j) y[j] = real_row ? (y[j] - mean) * inv * gam[col0 + j] + bet[col0 + j] : 0.0f;
-            }
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t w4[4];
 #pragma unroll
-            for (int c = 0; c < 4; ++c)
-                *reinterpret_cast<uint4*>(sA2 + umma::sw128_offset(128, row, col0 + 8 * c)) = umma::gelu_chunk<H>(y + 8 * c);
+                    for (int j = 0; j < 4; ++j) {
+                        const int k = 8 * c + 2 * j;
+                        w4[j] = real_row ? umma::ln_gelu2<H>(y[k] * inv + nm, y[k + 1] * inv + nm, col0 + k, gam, bet,
+                                                             S.gb2[blk][1])
+                                         : 0u;
+                    }
+                    *reinterpret_cast<uint4*>(sA2 + umma::sw128_offset(128, row, col0 + 8 * c)) =
+                        make_uint4(w4[0], w4[1], w4[2], w4[3]);
+                }
+            }
             umma::fence_async_smem();
             umma::fence_before_sync();
             __syncthreads();
@@ -478,9 +500,15 @@ __global__ void __launch_bounds__(384, 1)
             {
                 float v[32];
                 umma::tmem_ld32(tmem + lane_off + 128 + col0, v);
-                const wc::NetSpan ou = L.out[blk];
+                const float4* ob = reinterpret_cast<const float4*>(fn.trunk_ob + blk * C + col0);
 #pragma unroll
-                for (int j = 0; j < 32; ++j) x[j] += v[j] + B[ou.b + col0 + j];
+                for (int j4 = 0; j4 < 8; ++j4) {
+                    const float4 b4 = __ldg(ob + j4);
+                    x[4 * j4] += v[4 * j4] + b4.x;
+                    x[4 * j4 + 1] += v[4 * j4 + 1] + b4.y;
+                    x[4 * j4 + 2] += v[4 * j4 + 2] + b4.z;
+                    x[4 * j4 + 3] += v[4 * j4 + 3] + b4.w;
+                }
             }
             if (S.abort_flag) break;
         }
@@ -629,8 +657,9 @@ void launch_tokproj(const JobDev* jobs, uint32_t njobs, const float* W, cudaStre
 }
 
 void launch_trunk_fast(const JobDev* jobs, const uint32_t* row_job, const uint32_t* row_local, uint32_t total_rows,
-                       const uint8_t* tiles, const float* W, const float* B, const float* LN, const float* pile_tok,
-                       uint16_t* g_pb, uint16_t* g_jp, bool half, int* err, cudaStream_t s) {
+                       const uint8_t* tiles, const float* W, const float* B, const float* LN, const FastNetDev& fn,
+                       uint16_t* g_pb, uint16_t* g_jp, int* err, cudaStream_t s) {
+    const bool half = fn.half != 0;
     if (!total_rows) return;
     const size_t smem = 2 * BLOCK_BYTES + A1_BYTES + A2_BYTES + sizeof(TrunkSmem) + 1024;
     auto kern = half ? k_trunk_fast<true> : k_trunk_fast<false>;
@@ -640,7 +669,7 @@ void launch_trunk_fast(const JobDev* jobs, const uint32_t* row_job, const uint32
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     uint32_t ntiles = (total_rows + BOARDS - 1) / BOARDS;
     uint32_t grid = std::min<uint32_t>(ntiles, (uint32_t)sms);
-    kern<<<grid, 384, smem, s>>>(jobs, row_job, row_local, total_rows, tiles, W, B, LN, pile_tok, g_pb, g_jp, err);
+    kern<<<grid, 384, smem, s>>>(jobs, row_job, row_local, total_rows, tiles, W, B, LN, fn, g_pb, g_jp, err);
 }
 
 }  // namespace wcdev

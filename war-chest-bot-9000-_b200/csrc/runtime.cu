@@ -135,6 +135,14 @@ void build_fast_pack(DeviceCtx& d, const float* W, const float* B, const float* 
             pile_tok[k * NET_C + c] = (float)acc;
         }
     size_t o_ptok = push(pile_tok.data(), pile_tok.size());
+    // per trunk block: y = mix + b_mix + (pooled W_pool + b_pool), so the two biases travel as one
+    std::vector<float> tpb(NET_BLOCKS * NET_C), tob(NET_BLOCKS * NET_C);
+    for (int i = 0; i < NET_BLOCKS; ++i)
+        for (int c = 0; c < NET_C; ++c) {
+            tpb[i * NET_C + c] = B[L.pool[i].b + c] + B[L.mix[i].b + c];
+            tob[i * NET_C + c] = B[L.out[i].b + c];
+        }
+    size_t o_tpb = push(tpb.data(), tpb.size()), o_tob = push(tob.data(), tob.size());
     size_t o_g[5], o_b[5];
     for (int i = 0; i < 5; ++i) {
         int norm = NetLayout::LN_JOIN + i;
@@ -169,6 +177,8 @@ void build_fast_pack(DeviceCtx& d, const float* W, const float* B, const float* 
     }
     d.fast.vbias = B[L.value_bias];
     d.fast.pile_tok = F + o_ptok;
+    d.fast.trunk_pb = F + o_tpb;
+    d.fast.trunk_ob = F + o_tob;
     d.fast.half = h ? 1 : 0;
 }
 
@@ -623,7 +633,7 @@ void enqueue_leaf_values(Batch& b, int p) {
                 S.timed(TC_TRUNK, [&] {
                     b.count_launch(nj), wcdev::launch_tokproj(S.J, nj, dv.W, S.s);
                     b.count_launch(b.total_rows), wcdev::launch_trunk_fast(S.J, b.d_row_job, b.d_row_local, b.total_rows, dv.fast.trunk_tiles, dv.W,
-                                             dv.B, dv.LN, dv.fast.pile_tok, b.g_pb, b.g_jp, dv.half, b.d_err, S.s);
+                                             dv.B, dv.LN, dv.fast, b.g_pb, b.g_jp, b.d_err, S.s);
                 });
             }
             b.count_launch(b.total_cfgs), wcdev::launch_configs(S.J, b.d_cfg_job, b.d_cfg_local, b.total_cfgs, dv.W, dv.B, dv.LN, S.s);
@@ -715,7 +725,7 @@ void enqueue_solve(Batch& b) {
                 S.timed(TC_TRUNK, [&] {
                     b.count_launch(nj), wcdev::launch_tokproj(S.J, nj, dv.W, S.s);
                     b.count_launch(b.total_rows), wcdev::launch_trunk_fast(S.J, b.d_row_job, b.d_row_local, b.total_rows, dv.fast.trunk_tiles, dv.W,
-                                             dv.B, dv.LN, dv.fast.pile_tok, b.g_pb, b.g_jp, dv.half, b.d_err, S.s);
+                                             dv.B, dv.LN, dv.fast, b.g_pb, b.g_jp, b.d_err, S.s);
                 });
             }
             b.count_launch(b.total_cfgs), wcdev::launch_configs(S.J, b.d_cfg_job, b.d_cfg_local, b.total_cfgs, dv.W, dv.B, dv.LN, S.s);
