@@ -814,26 +814,28 @@ __global__ void __launch_bounds__(544, 1)
             umma::fence_before_sync();
             __syncwarp();
             if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(umma::smem_u32(&h_ready)) : "memory");
-            // the row's opponent reach mass (kept by the pooling kernel), its
-            // readout columns and value slots (prefetched into L2)
-            const bool valid = (uint32_t)row < ht.count;
-            const uint32_t r = ht.first + row;          // job-local network row
-            float opp_mass = 0.0f;
-            uint32_t ncfg_row = 0;
-            const uint32_t* lcol = nullptr;
-            float* out = nullptr;
-            if (valid) {
-                opp_mass = mass[(size_t)(J.row_base + r) * 2 + 1 - p];
-                ncfg_row = J.lr_nc[2 * r + p];
-                lcol = J.leaf_col + J.leaf_coff[2 * r + p];
-                out = J.vals[p] + J.lr_vidx[2 * r + p];
+            // the scatter: warp w writes the values of rows 8 w .. 8 w + 7, a
+            // row's entries across the lanes (coalesced column reads and value
+            // writes). Lane i < 8 holds row 8 w + i's opponent reach mass (kept
+            // by the pooling kernel), entry count, readout columns and value
+            // slots (prefetched into L2); colv[i] is entry `lane` of row
+            // 8 w + i, all eight loaded at once, during the readout product.
+            float s_mass = 0.0f;
+            uint32_t s_nc = 0;
+            unsigned long long s_lcol = 0, s_out = 0;
+            if (lane < 8 && (uint32_t)(8 * warp + lane) < ht.count) {
+                const uint32_t r = ht.first + 8 * warp + lane;      // job-local network row
+                s_mass = mass[(size_t)(J.row_base + r) * 2 + 1 - p];
+                s_nc = J.lr_nc[2 * r + p];
+                s_lcol = reinterpret_cast<unsigned long long>(J.leaf_col + J.leaf_coff[2 * r + p]);
+                s_out = reinterpret_cast<unsigned long long>(J.vals[p] + J.lr_vidx[2 * r + p]);
             }
-            // this thread's first eight readout columns (entries cg, cg + 4, ...)
-            uint32_t lc8[8];
+            uint32_t colv[8];
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                const uint32_t e = (uint32_t)cg + 4u * k;
-                lc8[k] = e < ncfg_row ? lcol[e] : 0xffffffffu;
+            for (int i = 0; i < 8; ++i) {
+                const uint32_t nc = __shfl_sync(0xffffffffu, s_nc, i);
+                const uint32_t* lc = reinterpret_cast<const uint32_t*>(__shfl_sync(0xffffffffu, s_lcol, i));
+                colv[i] = (uint32_t)lane < nc ? lc[lane] : 0xffffffffu;
             }
             for (uint32_t k = 0; k < npass; ++k) {
                 const uint32_t nb = 128 * k;
@@ -849,18 +851,23 @@ __global__ void __launch_bounds__(544, 1)
                 }
                 umma::fence_before_sync();
                 if (bar_or(bad)) { bad = true; break; }
-                {
-                    // thread (row, cg) writes every fourth of the row's values
-                    const float* st = stage + row * 128;
 #pragma unroll
-                    for (int k8 = 0; k8 < 8; ++k8) {
-                        const uint32_t col = lc8[k8] - nb;
-                        if (col < 128)
-                            out[cg + 4 * k8] = (st[(col & ~31u) | ((col & 31u) ^ (uint32_t)lane)] + fn.vbias) * opp_mass;
-                    }
-                    for (uint32_t c = cg + 32; c < ncfg_row; c += 4) {
-                        const uint32_t col = lcol[c] - nb;
-                        if (col < 128) out[c] = (st[(col & ~31u) | ((col & 31u) ^ (uint32_t)lane)] + fn.vbias) * opp_mass;
+                for (int i = 0; i < 8; ++i) {
+                    // staging row R was written with the XOR key R & 31
+                    const int R = 8 * warp + i;
+                    const float* st = stage + R * 128;
+                    const uint32_t key = (uint32_t)(R & 31);
+                    const float om = __shfl_sync(0xffffffffu, s_mass, i);
+                    float* o = reinterpret_cast<float*>(__shfl_sync(0xffffffffu, s_out, i));
+                    const uint32_t col = colv[i] - nb;
+                    if (col < 128) o[lane] = (st[(col & ~31u) | ((col & 31u) ^ key)] + fn.vbias) * om;
+                    const uint32_t nc = __shfl_sync(0xffffffffu, s_nc, i);
+                    if (nc > 32) {  // the row's further entries
+                        const uint32_t* lc = reinterpret_cast<const uint32_t*>(__shfl_sync(0xffffffffu, s_lcol, i));
+                        for (uint32_t e = 32 + lane; e < nc; e += 32) {
+                            const uint32_t c2 = lc[e] - nb;
+                            if (c2 < 128) o[e] = (st[(c2 & ~31u) | ((c2 & 31u) ^ key)] + fn.vbias) * om;
+                        }
                     }
                 }
                 umma::fence_async_smem();  // the staging reads precede the next bulk copy into sF
