@@ -452,7 +452,7 @@ KERNELS = {"rows": "k_rows", "vgather": "k_vgather", "reach": "k_rgather", "pool
 # rows, seeds 0..63, depth 3); a launch's traffic grows with
 # its rows, so the full launch's traffic is this times the workload's rows.
 # The pooling figure is of a launch that pooled both players.
-TRAFFIC_PER_ROW = {"head": 1029.6, "join": 683.4, "pool": 353.3, "trunk": 886.7}
+TRAFFIC_PER_ROW = {"head": 1025.4, "join": 796.9, "pool": 349.2, "trunk": 880.5}
 DTYPES = {"f16": "f32 CFR state, f16 tensor-core value net (fp32 accumulate)",
           "bf16": "f32 CFR state, bf16 tensor-core value net (fp32 accumulate)",
           "exact": "f32", "none": "f32"}
