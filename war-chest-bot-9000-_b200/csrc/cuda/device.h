@@ -97,6 +97,8 @@ struct FastNetDev {
     const float* pile_tok;      // [4][96] = W_pile W_tok: pile counts straight to the token projection
     const float* trunk_pb;      // per trunk block [96]: the pooling bias plus the mix bias (both add to y)
     const float* trunk_ob;      // per trunk block [96]: the out bias
+    const float* stem_w;        // [6][96] the hex stem weights (16-byte aligned copy)
+    const float* stem_pb;       // [37][96] the hex's position embedding plus the hex stem bias
     int half;                   // operand type of every tile and stored row: 1 = f16, 0 = bf16
 };
 

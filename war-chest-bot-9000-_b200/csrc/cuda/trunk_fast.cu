@@ -62,8 +62,9 @@ __device__ __forceinline__ void put_x32(uint8_t* tile, uint32_t R, uint32_t r, u
 // several are in flight (the weights come from L2). With KS > 1 the K slices
 // meet in `part` (KS * NB * N floats). `in` has row stride ldi, `out` ldo.
 // With RS > 1 (and KS == 1) the rows are split into RS groups as well, so
-// N * RS threads share the work.
-template <int NB, int K, int N, int KS, int RS = 1>
+// N * RS threads share the work. U weight loads are unrolled, so about U are
+// in flight per thread (each batch of U costs one L2 round trip).
+template <int NB, int K, int N, int KS, int RS = 1, int U = 8>
 __device__ __forceinline__ void rows_gemm(const float* in, int ldi, const float* __restrict__ W,
                                           const float* __restrict__ bias, float* out, int ldo, float* part) {
     static_assert(RS == 1 || KS == 1, "split rows or K, not both");
@@ -76,7 +77,7 @@ __device__ __forceinline__ void rows_gemm(const float* in, int ldi, const float*
         float acc[NR];
 #pragma unroll
         for (int i = 0; i < NR; ++i) acc[i] = 0.0f;
-#pragma unroll 8
+#pragma unroll U
         for (int k = k0; k < k1; ++k) {
             const float w = __ldg(W + (size_t)k * N + n);
 #pragma unroll
@@ -148,7 +149,7 @@ struct HeadSmem {
     float input[BOARDS][2 * C + LOOSE];
     float P[BOARDS][D];
     float jp[BOARDS][JW];
-    float part[3 * BOARDS * JW];
+    float part[3 * BOARDS * D];  // K-slice partial sums of the readout GEMMs
 };
 
 template <bool H>
@@ -195,6 +196,14 @@ __global__ void __launch_bounds__(384, 1)
     umma::fence_after_sync();
     const uint32_t tmem = S.tmem_slot;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    // this thread's row is fixed: its six neighbour rows (-1: none), read
+    // once from the constant table (a per-lane gather there serialises)
+    int nbr[6];
+#pragma unroll
+    for (int d = 0; d < 6; ++d) {
+        const uint8_t nbh = real_row ? c_nbt[hex][d] : (uint8_t)255;
+        nbr[d] = nbh == 255 ? -1 : board * NH + nbh;
+    }
     uint32_t wphase[2] = {0, 0}, mphase = 0;
     if (tid == 0 && blockIdx.x < ntiles) fetch_block(sW[0], tiles, 0, &S.wbar[0]);
 
@@ -280,18 +289,34 @@ __global__ void __launch_bounds__(384, 1)
             St.tpool[i][c] = acc;
         }
         __syncthreads();
+        // x = facts W_hex + (pos[hex] + b_hex) + occupant's token projection + glob + tpool
         float x[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-            const int c = col0 + j;
-            float v = 0.0f;
-            if (real_row && board < nb) {
-                for (int k = 0; k < HEX_FACTS; ++k) v += St.facts[row][k] * W[L.hex_stem.w + k * C + c];
-                v += B[L.hex_stem.b + c];
-                float occ = St.occ[row] >= 0 ? St.proj[board][St.occ[row] * C + c] : 0.0f;
-                v += occ + W[L.pos + hex * C + c] + St.glob[board][c] + St.tpool[board][c];
+        for (int j = 0; j < 32; ++j) x[j] = 0.0f;
+        if (real_row && board < nb) {
+            float f[HEX_FACTS];
+#pragma unroll
+            for (int k = 0; k < HEX_FACTS; ++k) f[k] = St.facts[row][k];
+            const int occ = St.occ[row];
+#pragma unroll
+            for (int j4 = 0; j4 < 8; ++j4) {
+                const int c = col0 + 4 * j4;
+                float4 v = __ldg(reinterpret_cast<const float4*>(fn.stem_pb + hex * C + c));
+#pragma unroll
+                for (int k = 0; k < HEX_FACTS; ++k) {
+                    const float4 w = __ldg(reinterpret_cast<const float4*>(fn.stem_w + k * C + c));
+                    v.x += f[k] * w.x;
+                    v.y += f[k] * w.y;
+                    v.z += f[k] * w.z;
+                    v.w += f[k] * w.w;
+                }
+                const float* g = &St.glob[board][c];
+                const float* tp = &St.tpool[board][c];
+                x[4 * j4] = v.x + (occ >= 0 ? St.proj[board][occ * C + c] : 0.0f) + g[0] + tp[0];
+                x[4 * j4 + 1] = v.y + (occ >= 0 ? St.proj[board][occ * C + c + 1] : 0.0f) + g[1] + tp[1];
+                x[4 * j4 + 2] = v.z + (occ >= 0 ? St.proj[board][occ * C + c + 2] : 0.0f) + g[2] + tp[2];
+                x[4 * j4 + 3] = v.w + (occ >= 0 ? St.proj[board][occ * C + c + 3] : 0.0f) + g[3] + tp[3];
             }
-            x[j] = v;
         }
         __syncthreads();  // stem scratch is dead from here
 
@@ -341,11 +366,11 @@ __global__ void __launch_bounds__(384, 1)
                     __half2 acc[16];
 #pragma unroll
                     for (int j = 0; j < 16; ++j) acc[j] = __float2half2_rn(0.0f);
-                    if (real_row) {
+                    {
+#pragma unroll
                         for (int d = 0; d < 6; ++d) {
-                            uint8_t nbh = c_nbt[hex][d];
-                            if (nbh == 255) continue;
-                            const int nr = board * NH + nbh;
+                            const int nr = nbr[d];
+                            if (nr < 0) continue;
 #pragma unroll
                             for (int c = 0; c < 4; ++c) {
                                 const uint4 q = *reinterpret_cast<const uint4*>(sA1 + umma::sw128_offset(128, nr, col0 + 8 * c));
@@ -366,11 +391,11 @@ __global__ void __launch_bounds__(384, 1)
                         *reinterpret_cast<uint4*>(sA1 + umma::sw128_offset(128, row, C + col0 + 8 * c)) = o;
                     }
                 } else {
-                    if (real_row) {
+                    {
+#pragma unroll
                         for (int d = 0; d < 6; ++d) {
-                            uint8_t nbh = c_nbt[hex][d];
-                            if (nbh == 255) continue;
-                            const int nr = board * NH + nbh;
+                            const int nr = nbr[d];
+                            if (nr < 0) continue;
 #pragma unroll
                             for (int c = 0; c < 4; ++c) {
                                 float v[8];
@@ -420,8 +445,8 @@ __global__ void __launch_bounds__(384, 1)
                 }
             }
             __syncthreads();
-            rows_gemm<BOARDS, 2 * C, C, 4>(&S.pooled[0][0], 2 * C, W + L.pool[blk].w, fn.trunk_pb + blk * C, &S.gb[0][0],
-                                           C, S.part);
+            rows_gemm<BOARDS, 2 * C, C, 4, 1, 16>(&S.pooled[0][0], 2 * C, W + L.pool[blk].w, fn.trunk_pb + blk * C,
+                                                  &S.gb[0][0], C, S.part);
             // mix product (weights of this block must have landed)
             if (!umma::mbar_wait(&S.wbar[buf], wphase[buf], WAIT_LIMIT)) S.abort_flag = 1;
             wphase[buf] ^= 1u;
@@ -575,8 +600,8 @@ __global__ void __launch_bounds__(384, 1)
             Hd.input[i][2 * C + j] = v;
         }
         __syncthreads();
-        rows_gemm<BOARDS, 2 * C + LOOSE, D, 1>(&Hd.input[0][0], 2 * C + LOOSE, W + L.board_out.w, B + L.board_out.b,
-                                               &Hd.P[0][0], D, nullptr);
+        rows_gemm<BOARDS, 2 * C + LOOSE, D, 3, 1, 23>(&Hd.input[0][0], 2 * C + LOOSE, W + L.board_out.w,
+                                                      B + L.board_out.b, &Hd.P[0][0], D, Hd.part);
         __syncthreads();
         // P + bout (the join output bias, which the readout adds to every row)
         // and jp are stored as 16-bit operands minus their row mean: every
@@ -605,7 +630,7 @@ __global__ void __launch_bounds__(384, 1)
                     umma::Op16<H>::one(Hd.P[i][c] + bout[c] - S.gb[i][0]);
             }
         }
-        rows_gemm<BOARDS, D, JW, 3>(&Hd.P[0][0], D, W + L.join_p.w, nullptr, &Hd.jp[0][0], JW, Hd.part);
+        rows_gemm<BOARDS, D, JW, 3, 1, 22>(&Hd.P[0][0], D, W + L.join_p.w, nullptr, &Hd.jp[0][0], JW, Hd.part);
         __syncthreads();
         if (tid < BOARDS * 32) {
             const int i = tid / 32, l = tid % 32;

@@ -143,6 +143,11 @@ void build_fast_pack(DeviceCtx& d, const float* W, const float* B, const float* 
             tob[i * NET_C + c] = B[L.out[i].b + c];
         }
     size_t o_tpb = push(tpb.data(), tpb.size()), o_tob = push(tob.data(), tob.size());
+    // the trunk stem: x = facts W_hex + (pos[hex] + b_hex) + ...; aligned copies for vector loads
+    std::vector<float> spb(37 * NET_C);
+    for (int h = 0; h < 37; ++h)
+        for (int c = 0; c < NET_C; ++c) spb[h * NET_C + c] = W[L.pos + h * NET_C + c] + B[L.hex_stem.b + c];
+    size_t o_sw = push(W + L.hex_stem.w, 6 * NET_C), o_spb = push(spb.data(), spb.size());
     size_t o_g[5], o_b[5];
     for (int i = 0; i < 5; ++i) {
         int norm = NetLayout::LN_JOIN + i;
@@ -179,6 +184,8 @@ void build_fast_pack(DeviceCtx& d, const float* W, const float* B, const float* 
     d.fast.pile_tok = F + o_ptok;
     d.fast.trunk_pb = F + o_tpb;
     d.fast.trunk_ob = F + o_tob;
+    d.fast.stem_w = F + o_sw;
+    d.fast.stem_pb = F + o_spb;
     d.fast.half = h ? 1 : 0;
 }
 
