@@ -77,21 +77,16 @@ def cfr_plus(wc):
 
 
 def build_jobs(wc, seeds, cfg, threads):
-    """Roots and flattened jobs on host threads (the C calls release the GIL).
-    Roots whose tree hits the node cap are counted and skipped, as the
-    reference's tape builder does (wave_tape.rs:51-56)."""
-    out = [None] * len(seeds)
+    """Seeded roots on host threads (the C calls release the GIL), then the
+    jobs by the library's parallel builder (wc_job_build_batch: native
+    threads, roots taken from a shared queue). Roots whose tree hits the node
+    cap are counted and skipped, as the reference's tape builder does
+    (wave_tape.rs:51-56)."""
     roots = [None] * len(seeds)
 
     def work(lo, hi):
         for i in range(lo, hi):
-            r = wc.generate_root(seeds[i], PLIES)
-            roots[i] = r
-            try:
-                out[i] = wc.PackedJob.from_root(r, cfg)
-            except wc.SolveError as e:
-                if e.code != 3:  # WC_E_CAPPED
-                    raise
+            roots[i] = wc.generate_root(seeds[i], PLIES)
 
     n = len(seeds)
     th = [threading.Thread(target=work, args=(n * k // threads, n * (k + 1) // threads)) for k in range(threads)]
@@ -99,8 +94,9 @@ def build_jobs(wc, seeds, cfg, threads):
         t.start()
     for t in th:
         t.join()
-    keep = [i for i in range(len(seeds)) if out[i] is not None]
-    return [roots[i] for i in keep], [out[i] for i in keep]
+    jobs = wc.PackedJob.build_many(roots, cfg, threads=threads)
+    keep = [i for i in range(n) if jobs[i] is not None]
+    return [roots[i] for i in keep], [jobs[i] for i in keep]
 
 
 class Clocks:

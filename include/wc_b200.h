@@ -124,8 +124,24 @@ int wc_root_generate(uint64_t seed, int plies, int random_draft, uint8_t* buf, s
  * ncarried == 0 the live root belief is valued. */
 int wc_job_build(const uint8_t* root, size_t len, const wc_solve_cfg* cfg, const float* carried, uint32_t ncarried,
                  wc_job** out);
+/* Build many jobs at once on `threads` host threads (0: one per hardware
+ * thread), each root taken in turn from a shared queue: the parallel form of
+ * the reference tape builder's loop (engine/examples/wave_tape.rs:48-61,
+ * Solver::new + PackedJob::from_solver per root, with capped roots counted and
+ * skipped). All roots share cfg and carry no carried beliefs. status[i] is
+ * wc_job_build's status for root i; out[i] is its job, or NULL when the build
+ * did not succeed (WC_E_CAPPED for a tree over the node cap). Each job is the
+ * one wc_job_build makes from the same root, byte for byte. Returns WC_OK when
+ * every root either built or was capped, else the first other failure (its
+ * message through wc_last_error); the jobs that did build are the caller's in
+ * either case. */
+int wc_job_build_batch(const uint8_t* const* roots, const size_t* lens, size_t n, const wc_solve_cfg* cfg,
+                       int threads, wc_job** out, int* status);
 int wc_job_info_get(const wc_job* job, wc_job_info* out);
 void wc_job_free(wc_job* job);
+/* A 64-bit digest (FNV-1a) of the job's flattened tables, for checking that
+ * two builds are identical and as a cache key. */
+int wc_job_digest(const wc_job* job, uint64_t* out);
 /* Work counts for roofline accounting, 20 slots, [p] = player 0 / 1:
  * [0+p] regret-matching cells of p's nodes, [2+p] their rows, [4+p] value-
  * gather entries for traverser p, [6+p] value-gather outputs, [8+p] reach

@@ -46,3 +46,44 @@ def test_node_cap_is_reported(wc):
     with pytest.raises(wc.SolveError) as e:
         wc.PackedJob.from_root(root, wc.Cfg(depth=3, iters=4, snapshots=False, cfr=wc.Cfr.PLUS, node_cap=50))
     assert e.value.code == 3  # WC_E_CAPPED
+
+
+def test_batch_build_equals_one_at_a_time(wc):
+    """wc_job_build_batch (the parallel tape builder) gives, root for root, the
+    job wc_job_build gives: the same bytes (digest), including the capped
+    roots, which come back empty as the reference's tape builder skips them
+    (wave_tape.rs:48-61)."""
+    roots = [wc.generate_root(s) for s in range(12)]
+    for cap in (0, 3000):
+        cfg = wc.Cfg(depth=3, iters=8, snapshots=False, cfr=wc.Cfr.PLUS, node_cap=cap)
+        one = []
+        for r in roots:
+            try:
+                one.append(wc.PackedJob.from_root(r, cfg))
+            except wc.SolveError as e:
+                assert e.code == 3  # WC_E_CAPPED
+                one.append(None)
+        for threads in (1, 4):
+            many = wc.PackedJob.build_many(roots, cfg, threads=threads)
+            assert [j is None for j in many] == [j is None for j in one]
+            for a, b in zip(one, many):
+                if a is not None:
+                    assert a.digest == b.digest
+                    assert a.info == b.info
+        if cap:
+            assert any(j is None for j in one) and any(j is not None for j in one)
+
+
+def test_batch_build_reports_a_bad_root(wc):
+    cfg = wc.Cfg(depth=2, iters=4, snapshots=False, cfr=wc.Cfr.PLUS)
+    good = wc.generate_root(0)
+    with pytest.raises(wc.SolveError) as e:
+        wc.PackedJob.build_many([good, b"\x00\x01"], cfg, threads=2)
+    assert "root 1" in str(e.value)
+    assert wc.PackedJob.build_many([], cfg) == []
+
+
+def test_digest_separates_different_jobs(wc):
+    cfg = wc.Cfg(depth=2, iters=4, snapshots=False, cfr=wc.Cfr.PLUS)
+    d = {wc.PackedJob.from_root(wc.generate_root(s), cfg).digest for s in range(6)}
+    assert len(d) == 6

@@ -1,4 +1,5 @@
 // The C ABI (include/wc_b200.h) over the host builder and the device runtime.
+#include <atomic>
 #include <cmath>
 #include <condition_variable>
 #include <cstring>
@@ -346,21 +347,33 @@ int wc_root_generate(uint64_t seed, int plies, int random_draft, uint8_t* buf, s
     });
 }
 
-int wc_job_build(const uint8_t* root, size_t len, const wc_solve_cfg* cfg, const float* carried, uint32_t ncarried,
-                 wc_job** out) {
-    if (!root || !cfg || !out) return fail(WC_E_ARG, "null argument");
-    return guarded([&] {
+namespace {
+
+SolveCfg solve_cfg(const wc_solve_cfg* cfg) {
+    SolveCfg sc;
+    sc.depth = cfg->depth;
+    sc.iters = cfg->iters;
+    sc.snapshots = cfg->snapshots != 0;
+    sc.cfr = {cfg->alpha, cfg->beta, cfg->gamma, cfg->predict};
+    sc.node_cap = (size_t)cfg->node_cap;
+    return sc;
+}
+
+// One job from one root (search.rs Solver::new + serialize.rs
+// PackedJob::from_solver). Never throws: the status comes back, and *msg
+// holds the error message of a failed build.
+int build_one(const uint8_t* root, size_t len, const SolveCfg& sc, const float* carried, uint32_t ncarried,
+              wc_job** out, std::string* msg) {
+    *out = nullptr;
+    auto err = [&](int code, const std::string& m) {
+        *msg = m;
+        return code;
+    };
+    try {
         Root r;
-        if (!root_from_bytes(root, len, &r)) return fail(WC_E_ARG, "malformed root bytes");
-        SolveCfg sc;
-        sc.depth = cfg->depth;
-        sc.iters = cfg->iters;
-        sc.snapshots = cfg->snapshots != 0;
-        sc.cfr = {cfg->alpha, cfg->beta, cfg->gamma, cfg->predict};
-        sc.node_cap = (size_t)cfg->node_cap;
-        if (sc.depth < 1 || sc.iters < 0) return fail(WC_E_ARG, "depth must be >= 1 and iters >= 0");
+        if (!root || !root_from_bytes(root, len, &r)) return err(WC_E_ARG, "malformed root bytes");
         auto tree = build_tree(r.s, r.ctx, sc, r.bel);
-        if (tree->capped) return fail(WC_E_CAPPED, "the tree hit the node cap");
+        if (tree->capped) return err(WC_E_CAPPED, "the tree hit the node cap");
         size_t w = tree->nc(0, 0) + tree->nc(0, 1);
         std::vector<float> car;
         if (ncarried) car.assign(carried, carried + (size_t)ncarried * w);
@@ -369,7 +382,73 @@ int wc_job_build(const uint8_t* root, size_t len, const wc_solve_cfg* cfg, const
         j->blob = make_blob(std::move(img));
         *out = j.release();
         return (int)WC_OK;
+    } catch (const std::bad_alloc&) {
+        return err(WC_E_NOMEM, "out of host memory");
+    } catch (const std::exception& e) {
+        return err(WC_E_CUDA, e.what());
+    }
+}
+
+}  // namespace
+
+int wc_job_build(const uint8_t* root, size_t len, const wc_solve_cfg* cfg, const float* carried, uint32_t ncarried,
+                 wc_job** out) {
+    if (!root || !cfg || !out) return fail(WC_E_ARG, "null argument");
+    const SolveCfg sc = solve_cfg(cfg);
+    if (sc.depth < 1 || sc.iters < 0) return fail(WC_E_ARG, "depth must be >= 1 and iters >= 0");
+    std::string msg;
+    const int rc = build_one(root, len, sc, carried, ncarried, out, &msg);
+    return rc == WC_OK ? rc : fail(rc, msg);
+}
+
+int wc_job_build_batch(const uint8_t* const* roots, const size_t* lens, size_t n, const wc_solve_cfg* cfg, int threads,
+                       wc_job** out, int* status) {
+    if (!cfg || (n && (!roots || !lens || !out || !status))) return fail(WC_E_ARG, "null argument");
+    const SolveCfg sc = solve_cfg(cfg);
+    if (sc.depth < 1 || sc.iters < 0) return fail(WC_E_ARG, "depth must be >= 1 and iters >= 0");
+    for (size_t i = 0; i < n; ++i) {
+        out[i] = nullptr;
+        status[i] = WC_OK;
+    }
+    if (!n) return WC_OK;
+    return guarded([&] {
+        size_t nt = threads > 0 ? (size_t)threads : std::max<size_t>(1, std::thread::hardware_concurrency());
+        nt = std::min(nt, n);
+        // roots are taken one at a time from a shared counter: tree sizes are
+        // heavy-tailed, so a fixed split would leave threads idle
+        std::atomic<size_t> next{0};
+        std::vector<std::string> msg(n);
+        auto work = [&] {
+            for (size_t i; (i = next.fetch_add(1)) < n;)
+                status[i] = build_one(roots[i], lens[i], sc, nullptr, 0, &out[i], &msg[i]);
+        };
+        std::vector<std::thread> pool;
+        try {
+            for (size_t k = 1; k < nt; ++k) pool.emplace_back(work);
+        } catch (...) {
+            // fewer threads than asked: the ones running (and this one) finish the work
+        }
+        work();
+        for (auto& t : pool) t.join();
+        for (size_t i = 0; i < n; ++i)
+            if (status[i] != WC_OK && status[i] != WC_E_CAPPED)
+                return fail(status[i], "root " + std::to_string(i) + ": " + msg[i]);
+        return (int)WC_OK;
     });
+}
+
+int wc_job_digest(const wc_job* job, uint64_t* out) {
+    if (!job || !out) return fail(WC_E_ARG, "null argument");
+    const JobBlob& b = *job->blob;
+    // FNV-1a over the blob's 64-bit words (its size is a multiple of 16)
+    uint64_t h = 1469598103934665603ull;
+    for (size_t i = 0; i + 8 <= b.bytes; i += 8) {
+        uint64_t w;
+        std::memcpy(&w, b.host + i, 8);
+        h = (h ^ w) * 1099511628211ull;
+    }
+    *out = h ^ (uint64_t)b.bytes;
+    return WC_OK;
 }
 
 int wc_job_info_get(const wc_job* job, wc_job_info* o) {
@@ -418,25 +497,29 @@ int wc_debug_umma_gemm_static(const uint16_t* a, const uint16_t* b, int k, int n
 int wc_job_counts(const wc_job* job, uint64_t* out, int n) {
     if (!job || !out || n < 20) return fail(WC_E_ARG, "wc_job_counts needs 20 slots");
     const JobImage& J = *job->blob->img;
+    const JobBlob& B = *job->blob;
+    const uint32_t *row_off = B.arr<uint32_t>(JobBlob::ROW_OFF), *vg_start = B.arr<uint32_t>(JobBlob::VG_START),
+                   *rg_start = B.arr<uint32_t>(JobBlob::RG_START), *rge_w = B.arr<uint32_t>(JobBlob::RGE_W),
+                   *lr_nc = B.arr<uint32_t>(JobBlob::LR_NC), *tl_nc = B.arr<uint32_t>(JobBlob::TL_NC);
     for (int i = 0; i < 20; ++i) out[i] = 0;
     for (uint32_t lv = 0; lv < J.nlevels; ++lv)
         for (int p = 0; p < 2; ++p) {
             const LevelRange& rr = J.rows_rng[lv * 2 + p];
-            out[0 + p] += J.row_off[rr.first + rr.count] - J.row_off[rr.first];
+            out[0 + p] += row_off[rr.first + rr.count] - row_off[rr.first];
             out[2 + p] += rr.count;
             const LevelRange& vr = J.vg_rng[lv * 2 + p];
-            out[4 + p] += J.vg_start[vr.first + vr.count] - J.vg_start[vr.first];
+            out[4 + p] += vg_start[vr.first + vr.count] - vg_start[vr.first];
             out[6 + p] += vr.count;
             if (lv == 0) continue;
             const LevelRange& gr = J.rg_rng[lv * 2 + p];
-            for (uint32_t e = J.rg_start[gr.first]; e < J.rg_start[gr.first + gr.count]; ++e) {
-                if (J.rge_w[e] < J.ncells) out[8 + p] += 1;
+            for (uint32_t e = rg_start[gr.first]; e < rg_start[gr.first + gr.count]; ++e) {
+                if (rge_w[e] < J.ncells) out[8 + p] += 1;
                 else out[10 + p] += 1;
             }
             out[12 + p] += gr.count;
         }
-    for (uint32_t r = 0; r < J.nrows_net; ++r) { out[14] += J.lr_nc[2 * r]; out[15] += J.lr_nc[2 * r + 1]; }
-    for (uint32_t k = 0; k < J.nterm; ++k) { out[16] += J.tl_nc[2 * k]; out[17] += J.tl_nc[2 * k + 1]; }
+    for (uint32_t r = 0; r < J.nrows_net; ++r) { out[14] += lr_nc[2 * r]; out[15] += lr_nc[2 * r + 1]; }
+    for (uint32_t k = 0; k < J.nterm; ++k) { out[16] += tl_nc[2 * k]; out[17] += tl_nc[2 * k + 1]; }
     out[18] = J.reach_len;
     out[19] = (uint64_t)J.val_len[0] + J.val_len[1];
     return WC_OK;
@@ -445,7 +528,7 @@ int wc_job_counts(const wc_job* job, uint64_t* out, int n) {
 int wc_job_root_belief(const wc_job* job, float* out) {
     if (!job || !out) return fail(WC_E_ARG, "null argument");
     const JobImage& J = *job->blob->img;
-    std::memcpy(out, J.root_belief.data(), 4 * J.root_belief.size());
+    std::memcpy(out, job->blob->arr<float>(JobBlob::ROOT_BELIEF), 4ull * (J.root_nc[0] + J.root_nc[1]));
     return WC_OK;
 }
 

@@ -68,8 +68,21 @@ std::unique_ptr<JobBlob> make_blob(std::unique_ptr<JobImage> img) {
         if (!b->host) throw std::bad_alloc();
         b->pinned = false;
     }
-    for (int i = 0; i < JobBlob::N_ARR; ++i)
+    for (int i = 0; i < JobBlob::N_ARR; ++i) {
         if (src[i].bytes) std::memcpy(b->host + b->off[i], src[i].p, src[i].bytes);
+        // the alignment gap after the array is zeroed: the blob's bytes are a
+        // function of the job alone (wc_job_digest)
+        const size_t end = b->off[i] + src[i].bytes, next = i + 1 < JobBlob::N_ARR ? b->off[i + 1] : b->bytes;
+        if (next > end) std::memset(b->host + end, 0, next - end);
+    }
+    // the blob is now the only copy of the arrays (readers use JobBlob::arr):
+    // a batch of thousands of jobs keeps half the host memory
+    auto drop = [](auto& v) { std::decay_t<decltype(v)>().swap(v); };
+    drop(J.cell_vidx), drop(J.row_off), drop(J.row_player), drop(J.vg_start), drop(J.vge_idx), drop(J.vge_w);
+    drop(J.rg_start), drop(J.rge_src), drop(J.rge_w), drop(J.drawp), drop(J.cell_ref), drop(J.lr_ridx);
+    drop(J.lr_nc), drop(J.lr_vidx), drop(J.leaf_coff), drop(J.leaf_cidx), drop(J.tl_ridx), drop(J.tl_nc);
+    drop(J.tl_vidx), drop(J.tl_util0), drop(J.gpu_rows), drop(J.cphi), drop(J.cplayer), drop(J.card_feat);
+    drop(J.root_belief), drop(J.carried), drop(J.cfg_col), drop(J.leaf_col);
     b->img = std::move(img);
     return b;
 }
@@ -228,7 +241,7 @@ struct Alloc {
 // item (a longer single row gets an item of its own), so the kernel can stage
 // an item's cells in shared memory.
 void add_row_items(std::vector<wcdev::WorkItem>& items, uint32_t job, uint32_t first, uint32_t count,
-                   uint32_t out_first, const std::vector<uint32_t>& row_off) {
+                   uint32_t out_first, const uint32_t* row_off) {
     uint32_t k = 0;
     while (k < count) {
         uint32_t n = 1;
@@ -313,7 +326,7 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
                     const JobImage& J = *jobs[j]->img;
                     if (lv >= J.nlevels) continue;
                     const LevelRange& r = J.rows_rng[lv * 2 + p];
-                    add_row_items(items, j, r.first, r.count, r.out_first, J.row_off);
+                    add_row_items(items, j, r.first, r.count, r.out_first, jobs[j]->arr<uint32_t>(JobBlob::ROW_OFF));
                 }
             });
             b.vg[lv * 2 + p] = range_of([&] {
@@ -660,6 +673,8 @@ void enqueue_leaf_values(Batch& b, int p) {
 
 void download_leaf_values(Batch& b, size_t job, int p, float* out) {
     const JobImage& J = *b.jobs[job]->img;
+    const uint32_t* lr_vidx = b.jobs[job]->arr<uint32_t>(JobBlob::LR_VIDX);
+    const uint32_t* lr_nc = b.jobs[job]->arr<uint32_t>(JobBlob::LR_NC);
     const wcdev::JobDev& d = b.hj[job];
     cudaStream_t s = b.dev->stream;
     std::vector<float> vals(J.val_len[p]);
@@ -667,7 +682,7 @@ void download_leaf_values(Batch& b, size_t job, int p, float* out) {
     check(cudaStreamSynchronize(s), "download values");
     size_t at = 0;
     for (uint32_t r = 0; r < J.nrows_net; ++r) {
-        uint32_t v0 = J.lr_vidx[2 * r + p], n = J.lr_nc[2 * r + p];
+        uint32_t v0 = lr_vidx[2 * r + p], n = lr_nc[2 * r + p];
         for (uint32_t c = 0; c < n; ++c) out[at++] = vals[v0 + c];
     }
 }

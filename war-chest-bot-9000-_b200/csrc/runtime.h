@@ -49,6 +49,13 @@ struct JobBlob {
         CPLAYER, CARD_FEAT, ROOT_BELIEF, CARRIED, CARRY_OFF, CFG_COL, LEAF_COL, N_ARR
     };
     size_t off[N_ARR] = {};
+    // A packed array. The blob is the only copy: make_blob releases the
+    // image's vectors once they are packed, and keeps its scalars, level
+    // ranges, exit nodes and snapshot list.
+    template <class T>
+    const T* arr(Arr a) const {
+        return reinterpret_cast<const T*>(host + off[a]);
+    }
     uint32_t nexit = 0, carry_width = 0, nsnaps_kept = 0;
     ~JobBlob();
 };
