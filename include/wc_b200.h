@@ -128,15 +128,18 @@ int wc_job_build(const uint8_t* root, size_t len, const wc_solve_cfg* cfg, const
  * thread), each root taken in turn from a shared queue: the parallel form of
  * the reference tape builder's loop (engine/examples/wave_tape.rs:48-61,
  * Solver::new + PackedJob::from_solver per root, with capped roots counted and
- * skipped). All roots share cfg and carry no carried beliefs. status[i] is
- * wc_job_build's status for root i; out[i] is its job, or NULL when the build
- * did not succeed (WC_E_CAPPED for a tree over the node cap). Each job is the
- * one wc_job_build makes from the same root, byte for byte. Returns WC_OK when
- * every root either built or was capped, else the first other failure (its
- * message through wc_last_error); the jobs that did build are the caller's in
- * either case. */
+ * skipped). All roots share cfg. carried and ncarried are wc_job_build's
+ * arguments per root (carried[i] holds ncarried[i] root pairs); either array
+ * may be NULL for no carried beliefs anywhere. status[i] is wc_job_build's
+ * status for root i; out[i] is its job, or NULL when the build did not succeed
+ * (WC_E_CAPPED for a tree over the node cap). Each job is the one
+ * wc_job_build makes from the same arguments, byte for byte. Returns WC_OK
+ * when every root either built or was capped, else the first other failure
+ * (its message through wc_last_error); the jobs that did build are the
+ * caller's in either case. */
 int wc_job_build_batch(const uint8_t* const* roots, const size_t* lens, size_t n, const wc_solve_cfg* cfg,
-                       int threads, wc_job** out, int* status);
+                       const float* const* carried, const uint32_t* ncarried, int threads, wc_job** out,
+                       int* status);
 int wc_job_info_get(const wc_job* job, wc_job_info* out);
 void wc_job_free(wc_job* job);
 /* A 64-bit digest (FNV-1a) of the job's flattened tables, for checking that

@@ -87,3 +87,25 @@ def test_digest_separates_different_jobs(wc):
     cfg = wc.Cfg(depth=2, iters=4, snapshots=False, cfr=wc.Cfr.PLUS)
     d = {wc.PackedJob.from_root(wc.generate_root(s), cfg).digest for s in range(6)}
     assert len(d) == 6
+
+
+def test_batch_build_with_carried_beliefs(wc):
+    """Per-root carried root pairs (the tape builder carries the live belief,
+    wave_tape.rs:57-58) give the job from_root gives with the same pairs; a
+    root without any values its live belief as the one Phase-2 root."""
+    cfg = wc.Cfg(depth=2, iters=4, snapshots=True, cfr=wc.Cfr.PLUS)
+    roots = [wc.generate_root(s) for s in range(5)]
+    rng = np.random.default_rng(7)
+    carried = []
+    for i, r in enumerate(roots):
+        if i == 2:
+            carried.append(None)
+            continue
+        j = wc.PackedJob.from_root(r, cfg)
+        w = j.info["root_nc0"] + j.info["root_nc1"]
+        carried.append(rng.random((i + 1, w), dtype=np.float32))
+    many = wc.PackedJob.build_many(roots, cfg, threads=3, carried=carried)
+    for r, c, b in zip(roots, carried, many):
+        a = wc.PackedJob.from_root(r, cfg, c)
+        assert a.digest == b.digest
+        assert b.info["ncarried"] == (1 if c is None else c.shape[0])

@@ -401,8 +401,9 @@ int wc_job_build(const uint8_t* root, size_t len, const wc_solve_cfg* cfg, const
     return rc == WC_OK ? rc : fail(rc, msg);
 }
 
-int wc_job_build_batch(const uint8_t* const* roots, const size_t* lens, size_t n, const wc_solve_cfg* cfg, int threads,
-                       wc_job** out, int* status) {
+int wc_job_build_batch(const uint8_t* const* roots, const size_t* lens, size_t n, const wc_solve_cfg* cfg,
+                       const float* const* carried, const uint32_t* ncarried, int threads, wc_job** out,
+                       int* status) {
     if (!cfg || (n && (!roots || !lens || !out || !status))) return fail(WC_E_ARG, "null argument");
     const SolveCfg sc = solve_cfg(cfg);
     if (sc.depth < 1 || sc.iters < 0) return fail(WC_E_ARG, "depth must be >= 1 and iters >= 0");
@@ -419,8 +420,15 @@ int wc_job_build_batch(const uint8_t* const* roots, const size_t* lens, size_t n
         std::atomic<size_t> next{0};
         std::vector<std::string> msg(n);
         auto work = [&] {
-            for (size_t i; (i = next.fetch_add(1)) < n;)
-                status[i] = build_one(roots[i], lens[i], sc, nullptr, 0, &out[i], &msg[i]);
+            for (size_t i; (i = next.fetch_add(1)) < n;) {
+                const uint32_t nc = carried && ncarried ? ncarried[i] : 0;
+                if (nc && !carried[i]) {
+                    status[i] = WC_E_ARG;
+                    msg[i] = "carried beliefs missing";
+                    continue;
+                }
+                status[i] = build_one(roots[i], lens[i], sc, nc ? carried[i] : nullptr, nc, &out[i], &msg[i]);
+            }
         };
         std::vector<std::thread> pool;
         try {

@@ -72,7 +72,8 @@ def _load() -> C.CDLL:
         "wc_set_cap_marker_value": (None, [C.c_float]),
         "wc_root_generate": (I, [U64, I, I, C.c_char_p, C.c_size_t, P(C.c_size_t)]),
         "wc_job_build": (I, [C.c_char_p, C.c_size_t, P(_SolveCfg), VP, C.c_uint32, P(VP)]),
-        "wc_job_build_batch": (I, [P(C.c_char_p), P(C.c_size_t), C.c_size_t, P(_SolveCfg), I, P(VP), P(C.c_int)]),
+        "wc_job_build_batch": (I, [P(C.c_char_p), P(C.c_size_t), C.c_size_t, P(_SolveCfg), P(VP), P(C.c_uint32), I,
+                                   P(VP), P(C.c_int)]),
         "wc_job_digest": (I, [VP, P(U64)]),
         "wc_job_info_get": (I, [VP, P(_JobInfo)]),
         "wc_job_free": (None, [VP]),
@@ -230,17 +231,27 @@ class PackedJob:
         return cls(h.value, root, cfg)
 
     @classmethod
-    def build_many(cls, roots: Sequence[bytes], cfg: Cfg, threads: int = 0) -> List[Optional["PackedJob"]]:
+    def build_many(cls, roots: Sequence[bytes], cfg: Cfg, threads: int = 0,
+                   carried: Optional[Sequence[Optional[np.ndarray]]] = None) -> List[Optional["PackedJob"]]:
         """Jobs for many roots on native host threads (wc_job_build_batch): the
-        parallel form of the reference tape builder (wave_tape.rs:48-61). A
-        root whose tree hits the node cap gives None, as the tape builder skips
-        it; any other failure raises."""
+        parallel form of the reference tape builder (wave_tape.rs:48-61).
+        carried[i], if given, is root i's carried root pairs as in from_root.
+        A root whose tree hits the node cap gives None, as the tape builder
+        skips it; any other failure raises."""
         n = len(roots)
         arr = (C.c_char_p * n)(*roots)
         lens = (C.c_size_t * n)(*[len(r) for r in roots])
         out = (C.c_void_p * n)()
         status = (C.c_int * n)()
-        rc = lib().wc_job_build_batch(arr, lens, n, C.byref(cfg._c()), threads, out, status)
+        cptr, ncar, keep = None, None, []
+        if carried is not None:
+            cptr, ncar = (C.c_void_p * n)(), (C.c_uint32 * n)()
+            for i, c in enumerate(carried):
+                if c is not None:
+                    c = np.ascontiguousarray(c, np.float32)
+                    keep.append(c)
+                    cptr[i], ncar[i] = c.ctypes.data, c.shape[0]
+        rc = lib().wc_job_build_batch(arr, lens, n, C.byref(cfg._c()), cptr, ncar, threads, out, status)
         jobs = [cls(out[i], roots[i], cfg) if out[i] else None for i in range(n)]
         _check(rc)
         return jobs
