@@ -119,6 +119,13 @@ void wc_set_cap_marker_value(float v);
  * with the Bayes belief filter, then on to the next MainPlay. Serialized as
  * the State bytes then both beliefs. */
 int wc_root_generate(uint64_t seed, int plies, int random_draft, uint8_t* buf, size_t cap, size_t* len);
+/* A belief-heavy root: wc_root_generate's position,
+ * each player's belief replaced by up to ncfg configs drawn (seeded, without
+ * replacement) from every config consistent with the public counts
+ * (rebel.rs:270 enumerate_configs), the true config always among them, with
+ * Dirichlet(1) weights. Same byte form as wc_root_generate. */
+int wc_root_generate_wide(uint64_t seed, int plies, int random_draft, uint32_t ncfg, uint8_t* buf, size_t cap,
+                          size_t* len);
 /* Build and flatten the subgame tree at a serialized root. carried holds
  * ncarried root pairs (player 0 then player 1 over the root supports); with
  * ncarried == 0 the live root belief is valued. */

@@ -109,3 +109,26 @@ def test_batch_build_with_carried_beliefs(wc):
         a = wc.PackedJob.from_root(r, cfg, c)
         assert a.digest == b.digest
         assert b.info["ncarried"] == (1 if c is None else c.shape[0])
+
+
+def test_wide_roots(wc, oracle):
+    """Belief-heavy roots: each player's belief covers
+    min(ncfg, |consistent configs|) configs with positive weights summing to
+    one, the same seed gives the same bytes, and the oracle builds the same
+    tree from them."""
+    cfg = wc.Cfg(depth=2, iters=4, snapshots=True, cfr=wc.Cfr.PLUS)
+    for seed in range(3):
+        full = wc.PackedJob.from_root(wc.generate_wide_root(seed, 100000), cfg)
+        n_all = (full.info["root_nc0"], full.info["root_nc1"])
+        for ncfg in (4, 256):
+            r = wc.generate_wide_root(seed, ncfg)
+            assert r == wc.generate_wide_root(seed, ncfg)
+            job = wc.PackedJob.from_root(r, cfg)
+            n = (job.info["root_nc0"], job.info["root_nc1"])
+            assert n == tuple(min(ncfg, a) for a in n_all)
+            rb = job.root_belief()
+            for part in (rb[: n[0]], rb[n[0]:]):
+                assert np.all(part > 0) and abs(part.sum() - 1) < 1e-5
+            o = oracle.Oracle(r, cfg)
+            for k in ("nodes", "cells", "net_rows", "configs"):
+                assert job.info[k] == o.shape[k]

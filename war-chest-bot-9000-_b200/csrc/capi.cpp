@@ -391,6 +391,20 @@ int build_one(const uint8_t* root, size_t len, const SolveCfg& sc, const float* 
 
 }  // namespace
 
+int wc_root_generate_wide(uint64_t seed, int plies, int random_draft, uint32_t ncfg, uint8_t* buf, size_t cap,
+                          size_t* len) {
+    return guarded([&] {
+        Root r;
+        if (!make_wide_root(seed, plies, random_draft != 0, ncfg, &r))
+            return fail(WC_E_ARG, "the game ended before the root");
+        std::vector<uint8_t> b = root_to_bytes(r);
+        if (len) *len = b.size();
+        if (!buf || b.size() > cap) return fail(WC_E_ARG, "root buffer too small");
+        std::memcpy(buf, b.data(), b.size());
+        return (int)WC_OK;
+    });
+}
+
 int wc_job_build(const uint8_t* root, size_t len, const wc_solve_cfg* cfg, const float* carried, uint32_t ncarried,
                  wc_job** out) {
     if (!root || !cfg || !out) return fail(WC_E_ARG, "null argument");

@@ -1,6 +1,8 @@
 // Seeded root generation (selfplay.rs / policy.rs of the reference).
 #include "roots.h"
 
+#include <algorithm>
+#include <cmath>
 #include <cstring>
 #include <stdexcept>
 
@@ -149,6 +151,31 @@ Belief uniform_belief(const State& s, const Ctx& ctx, uint8_t p) {
     float n = (float)b.cfg.size();
     b.p.assign(b.cfg.size(), 1.0f / n);
     return b;
+}
+
+bool make_wide_root(uint64_t seed, int plies, bool random_draft, uint32_t ncfg, Root* out) {
+    if (!make_root(seed, plies, random_draft, out)) return false;
+    Rng rng(seed ^ 0x5EEDB17EF0C0FFEEull);  // a stream of its own, apart from the game's
+    for (int p = 0; p < 2; ++p) {
+        Belief all = uniform_belief(out->s, out->ctx, (uint8_t)p);
+        std::vector<Config>& c = all.cfg;
+        // the true config first, then a partial Fisher-Yates draw of the rest
+        const int ti = all.index_of(true_config(out->s, (uint8_t)p, out->ctx));
+        if (ti > 0) std::swap(c[0], c[(size_t)ti]);
+        const size_t k = std::max<size_t>(1, std::min<size_t>(ncfg, c.size()));
+        for (size_t i = 1; i < k; ++i) std::swap(c[i], c[i + rng.below(c.size() - i)]);
+        std::vector<double> e(k);
+        double tot = 0.0;
+        for (size_t i = 0; i < k; ++i) {
+            e[i] = -std::log(1.0 - rng.unit_f64());  // unit exponential; 1 - u is in (0, 1]
+            tot += e[i];
+        }
+        std::vector<std::pair<Config, float>> pairs;
+        pairs.reserve(k);
+        for (size_t i = 0; i < k; ++i) pairs.emplace_back(c[i], (float)(e[i] / tot));
+        out->bel[p] = Belief::from_pairs(std::move(pairs));
+    }
+    return true;
 }
 
 std::vector<uint8_t> root_to_bytes(const Root& r) {

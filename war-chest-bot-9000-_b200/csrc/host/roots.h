@@ -43,6 +43,14 @@ bool make_root(uint64_t seed, int plies, bool random_draft, Root* out);
 // (tests/rebel_solver.rs:50-64).
 Belief uniform_belief(const State& s, const Ctx& ctx, uint8_t p);
 
+// A belief-heavy root: make_root's position, then each player's belief
+// replaced by up to `ncfg` configs drawn (seeded, without replacement) from
+// every config consistent with the public counts (enumerate_configs,
+// rebel.rs:270), the true config always among them, with Dirichlet(1)
+// weights (normalised unit exponentials). Returns false if the game ended
+// before the root.
+bool make_wide_root(uint64_t seed, int plies, bool random_draft, uint32_t ncfg, Root* out);
+
 // Serialized root: the State bytes, then per player u32 n, n configs
 // (hand[5], fd[5], inflight i8), n f32 weights.
 std::vector<uint8_t> root_to_bytes(const Root& r);

@@ -71,6 +71,7 @@ def _load() -> C.CDLL:
         "wc_weights_fill": (I, [I, U64, VP, VP, VP]),
         "wc_set_cap_marker_value": (None, [C.c_float]),
         "wc_root_generate": (I, [U64, I, I, C.c_char_p, C.c_size_t, P(C.c_size_t)]),
+        "wc_root_generate_wide": (I, [U64, I, I, C.c_uint32, C.c_char_p, C.c_size_t, P(C.c_size_t)]),
         "wc_job_build": (I, [C.c_char_p, C.c_size_t, P(_SolveCfg), VP, C.c_uint32, P(VP)]),
         "wc_job_build_batch": (I, [P(C.c_char_p), P(C.c_size_t), C.c_size_t, P(_SolveCfg), P(VP), P(C.c_uint32), I,
                                    P(VP), P(C.c_int)]),
@@ -174,6 +175,17 @@ def generate_root(seed: int, plies: int = 20, random_draft: bool = True) -> byte
     buf = C.create_string_buffer(cap)
     n = C.c_size_t()
     _check(lib().wc_root_generate(seed, plies, int(random_draft), buf, cap, C.byref(n)))
+    return buf.raw[: n.value]
+
+
+def generate_wide_root(seed: int, ncfg: int = 256, plies: int = 20, random_draft: bool = True) -> bytes:
+    """A belief-heavy root: generate_root's position
+    with each player's belief over up to ncfg consistent configs, Dirichlet(1)
+    weights (wc_root_generate_wide)."""
+    cap = 1 << 22
+    buf = C.create_string_buffer(cap)
+    n = C.c_size_t()
+    _check(lib().wc_root_generate_wide(seed, plies, int(random_draft), ncfg, buf, cap, C.byref(n)))
     return buf.raw[: n.value]
 
 
