@@ -24,6 +24,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import threading
 import time
 
@@ -105,10 +106,9 @@ class Clocks:
     def __init__(self, index):
         self.index = index
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{index}.csv")
+        self.path = os.path.join(tempfile.gettempdir(), f"wcb200_clocks_{os.getpid()}_{index}.csv")
 
     def start(self):
-        os.makedirs(os.path.dirname(self.path), exist_ok=True)
         q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -298,7 +298,9 @@ def main():
             print(json.dumps(line), flush=True)
         return
 
-    threads = args.build_threads or max(1, (os.cpu_count() or 1))
+    # host threads per rank: the ranks of one node share its cores
+    local_world = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
+    threads = args.build_threads or max(1, (os.cpu_count() or 1) // max(1, local_world))
     t0 = time.perf_counter()
     roots, jobs = build_jobs(wc, seeds, cfg, threads)
     build_s = time.perf_counter() - t0

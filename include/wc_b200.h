@@ -115,9 +115,16 @@ int wc_weights_fill(int kind, uint64_t seed, float* w, float* b, float* ln);
 void wc_set_cap_marker_value(float v);
 
 /* ---- roots and jobs ------------------------------------------------------ */
+/* Root bytes are the reference's own root encoding, format v3
+ * (engine/src/roots.rs:247-313, write_root / read_root): the State field by
+ * field in little-endian (write_state, roots.rs:150-180), then per player a
+ * u32 count n, n configs (hand[5], fd[5], inflight or 0xff) and n f32
+ * weights. A Rust engine hands `roots::write_root(&mut buf, &state, &bel)`'s
+ * bytes straight to wc_job_build. */
+
 /* A seeded root: make_game(seed, random draft) then `plies` uniform decisions
- * with the Bayes belief filter, then on to the next MainPlay. Serialized as
- * the State bytes then both beliefs. */
+ * with the Bayes belief filter, then on to the next MainPlay
+ * (engine/src/selfplay.rs:59-81,588-905), in the root encoding above. */
 int wc_root_generate(uint64_t seed, int plies, int random_draft, uint8_t* buf, size_t cap, size_t* len);
 /* A belief-heavy root: wc_root_generate's position,
  * each player's belief replaced by up to ncfg configs drawn (seeded, without
@@ -165,6 +172,34 @@ int wc_job_root_belief(const wc_job* job, float* out);
 /* Carry layout: nexit + 1 offsets into a carry row, and the exit nodes'
  * reference ids (network rows then terminal leaves). Either may be NULL. */
 int wc_job_carry_offsets(const wc_job* job, uint32_t* offsets, uint32_t* exit_nodes);
+
+/* A roots file as write_roots writes it (engine/src/roots.rs:323-363: magic
+ * 0x57107207, version 3, u32 count, the roots back to back): the byte offset
+ * and length of each root, for wc_job_build. Replaces read_roots. cap bounds
+ * offsets / lengths; *n receives the root count. */
+int wc_roots_file_split(const uint8_t* file, size_t len, uint64_t* offsets, uint64_t* lengths, size_t cap,
+                        size_t* n);
+
+/* ---- rules over encoded states ------------------------------------------- */
+/* A State in the reference's write_state encoding (the State part of a root).
+ * wc_state_legal_actions replaces State::legal_actions
+ * (engine/src/rules.rs:1027-1146): the action codes (Action::encode,
+ * engine/src/actions.rs:252-295) in the engine's order, deduplicated; cap
+ * bounds codes, *n receives the count. wc_state_apply replaces
+ * State::apply (engine/src/rules.rs:1155): the successor state, in the same
+ * encoding. With unchecked == 0 an action that is not legal in the state is
+ * refused (WC_E_ARG). With unchecked != 0 it is applied as the reference's
+ * apply does, without a legality test (its own tests apply hand-picked
+ * actions that way, e.g. an attack between non-adjacent hexes): the action
+ * must still name in-range fields and a unit on its source hex, else it is
+ * refused (where the reference would panic). Every call refuses a state
+ * whose fields are out of range (WC_E_ARG).
+ * wc_state_query writes 4 values: to_act (state.rs), winner (-1 = none),
+ * is_terminal, is_chance. */
+int wc_state_legal_actions(const uint8_t* state, size_t len, uint32_t* codes, size_t cap, size_t* n);
+int wc_state_apply(const uint8_t* state, size_t len, uint32_t code, int unchecked, uint8_t* out, size_t cap,
+                   size_t* out_len);
+int wc_state_query(const uint8_t* state, size_t len, int32_t* out);
 
 /* ---- batched solves ------------------------------------------------------ */
 /* Synchronous: upload, solve and download n jobs on device 0 of the
@@ -218,11 +253,13 @@ int wc_debug_umma_gemm(const uint16_t* a, const uint16_t* b, int k, int n, float
  * outputs and kernel; the device copies of a and b, the result and a status
  * word live in one static device array of 327,936 bytes that every GPU
  * loading this library holds until exit, so k <= 256 (n <= 256 as before);
- * larger k is rejected with WC_E_ARG. The first call on a device looks up the
- * array's device address (cudaGetSymbolAddress); make that first call before
- * any stream capture. All calls share the one array: calls that overlap on
- * the GPU (from several host threads, say) race and must be serialised by the
- * caller. */
+ * larger k is rejected with WC_E_ARG. The call runs on a private
+ * non-blocking stream and waits for that stream only (copies from and to
+ * pageable host memory). The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress) and creates that stream; make that
+ * first call before any stream capture. All calls share the one array: calls
+ * that overlap on the GPU (from several host threads, say) race and must be
+ * serialised by the caller. */
 int wc_debug_umma_gemm_static(const uint16_t* a, const uint16_t* b, int k, int n, float* d);
 
 /* ---- streaming submit / wait ---------------------------------------------- */

@@ -55,6 +55,25 @@ def test_static_scratch_gemm_matches_allocating_entry_point(wc):
         np.testing.assert_array_equal(got, want)
 
 
+def test_static_scratch_gemm_small_then_large(wc):
+    """A small static call, a small allocating call, then the largest static
+    call: each launch must be allowed the shared memory it needs whatever ran
+    before it, so the large call returns its own product, not the small
+    call's leftovers in the shared array."""
+    lib = wc.lib()
+    rng = np.random.default_rng(7)
+    order = [("wc_debug_umma_gemm_static", 64, 16), ("wc_debug_umma_gemm", 64, 16),
+             ("wc_debug_umma_gemm_static", 256, 256)]
+    for fn, k, n in order:
+        a = bf16_bits(rng.standard_normal((128, k)))
+        b = bf16_bits(rng.standard_normal((n, k)))
+        rc_ref, want = gemm(lib, "wc_debug_umma_gemm", a, b)
+        assert rc_ref == 0, last_error(lib)
+        rc, got = gemm(lib, fn, a, b)
+        assert rc == 0, last_error(lib)
+        np.testing.assert_array_equal(got, want)
+
+
 def test_static_scratch_gemm_refuses_oversize(wc):
     lib = wc.lib()
     a = np.zeros((128, 320), np.uint16)

@@ -391,6 +391,81 @@ int build_one(const uint8_t* root, size_t len, const SolveCfg& sc, const float* 
 
 }  // namespace
 
+// ---- rules over the reference's State encoding (write_state, roots.rs:150-180)
+
+namespace {
+bool parse_state(const uint8_t* st, size_t len, State* s) {
+    size_t at = 0;
+    return st && read_state(st, len, &at, s) && at == len;
+}
+}  // namespace
+
+int wc_state_legal_actions(const uint8_t* state, size_t len, uint32_t* codes, size_t cap, size_t* n) {
+    return guarded([&] {
+        State s;
+        if (!parse_state(state, len, &s)) return fail(WC_E_ARG, "malformed state bytes");
+        std::vector<Action> acts = s.legal_actions();
+        if (n) *n = acts.size();
+        if (acts.size() > cap || (!codes && !acts.empty())) return fail(WC_E_ARG, "action buffer too small");
+        for (size_t i = 0; i < acts.size(); ++i) codes[i] = acts[i].encode();
+        return (int)WC_OK;
+    });
+}
+
+int wc_state_apply(const uint8_t* state, size_t len, uint32_t code, int unchecked, uint8_t* out, size_t cap,
+                   size_t* out_len) {
+    return guarded([&] {
+        State s;
+        if (!parse_state(state, len, &s)) return fail(WC_E_ARG, "malformed state bytes");
+        Action a;
+        if (!Action::decode(code, &a)) return fail(WC_E_ARG, "undecodable action code");
+        if (!unchecked) {
+            bool legal = false;
+            for (const Action& x : s.legal_actions()) legal = legal || x == a;
+            if (!legal) return fail(WC_E_ARG, "action " + a.to_string() + " is not legal in this state");
+        } else if (!action_well_formed(s, a)) {
+            return fail(WC_E_ARG, "action " + a.to_string() + " names an empty hex, a missing unit or a field "
+                                  "out of range");
+        }
+        s.apply_inplace(a);
+        std::vector<uint8_t> b;
+        write_state(b, s);
+        if (out_len) *out_len = b.size();
+        if (!out || b.size() > cap) return fail(WC_E_ARG, "state buffer too small");
+        std::memcpy(out, b.data(), b.size());
+        return (int)WC_OK;
+    });
+}
+
+int wc_state_query(const uint8_t* state, size_t len, int32_t* out) {
+    return guarded([&] {
+        State s;
+        if (!out || !parse_state(state, len, &s)) return fail(WC_E_ARG, "malformed state bytes");
+        out[0] = s.to_act();
+        out[1] = s.winner == NONE ? -1 : (int32_t)s.winner;
+        out[2] = s.is_terminal() ? 1 : 0;
+        out[3] = s.is_chance() ? 1 : 0;
+        return (int)WC_OK;
+    });
+}
+
+int wc_roots_file_split(const uint8_t* file, size_t len, uint64_t* offsets, uint64_t* lengths, size_t cap,
+                        size_t* n) {
+    return guarded([&] {
+        std::vector<std::pair<size_t, size_t>> spans;
+        if (!file || !roots_file_split(file, len, &spans))
+            return fail(WC_E_ARG, "not a version-3 roots file, or a malformed root in it");
+        if (n) *n = spans.size();
+        if (spans.size() > cap || (!spans.empty() && (!offsets || !lengths)))
+            return fail(WC_E_ARG, "span buffers too small");
+        for (size_t i = 0; i < spans.size(); ++i) {
+            offsets[i] = spans[i].first;
+            lengths[i] = spans[i].second;
+        }
+        return (int)WC_OK;
+    });
+}
+
 int wc_root_generate_wide(uint64_t seed, int plies, int random_draft, uint32_t ncfg, uint8_t* buf, size_t cap,
                           size_t* len) {
     return guarded([&] {

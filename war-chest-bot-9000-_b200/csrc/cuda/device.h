@@ -100,6 +100,7 @@ struct FastNetDev {
     const float* stem_w;        // [6][96] the hex stem weights (16-byte aligned copy)
     const float* stem_pb;       // [37][96] the hex's position embedding plus the hex stem bias
     int half;                   // operand type of every tile and stored row: 1 = f16, 0 = bf16
+    uint64_t wait_ns;           // limit of each mbarrier wait, ns of %globaltimer (umma::WAIT_NS)
 };
 
 struct WorkItem {

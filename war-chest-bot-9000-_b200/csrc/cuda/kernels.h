@@ -51,7 +51,7 @@ int umma_selftest(const uint16_t* A, const uint16_t* B, int K, int N, float* D);
 // 5 the array's device address could not be looked up.
 int umma_selftest_static(const uint16_t* A, const uint16_t* B, int K, int N, float* D);
 void launch_pool_fast(const JobDev* jobs, const void* tiles, uint32_t ntiles, int mask, uint16_t* pool_img, float* mass,
-                      bool half, int* err, cudaStream_t s);
+                      bool half, int* err, uint64_t wait_ns, cudaStream_t s);
 void launch_join_fast(const JobDev* jobs, const void* tiles, uint32_t ntiles, const FastNetDev& fn, int p,
                       const uint16_t* pool_img, const uint16_t* jp, uint16_t* zout_img, int* err, cudaStream_t s);
 void launch_head_fast(const JobDev* jobs, const void* tiles, uint32_t ntiles, const FastNetDev& fn, int p,

@@ -58,28 +58,41 @@ __global__ void k_umma_selftest(const __nv_bfloat16* __restrict__ A, const __nv_
                            idesc, k0 > 0);
         umma::commit(&mbar);
     }
-    bool ok = umma::mbar_wait(&mbar, 0);
+    __shared__ int drained;
+    const bool ok = umma::mbar_wait(&mbar, 0);
+    umma::fence_before_sync();
+    const bool bad = __syncthreads_or(!ok) != 0;
     umma::fence_after_sync();
-    if (!ok) {
-        if (tid == 0) *status = 1;
-    } else {
+    if (!bad) {
         float v[32];
         for (int c = 0; c < N; c += 32) {
             umma::tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + c, v);
             for (int j = 0; j < 32 && c + j < N; ++j) D[(size_t)tid * N + c + j] = v[j];
         }
     }
+    if (tid == 0) {
+        // the product still runs after a timed-out wait: it must finish before
+        // the tensor memory is released (if it never does, the memory stays
+        // allocated, status 2, and the context can no longer be trusted)
+        drained = bad ? (umma::mbar_wait(&mbar, 0, umma::DRAIN_NS) ? 1 : 0) : 1;
+        if (bad) *status = drained ? 1 : 2;
+    }
     umma::fence_before_sync();
     __syncthreads();
-    if (warp == 0) umma::tmem_dealloc(tmem, ncols);
+    umma::fence_after_sync();
+    if (warp == 0 && drained) umma::tmem_dealloc(tmem, ncols);
 }
+
+// The self-test kernel's dynamic shared-memory limit: the most a CTA may use
+// (227 KB). Both entry points set this one value on every call, so no call
+// can leave the limit below what another call's launch needs.
+constexpr int SELFTEST_SMEM_MAX = 227 * 1024;
 
 // ------------------------------------------------------------- fast kernels
 
 constexpr int POOL = wc::NET_POOL, JW = wc::NET_JW, D = wc::NET_D;
 constexpr uint32_t TILE_J = 128u * 128u * 2u;  // one [128][128] 16-bit operand tile
 constexpr uint32_t ATOM = 128u * 128u;         // one 128-row x 64-column atom of 16-bit operands
-constexpr uint32_t WAIT_LIMIT = 1u << 26;
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
     return p + ((1024u - (umma::smem_u32(p) & 1023u)) & 1023u);
@@ -204,7 +217,13 @@ __global__ void __launch_bounds__(128, 3)
         load_weight(0);
         if (blockIdx.x + gridDim.x < ntiles) prefetch_jp(blockIdx.x + gridDim.x);
     }
+    // The parity each barrier completes next (the same in every thread);
+    // pend_in / pend_w (thread 0, which issues the copies) and pend_mma (every
+    // thread) mark work issued but not yet seen to complete. Every stop
+    // decision is block-uniform (__syncthreads_or), and nothing is issued
+    // after a failed wait.
     uint32_t ph_in = 0, ph_w = 0, ph_mma = 0;
+    bool pend_mma = false, dead = false;
     uint64_t k = 0;
     const uint32_t idesc = umma::idesc16(128, 128, umma::Op16<H>::fmt);
     for (uint32_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
@@ -236,27 +255,41 @@ __global__ void __launch_bounds__(128, 3)
         umma::fence_after_sync();
 #pragma unroll 1
         for (int L = 0; L < 4; ++L, ++k) {
-            if (tid == 0) {
+            // the layer's operands: the pooled images (first layer) and its
+            // weight tile; the previous layer's A writes precede this barrier
+            {
                 bool ok = true;
+                if (tid == 0) {
+                    if (L == 0) ok = umma::mbar_wait(&bar_in, ph_in, fn.wait_ns);
+                    ok = ok && umma::mbar_wait(&bar_w, ph_w, fn.wait_ns);
+                }
+                dead = __syncthreads_or(!ok) != 0;
+                umma::fence_after_sync();
+                if (dead) break;
                 if (L == 0) {
-                    ok = umma::mbar_wait(&bar_in, ph_in, WAIT_LIMIT) && ok;
+                    ph_in ^= 1u;
                     pend_in = false;
                 }
-                ok = umma::mbar_wait(&bar_w, ph_w, WAIT_LIMIT) && ok;
+                ph_w ^= 1u;
                 pend_w = false;
-                if (!ok) abort_flag = 1;
-                umma::fence_after_sync();
+            }
+            if (tid == 0) {
                 const uint32_t a = umma::smem_u32(sA), b = umma::smem_u32(sWt);
 #pragma unroll
                 for (int k0 = 0; k0 < JW; k0 += 16)
                     umma::mma16(tmem, umma::desc_at(a, 128, k0), umma::desc_at(b, 128, k0), idesc, 1u);
                 umma::commit(&bar_mma);
             }
-            if (L == 0) ph_in ^= 1u;
-            ph_w ^= 1u;
-            if (!umma::mbar_wait(&bar_mma, ph_mma, WAIT_LIMIT)) abort_flag = 1;
-            ph_mma ^= 1u;
-            umma::fence_after_sync();
+            pend_mma = true;
+            {
+                const bool ok = umma::mbar_wait(&bar_mma, ph_mma, fn.wait_ns);
+                umma::fence_before_sync();
+                dead = __syncthreads_or(!ok) != 0;
+                umma::fence_after_sync();
+                if (dead) break;
+                ph_mma ^= 1u;
+                pend_mma = false;
+            }
             if (tid == 0) {  // the slot and (after the last layer) sA are free again
                 if (k + 1 < uses) load_weight(k + 1);
                 if (L == 3 && t + gridDim.x < ntiles) load_pooled(t + gridDim.x);
@@ -312,26 +345,31 @@ __global__ void __launch_bounds__(128, 3)
                         *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(zout_img) + (size_t)t * TILE_J + off) = o;
                 }
             }
-            if (L < 3) {
+            if (L < 3) {  // the next layer's operand wait is the barrier
                 umma::fence_async_smem();
                 umma::fence_before_sync();
-                __syncthreads();
-                umma::fence_after_sync();
             }
         }
+        if (dead) break;
         __syncthreads();
-        if (abort_flag) break;
     }
+    // Copies and a product still in flight after an early exit complete on
+    // their own and must land before the shared memory and the tensor memory
+    // go away. A drain that does not finish leaves the tensor memory
+    // allocated and reports code 11: the device context can no longer be
+    // trusted.
     if (tid == 0) {
-        if (abort_flag) atomicExch(err, 1);
-        // copies still in flight after an early exit must land before the
-        // shared memory goes away
-        if (pend_in) umma::mbar_wait(&bar_in, ph_in, WAIT_LIMIT);
-        if (pend_w) umma::mbar_wait(&bar_w, ph_w, WAIT_LIMIT);
+        bool drained = true;
+        if (pend_mma) drained = umma::mbar_wait(&bar_mma, ph_mma, umma::DRAIN_NS) && drained;
+        if (pend_in) drained = umma::mbar_wait(&bar_in, ph_in, umma::DRAIN_NS) && drained;
+        if (pend_w) drained = umma::mbar_wait(&bar_w, ph_w, umma::DRAIN_NS) && drained;
+        abort_flag = drained ? 0 : 1;
+        if (dead || !drained) atomicExch(err, drained ? 1 : 11);
     }
     umma::fence_before_sync();
     __syncthreads();
-    if (warp == 0) umma::tmem_dealloc(tmem, 128);
+    umma::fence_after_sync();
+    if (warp == 0 && !abort_flag) umma::tmem_dealloc(tmem, 128);
 }
 
 // Pooled belief embeddings (search.rs:1512-1547) of one 128-row tile on the
@@ -346,7 +384,7 @@ __global__ void __launch_bounds__(128, 3)
 template <bool H>
 __global__ void __launch_bounds__(128, 4)
     k_pool_fast(const JobDev* __restrict__ jobs, const HeadTile* __restrict__ tiles, uint32_t ntiles, int mask,
-                uint16_t* __restrict__ pool_img, float* __restrict__ mass, int* __restrict__ err) {
+                uint16_t* __restrict__ pool_img, float* __restrict__ mass, int* __restrict__ err, uint64_t wait_ns) {
     extern __shared__ uint8_t smem_raw[];
     __shared__ uint64_t bar_g, bar_mma;
     __shared__ uint32_t tmem_slot;
@@ -368,7 +406,11 @@ __global__ void __launch_bounds__(128, 4)
     const uint32_t tmem = tmem_slot;
     const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
     const uint32_t idesc = umma::idesc16(128, 64, umma::Op16<H>::fmt);
+    // Parities and pending work as in the join: the same in every thread
+    // (pend_g is thread 0's, which issues the copy), stop decisions
+    // block-uniform, nothing issued after a failed wait.
     uint32_t ph_g = 0, ph_mma = 0;
+    bool pend_g = false, pend_mma = false, dead = false;
     for (uint32_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
         const HeadTile ht = tiles[t];
         const JobDev& J = jobs[ht.job];
@@ -415,6 +457,7 @@ __global__ void __launch_bounds__(128, 4)
                 if (tid == 0) {
                     umma::expect_tx(&bar_g, ATOM);
                     umma::bulk_g2s(sG, gsrc + (size_t)c * ATOM, ATOM, &bar_g);
+                    pend_g = true;
                 }
 #pragma unroll
                 for (int k = 0; k < 128; k += 8)
@@ -432,13 +475,18 @@ __global__ void __launch_bounds__(128, 4)
                         *reinterpret_cast<uint16_t*>(sBeta + umma::sw128_offset(128, tid, col)) =
                             umma::Op16<H>::one(w[e] * scale + flat);
                 }
-                umma::fence_async_smem();
-                umma::fence_before_sync();
-                __syncthreads();
-                umma::fence_after_sync();
-                if (tid == 0) {
-                    if (!umma::mbar_wait(&bar_g, ph_g, WAIT_LIMIT)) abort_flag = 1;
+                {  // the scatter is done and (thread 0) the g chunk has landed
+                    bool ok = true;
+                    if (tid == 0) ok = umma::mbar_wait(&bar_g, ph_g, wait_ns);
+                    umma::fence_async_smem();
+                    umma::fence_before_sync();
+                    dead = __syncthreads_or(!ok) != 0;
                     umma::fence_after_sync();
+                    if (dead) break;
+                    ph_g ^= 1u;
+                    pend_g = false;
+                }
+                if (tid == 0) {
                     const uint32_t a = umma::smem_u32(sBeta), b = umma::smem_u32(sG);
 #pragma unroll
                     for (int k0 = 0; k0 < 128; k0 += 16)
@@ -446,11 +494,18 @@ __global__ void __launch_bounds__(128, 4)
                                     (c > 0 || k0 > 0) ? 1u : 0u);
                     umma::commit(&bar_mma);
                 }
-                ph_g ^= 1u;
-                if (!umma::mbar_wait(&bar_mma, ph_mma, WAIT_LIMIT)) abort_flag = 1;
-                ph_mma ^= 1u;
-                umma::fence_after_sync();
+                pend_mma = true;
+                {
+                    const bool ok = umma::mbar_wait(&bar_mma, ph_mma, wait_ns);
+                    umma::fence_before_sync();
+                    dead = __syncthreads_or(!ok) != 0;
+                    umma::fence_after_sync();
+                    if (dead) break;
+                    ph_mma ^= 1u;
+                    pend_mma = false;
+                }
             }
+            if (dead) break;
             // the row of the player's pooled atom in the tile image
             uint8_t* img = reinterpret_cast<uint8_t*>(pool_img) + (size_t)t * (2 * ATOM) + q * ATOM + tid * 128;
 #pragma unroll
@@ -470,12 +525,21 @@ __global__ void __launch_bounds__(128, 4)
             __syncthreads();  // TMEM and sBeta are reused by the next player or tile
             umma::fence_after_sync();
         }
-        if (abort_flag) break;
+        if (dead) break;
     }
-    if (tid == 0 && abort_flag) atomicExch(err, 4);
+    // Drain what an early exit left in flight; code 14 when a drain does not
+    // finish (the tensor memory then stays allocated).
+    if (tid == 0) {
+        bool drained = true;
+        if (pend_mma) drained = umma::mbar_wait(&bar_mma, ph_mma, umma::DRAIN_NS) && drained;
+        if (pend_g) drained = umma::mbar_wait(&bar_g, ph_g, umma::DRAIN_NS) && drained;
+        abort_flag = drained ? 0 : 1;
+        if (dead || !drained) atomicExch(err, drained ? 4 : 14);
+    }
     umma::fence_before_sync();
     __syncthreads();
-    if (warp == 0) umma::tmem_dealloc(tmem, 64);
+    umma::fence_after_sync();
+    if (warp == 0 && !abort_flag) umma::tmem_dealloc(tmem, 64);
 }
 
 // The join output layer, the readout LayerNorm and the per-config readout for
@@ -511,7 +575,7 @@ __global__ void __launch_bounds__(544, 1)
     extern __shared__ uint8_t smem_raw[];
     __shared__ uint64_t bar_y, bar_v, bar_a, bar_f, bar_p, h_ready, s_done;
     __shared__ uint32_t tmem_slot;
-    __shared__ int abort_flag;
+    __shared__ int abort_flag, stuck;
     __shared__ uint32_t gb2[D];   // f16: the LayerNorm's (gamma, beta) per column pair, packed
     uint8_t* smem = align1024(smem_raw);
     uint8_t* sW = smem;                  // [256][128] Wout: 64 KB
@@ -536,6 +600,7 @@ __global__ void __launch_bounds__(544, 1)
         umma::mbar_init(&s_done, NWORK / 32);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         abort_flag = 0;
+        stuck = 0;
     }
     if (warp == 16) umma::tmem_alloc(&tmem_slot, 512);
     umma::fence_async_smem();
@@ -548,17 +613,14 @@ __global__ void __launch_bounds__(544, 1)
     // recorded an abort (so no role waits out its limit on a dead partner)
     auto wait = [&](uint64_t* bar, uint32_t parity) {
         const uint32_t addr = umma::smem_u32(bar);
-        for (uint32_t i = 0; i < WAIT_LIMIT; ++i) {
-            uint32_t done;
-            asm volatile(
-                "{\n\t.reg .pred q;\n\t"
-                "mbarrier.try_wait.parity.shared::cta.b64 q, [%1], %2;\n\t"
-                "selp.u32 %0, 1, 0, q;\n\t}\n"
-                : "=r"(done)
-                : "r"(addr), "r"(parity)
-                : "memory");
-            if (done) return true;
-            if ((i & 15u) == 15u && *abort_v) return false;
+        if (umma::mbar_test(addr, parity)) return true;
+        const uint64_t t0 = umma::now_ns();
+        for (uint32_t i = 1;; ++i) {
+            if (umma::mbar_test(addr, parity)) return true;
+            if ((i & 15u) == 0u) {
+                if (*abort_v) return false;
+                if (umma::now_ns() - t0 >= fn.wait_ns) break;
+            }
         }
         *abort_v = 1;
         return false;
@@ -677,13 +739,18 @@ __global__ void __launch_bounds__(544, 1)
                     if (jobs[jn].ncfg_player[p]) load_f(jn, 0);
                 }
             }
-            if (!ok) atomicExch(err, 2);
-            // nothing may be in flight when the tensor memory is released
-            if (pend_y) umma::mbar_wait(&bar_y, ph_y, WAIT_LIMIT);
-            if (pend_v) umma::mbar_wait(&bar_v, ph_v ^ 1u, WAIT_LIMIT);
-            if (pend_a) umma::mbar_wait(&bar_a, ph_a, WAIT_LIMIT);
-            if (pend_f) umma::mbar_wait(&bar_f, ph_f, WAIT_LIMIT);
-            if (pend_p) umma::mbar_wait(&bar_p, ph_p ^ 1u, WAIT_LIMIT);
+            // nothing may be in flight when the shared and tensor memory are
+            // released: issued products and copies complete on their own.
+            // A drain that does not finish leaves the tensor memory allocated
+            // and reports code 12 (the device context can no longer be trusted).
+            bool drained = true;
+            if (pend_y) drained = umma::mbar_wait(&bar_y, ph_y, umma::DRAIN_NS) && drained;
+            if (pend_v) drained = umma::mbar_wait(&bar_v, ph_v ^ 1u, umma::DRAIN_NS) && drained;
+            if (pend_a) drained = umma::mbar_wait(&bar_a, ph_a, umma::DRAIN_NS) && drained;
+            if (pend_f) drained = umma::mbar_wait(&bar_f, ph_f, umma::DRAIN_NS) && drained;
+            if (pend_p) drained = umma::mbar_wait(&bar_p, ph_p ^ 1u, umma::DRAIN_NS) && drained;
+            stuck = drained ? 0 : 1;
+            if (!ok || !drained) atomicExch(err, drained ? 2 : 12);
         }
         __syncwarp();
     } else {
@@ -879,7 +946,8 @@ __global__ void __launch_bounds__(544, 1)
     }
     umma::fence_before_sync();
     __syncthreads();
-    if (warp == 16) umma::tmem_dealloc(tmem, 512);
+    umma::fence_after_sync();
+    if (warp == 16 && !stuck) umma::tmem_dealloc(tmem, 512);
 }
 
 // f(c) of every config as the readout's B-operand images: for each player,
@@ -913,13 +981,14 @@ static int num_sms() {
 }
 
 void launch_pool_fast(const JobDev* jobs, const void* tiles, uint32_t ntiles, int mask, uint16_t* pool_img, float* mass,
-                      bool half, int* err, cudaStream_t s) {
+                      bool half, int* err, uint64_t wait_ns, cudaStream_t s) {
     if (!ntiles || !mask) return;
     const size_t smem = TILE_J + ATOM + 1024;
     auto kern = half ? k_pool_fast<true> : k_pool_fast<false>;
     if (!raise_smem_limit((const void*)kern, smem)) return;
     const uint32_t grid = std::min<uint32_t>(ntiles, 4u * (uint32_t)num_sms());
-    kern<<<grid, 128, smem, s>>>(jobs, reinterpret_cast<const HeadTile*>(tiles), ntiles, mask, pool_img, mass, err);
+    kern<<<grid, 128, smem, s>>>(jobs, reinterpret_cast<const HeadTile*>(tiles), ntiles, mask, pool_img, mass, err,
+                                 wait_ns);
 }
 
 bool raise_smem_limit(const void* fn, size_t smem) {
@@ -963,30 +1032,35 @@ void launch_pack_f16(const JobDev* jobs, const uint32_t* cfg_job, const uint32_t
 }
 
 int umma_selftest(const uint16_t* A, const uint16_t* B, int K, int N, float* D) {
-    if (K % 64 || N % 16 || N < 16 || N > 256) return 1;
-    __nv_bfloat16 *dA, *dB;
-    float* dD;
-    int* dS;
-    cudaMalloc(&dA, 128ull * K * 2);
-    cudaMalloc(&dB, (size_t)N * K * 2);
-    cudaMalloc(&dD, 128ull * N * 4);
-    cudaMalloc(&dS, 4);
-    cudaMemcpy(dA, A, 128ull * K * 2, cudaMemcpyHostToDevice);
-    cudaMemcpy(dB, B, (size_t)N * K * 2, cudaMemcpyHostToDevice);
-    cudaMemset(dS, 0, 4);
-    size_t smem = 128ull * K * 2 + (size_t)N * K * 2 + 1024;
-    cudaFuncSetAttribute(k_umma_selftest, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    k_umma_selftest<<<1, 128, smem>>>(dA, dB, K, N, dD, dS);
-    int status = 0;
-    cudaError_t e = cudaDeviceSynchronize();
-    cudaMemcpy(D, dD, 128ull * N * 4, cudaMemcpyDeviceToHost);
-    cudaMemcpy(&status, dS, 4, cudaMemcpyDeviceToHost);
+    if (K <= 0 || K % 64 || N % 16 || N < 16 || N > 256) return 1;
+    const size_t a_bytes = 128ull * K * 2, b_bytes = (size_t)N * K * 2, d_bytes = 128ull * N * 4;
+    const size_t smem = a_bytes + b_bytes + 1024;
+    if (smem > (size_t)SELFTEST_SMEM_MAX) return 1;
+    __nv_bfloat16 *dA = nullptr, *dB = nullptr;
+    float* dD = nullptr;
+    int* dS = nullptr;
+    int status = 0, rc = 0;
+    if (cudaMalloc(&dA, a_bytes) != cudaSuccess || cudaMalloc(&dB, b_bytes) != cudaSuccess ||
+        cudaMalloc(&dD, d_bytes) != cudaSuccess || cudaMalloc(&dS, 4) != cudaSuccess ||
+        cudaMemcpy(dA, A, a_bytes, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(dB, B, b_bytes, cudaMemcpyHostToDevice) != cudaSuccess || cudaMemset(dS, 0, 4) != cudaSuccess ||
+        cudaFuncSetAttribute(k_umma_selftest, cudaFuncAttributeMaxDynamicSharedMemorySize, SELFTEST_SMEM_MAX) !=
+            cudaSuccess) {
+        rc = 2;
+    } else {
+        k_umma_selftest<<<1, 128, smem>>>(dA, dB, K, N, dD, dS);
+        if (cudaGetLastError() != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess ||
+            cudaMemcpy(D, dD, d_bytes, cudaMemcpyDeviceToHost) != cudaSuccess ||
+            cudaMemcpy(&status, dS, 4, cudaMemcpyDeviceToHost) != cudaSuccess)
+            rc = 2;
+        else if (status)
+            rc = 3;
+    }
     cudaFree(dA);
     cudaFree(dB);
     cudaFree(dD);
     cudaFree(dS);
-    if (e != cudaSuccess) return 2;
-    return status ? 3 : 0;
+    return rc;
 }
 
 // ------------------------------------------ allocation-free GEMM self-test
@@ -1003,49 +1077,64 @@ constexpr size_t SCR_STATUS = 0, SCR_A = 256, SCR_B = SCR_A + 128 * 256 * 2, SCR
 constexpr size_t STATIC_SCRATCH_BYTES = SCR_D + 128 * 256 * 4;  // 327,936 bytes
 static __device__ __align__(256) uint8_t g_gemm_scratch[STATIC_SCRATCH_BYTES];
 
-// Device address of g_gemm_scratch on the current device. Host code cannot
-// use the array's name as a device pointer (it names a host-side stand-in),
-// so the address is looked up once per device, on that device's first call.
-static uint8_t* gemm_scratch_address(cudaError_t* e) {
+// Per-device set-up of the static path: the device address of
+// g_gemm_scratch (host code cannot use the array's name as a device pointer:
+// it names a host-side stand-in) and a private non-blocking stream, so the
+// call synchronises with nothing but its own work. Done once per device, on
+// that device's first call, with the device current.
+struct StaticSetup {
+    uint8_t* scratch = nullptr;
+    cudaStream_t stream = nullptr;
+};
+
+static bool static_setup(StaticSetup* out) {
     static std::mutex mu;
-    static std::map<int, uint8_t*> addr;
+    static std::map<int, StaticSetup> per_dev;
     int dev = 0;
-    *e = cudaGetDevice(&dev);
-    if (*e != cudaSuccess) return nullptr;
+    if (cudaGetDevice(&dev) != cudaSuccess) return false;
     std::lock_guard<std::mutex> lock(mu);
-    auto it = addr.find(dev);
-    if (it != addr.end()) return it->second;
-    uint8_t* ptr = nullptr;
-    *e = cudaGetSymbolAddress((void**)&ptr, g_gemm_scratch);
-    if (*e != cudaSuccess) return nullptr;
-    addr[dev] = ptr;
-    return ptr;
+    auto it = per_dev.find(dev);
+    if (it != per_dev.end()) {
+        *out = it->second;
+        return true;
+    }
+    StaticSetup st;
+    if (cudaGetSymbolAddress((void**)&st.scratch, g_gemm_scratch) != cudaSuccess) return false;
+    if (cudaStreamCreateWithFlags(&st.stream, cudaStreamNonBlocking) != cudaSuccess) return false;
+    per_dev[dev] = st;
+    *out = st;
+    return true;
 }
 
 int umma_selftest_static(const uint16_t* A, const uint16_t* B, int K, int N, float* D) {
     if (K <= 0 || K % 64 || N % 16 || N < 16 || N > 256) return 1;
     if (K > 256) return 4;  // beyond the static scratch
-    cudaError_t e = cudaSuccess;
-    uint8_t* scr = gemm_scratch_address(&e);
-    if (!scr) return 5;
+    StaticSetup st;
+    if (!static_setup(&st)) return 5;
+    uint8_t* scr = st.scratch;
+    cudaStream_t s = st.stream;
     const size_t a_bytes = 128ull * K * 2, b_bytes = (size_t)N * K * 2, d_bytes = 128ull * N * 4;
     auto* dA = reinterpret_cast<__nv_bfloat16*>(scr + SCR_A);
     auto* dB = reinterpret_cast<__nv_bfloat16*>(scr + SCR_B);
     auto* dD = reinterpret_cast<float*>(scr + SCR_D);
     auto* dS = reinterpret_cast<int*>(scr + SCR_STATUS);
-    // The array keeps the previous call's contents: A, B and D are rewritten
-    // in full; the status word must start at zero.
-    if (cudaMemcpy(dA, A, a_bytes, cudaMemcpyHostToDevice) != cudaSuccess ||
-        cudaMemcpy(dB, B, b_bytes, cudaMemcpyHostToDevice) != cudaSuccess || cudaMemset(dS, 0, 4) != cudaSuccess)
+    // The array keeps the previous call's contents: A and B are rewritten in
+    // full, D in full by a successful kernel, and the status word must start
+    // at zero.
+    if (cudaMemcpyAsync(dA, A, a_bytes, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+        cudaMemcpyAsync(dB, B, b_bytes, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+        cudaMemsetAsync(dS, 0, 4, s) != cudaSuccess)
         return 2;
-    size_t smem = a_bytes + b_bytes + 1024;
-    if (!raise_smem_limit((const void*)k_umma_selftest, smem)) return 2;
-    k_umma_selftest<<<1, 128, smem>>>(dA, dB, K, N, dD, dS);
+    if (cudaFuncSetAttribute(k_umma_selftest, cudaFuncAttributeMaxDynamicSharedMemorySize, SELFTEST_SMEM_MAX) !=
+        cudaSuccess)
+        return 2;
+    const size_t smem = a_bytes + b_bytes + 1024;
+    k_umma_selftest<<<1, 128, smem, s>>>(dA, dB, K, N, dD, dS);
+    if (cudaGetLastError() != cudaSuccess) return 2;  // not launched: D would be a previous call's
     int status = 0;
-    e = cudaDeviceSynchronize();
-    if (e != cudaSuccess) return 2;
-    if (cudaMemcpy(D, dD, d_bytes, cudaMemcpyDeviceToHost) != cudaSuccess ||
-        cudaMemcpy(&status, dS, 4, cudaMemcpyDeviceToHost) != cudaSuccess)
+    if (cudaMemcpyAsync(D, dD, d_bytes, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaMemcpyAsync(&status, dS, 4, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess)
         return 2;
     return status ? 3 : 0;
 }

@@ -41,7 +41,6 @@ constexpr uint32_t OUT_BYTES = 96 * 2 * 128;   // [96][96]: 2 atoms (second half
 constexpr uint32_t BLOCK_BYTES = MIX_BYTES + OUT_BYTES;  // 61440
 constexpr uint32_t A1_BYTES = 128 * 3 * 128;   // [128][192]
 constexpr uint32_t A2_BYTES = 128 * 2 * 128;   // [128][96]
-constexpr uint32_t WAIT_LIMIT = 1u << 26;
 
 // One elected thread: fetch a block's weight tiles into `dst`.
 __device__ __forceinline__ void fetch_block(uint8_t* dst, const uint8_t* tiles, int blk, uint64_t* bar) {
@@ -204,8 +203,15 @@ __global__ void __launch_bounds__(384, 1)
         const uint8_t nbh = real_row ? c_nbt[hex][d] : (uint8_t)255;
         nbr[d] = nbh == 255 ? -1 : board * NH + nbh;
     }
+    // Barrier bookkeeping, identical in every thread (each decision below is
+    // block-uniform): the parity each barrier completes next, and whether an
+    // issued copy or product has not yet been seen to complete on it.
     uint32_t wphase[2] = {0, 0}, mphase = 0;
-    if (tid == 0 && blockIdx.x < ntiles) fetch_block(sW[0], tiles, 0, &S.wbar[0]);
+    bool wpend[2] = {false, false}, mpend = false, dead = false;
+    if (blockIdx.x < ntiles) {
+        if (tid == 0) fetch_block(sW[0], tiles, 0, &S.wbar[0]);
+        wpend[0] = true;
+    }
 
     for (uint32_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
         // ---------------------------------------------------------- stem
@@ -448,12 +454,16 @@ __global__ void __launch_bounds__(384, 1)
             rows_gemm<BOARDS, 2 * C, C, 4, 1, 16>(&S.pooled[0][0], 2 * C, W + L.pool[blk].w, fn.trunk_pb + blk * C,
                                                   &S.gb[0][0], C, S.part);
             // mix product (weights of this block must have landed)
-            if (!umma::mbar_wait(&S.wbar[buf], wphase[buf], WAIT_LIMIT)) S.abort_flag = 1;
-            wphase[buf] ^= 1u;
-            umma::fence_async_smem();
-            umma::fence_before_sync();
-            __syncthreads();
-            umma::fence_after_sync();
+            {
+                const bool ok = umma::mbar_wait(&S.wbar[buf], wphase[buf], fn.wait_ns);
+                umma::fence_async_smem();
+                umma::fence_before_sync();
+                dead = __syncthreads_or(!ok) != 0;
+                umma::fence_after_sync();
+                if (dead) break;  // the copy stays pending: drained at the exit
+                wphase[buf] ^= 1u;
+                wpend[buf] = false;
+            }
             if (tid == 0) {
                 const uint32_t aa = umma::smem_u32(sA1), wb = umma::smem_u32(sW[buf]);
                 const uint32_t idesc = umma::idesc16(128, 96, umma::Op16<H>::fmt);
@@ -462,9 +472,16 @@ __global__ void __launch_bounds__(384, 1)
                     umma::mma16(tmem, umma::desc_at(aa, 128, k0), umma::desc_at(wb, 96, k0), idesc, k0 > 0);
                 umma::commit(&S.mbar);
             }
-            if (!umma::mbar_wait(&S.mbar, mphase, WAIT_LIMIT)) S.abort_flag = 1;
-            mphase ^= 1u;
-            umma::fence_after_sync();
+            mpend = true;
+            {
+                const bool ok = umma::mbar_wait(&S.mbar, mphase, fn.wait_ns);
+                umma::fence_before_sync();
+                dead = __syncthreads_or(!ok) != 0;
+                umma::fence_after_sync();
+                if (dead) break;
+                mphase ^= 1u;
+                mpend = false;
+            }
             // y = mix + (b_mix + pooled W_pool + b_pool); LNGELU -> A2
             float y[32];
             {
@@ -514,13 +531,20 @@ __global__ void __launch_bounds__(384, 1)
                     umma::mma16(tmem + 128, umma::desc_at(aa, 128, k0), umma::desc_at(wb, 96, k0), idesc, k0 > 0);
                 umma::commit(&S.mbar);
             }
-            if (!umma::mbar_wait(&S.mbar, mphase, WAIT_LIMIT)) S.abort_flag = 1;
-            mphase ^= 1u;
-            umma::fence_after_sync();
+            mpend = true;
+            {
+                const bool ok = umma::mbar_wait(&S.mbar, mphase, fn.wait_ns);
+                umma::fence_before_sync();
+                dead = __syncthreads_or(!ok) != 0;
+                umma::fence_after_sync();
+                if (dead) break;
+                mphase ^= 1u;
+                mpend = false;
+            }
             // the other buffer is free: fetch the next block (or the next tile's first)
-            if (tid == 0) {
-                const bool more = blk + 1 < wc::NET_BLOCKS || tile + gridDim.x < ntiles;
-                if (more) fetch_block(sW[buf ^ 1], tiles, (blk + 1) % wc::NET_BLOCKS, &S.wbar[buf ^ 1]);
+            if (blk + 1 < wc::NET_BLOCKS || tile + gridDim.x < ntiles) {
+                if (tid == 0) fetch_block(sW[buf ^ 1], tiles, (blk + 1) % wc::NET_BLOCKS, &S.wbar[buf ^ 1]);
+                wpend[buf ^ 1] = true;
             }
             {
                 float v[32];
@@ -535,8 +559,8 @@ __global__ void __launch_bounds__(384, 1)
                     x[4 * j4 + 3] += v[4 * j4 + 3] + b4.w;
                 }
             }
-            if (S.abort_flag) break;
         }
+        if (dead) break;
         // -------------------------------------- final norm and the readout
         {
             float s = 0.0f;
@@ -647,12 +671,26 @@ __global__ void __launch_bounds__(384, 1)
                 g_jp[(size_t)gb_[i] * JW + c] = umma::Op16<H>::one(Hd.jp[i][c] - S.gb[i][1]);
         }
         __syncthreads();
-        if (S.abort_flag) break;
     }
-    if (tid == 0 && S.abort_flag) atomicExch(err, 3);
+    // Every thread leaves the loops at the same point (`dead` comes from
+    // __syncthreads_or). Nothing was issued after a failed wait, so what may
+    // still be in flight is exactly what is marked pending: it completes on
+    // its own and must land before the shared memory and the tensor memory
+    // are released. A drain that does not finish leaves the tensor memory
+    // allocated (a product may still write it) and reports code 13: the
+    // device context can no longer be trusted.
+    if (tid == 0) {
+        bool drained = true;
+        if (mpend) drained = umma::mbar_wait(&S.mbar, mphase, umma::DRAIN_NS) && drained;
+        for (int b = 0; b < 2; ++b)
+            if (wpend[b]) drained = umma::mbar_wait(&S.wbar[b], wphase[b], umma::DRAIN_NS) && drained;
+        S.abort_flag = drained ? 0 : 1;
+        if (dead || !drained) atomicExch(err, drained ? 3 : 13);
+    }
     umma::fence_before_sync();
     __syncthreads();
-    if (warp == 0) umma::tmem_dealloc(tmem, 256);
+    umma::fence_after_sync();
+    if (warp == 0 && !S.abort_flag) umma::tmem_dealloc(tmem, 256);
 }
 
 void trunk_set_constants(const NetLayout& L, const uint8_t* neighbors, const uint8_t* is_location) {

@@ -116,22 +116,47 @@ __device__ __forceinline__ void mbar_init(uint64_t* mbar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(mbar)), "r"(count) : "memory");
 }
 
-// Bounded wait on phase `parity`: returns false if it gave up (the caller
-// records an error and skips its dependent work instead of hanging).
-__device__ __forceinline__ bool mbar_wait(uint64_t* mbar, uint32_t parity, uint32_t max_iter = (1u << 26)) {
-    uint32_t addr = smem_u32(mbar);
-    for (uint32_t i = 0; i < max_iter; ++i) {
-        uint32_t done;
-        asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-            "selp.u32 %0, 1, 0, p;\n\t}\n"
-            : "=r"(done)
-            : "r"(addr), "r"(parity)
-            : "memory");
-        if (done) return true;
+// Wait limits, in nanoseconds of %globaltimer. A product or a bulk copy takes
+// microseconds, so a wait that runs for WAIT_NS has met a partner that will
+// never arrive; the caller records an error and stops issuing work. DRAIN_NS
+// bounds the waits at a kernel's exit for work that is already in flight
+// (an issued product or copy, which completes on its own).
+constexpr uint64_t WAIT_NS = 2000000000ull;
+constexpr uint64_t DRAIN_NS = 4000000000ull;
+
+__device__ __forceinline__ uint64_t now_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// One test of phase `parity` of the barrier at shared address `addr`.
+__device__ __forceinline__ bool mbar_test(uint32_t addr, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(done)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// Bounded wait on phase `parity`: returns false if the phase has not
+// completed after `limit_ns` (the caller records an error and skips its
+// dependent work instead of hanging). The limit is wall time, so it does not
+// depend on try_wait's suspend time or on profiler instrumentation.
+__device__ __forceinline__ bool mbar_wait(uint64_t* mbar, uint32_t parity, uint64_t limit_ns = WAIT_NS) {
+    const uint32_t addr = smem_u32(mbar);
+    if (mbar_test(addr, parity)) return true;
+    const uint64_t t0 = now_ns();
+    for (;;) {
+#pragma unroll 1
+        for (int i = 0; i < 16; ++i)
+            if (mbar_test(addr, parity)) return true;
+        if (now_ns() - t0 >= limit_ns) return false;
     }
-    return false;
 }
 
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }

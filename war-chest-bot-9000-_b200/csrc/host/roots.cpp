@@ -178,51 +178,258 @@ bool make_wide_root(uint64_t seed, int plies, bool random_draft, uint32_t ncfg, 
     return true;
 }
 
-std::vector<uint8_t> root_to_bytes(const Root& r) {
-    std::vector<uint8_t> out(sizeof(State));
-    std::memcpy(out.data(), &r.s, sizeof(State));
-    for (int p = 0; p < 2; ++p) {
-        uint32_t n = (uint32_t)r.bel[p].cfg.size();
-        const uint8_t* np = reinterpret_cast<const uint8_t*>(&n);
-        out.insert(out.end(), np, np + 4);
-        for (const Config& c : r.bel[p].cfg) {
-            out.insert(out.end(), c.hand, c.hand + NSLOT);
-            out.insert(out.end(), c.fd, c.fd + NSLOT);
-            out.push_back((uint8_t)c.inflight);
+// ------------------------------------------------------------ root bytes
+// The reference's root encoding, format v3 (engine/src/roots.rs:247-313,
+// write_root / read_root): the State field by field in little-endian
+// (write_state, roots.rs:150-180), then per player u32 n, n configs
+// (hand[5], fd[5], inflight or 0xff) and n f32 weights. Cont tags and
+// payloads follow write_cont (roots.rs:49-104); the Cont kinds here are
+// numbered as those tags.
+
+namespace {
+
+struct Writer {
+    std::vector<uint8_t>& out;
+    void u8(uint8_t x) { out.push_back(x); }
+    void u32(uint32_t x) { for (int i = 0; i < 4; ++i) out.push_back((uint8_t)(x >> (8 * i))); }
+    void u64(uint64_t x) { for (int i = 0; i < 8; ++i) out.push_back((uint8_t)(x >> (8 * i))); }
+    void f32(float x) { uint32_t u; std::memcpy(&u, &x, 4); u32(u); }
+};
+
+struct Reader {
+    const uint8_t* p;
+    size_t n, at = 0;
+    bool ok = true;
+    bool need(size_t k) { if (!ok || at + k > n) ok = false; return ok; }
+    uint8_t u8() { if (!need(1)) return 0; return p[at++]; }
+    uint32_t u32() {
+        if (!need(4)) return 0;
+        uint32_t x = 0;
+        for (int i = 0; i < 4; ++i) x |= (uint32_t)p[at + i] << (8 * i);
+        at += 4;
+        return x;
+    }
+    uint64_t u64() {
+        if (!need(8)) return 0;
+        uint64_t x = 0;
+        for (int i = 0; i < 8; ++i) x |= (uint64_t)p[at + i] << (8 * i);
+        at += 8;
+        return x;
+    }
+    float f32() { uint32_t u = u32(); float x; std::memcpy(&x, &u, 4); return x; }
+};
+
+void write_cont(Writer& w, const Cont& c) {
+    w.u8(c.kind);
+    switch (c.kind) {
+        case C_MAINPLAY: break;
+        case C_RGCHOICE: case C_WPDRAW: w.u8(c.a); w.u8(c.b); break;
+        case C_BERSCHAIN: w.u8(c.a); w.u8(c.b ? 1 : 0); break;
+        case C_FOOTMAN: w.u64(c.hexes); break;
+        default: w.u8(c.a); break;  // Draw, SwordsmanMove, CavalryAttack, Mercenary, FID, WPPlay, _AttackPost
+    }
+}
+
+bool read_cont(Reader& r, Cont* c) {
+    const uint8_t tag = r.u8();
+    if (tag > C_ATKPOST) return false;
+    *c = Cont::make(tag);
+    switch (tag) {
+        case C_MAINPLAY: break;
+        case C_RGCHOICE: case C_WPDRAW: c->a = r.u8(); c->b = r.u8(); break;
+        case C_BERSCHAIN: c->a = r.u8(); c->b = r.u8() != 0 ? 1 : 0; break;
+        case C_FOOTMAN: c->hexes = r.u64(); break;
+        default: c->a = r.u8(); break;
+    }
+    return r.ok;
+}
+
+}  // namespace
+
+// Every index a State carries is in range: units < N_UNITS, hexes <
+// N_HEXES, players 0 / 1 (NONE where the field allows it). The engine indexes
+// tables with these fields unchecked, so bytes from outside are checked once
+// here.
+bool state_in_range(const State& s) {
+    auto unit = [](uint8_t u) { return u < N_UNITS; };
+    auto hex = [](uint8_t h) { return h < N_HEXES; };
+    auto player = [](uint8_t p) { return p < 2; };
+    for (int h = 0; h < N_HEXES; ++h) {
+        const bool empty = s.hex_type[h] == NONE;
+        if (!empty && (!unit(s.hex_type[h]) || !player(s.hex_owner[h]))) return false;
+        if (empty && s.hex_owner[h] != NONE) return false;
+        if (s.loc_marker[h] != NONE && !player(s.loc_marker[h])) return false;
+    }
+    if (!player(s.initiative) || !player(s.first_player) || !player(s.active)) return false;
+    if (s.winner != NONE && !player(s.winner)) return false;
+    auto cont_ok = [&](const Cont& c) {
+        switch (c.kind) {
+            case C_MAINPLAY: return true;
+            case C_DRAW: case C_WPPLAY: return player(c.a);
+            case C_RGCHOICE: return player(c.a) && hex(c.b);
+            case C_WPDRAW: return player(c.a) && (c.b == NONE || hex(c.b));
+            case C_BERSCHAIN: return hex(c.a);
+            case C_FOOTMAN: return (c.hexes >> N_HEXES) == 0;
+            case C_FID: return unit(c.a);
+            default: return hex(c.a);  // SwordsmanMove, CavalryAttack, Mercenary, _AttackPost
         }
-        const uint8_t* wp = reinterpret_cast<const uint8_t*>(r.bel[p].p.data());
-        out.insert(out.end(), wp, wp + 4 * n);
+    };
+    if (!cont_ok(s.pending)) return false;
+    for (int i = 0; i < s.conts.n; ++i)
+        if (!cont_ok(s.conts.v[i])) return false;
+    return true;
+}
+
+bool action_well_formed(const State& s, const Action& a) {
+    auto unit = [](uint8_t u) { return u < N_UNITS; };
+    auto hex = [](uint8_t h) { return h < N_HEXES; };
+    auto unit_at = [&](uint8_t h) { return hex(h) && s.hex_type[h] != NONE; };
+    switch (a.kind) {
+        case K_DEPLOY: case K_BOLSTER: return unit(a.a) && hex(a.b);
+        case K_CLAIM: case K_PASS: case K_TAC_FOOTMAN: return unit(a.a);
+        case K_RECRUIT: return unit(a.a) && unit(a.b);
+        case K_DRAW: return a.a == NONE || unit(a.a);
+        case K_RG_SUPPLY: case K_RG_STACK: case K_SWORD_DECLINE: case K_BERS_STOP: case K_MERC_DECLINE:
+        case K_FID_DECLINE: return true;
+        case K_FID_DEPLOY: return hex(a.a);
+        case K_CONTROL: case K_FOOTCTRL: case K_BERS_CTRL: case K_MERC_CTRL: case K_GRANT_CTRL: return unit_at(a.a);
+        case K_LANCER: return unit_at(a.a) && hex(a.b) && hex(a.c);
+        default: return unit_at(a.a) && hex(a.b);  // the two-hex maneuvers, attacks and tactics
+    }
+}
+
+void write_state(std::vector<uint8_t>& out, const State& s) {
+    Writer w{out};
+    for (int h = 0; h < N_HEXES; ++h) {
+        w.u8(s.hex_type[h]);
+        w.u8(s.hex_owner[h]);
+        w.u8(s.hex_height[h]);
+        w.u8(s.loc_marker[h]);
+    }
+    for (int p = 0; p < N_PLAYERS; ++p)
+        for (int z = 0; z < N_ZONES; ++z)
+            for (int u = 0; u < N_UNITS; ++u) w.u8(s.zones[p][z][u]);
+    w.u8(s.markers_hand[0]);
+    w.u8(s.markers_hand[1]);
+    w.u8(s.initiative);
+    w.u8(s.initiative_moved ? 1 : 0);
+    w.u32(s.round);
+    w.u8(s.first_player);
+    w.u8(s.active);
+    w.u8(s.turns_taken[0]);
+    w.u8(s.turns_taken[1]);
+    w.u32(s.main_plays);
+    w.u8(s.winner);
+    w.u8(s.adjudicated_draw ? 1 : 0);
+    write_cont(w, s.pending);
+    w.u8(s.conts.n);
+    for (int i = (int)s.conts.n - 1; i >= 0; --i) write_cont(w, s.conts.v[i]);  // pop order: top first
+    w.u8(s.wp_v2_triggered ? 1 : 0);
+    w.u8(s.interrupt ? 1 : 0);
+}
+
+bool read_state(const uint8_t* data, size_t n, size_t* at, State* out) {
+    Reader r{data, n, *at};
+    State s = State::blank(0);
+    for (int h = 0; h < N_HEXES; ++h) {
+        s.hex_type[h] = r.u8();
+        s.hex_owner[h] = r.u8();
+        s.hex_height[h] = r.u8();
+        s.loc_marker[h] = r.u8();
+    }
+    for (int p = 0; p < N_PLAYERS; ++p)
+        for (int z = 0; z < N_ZONES; ++z)
+            for (int u = 0; u < N_UNITS; ++u) s.zones[p][z][u] = r.u8();
+    s.markers_hand[0] = r.u8();
+    s.markers_hand[1] = r.u8();
+    s.initiative = r.u8();
+    s.initiative_moved = r.u8() != 0;
+    s.round = (uint16_t)r.u32();
+    s.first_player = r.u8();
+    s.active = r.u8();
+    s.turns_taken[0] = r.u8();
+    s.turns_taken[1] = r.u8();
+    s.main_plays = (uint16_t)r.u32();
+    s.winner = r.u8();
+    s.adjudicated_draw = r.u8() != 0;
+    if (!read_cont(r, &s.pending)) return false;
+    const uint8_t nc = r.u8();
+    if (!r.ok || nc > CONT_CAP) return false;
+    Cont items[CONT_CAP];
+    for (int i = 0; i < nc; ++i)
+        if (!read_cont(r, &items[i])) return false;
+    s.conts.clear();
+    for (int i = (int)nc - 1; i >= 0; --i) s.conts.push(items[i]);  // written top first
+    s.wp_v2_triggered = r.u8() != 0;
+    s.interrupt = r.u8() != 0;
+    if (!r.ok || !state_in_range(s)) return false;
+    *out = s;
+    *at = r.at;
+    return true;
+}
+
+std::vector<uint8_t> root_to_bytes(const Root& r) {
+    std::vector<uint8_t> out;
+    write_state(out, r.s);
+    Writer w{out};
+    for (int p = 0; p < 2; ++p) {
+        const Belief& b = r.bel[p];
+        w.u32((uint32_t)b.cfg.size());
+        for (const Config& c : b.cfg) {
+            for (int k = 0; k < NSLOT; ++k) w.u8(c.hand[k]);
+            for (int k = 0; k < NSLOT; ++k) w.u8(c.fd[k]);
+            w.u8(c.inflight < 0 ? 0xff : (uint8_t)c.inflight);
+        }
+        for (float x : b.p) w.f32(x);
     }
     return out;
 }
 
-bool root_from_bytes(const uint8_t* data, size_t n, Root* out) {
-    if (n < sizeof(State)) return false;
-    std::memcpy(&out->s, data, sizeof(State));
-    size_t at = sizeof(State);
+bool root_from_bytes(const uint8_t* data, size_t n, Root* out, size_t* used) {
+    size_t at = 0;
+    if (!read_state(data, n, &at, &out->s)) return false;
+    Reader r{data, n, at};
     for (int p = 0; p < 2; ++p) {
-        if (at + 4 > n) return false;
-        uint32_t cnt;
-        std::memcpy(&cnt, data + at, 4);
-        at += 4;
-        if (at + (size_t)cnt * 11 > n) return false;
-        out->bel[p].cfg.resize(cnt);
+        const uint32_t cnt = r.u32();
+        if (!r.ok || cnt > 100000 || (size_t)cnt * 15 > n - r.at) return false;  // read_root's bound
+        Belief& b = out->bel[p];
+        b.cfg.resize(cnt);
         for (uint32_t i = 0; i < cnt; ++i) {
-            Config& c = out->bel[p].cfg[i];
-            std::memcpy(c.hand, data + at, NSLOT);
-            std::memcpy(c.fd, data + at + NSLOT, NSLOT);
-            c.inflight = (int8_t)data[at + 2 * NSLOT];
-            at += 11;
+            Config& c = b.cfg[i];
+            for (int k = 0; k < NSLOT; ++k) c.hand[k] = r.u8();
+            for (int k = 0; k < NSLOT; ++k) c.fd[k] = r.u8();
+            const uint8_t f = r.u8();
+            c.inflight = f == 0xff ? (int8_t)-1 : (int8_t)f;
         }
-        if (at + (size_t)cnt * 4 > n) return false;
-        out->bel[p].p.resize(cnt);
-        std::memcpy(out->bel[p].p.data(), data + at, (size_t)cnt * 4);
-        at += (size_t)cnt * 4;
+        b.p.resize(cnt);
+        for (uint32_t i = 0; i < cnt; ++i) b.p[i] = r.f32();
+        if (!r.ok) return false;
     }
     try {
         out->ctx = Ctx::make(out->s);
     } catch (...) {
         return false;
+    }
+    if (used) {
+        *used = r.at;
+        return true;
+    }
+    return r.at == n;
+}
+
+bool roots_file_split(const uint8_t* data, size_t n, std::vector<std::pair<size_t, size_t>>* spans) {
+    Reader r{data, n};
+    if (r.u32() != ROOTS_MAGIC || r.u32() != ROOTS_VERSION) return false;
+    const uint32_t count = r.u32();
+    if (!r.ok) return false;
+    spans->clear();
+    size_t at = r.at;
+    for (uint32_t i = 0; i < count; ++i) {
+        Root tmp;
+        size_t used = 0;
+        if (!root_from_bytes(data + at, n - at, &tmp, &used)) return false;
+        spans->emplace_back(at, used);
+        at += used;
     }
     return at == n;
 }

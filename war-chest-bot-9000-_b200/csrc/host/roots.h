@@ -51,9 +51,26 @@ Belief uniform_belief(const State& s, const Ctx& ctx, uint8_t p);
 // before the root.
 bool make_wide_root(uint64_t seed, int plies, bool random_draft, uint32_t ncfg, Root* out);
 
-// Serialized root: the State bytes, then per player u32 n, n configs
-// (hand[5], fd[5], inflight i8), n f32 weights.
+// Serialized root in the reference's format v3 (engine/src/roots.rs:247-313):
+// the State field by field, little-endian (write_state), then per player
+// u32 n, n configs (hand[5], fd[5], inflight or 0xff), n f32 weights.
+// root_from_bytes fails on malformed or truncated input; with `used` it
+// accepts trailing bytes and reports how many the root took, without it the
+// root must fill the buffer exactly.
 std::vector<uint8_t> root_to_bytes(const Root& r);
-bool root_from_bytes(const uint8_t* data, size_t n, Root* out);
+bool root_from_bytes(const uint8_t* data, size_t n, Root* out, size_t* used = nullptr);
+void write_state(std::vector<uint8_t>& out, const State& s);
+// read_state refuses a state whose fields would index out of range.
+bool state_in_range(const State& s);
+// The action names in-range fields and units on its source hexes, so apply
+// indexes nothing out of range (legality aside).
+bool action_well_formed(const State& s, const Action& a);
+bool read_state(const uint8_t* data, size_t n, size_t* at, State* out);
+
+// A roots file (write_roots, roots.rs:323-333): magic, version 3, count, then
+// the roots back to back. Fills (offset, length) per root; false on a bad
+// magic or version, or a malformed root.
+constexpr uint32_t ROOTS_MAGIC = 0x57107207u, ROOTS_VERSION = 3;
+bool roots_file_split(const uint8_t* data, size_t n, std::vector<std::pair<size_t, size_t>>* spans);
 
 }  // namespace wc

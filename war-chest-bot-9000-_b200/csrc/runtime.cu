@@ -200,6 +200,7 @@ void build_fast_pack(DeviceCtx& d, const float* W, const float* B, const float* 
     d.fast.stem_w = F + o_sw;
     d.fast.stem_pb = F + o_spb;
     d.fast.half = h ? 1 : 0;
+    d.fast.wait_ns = d.wait_ns;
 }
 
 // ---------------------------------------------------------------- batches
@@ -594,7 +595,7 @@ struct Sched {
         if (dv.have_net && !dv.precise) {
             timed(TC_POOL, [&] {
                 b.count_launch((pool_mask ? b.n_head_tiles : 0)), wcdev::launch_pool_fast(J, b.d_head_tiles, b.n_head_tiles, pool_mask, b.g_pool_img, b.g_mass, dv.half,
-                                        b.d_err, s);
+                                        b.d_err, dv.fast.wait_ns, s);
             });
             timed(TC_JOIN, [&] {
                 b.count_launch(b.n_head_tiles), wcdev::launch_join_fast(J, b.d_head_tiles, b.n_head_tiles, dv.fast, p, b.g_pool_img, b.g_jp,
@@ -811,7 +812,9 @@ void check_batch_error(Batch& b) {
     int e[4] = {0, 0, 0, 0};
     check(cudaMemcpyAsync(e, b.d_err, 16, cudaMemcpyDeviceToHost, b.dev->stream), "read error flag");
     check(cudaStreamSynchronize(b.dev->stream), "read error flag");
-    if (e[0]) throw std::runtime_error("a tensor-core wait exceeded its iteration limit (code " + std::to_string(e[0]) + ")");
+    if (e[0])
+        throw std::runtime_error("a tensor-core wait exceeded its time limit (code " + std::to_string(e[0]) +
+                                 (e[0] > 10 ? ", in-flight work did not drain: reset the device context" : "") + ")");
 }
 
 void download(Batch& b, size_t job, float* strategy, float* roots, uint16_t* carries) {

@@ -25,6 +25,7 @@ struct DeviceCtx {
     bool have_net = false;
     bool precise = true;  // fp32 network in the reference's operation order
     bool half = true;     // tensor-core network operands: f16 (true) or bf16
+    uint64_t wait_ns = 2000000000ull;  // limit of each tensor-core mbarrier wait (ns)
     uint64_t version = 0;
     NetLayout L;
     // 16-bit tensor-core copy of the network (fast path)

@@ -98,6 +98,10 @@ def _load() -> C.CDLL:
         "wc_queued_work": (U64, [VP]),
         "wc_debug_umma_gemm": (I, [VP, VP, I, I, VP]),
         "wc_debug_umma_gemm_static": (I, [VP, VP, I, I, VP]),
+        "wc_state_legal_actions": (I, [C.c_char_p, C.c_size_t, P(C.c_uint32), C.c_size_t, P(C.c_size_t)]),
+        "wc_state_apply": (I, [C.c_char_p, C.c_size_t, C.c_uint32, I, C.c_char_p, C.c_size_t, P(C.c_size_t)]),
+        "wc_state_query": (I, [C.c_char_p, C.c_size_t, P(C.c_int32)]),
+        "wc_roots_file_split": (I, [C.c_char_p, C.c_size_t, P(U64), P(U64), C.c_size_t, P(C.c_size_t)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -167,6 +171,50 @@ def snapshot_iters(iters: int) -> List[int]:
 
 def set_cap_marker_value(v: float) -> None:
     lib().wc_set_cap_marker_value(v)
+
+
+# ------------------------------------------------------------------ rules
+# States travel in the reference's write_state encoding (engine/src/roots.rs:
+# 150-180); action codes are Action::encode's (engine/src/actions.rs:252-295).
+
+def legal_actions(state: bytes) -> List[int]:
+    """State::legal_actions (engine/src/rules.rs:1027-1146): action codes in
+    the engine's order."""
+    codes = (C.c_uint32 * 512)()
+    n = C.c_size_t()
+    _check(lib().wc_state_legal_actions(state, len(state), codes, 512, C.byref(n)))
+    return list(codes[: n.value])
+
+
+def apply_action(state: bytes, code: int, unchecked: bool = False) -> bytes:
+    """State::apply (engine/src/rules.rs:1155): the successor state's bytes.
+    A non-legal action is refused unless `unchecked`, which applies it as the
+    reference's apply does (no legality test; fields must still be in
+    range)."""
+    buf = C.create_string_buffer(4096)
+    n = C.c_size_t()
+    _check(lib().wc_state_apply(state, len(state), code, int(unchecked), buf, 4096, C.byref(n)))
+    return buf.raw[: n.value]
+
+
+def state_query(state: bytes) -> dict:
+    """to_act, winner (None while undecided), is_terminal, is_chance."""
+    out = (C.c_int32 * 4)()
+    _check(lib().wc_state_query(state, len(state), out))
+    return {"to_act": out[0], "winner": None if out[1] < 0 else out[1], "terminal": bool(out[2]),
+            "chance": bool(out[3])}
+
+
+def split_roots_file(data: bytes) -> List[bytes]:
+    """The roots of a version-3 roots file (roots::read_roots,
+    engine/src/roots.rs:337-363), each in the root encoding wc_job_build
+    takes."""
+    n = C.c_size_t()
+    cap = max(1, len(data) // 16)
+    off = (C.c_uint64 * cap)()
+    ln = (C.c_uint64 * cap)()
+    _check(lib().wc_roots_file_split(data, len(data), off, ln, cap, C.byref(n)))
+    return [data[off[i]: off[i] + ln[i]] for i in range(n.value)]
 
 
 def generate_root(seed: int, plies: int = 20, random_draft: bool = True) -> bytes:
