@@ -83,10 +83,12 @@ __global__ void k_umma_selftest(const __nv_bfloat16* __restrict__ A, const __nv_
     if (warp == 0 && drained) umma::tmem_dealloc(tmem, ncols);
 }
 
-// The self-test kernel's dynamic shared-memory limit: the most a CTA may use
-// (227 KB). Both entry points set this one value on every call, so no call
-// can leave the limit below what another call's launch needs.
-constexpr int SELFTEST_SMEM_MAX = 227 * 1024;
+// The self-test kernel's dynamic shared-memory limit: 200 KB, above the
+// largest static-path problem (k = n = 256: 193 KB) and below the 227 KB a
+// CTA may hold with the kernel's own static shared memory. Both entry points
+// set this one value on every call, so no call can leave the limit below
+// what another call's launch needs.
+constexpr int SELFTEST_SMEM_MAX = 200 * 1024;
 
 // ------------------------------------------------------------- fast kernels
 
@@ -152,6 +154,11 @@ __global__ void __launch_bounds__(128, 3)
     __shared__ uint64_t bar_in, bar_w, bar_mma;
     __shared__ uint32_t tmem_slot;
     __shared__ int abort_flag;
+    if (umma::misaligned16(fn.join_tiles) || umma::misaligned16(pool_img) || umma::misaligned16(jp) ||
+        umma::misaligned16(zout_img)) {  // entry self-check: a launch contract broken, nothing touched
+        if (threadIdx.x == 0) atomicExch(err, 31);
+        return;
+    }
     uint8_t* smem = align1024(smem_raw);
     uint8_t* sWt = smem;               // the current layer's weight tile
     uint8_t* sA = smem + TILE_J;
@@ -224,6 +231,7 @@ __global__ void __launch_bounds__(128, 3)
     // after a failed wait.
     uint32_t ph_in = 0, ph_w = 0, ph_mma = 0;
     bool pend_mma = false, dead = false;
+    const uint64_t wait_ns = fn.wait_ns;
     uint64_t k = 0;
     const uint32_t idesc = umma::idesc16(128, 128, umma::Op16<H>::fmt);
     for (uint32_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
@@ -260,8 +268,8 @@ __global__ void __launch_bounds__(128, 3)
             {
                 bool ok = true;
                 if (tid == 0) {
-                    if (L == 0) ok = umma::mbar_wait(&bar_in, ph_in, fn.wait_ns);
-                    ok = ok && umma::mbar_wait(&bar_w, ph_w, fn.wait_ns);
+                    if (L == 0) ok = umma::mbar_wait(&bar_in, ph_in, wait_ns);
+                    ok = ok && umma::mbar_wait(&bar_w, ph_w, wait_ns);
                 }
                 dead = __syncthreads_or(!ok) != 0;
                 umma::fence_after_sync();
@@ -282,7 +290,7 @@ __global__ void __launch_bounds__(128, 3)
             }
             pend_mma = true;
             {
-                const bool ok = umma::mbar_wait(&bar_mma, ph_mma, fn.wait_ns);
+                const bool ok = umma::mbar_wait(&bar_mma, ph_mma, wait_ns);
                 umma::fence_before_sync();
                 dead = __syncthreads_or(!ok) != 0;
                 umma::fence_after_sync();
@@ -389,6 +397,10 @@ __global__ void __launch_bounds__(128, 4)
     __shared__ uint64_t bar_g, bar_mma;
     __shared__ uint32_t tmem_slot;
     __shared__ int abort_flag;
+    if (umma::misaligned16(pool_img)) {  // entry self-check: a launch contract broken, nothing touched
+        if (threadIdx.x == 0) atomicExch(err, 32);
+        return;
+    }
     uint8_t* smem = align1024(smem_raw);
     uint8_t* sBeta = smem;           // [128 rows][128 configs]: 32 KB
     uint8_t* sG = smem + TILE_J;     // [64 features][128 configs]: 16 KB
@@ -576,7 +588,14 @@ __global__ void __launch_bounds__(544, 1)
     __shared__ uint64_t bar_y, bar_v, bar_a, bar_f, bar_p, h_ready, s_done;
     __shared__ uint32_t tmem_slot;
     __shared__ int abort_flag, stuck;
-    __shared__ uint32_t gb2[D];   // f16: the LayerNorm's (gamma, beta) per column pair, packed
+    // f16: the LayerNorm's (gamma, beta) per column pair, packed; read as
+    // uint2, so the array needs 8-byte alignment (a uint32_t array alone is
+    // only guaranteed 4)
+    __shared__ __align__(16) uint32_t gb2[D];
+    if (umma::misaligned16(fn.out_tile) || umma::misaligned16(zout) || umma::misaligned16(pimg)) {
+        if (threadIdx.x == 0) atomicExch(err, 33);  // entry self-check: a launch contract broken
+        return;
+    }
     uint8_t* smem = align1024(smem_raw);
     uint8_t* sW = smem;                  // [256][128] Wout: 64 KB
     uint8_t* sF = sW + 2 * TILE_J;       // [128][256] f image of a pass, then its staging: 64 KB
@@ -609,6 +628,7 @@ __global__ void __launch_bounds__(544, 1)
     umma::fence_after_sync();
     const uint32_t tmem = tmem_slot;
     volatile int* abort_v = &abort_flag;
+    const uint64_t wait_ns = fn.wait_ns;
     // a bounded wait that also gives up as soon as another thread has
     // recorded an abort (so no role waits out its limit on a dead partner)
     auto wait = [&](uint64_t* bar, uint32_t parity) {
@@ -619,7 +639,7 @@ __global__ void __launch_bounds__(544, 1)
             if (umma::mbar_test(addr, parity)) return true;
             if ((i & 15u) == 0u) {
                 if (*abort_v) return false;
-                if (umma::now_ns() - t0 >= fn.wait_ns) break;
+                if (umma::now_ns() - t0 >= wait_ns) break;
             }
         }
         *abort_v = 1;

@@ -124,7 +124,9 @@ struct TrunkSmem {  // the non-operand scratch
     float pooled[BOARDS][2 * C];
     float gb[BOARDS][C];
     float part[4 * BOARDS * C];  // K-slice partial sums of the pooling GEMM
-    uint32_t gb2[wc::NET_BLOCKS][2][C];  // per block and LayerNorm: (gamma, beta) column pairs for ln_gelu2
+    // per block and LayerNorm: (gamma, beta) column pairs for ln_gelu2, which
+    // reads them as uint2 (8-byte alignment required)
+    alignas(16) uint32_t gb2[wc::NET_BLOCKS][2][C];
     uint64_t wbar[2];
     uint64_t mbar;
     uint32_t tmem_slot;
@@ -158,6 +160,11 @@ __global__ void __launch_bounds__(384, 1)
                  const float* __restrict__ W, const float* __restrict__ B, const float* __restrict__ LN,
                  const FastNetDev fn, uint16_t* __restrict__ g_pb, uint16_t* __restrict__ g_jp, int* __restrict__ err) {
     extern __shared__ uint8_t smem_raw[];
+    if (umma::misaligned16(tiles) || umma::misaligned16(fn.stem_pb) || umma::misaligned16(fn.stem_w) ||
+        umma::misaligned16(fn.trunk_ob)) {  // entry self-check: a launch contract broken, nothing touched
+        if (threadIdx.x == 0) atomicExch(err, 34);
+        return;
+    }
     uint8_t* smem = smem_raw + ((1024u - (umma::smem_u32(smem_raw) & 1023u)) & 1023u);
     uint8_t* sW[2] = {smem, smem + BLOCK_BYTES};
     uint8_t* sA1 = smem + 2 * BLOCK_BYTES;
@@ -208,6 +215,7 @@ __global__ void __launch_bounds__(384, 1)
     // issued copy or product has not yet been seen to complete on it.
     uint32_t wphase[2] = {0, 0}, mphase = 0;
     bool wpend[2] = {false, false}, mpend = false, dead = false;
+    const uint64_t wait_ns = fn.wait_ns;
     if (blockIdx.x < ntiles) {
         if (tid == 0) fetch_block(sW[0], tiles, 0, &S.wbar[0]);
         wpend[0] = true;
@@ -455,7 +463,7 @@ __global__ void __launch_bounds__(384, 1)
                                                   &S.gb[0][0], C, S.part);
             // mix product (weights of this block must have landed)
             {
-                const bool ok = umma::mbar_wait(&S.wbar[buf], wphase[buf], fn.wait_ns);
+                const bool ok = umma::mbar_wait(&S.wbar[buf], wphase[buf], wait_ns);
                 umma::fence_async_smem();
                 umma::fence_before_sync();
                 dead = __syncthreads_or(!ok) != 0;
@@ -474,7 +482,7 @@ __global__ void __launch_bounds__(384, 1)
             }
             mpend = true;
             {
-                const bool ok = umma::mbar_wait(&S.mbar, mphase, fn.wait_ns);
+                const bool ok = umma::mbar_wait(&S.mbar, mphase, wait_ns);
                 umma::fence_before_sync();
                 dead = __syncthreads_or(!ok) != 0;
                 umma::fence_after_sync();
@@ -533,7 +541,7 @@ __global__ void __launch_bounds__(384, 1)
             }
             mpend = true;
             {
-                const bool ok = umma::mbar_wait(&S.mbar, mphase, fn.wait_ns);
+                const bool ok = umma::mbar_wait(&S.mbar, mphase, wait_ns);
                 umma::fence_before_sync();
                 dead = __syncthreads_or(!ok) != 0;
                 umma::fence_after_sync();

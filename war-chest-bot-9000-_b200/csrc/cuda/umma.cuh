@@ -159,6 +159,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* mbar, uint32_t parity, uint6
     }
 }
 
+// Self-check of a pointer used by 16-byte vector or bulk accesses.
+__device__ __forceinline__ bool misaligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) != 0; }
+
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void fence_before_sync() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_after_sync() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }

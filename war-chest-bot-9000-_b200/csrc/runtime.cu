@@ -547,6 +547,24 @@ float factor(float t, float p) {
     return x / (x + 1.0f);
 }
 
+// WC_DEBUG_SYNC=1 in the environment: after every timed kernel class the
+// stream is synchronised and checked, so a device fault is reported with the
+// class that raised it (for diagnosis only; it serialises the solve).
+bool debug_sync() {
+    static const bool on = [] {
+        const char* e = std::getenv("WC_DEBUG_SYNC");
+        return e && e[0] == '1';
+    }();
+    return on;
+}
+
+const char* class_name(int cls) {
+    static const char* names[N_TC] = {"per-solve network", "leaf evaluation", "regret-matching rows",
+                                      "value gathers", "reach gathers", "snapshots", "phase 2", "init", "total",
+                                      "k_pool_fast", "k_join_fast", "k_head_fast", "k_trunk_fast"};
+    return cls >= 0 && cls < N_TC ? names[cls] : "kernel";
+}
+
 struct Sched {
     Batch& b;
     cudaStream_t s;
@@ -565,6 +583,12 @@ struct Sched {
     // Run `f`'s launches between two recorded events when profiling.
     template <class F>
     void timed(int cls, F&& f) {
+        if (debug_sync()) {  // WC_DEBUG_SYNC: each class's launches finish and are checked before the next
+            f();
+            check(cudaStreamSynchronize(s), class_name(cls));
+            check(cudaGetLastError(), class_name(cls));
+            return;
+        }
         if (!b.profile) { f(); return; }
         const int e0 = (int)b.events_used;
         check(cudaEventRecord(next_event(), s), "event");
