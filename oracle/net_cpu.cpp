@@ -264,6 +264,14 @@ void Net::join_cache(const float* p, size_t rows, std::vector<float>& out) const
 // net.rs:735-797.
 void Net::configs(const float* phi, const uint8_t* owner, size_t n, const float* cards, std::vector<float>& f,
                   std::vector<float>& g) const {
+    // A subgame with no network rows interns no configs and builds no card
+    // table (net.rs:778: the card views are counted from the table, so an
+    // empty one runs no product): nothing to encode, and `cards` is unset.
+    if (n == 0) {
+        f.clear();
+        g.clear();
+        return;
+    }
     size_t width = 3 + TYPE;
     std::vector<float> slots(n * NSLOT * width);
     for (size_t c = 0; c < n; ++c) {

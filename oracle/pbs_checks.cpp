@@ -6,11 +6,15 @@
 // returns 0, or writes a message and returns nonzero. The file:line of the
 // reference test is beside each.
 #include <algorithm>
+#include <array>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <atomic>
 #include <map>
+#include <mutex>
 #include <string>
+#include <thread>
 #include <utility>
 #include <vector>
 
@@ -116,6 +120,21 @@ bool same_state(const State& a, const State& b) {
     for (int i = 0; i < a.conts.n; ++i)
         if (!(a.conts.v[i] == b.conts.v[i])) return false;
     return true;
+}
+
+// Run body(seed) for every seed in [lo, hi) on the host's threads (the
+// seeds are independent positions); the results are combined by the caller
+// in seed order, so the outcome does not depend on the schedule.
+template <class F>
+void parallel_seeds(uint64_t lo, uint64_t hi, F&& body) {
+    std::atomic<uint64_t> next{lo};
+    const unsigned n = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
+    std::vector<std::thread> th;
+    for (unsigned i = 0; i < n; ++i)
+        th.emplace_back([&] {
+            for (uint64_t s; (s = next.fetch_add(1)) < hi;) body(s);
+        });
+    for (auto& t : th) t.join();
 }
 
 const uint16_t DRAFT_POOL[19] = {1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 16, 17, 18, 19, 52, 53, 54};
@@ -611,12 +630,13 @@ int oracle_check_solve_reads_only_beliefs(int* checked, char* msg, size_t cap) {
     cfg.depth = 2;
     cfg.iters = 8;
     cfg.snapshots = true;
-    *checked = 0;
-    for (uint64_t seed = 1; seed < 80; ++seed) {
+    // per seed: -1 no ambiguous position, 0 agreed, 1 values moved, 2 strategy moved
+    std::vector<int> outcome(80, -1);
+    parallel_seeds(1, 80, [&](uint64_t seed) {
         State s;
         Ctx ctx;
         Belief bel[2];
-        if (!position_with_ambiguous_facedown(seed, &s, &ctx, bel)) continue;
+        if (!position_with_ambiguous_facedown(seed, &s, &ctx, bel)) return;
         std::vector<std::vector<float>> runs[2];
         for (int pick = 0; pick < 2; ++pick) {
             State w = s;
@@ -634,9 +654,13 @@ int oracle_check_solve_reads_only_beliefs(int* checked, char* msg, size_t cap) {
             }
             runs[pick] = {v[0], strat};
         }
-        if (runs[0][0] != runs[1][0]) return failf(msg, cap, "root values moved with the true world (seed " + std::to_string(seed) + ")");
-        if (runs[0][1] != runs[1][1]) return failf(msg, cap, "the root strategy moved with the true world");
-        ++*checked;
+        outcome[seed] = runs[0][0] != runs[1][0] ? 1 : runs[0][1] != runs[1][1] ? 2 : 0;
+    });
+    *checked = 0;
+    for (uint64_t seed = 1; seed < 80; ++seed) {
+        if (outcome[seed] == 1) return failf(msg, cap, "root values moved with the true world (seed " + std::to_string(seed) + ")");
+        if (outcome[seed] == 2) return failf(msg, cap, "the root strategy moved with the true world (seed " + std::to_string(seed) + ")");
+        if (outcome[seed] == 0) ++*checked;
     }
     if (*checked <= 20) return failf(msg, cap, "only " + std::to_string(*checked) + " positions exercised");
     return 0;
@@ -672,12 +696,12 @@ int oracle_check_value_separates_configs(int* stats3, char* msg, size_t cap) {
     cfg.depth = 2;
     cfg.iters = 8;
     cfg.snapshots = true;
-    int positions = 0, val_differs = 0, strat_differs = 0;
-    for (uint64_t seed = 1; seed < 80; ++seed) {
+    std::vector<std::array<int, 3>> per(80, {0, 0, 0});  // per seed: pairs, values differ, strategies differ
+    parallel_seeds(1, 80, [&](uint64_t seed) {
         State s;
         Ctx ctx;
         Belief bel[2];
-        if (!position_with_ambiguous_facedown(seed, &s, &ctx, bel)) continue;
+        if (!position_with_ambiguous_facedown(seed, &s, &ctx, bel)) return;
         const uint8_t me = s.to_act();
         auto t = build_tree(s, ctx, cfg, bel);
         oracle::Solver sv(*t, &net);
@@ -686,16 +710,23 @@ int oracle_check_value_separates_configs(int* stats3, char* msg, size_t cap) {
         root.insert(root.end(), bel[1].p.begin(), bel[1].p.end());
         auto vals = sv.value_under({root});
         const float* v = vals[0].data() + (me == 0 ? 0 : bel[0].cfg.size());
+        std::array<int, 3>& st = per[seed];
         for (size_t i = 0; i < bel[me].cfg.size(); ++i)
             for (size_t j = 0; j < i; ++j) {
                 if (std::memcmp(bel[me].cfg[i].hand, bel[me].cfg[j].hand, NSLOT) != 0) continue;
-                ++positions;
-                if (std::fabs(v[i] - v[j]) > 1e-9f) ++val_differs;
+                ++st[0];
+                if (std::fabs(v[i] - v[j]) > 1e-9f) ++st[1];
                 std::vector<float> a = root_row(sv, *t, i), b = root_row(sv, *t, j);
                 bool d = false;
                 for (size_t k = 0; k < a.size() && k < b.size(); ++k) d = d || std::fabs(a[k] - b[k]) > 1e-9f;
-                if (d) ++strat_differs;
+                if (d) ++st[2];
             }
+    });
+    int positions = 0, val_differs = 0, strat_differs = 0;
+    for (const auto& st : per) {
+        positions += st[0];
+        val_differs += st[1];
+        strat_differs += st[2];
     }
     stats3[0] = positions;
     stats3[1] = val_differs;
