@@ -46,14 +46,42 @@ def test_device_entry_points_fail_loudly_without_a_gpu(wc):
     assert buf.value
 
 
-def test_root_bytes_match_the_oracle_build(wc, oracle):
-    for seed in range(4):
-        a = wc.generate_root(seed)
-        buf = C.create_string_buffer(1 << 20)
-        n = C.c_size_t()
-        assert oracle.lib().oracle_root_generate(C.c_uint64(seed), 20, 1, buf, C.c_size_t(1 << 20), C.byref(n)) == 0
-        assert a == buf.raw[: n.value]
-        assert a == wc.generate_root(seed)  # deterministic
+def test_reference_root_encoding_at_the_boundary(wc):
+    """wc_job_build reads the reference's own root encoding (write_root,
+    engine/src/roots.rs:247-313, format v3). A root written here field by
+    field, as the Rust engine writes it (tests/wc_state.py, independent of
+    the library's encoder), builds a job; a roots file of such roots splits
+    back into them (read_roots); and the library's generated roots decode
+    with the same independent reader and re-encode byte for byte."""
+    import struct
+
+    from wc_state import (BLACK, CAVALRY, CROSSBOWMAN, FOOTMAN, LANCER, PIKEMAN, ROYAL_COIN, SWORDSMAN,
+                          WARRIOR_PRIEST, WHITE, ARCHER, Z_BAG, Z_HAND, State, decode_root, encode_root)
+
+    s = State.blank(WHITE)
+    s.set_unit(17, WHITE, WARRIOR_PRIEST, 1)
+    s.set_unit(19, BLACK, FOOTMAN, 3)
+    for u in (WARRIOR_PRIEST, SWORDSMAN, PIKEMAN, CROSSBOWMAN, ROYAL_COIN):
+        s.add_zone(WHITE, Z_BAG, u, 1)
+    for u in (FOOTMAN, ARCHER, CAVALRY, LANCER, ROYAL_COIN):
+        s.add_zone(BLACK, Z_BAG, u, 1)
+    s.add_zone(WHITE, Z_HAND, WARRIOR_PRIEST, 1)
+    # slots are the owned unit types in index order: white's WP is slot 3
+    root = encode_root(s, [[(((0, 0, 0, 1, 0), (0,) * 5, None), 1.0)], [(((0,) * 5, (0,) * 5, None), 1.0)]])
+    job = wc.PackedJob.from_root(root, wc.Cfg(depth=2, iters=4, snapshots=True, cfr=wc.Cfr.PLUS))
+    assert job.info["nodes"] > 1 and job.info["root_nc0"] == 1 and job.info["root_nc1"] == 1
+    with pytest.raises(wc.SolveError):  # truncated: refused, not read past the end
+        wc.PackedJob.from_root(root[:-3], wc.Cfg(depth=2, iters=4))
+    g = wc.generate_root(0)
+    assert g == wc.generate_root(0)  # deterministic
+    st, bel = decode_root(g)
+    assert encode_root(st, bel) == g
+    for b in bel:
+        assert abs(sum(w for _, w in b) - 1.0) < 1e-5
+    roots_file = struct.pack("<III", 0x57107207, 3, 2) + root + g
+    assert wc.split_roots_file(roots_file) == [root, g]
+    with pytest.raises(wc.SolveError):
+        wc.split_roots_file(struct.pack("<III", 0x57107207, 1, 0))  # a version-1 file is refused
 
 
 def test_weight_blobs(wc, oracle):

@@ -63,3 +63,30 @@ def test_job_keeps_the_snapshot_list(wc):
     for iters in (1, 8, 64):
         job = wc.PackedJob.from_root(root, wc.Cfg(depth=1, iters=iters, snapshots=True, cfr=wc.Cfr.PLUS))
         assert job.info["carry_snapshots"] == len(wc.snapshot_iters(iters)) - 1
+
+
+# ---- structural tests of the tree, restated from engine/tests/rebel_solver.rs
+# (oracle/solver_checks.cpp drives the host tree builder and the CPU solver)
+
+def _check(fn, *args):
+    import ctypes as C
+
+    msg = C.create_string_buffer(2048)
+    rc = fn(*args, msg, 2048)
+    assert rc == 0, msg.value.decode()
+
+
+def test_draw_pass_through_consistency(oracle):  # rebel_solver.rs:449
+    import ctypes as C
+
+    st = (C.c_int * 5)()
+    _check(oracle.lib().oracle_check_draw_pass_through, st)
+    print(f"draw pass-through: rejected={st[0]} built={st[1]} toolarge={st[2]} nochance={st[3]} solved={st[4]}")
+
+
+def test_warrior_priest_draw_walks_through_the_tree(oracle):  # rebel_solver.rs:612
+    _check(oracle.lib().oracle_check_warrior_priest_draw_walk)
+
+
+def test_depth_is_spent_on_coin_plays_not_micro_choices(oracle):  # rebel_solver.rs:753
+    _check(oracle.lib().oracle_check_depth_counts_coin_plays)

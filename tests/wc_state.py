@@ -166,8 +166,14 @@ class State:
 
     @staticmethod
     def from_bytes(b: bytes) -> "State":
+        s, at = State.parse(b)
+        assert at == len(b), "trailing bytes after the state"
+        return s
+
+    @staticmethod
+    def parse(b: bytes, at: int = 0):
+        """read_state (roots.rs:182-230) from offset `at`: (state, end offset)."""
         s = State()
-        at = 0
         for h in range(N_HEXES):
             s.hex_type[h], s.hex_owner[h], s.hex_height[h], s.loc_marker[h] = b[at: at + 4]
             at += 4
@@ -196,8 +202,7 @@ class State:
         s.conts = list(reversed(items))
         s.wp_v2_triggered, s.interrupt = bool(b[at]), bool(b[at + 1])
         at += 2
-        assert at == len(b), "trailing bytes after the state"
-        return s
+        return s, at
 
     # ---- the engine, through the product library
     def legal_actions(self) -> List[int]:
@@ -219,6 +224,41 @@ class State:
 
     def is_terminal(self) -> bool:
         return wc.state_query(self.to_bytes())["terminal"]
+
+
+# ------------------------------------------------------------------ roots
+# write_root (roots.rs:247-262): the state, then per player u32 n, n configs
+# (hand[5], fd[5], inflight or 0xff) and n f32 weights.
+
+def encode_root(state: "State", beliefs) -> bytes:
+    """beliefs: per player a list of ((hand5, fd5, inflight or None), weight)."""
+    out = bytearray(state.to_bytes())
+    for bel in beliefs:
+        out += struct.pack("<I", len(bel))
+        for (hand, fd, inflight), _ in bel:
+            out += bytes(hand) + bytes(fd) + bytes([0xFF if inflight is None else inflight])
+        for _, w in bel:
+            out += struct.pack("<f", w)
+    return bytes(out)
+
+
+def decode_root(b: bytes):
+    """read_root (roots.rs:265-284): (state, beliefs) as encode_root takes them."""
+    s, at = State.parse(b)
+    beliefs = []
+    for _ in range(2):
+        (n,) = struct.unpack_from("<I", b, at)
+        at += 4
+        cfgs = []
+        for _ in range(n):
+            hand, fd, inf = tuple(b[at: at + 5]), tuple(b[at + 5: at + 10]), b[at + 10]
+            cfgs.append((hand, fd, None if inf == 0xFF else inf))
+            at += 11
+        ws = struct.unpack_from(f"<{n}f", b, at)
+        at += 4 * n
+        beliefs.append(list(zip(cfgs, ws)))
+    assert at == len(b), "trailing bytes after the root"
+    return s, beliefs
 
 
 # --------------------------------------------------------------- actions

@@ -178,6 +178,7 @@ struct Builder {
         nr.draw_off = (uint32_t)t.draw_start.size();
         nr.depth = level;
         t.nodes.push_back(nr);
+        if (t.cfg.keep_states) t.states.push_back(s);
         t.soff.push_back((uint32_t)t.legal_action.size());
         if (t.cfg.node_cap > 0 && t.nodes.size() >= t.cfg.node_cap) {
             t.capped = true;

@@ -37,6 +37,7 @@ struct SolveCfg {
     bool snapshots = true;
     CfrRule cfr = CfrRule::linear();
     size_t node_cap = 0;
+    bool keep_states = false;  // keep each node's State in Tree::states (search.rs:80, tests only)
 };
 
 std::vector<int> snapshot_iters(int iters);  // search.rs:102-110
@@ -68,6 +69,7 @@ struct Tree {
     Belief root_belief[2];
     bool capped = false;
     std::vector<NodeRec> nodes;
+    std::vector<State> states;  // parallel to nodes when cfg.keep_states
     std::vector<std::vector<Config>> supports;
     // actions, per node contiguous
     std::vector<Action> acts;
