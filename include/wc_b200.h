@@ -217,6 +217,13 @@ int wc_batch_solve(wc_batch* b);
  * class_ms needs 13 entries. */
 int wc_batch_solve_profiled(wc_batch* b, double* class_ms, int nclass);
 int wc_batch_download(wc_batch* b, size_t job, float* strategy, float* root_values, uint16_t* carries);
+/* After a solve: each job's exploitability under its average strategy, from
+ * its live root belief (Solver::nash_conv, engine/src/search.rs:1884-1907):
+ * nash[j] = sum over players of (best-response value - value under the
+ * average), zero_sum[j] = sum of the values under the average (0 for a
+ * zero-sum game up to rounding). Both of the depth-limited game the tree
+ * defines, with the network valuing its leaves. One float per job each. */
+int wc_batch_nash_conv(wc_batch* b, float* nash, float* zero_sum);
 /* Leaf evaluation alone (the per-solve network, then every network row's
  * values for traverser p at the initial uniform-strategy reaches), and its
  * read-back: rows in the reference's leaf_rows order, each row's p-configs

@@ -712,6 +712,37 @@ int wc_batch_solve_profiled(wc_batch* b, double* class_ms, int nclass) {
     });
 }
 
+int wc_batch_nash_conv(wc_batch* b, float* nash, float* zero_sum) {
+    if (!b || !nash || !zero_sum) return fail(WC_E_ARG, "bad nash-conv arguments");
+    return guarded([&] {
+        std::lock_guard<std::mutex> lk(b->b->dev->mu);
+        enqueue_nash_conv(*b->b);
+        check(cudaStreamSynchronize(b->b->dev->stream), "nash conv");
+        check_batch_error(*b->b);
+        for (size_t j = 0; j < b->b->jobs.size(); ++j) {
+            const JobBlob& jb = *b->b->jobs[j];
+            const JobImage& J = *jb.img;
+            const uint32_t n0 = J.root_nc[0], n1 = J.root_nc[1], w = n0 + n1;
+            std::vector<float> v(2ull * w);
+            download_conv(*b->b, j, v.data());
+            const float* root = jb.arr<float>(JobBlob::ROOT_BELIEF);
+            // search.rs:1895-1903, in its summation order
+            float nsh = 0.0f, zs = 0.0f;
+            for (int p = 0; p < 2; ++p) {
+                const uint32_t off = p == 0 ? 0 : n0, n = p == 0 ? n0 : n1;
+                float val = 0.0f, best = 0.0f;
+                for (uint32_t c = 0; c < n; ++c) val += root[off + c] * v[off + c];
+                for (uint32_t c = 0; c < n; ++c) best += root[off + c] * v[w + off + c];
+                nsh += best - val;
+                zs += val;
+            }
+            nash[j] = nsh;
+            zero_sum[j] = zs;
+        }
+        return (int)WC_OK;
+    });
+}
+
 int wc_batch_leaf_values(wc_batch* b, int p, double* class_ms) {
     if (!b || p < 0 || p > 1) return fail(WC_E_ARG, "bad leaf-values arguments");
     return guarded([&] {

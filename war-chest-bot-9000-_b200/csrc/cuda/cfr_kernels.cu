@@ -268,6 +268,17 @@ __global__ void k_collect_root(const JobDev* __restrict__ jobs, int root_index, 
     for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) out[i] = v[i];
 }
 
+// NashConv passes (search.rs:1884-1907): the root block of traverser p's
+// value arena into slot 0 (value under the average) or 1 (best response)
+// of the job's conv output, [slot][player 0 configs | player 1 configs].
+__global__ void k_collect_conv(const JobDev* __restrict__ jobs, int slot, int p) {
+    const JobDev& J = jobs[blockIdx.x];
+    const uint32_t n0 = J.root_nc[0], n = J.root_nc[p];
+    float* out = J.out_conv + (size_t)slot * (n0 + J.root_nc[1]) + (p == 1 ? n0 : 0);
+    const float* v = J.vals[p] + J.root_vblk[p];
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) out[i] = v[i];
+}
+
 // Normalised exit-leaf beliefs under one snapshot (search.rs:1937-1956),
 // stored as f16 like the reference's carry store.
 __global__ void k_carry(const JobDev* __restrict__ jobs, const WorkItem* __restrict__ items, int snap_index) {
@@ -330,6 +341,9 @@ void launch_unsort(const JobDev* jobs, const WorkItem* items, uint32_t n, cudaSt
 }
 void launch_collect_root(const JobDev* jobs, uint32_t njobs, int root_index, int p, cudaStream_t s) {
     if (njobs) k_collect_root<<<njobs, 128, 0, s>>>(jobs, root_index, p);
+}
+void launch_collect_conv(const JobDev* jobs, uint32_t njobs, int slot, int p, cudaStream_t s) {
+    if (njobs) k_collect_conv<<<njobs, 128, 0, s>>>(jobs, slot, p);
 }
 void launch_carry(const JobDev* jobs, const WorkItem* items, uint32_t n, int snap_index, cudaStream_t s) {
     if (n) k_carry<<<n, WI_TASKS, 0, s>>>(jobs, items, snap_index);

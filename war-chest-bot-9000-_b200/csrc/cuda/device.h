@@ -75,6 +75,7 @@ struct JobDev {
     float* out_strategy;   // ncells, reference order
     float* out_roots;      // ncarried * (root_nc0 + root_nc1)
     uint16_t* out_carry;   // (nsnaps - 1) * carry_width, f16
+    float* out_conv;       // 2 * (root_nc0 + root_nc1): root values under the average, then best responses
     // ---- sizes
     uint32_t ncells, ndraw, nrows_net, nterm, ncfg, ncarried, reach_len, nexit;
     uint32_t root_nc[2], root_rblk[2], root_vblk[2];

@@ -27,6 +27,7 @@ void launch_copy_cur_to_snap(const JobDev* jobs, const WorkItem* items, uint32_t
 void launch_unsort(const JobDev* jobs, const WorkItem* items, uint32_t n, cudaStream_t s);
 void launch_collect_root(const JobDev* jobs, uint32_t njobs, int root_index, int p, cudaStream_t s);
 void launch_carry(const JobDev* jobs, const WorkItem* items, uint32_t n, int snap_index, cudaStream_t s);
+void launch_collect_conv(const JobDev* jobs, uint32_t njobs, int slot, int p, cudaStream_t s);
 
 // net_precise.cu
 void net_set_constants(const wc::NetLayout& L, const uint8_t* neighbors, const uint8_t* is_location);

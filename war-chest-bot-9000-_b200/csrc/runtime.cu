@@ -275,7 +275,7 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
     Alloc A;
     struct Plan {
         size_t tables, cur, regret, sum, snap, reach, reach2, vals0, vals1, cards, cardm, tokproj, pb, jp, cf, cg, pooled,
-            out_strategy, out_roots, out_carry;
+            out_strategy, out_roots, out_carry, out_conv;
     };
     std::vector<Plan> plan(nj);
     for (size_t j = 0; j < nj; ++j) {
@@ -303,6 +303,7 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
         P.out_strategy = A.take(4ull * J.ncells);
         P.out_roots = A.take(4ull * J.ncarried * (J.root_nc[0] + J.root_nc[1]));
         P.out_carry = J.cfg.snapshots ? A.take(2ull * (jb.nsnaps_kept - 1) * jb.carry_width) : 0;
+        P.out_conv = A.take(8ull * (J.root_nc[0] + J.root_nc[1]));
         b.table_bytes += jb.bytes;
     }
     // ---- work items
@@ -407,7 +408,7 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
     b.hj.resize(nj);
     std::vector<uint32_t> row_base(nj, 0);
     for (size_t j = 1; j < nj; ++j) row_base[j] = row_base[j - 1] + jobs[j - 1]->img->nrows_net;
-    b.out_off.resize(3 * nj);
+    b.out_off.resize(4 * nj);
     for (size_t j = 0; j < nj; ++j) {
         const JobBlob& jb = *jobs[j];
         const JobImage& J = *jb.img;
@@ -476,6 +477,7 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
         d.out_strategy = reinterpret_cast<float*>(D + P.out_strategy);
         d.out_roots = reinterpret_cast<float*>(D + P.out_roots);
         d.out_carry = J.cfg.snapshots ? reinterpret_cast<uint16_t*>(D + P.out_carry) : nullptr;
+        d.out_conv = reinterpret_cast<float*>(D + P.out_conv);
         d.ncells = J.ncells;
         d.ndraw = J.ndraw;
         d.nrows_net = J.nrows_net;
@@ -490,9 +492,10 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
             d.root_rblk[q] = J.root_rblk[q];
             d.root_vblk[q] = J.root_vblk[q];
         }
-        b.out_off[3 * j] = P.out_strategy;
-        b.out_off[3 * j + 1] = P.out_roots;
-        b.out_off[3 * j + 2] = P.out_carry;
+        b.out_off[4 * j] = P.out_strategy;
+        b.out_off[4 * j + 1] = P.out_roots;
+        b.out_off[4 * j + 2] = P.out_carry;
+        b.out_off[4 * j + 3] = P.out_conv;
     }
     b.d_jobs = reinterpret_cast<wcdev::JobDev*>(D + o_jobs);
     b.d_items = reinterpret_cast<wcdev::WorkItem*>(D + o_items);
@@ -831,6 +834,36 @@ void enqueue_solve(Batch& b) {
     check(cudaGetLastError(), "solve launch");
 }
 
+void enqueue_nash_conv(Batch& b) {
+    if (b.jobs.empty()) return;
+    b.launches = 0;
+    DeviceCtx& dv = *b.dev;
+    check(cudaSetDevice(dv.device), "set device");
+    Sched S(b);
+    const uint32_t nj = (uint32_t)b.jobs.size();
+    // search.rs:1884-1907: reaches of the live root belief under the average,
+    // both players' leaf beliefs pooled once, then per player a value pass
+    // and a best-response pass over the same leaf values
+    b.count_launch(nj), wcdev::launch_seed_root(S.J, nj, 0, -1, S.s);
+    S.propagate(wcdev::STRAT_SNAP, 0, 3, 0, 1.0f);
+    for (int p = 0; p < 2; ++p) {
+        S.leaf_values(p, p == 0 ? 3 : 0);
+        S.backprop(p, wcdev::BACK_VALUE, wcdev::STRAT_SNAP, 0.0f, 0.0f, 0.0f);
+        b.count_launch(nj), wcdev::launch_collect_conv(S.J, nj, 0, p, S.s);
+        S.backprop(p, wcdev::BACK_BEST, wcdev::STRAT_SNAP, 0.0f, 0.0f, 0.0f);
+        b.count_launch(nj), wcdev::launch_collect_conv(S.J, nj, 1, p, S.s);
+    }
+    check(cudaGetLastError(), "nash conv launch");
+}
+
+void download_conv(Batch& b, size_t job, float* out) {
+    const JobImage& J = *b.jobs[job]->img;
+    cudaStream_t s = b.dev->stream;
+    check(cudaMemcpyAsync(out, b.dmem + b.out_off[4 * job + 3], 8ull * (J.root_nc[0] + J.root_nc[1]),
+                          cudaMemcpyDeviceToHost, s), "download conv");
+    check(cudaStreamSynchronize(s), "download conv");
+}
+
 void check_batch_error(Batch& b) {
     if (!b.d_err) return;
     int e[4] = {0, 0, 0, 0};
@@ -846,12 +879,12 @@ void download(Batch& b, size_t job, float* strategy, float* roots, uint16_t* car
     const JobImage& J = *jb.img;
     cudaStream_t s = b.dev->stream;
     if (strategy)
-        check(cudaMemcpyAsync(strategy, b.dmem + b.out_off[3 * job], 4ull * J.ncells, cudaMemcpyDeviceToHost, s), "download strategy");
+        check(cudaMemcpyAsync(strategy, b.dmem + b.out_off[4 * job], 4ull * J.ncells, cudaMemcpyDeviceToHost, s), "download strategy");
     if (roots)
-        check(cudaMemcpyAsync(roots, b.dmem + b.out_off[3 * job + 1], 4ull * J.ncarried * (J.root_nc[0] + J.root_nc[1]),
+        check(cudaMemcpyAsync(roots, b.dmem + b.out_off[4 * job + 1], 4ull * J.ncarried * (J.root_nc[0] + J.root_nc[1]),
                               cudaMemcpyDeviceToHost, s), "download roots");
     if (carries && J.cfg.snapshots)
-        check(cudaMemcpyAsync(carries, b.dmem + b.out_off[3 * job + 2], 2ull * (jb.nsnaps_kept - 1) * jb.carry_width,
+        check(cudaMemcpyAsync(carries, b.dmem + b.out_off[4 * job + 2], 2ull * (jb.nsnaps_kept - 1) * jb.carry_width,
                               cudaMemcpyDeviceToHost, s), "download carries");
     check(cudaStreamSynchronize(s), "download");
 }

@@ -90,7 +90,7 @@ struct Batch {
     void* d_head_tiles = nullptr;
     uint32_t n_head_tiles = 0;
     int* d_err = nullptr;
-    std::vector<size_t> out_off;  // per job: strategy, roots, carry offsets in dmem
+    std::vector<size_t> out_off;  // per job: strategy, roots, carry, conv offsets in dmem
     double node_updates = 0.0;    // sum over jobs of nodes * iters
     double leaf_evals = 0.0;      // network-row joins per solve
     size_t table_bytes = 0;
@@ -136,6 +136,13 @@ void download_leaf_values(Batch& b, size_t job, int p, float* out);
 void download_board_rows(Batch& b, size_t job, float* pb, float* jp);
 // Copy one job's results to host buffers (synchronous). Any pointer may be null.
 void download(Batch& b, size_t job, float* strategy, float* roots, uint16_t* carries);
+
+// After a solve: exploitability passes of every job's live root under its
+// average strategy (Solver::nash_conv, search.rs:1884-1907); download_conv
+// reads one job's 2 * (nc0 + nc1) root values: under the average, then the
+// best responses, each [player 0 | player 1].
+void enqueue_nash_conv(Batch& b);
+void download_conv(Batch& b, size_t job, float* out);
 
 void check(cudaError_t e, const char* what);
 // Throw if a kernel recorded a bounded-wait timeout during the last solve.

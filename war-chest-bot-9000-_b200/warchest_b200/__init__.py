@@ -90,6 +90,7 @@ def _load() -> C.CDLL:
         "wc_batch_download_leaf_values": (I, [VP, C.c_size_t, I, VP]),
         "wc_batch_download_board_rows": (I, [VP, C.c_size_t, VP, VP]),
         "wc_batch_download": (I, [VP, C.c_size_t, VP, VP, VP]),
+        "wc_batch_nash_conv": (I, [VP, VP, VP]),
         "wc_batch_stats": (None, [VP, P(C.c_double), P(C.c_double), P(U64), P(U64)]),
         "wc_batch_free": (None, [VP]),
         "wc_batch_launches": (U64, [VP]),
@@ -468,6 +469,16 @@ class DeviceBatch:
         jp = np.zeros((max(n, 1), 128), np.float32)
         _check(lib().wc_batch_download_board_rows(self._h, j, pb.ctypes.data, jp.ctypes.data))
         return pb[:n], jp[:n]
+
+    def nash_conv(self):
+        """After solve(): per job (nash_conv, zero_sum) of the average strategy
+        from the live root belief (Solver::nash_conv, search.rs:1884-1907),
+        computed on the device."""
+        n = len(self.jobs)
+        nash = np.zeros(max(n, 1), np.float32)
+        zs = np.zeros(max(n, 1), np.float32)
+        _check(lib().wc_batch_nash_conv(self._h, nash.ctypes.data, zs.ctypes.data))
+        return nash[:n], zs[:n]
 
     def launches(self) -> int:
         """Kernel launches of the last solve or leaf evaluation."""
