@@ -332,6 +332,15 @@ int oracle_leaf_parts(void* h, int p, float* hout, float* opp_reach, uint32_t* c
     return 0;
 }
 
+// Per network row, the number of player-p configs it carries (the row
+// structure of oracle_leaf_values / oracle_leaf_parts). Returns the rows.
+size_t oracle_leaf_row_counts(void* h, int p, uint32_t* out) {
+    const wc::Tree& t = *static_cast<Handle*>(h)->tree;
+    if (out)
+        for (size_t r = 0; r < t.leaf_rows.size(); ++r) out[r] = (uint32_t)t.nc(t.leaf_rows[r], p);
+    return t.leaf_rows.size();
+}
+
 // Fraction of network leaf rows whose player-q reach mass is exactly zero at
 // the solver's current reaches (the rows whose values for the other player
 // are all zero).
