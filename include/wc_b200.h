@@ -85,6 +85,12 @@ typedef struct wc_result {
     uint64_t carry_snapshots;
     uint64_t carry_width;
     uint64_t weight_version;
+    /* SolveResult::oversize_route / card_exclusive_route: the job's device
+     * reservation (mutable bytes plus the tables rounded up to a power of two,
+     * serialize.rs:166-203) reached 4 / 6 GiB, so it was solved in a wave of
+     * its own. */
+    int32_t oversize_route;
+    int32_t card_exclusive_route;
 } wc_result;
 
 /* ---- service ------------------------------------------------------------ */
@@ -202,8 +208,13 @@ int wc_state_apply(const uint8_t* state, size_t len, uint32_t code, int unchecke
 int wc_state_query(const uint8_t* state, size_t len, int32_t* out);
 
 /* ---- batched solves ------------------------------------------------------ */
-/* Synchronous: upload, solve and download n jobs on device 0 of the
- * context. out has n entries, filled with library-owned arrays. */
+/* Synchronous: upload, solve and download n jobs on the context's devices.
+ * Jobs go to devices longest-first by the reference router's cost
+ * (engine/src/gpu/client.rs:282-291), each to the least-loaded device. On a
+ * device they run in memory-bounded waves (at most 44% of the free device
+ * memory each, or WC_WAVE_BYTES; at least two above 4 GiB so a wave's tables
+ * upload while the previous wave solves), in two device arenas the context
+ * keeps across calls. out has n entries, filled with library-owned arrays. */
 int wc_solve_batch(wc_ctx* ctx, wc_job* const* jobs, size_t n, wc_result* out);
 void wc_result_free(wc_result* r);
 /* Device-resident form: upload once, solve any number of times, read back. */

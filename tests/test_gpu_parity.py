@@ -3,6 +3,8 @@
 Fixtures follow the reference's GPU tests (engine/src/gpu/tests.rs:17-118):
 seeded solve-site roots, a few CFR iterations with snapshots, three skewed
 carried roots (tests.rs:56-70), and the test weight blob (tests.rs:34-48).
+Every CFR rule of search.rs:133-185 runs (linear, plus, dcfr, and the
+predictive pcfr / sapcfr, whose regret-matching step adds predict x delta).
 Tolerances:
   * no network / zero network: bit-exact strategies, root values and carries
     (the kernels keep the oracle's operation order and rounding);
@@ -80,7 +82,7 @@ def client_nonet(wc):
     c.close()
 
 
-@pytest.mark.parametrize("rule", ["plus", "linear"])
+@pytest.mark.parametrize("rule", ["plus", "linear", "dcfr", "pcfr", "sapcfr"])
 def test_no_network_bit_exact(wc, oracle, client_nonet, rule):
     cfg = wc.Cfg(depth=2, iters=16, snapshots=True, cfr=wc.Cfr.NAMED[rule])
     solve_and_compare(wc, oracle, client_nonet, roots_for(wc, SEEDS), cfg, None, exact=True)
@@ -102,7 +104,7 @@ def test_zero_network_bit_exact(wc, oracle):
         client.close()
 
 
-@pytest.mark.parametrize("rule", ["linear", "plus"])
+@pytest.mark.parametrize("rule", ["linear", "plus", "dcfr", "pcfr", "sapcfr"])
 def test_precise_network_parity(wc, oracle, rule):
     weights = wc.seeded_weights("test", 0xD15EA5E)
     client = wc.spawn(0, *weights, precise=True)
@@ -133,3 +135,34 @@ def test_submit_wait_matches_batch(wc, client_nonet):
     want = client_nonet.solve_batch(jobs)
     for g, w in zip(got, want):
         np.testing.assert_array_equal(g.strategy, w.strategy)
+
+
+def test_memory_bounded_waves_match_one_batch(wc, monkeypatch):
+    """wc_solve_batch in waves (WC_WAVE_BYTES forces several; each wave's
+    upload overlaps the previous wave's solve, in two arenas reused across
+    calls) gives, job for job, the results of one resident batch; the
+    reference's route flags stay clear for jobs this small."""
+    weights = wc.seeded_weights("test", 0xD15EA5E)
+    cfg = wc.Cfg(depth=2, iters=8, snapshots=True, cfr=wc.Cfr.PLUS)
+    jobs = [wc.PackedJob.from_root(r, cfg) for r in roots_for(wc, range(12))]
+    ref = wc.spawn(0, *weights, net="f16")
+    try:
+        b = ref.upload(jobs)
+        b.solve()
+        want = [b.result(j) for j in range(len(jobs))]
+        b.free()
+    finally:
+        ref.close()
+    total = sum(j.info["table_bytes"] for j in jobs)
+    monkeypatch.setenv("WC_WAVE_BYTES", str(max(1, 4 * total // 12)))  # a few jobs per wave
+    c = wc.spawn(0, *weights, net="f16")
+    try:
+        for _ in range(2):  # the second call reuses the arenas
+            got = c.solve_batch(jobs)
+            for g, w in zip(got, want):
+                np.testing.assert_array_equal(g.strategy, w.strategy)
+                np.testing.assert_array_equal(np.concatenate(g.root_values[0]), np.concatenate(w.root_values[0]))
+                np.testing.assert_array_equal(g.carries, w.carries)
+                assert not g.oversize_route and not g.card_exclusive_route
+    finally:
+        c.close()

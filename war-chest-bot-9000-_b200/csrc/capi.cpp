@@ -1,5 +1,7 @@
 // The C ABI (include/wc_b200.h) over the host builder and the device runtime.
+#include <algorithm>
 #include <atomic>
+#include <cstdlib>
 #include <cmath>
 #include <condition_variable>
 #include <cstring>
@@ -89,7 +91,7 @@ int upload_weights(DeviceCtx& d, const wc_weights* w) {
     return WC_OK;
 }
 
-void fill_result(Batch& b, size_t j, uint64_t version, wc_result* r) {
+void fill_result(Batch& b, size_t j, uint64_t version, wc_result* r, cudaStream_t stream = nullptr) {
     const JobBlob& jb = *b.jobs[j];
     const JobImage& J = *jb.img;
     std::memset(r, 0, sizeof *r);
@@ -104,7 +106,7 @@ void fill_result(Batch& b, size_t j, uint64_t version, wc_result* r) {
         r->carries = (uint16_t*)std::malloc(2ull * std::max<uint64_t>(r->carry_snapshots * r->carry_width, 1));
     }
     r->weight_version = version;
-    download(b, j, r->strategy, r->root_values, r->carries);
+    download(b, j, r->strategy, r->root_values, r->carries, stream);
 }
 
 bool same_schedule(const SolveCfg& a, const SolveCfg& b) {
@@ -113,15 +115,145 @@ bool same_schedule(const SolveCfg& a, const SolveCfg& b) {
            feq(a.cfr.beta, b.cfr.beta) && feq(a.cfr.gamma, b.cfr.gamma) && feq(a.cfr.predict, b.cfr.predict);
 }
 
-// Solve jobs[lo, hi) on one device, filling results.
-void solve_on(DeviceCtx& d, wc_job* const* jobs, size_t lo, size_t hi, wc_result* out) {
+// The reference's per-job reservation (engine/src/serialize.rs:166-203,
+// WorkVector::reserved_bytes): mutable bytes plus the table bytes rounded up
+// to a power of two. At 4 GiB the reference gives the job an isolated lane
+// wave (requires_exclusive_route, reported as oversize_route), at 6 GiB the
+// whole card (requires_card_exclusive_route); here both run in a wave of
+// their own and report the same flags.
+struct JobRoute {
+    size_t bytes = 0;
+    bool oversize = false, card_exclusive = false;
+};
+
+JobRoute route_of(const DeviceCtx& d, const JobBlob& jb) {
+    JobRoute r;
+    r.bytes = job_device_bytes(d, jb);
+    const size_t mut = r.bytes > jb.bytes ? r.bytes - jb.bytes : 0;
+    size_t tab = 1;
+    while (tab < jb.bytes) tab <<= 1;
+    const size_t reserved = mut + tab;
+    r.oversize = reserved >= (4ull << 30);
+    r.card_exclusive = reserved >= (6ull << 30);
+    return r;
+}
+
+// Bytes one wave may take: WC_WAVE_BYTES, else 44% of the device memory free
+// at first use (two waves are resident at once: one uploading, one solving).
+size_t wave_budget(DeviceCtx& d) {
+    if (!d.wave_budget) {
+        if (const char* e = std::getenv("WC_WAVE_BYTES")) d.wave_budget = (size_t)std::strtoull(e, nullptr, 10);
+        if (!d.wave_budget) {
+            size_t fr = 0, tot = 0;
+            check(cudaMemGetInfo(&fr, &tot), "device memory info");
+            d.wave_budget = (size_t)((double)fr * 0.44);
+        }
+    }
+    return d.wave_budget;
+}
+
+void ensure_arena(DeviceCtx& d, int a, size_t bytes) {
+    if (d.arena_bytes[a] >= bytes) return;
+    if (d.arena[a]) check(cudaFree(d.arena[a]), "free wave arena");
+    d.arena[a] = nullptr;
+    d.arena_bytes[a] = 0;
+    check(cudaMalloc((void**)&d.arena[a], bytes), "wave arena (out of memory)");
+    d.arena_bytes[a] = bytes;
+}
+
+// Solve jobs[idx] on one device in memory-bounded waves, filling out[idx].
+// The jobs are split into waves of at most wave_budget bytes (at least two
+// when the batch is larger than 4 GiB, so the next wave's tables upload on
+// the copy stream while this wave solves); a job the reference would route
+// alone gets a wave of its own. Two arenas of the device context hold the
+// waves in turn and are kept across calls.
+void solve_on(DeviceCtx& d, wc_job* const* jobs, const std::vector<size_t>& idx, wc_result* out) {
+    if (idx.empty()) return;
     std::lock_guard<std::mutex> lk(d.mu);
-    std::vector<const JobBlob*> v;
-    for (size_t i = lo; i < hi; ++i) v.push_back(jobs[i]->blob.get());
-    auto b = upload_batch(d, v);
-    enqueue_solve(*b);
-    check_batch_error(*b);
-    for (size_t i = lo; i < hi; ++i) fill_result(*b, i - lo, d.version, out + i);
+    check(cudaSetDevice(d.device), "set device");
+    if (!d.copy_stream) check(cudaStreamCreateWithFlags(&d.copy_stream, cudaStreamNonBlocking), "copy stream");
+    const size_t budget = wave_budget(d);
+    std::vector<JobRoute> rt(idx.size());
+    size_t ordinary = 0;
+    for (size_t i = 0; i < idx.size(); ++i) {
+        rt[i] = route_of(d, *jobs[idx[i]]->blob);
+        if (!rt[i].oversize) ordinary += rt[i].bytes;
+    }
+    std::vector<std::vector<size_t>> waves;  // positions into idx
+    size_t nw = std::max<size_t>((ordinary + budget - 1) / std::max<size_t>(budget, 1),
+                                 ordinary > (4ull << 30) ? 2 : 1);
+    {
+        const size_t target = (ordinary + nw - 1) / nw;
+        std::vector<size_t> cur;
+        size_t acc = 0;
+        for (size_t i = 0; i < idx.size(); ++i) {
+            if (rt[i].oversize) continue;
+            if (!cur.empty() && acc + rt[i].bytes > target && waves.size() + 1 < nw) {
+                waves.push_back(std::move(cur));
+                cur.clear();
+                acc = 0;
+            }
+            cur.push_back(i);
+            acc += rt[i].bytes;
+        }
+        if (!cur.empty()) waves.push_back(std::move(cur));
+        for (size_t i = 0; i < idx.size(); ++i)
+            if (rt[i].oversize) waves.push_back({i});
+    }
+    const size_t W = waves.size();
+    std::vector<std::unique_ptr<Batch>> B(W);
+    std::vector<cudaEvent_t> up(W, nullptr), done(W, nullptr);
+    auto finish = [&](size_t k) {
+        check(cudaEventSynchronize(done[k]), "wave solve");
+        check_batch_error(*B[k], d.copy_stream);
+        for (size_t q = 0; q < waves[k].size(); ++q) {
+            const size_t i = waves[k][q];
+            wc_result* r = out + idx[i];
+            fill_result(*B[k], q, d.version, r, d.copy_stream);
+            r->oversize_route = rt[i].oversize ? 1 : 0;
+            r->card_exclusive_route = rt[i].card_exclusive ? 1 : 0;
+        }
+        B[k].reset();
+    };
+    try {
+        for (size_t k = 0; k < W; ++k) {
+            const int a = (int)(k % 2);
+            std::vector<const JobBlob*> v;
+            size_t need = 0;
+            for (size_t i : waves[k]) {
+                v.push_back(jobs[idx[i]]->blob.get());
+                need += rt[i].bytes;
+            }
+            ensure_arena(d, a, need);  // wave k - 2, its last user, has finished
+            B[k] = upload_batch(d, v, d.arena[a], d.arena_bytes[a], d.copy_stream);
+            check(cudaEventCreateWithFlags(&up[k], cudaEventDisableTiming), "event");
+            check(cudaEventCreateWithFlags(&done[k], cudaEventDisableTiming), "event");
+            check(cudaEventRecord(up[k], d.copy_stream), "event");
+            check(cudaStreamWaitEvent(d.stream, up[k], 0), "wait upload");
+            enqueue_solve(*B[k]);
+            check(cudaEventRecord(done[k], d.stream), "event");
+            if (k >= 1) finish(k - 1);
+        }
+        finish(W - 1);
+    } catch (...) {
+        cudaStreamSynchronize(d.stream);
+        cudaStreamSynchronize(d.copy_stream);
+        for (cudaEvent_t e : up)
+            if (e) cudaEventDestroy(e);
+        for (cudaEvent_t e : done)
+            if (e) cudaEventDestroy(e);
+        throw;
+    }
+    for (cudaEvent_t e : up) cudaEventDestroy(e);
+    for (cudaEvent_t e : done) cudaEventDestroy(e);
+}
+
+// The reference router's cost of a job (engine/src/gpu/client.rs:282-291).
+uint64_t job_cost(const JobBlob& jb) {
+    const JobImage& J = *jb.img;
+    const uint64_t iters = (uint64_t)std::max(J.cfg.iters, 1);
+    return std::max<uint64_t>(1, (uint64_t)J.nrows_net * iters * 16 + (uint64_t)J.ncells * iters +
+                                     (uint64_t)J.reach_len * iters + jb.bytes / 16);
 }
 
 void worker_loop(wc_ctx* ctx, DeviceCtx* d) {
@@ -151,7 +283,9 @@ void worker_loop(wc_ctx* ctx, DeviceCtx* d) {
         std::string err;
         int status = WC_OK;
         try {
-            solve_on(*d, jobs.data(), 0, jobs.size(), res.data());
+            std::vector<size_t> all(jobs.size());
+            for (size_t i = 0; i < all.size(); ++i) all[i] = i;
+            solve_on(*d, jobs.data(), all, res.data());
         } catch (const std::exception& e) {
             status = WC_E_CUDA;
             err = e.what();
@@ -330,6 +464,9 @@ void wc_shutdown(wc_ctx* ctx) {
         if (d->B) cudaFree(d->B);
         if (d->LN) cudaFree(d->LN);
         if (d->fast_mem) cudaFree(d->fast_mem);
+        for (int a = 0; a < 2; ++a)
+            if (d->arena[a]) cudaFree(d->arena[a]);
+        if (d->copy_stream) cudaStreamDestroy(d->copy_stream);
         if (d->stream) cudaStreamDestroy(d->stream);
     }
     delete ctx;
@@ -644,14 +781,28 @@ int wc_solve_batch(wc_ctx* ctx, wc_job* const* jobs, size_t n, wc_result* out) {
             return fail(WC_E_ARG, "every job of a batch needs the same iterations, snapshots and CFR rule");
     return guarded([&] {
         size_t nd = ctx->devs.size();
+        // longest processing time first by the reference's job cost: each job
+        // to the device with the least work so far (heavy-tailed trees)
+        std::vector<size_t> order(n);
+        for (size_t i = 0; i < n; ++i) order[i] = i;
+        std::vector<uint64_t> cost(n);
+        for (size_t i = 0; i < n; ++i) cost[i] = job_cost(*jobs[i]->blob);
+        std::stable_sort(order.begin(), order.end(), [&](size_t a, size_t b) { return cost[a] > cost[b]; });
+        std::vector<std::vector<size_t>> mine(nd);
+        std::vector<uint64_t> load(nd, 0);
+        for (size_t i : order) {
+            const size_t d = (size_t)(std::min_element(load.begin(), load.end()) - load.begin());
+            mine[d].push_back(i);
+            load[d] += cost[i];
+        }
+        for (auto& m : mine) std::sort(m.begin(), m.end());
         std::vector<std::thread> th;
         std::vector<std::string> errs(nd);
         for (size_t d = 0; d < nd; ++d) {
-            size_t lo = n * d / nd, hi = n * (d + 1) / nd;
-            if (lo == hi) continue;
-            th.emplace_back([&, d, lo, hi] {
+            if (mine[d].empty()) continue;
+            th.emplace_back([&, d] {
                 try {
-                    solve_on(*ctx->devs[d], jobs, lo, hi, out);
+                    solve_on(*ctx->devs[d], jobs, mine[d], out);
                 } catch (const std::exception& e) {
                     errs[d] = e.what();
                 }

@@ -206,7 +206,7 @@ void build_fast_pack(DeviceCtx& d, const float* W, const float* B, const float* 
 // ---------------------------------------------------------------- batches
 
 Batch::~Batch() {
-    if (dmem) cudaFree(dmem);
+    if (dmem && owns_dmem) cudaFree(dmem);
     for (cudaEvent_t e : events) cudaEventDestroy(e);
     for (cudaEvent_t e : marks)
         if (e) cudaEventDestroy(e);
@@ -264,7 +264,8 @@ void add_items(std::vector<wcdev::WorkItem>& items, uint32_t job, uint32_t first
 
 }  // namespace
 
-std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobBlob*>& jobs) {
+std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobBlob*>& jobs, uint8_t* mem,
+                                    size_t mem_bytes, cudaStream_t copy_stream) {
     auto bp = std::make_unique<Batch>();
     Batch& b = *bp;
     b.dev = &dev;
@@ -402,7 +403,13 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
     size_t o_rj = A.take(4ull * row_job.size()), o_rl = A.take(4ull * row_local.size());
     size_t o_cj = A.take(4ull * cfg_job.size()), o_cl = A.take(4ull * cfg_local.size());
     b.dbytes = A.at;
-    check(cudaMalloc((void**)&b.dmem, std::max<size_t>(b.dbytes, 256)), "batch device memory");
+    if (mem) {
+        if (b.dbytes > mem_bytes) throw std::runtime_error("batch plan exceeds its arena");
+        b.dmem = mem;
+        b.owns_dmem = false;
+    } else {
+        check(cudaMalloc((void**)&b.dmem, std::max<size_t>(b.dbytes, 256)), "batch device memory");
+    }
     uint8_t* D = b.dmem;
     // ---- descriptors
     b.hj.resize(nj);
@@ -513,7 +520,7 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
         b.n_head_tiles = (uint32_t)head_tiles.size();
         b.d_err = reinterpret_cast<int*>(D + o_err);
     }
-    cudaStream_t s = dev.stream;
+    cudaStream_t s = copy_stream ? copy_stream : dev.stream;
     for (size_t j = 0; j < nj; ++j)
         check(cudaMemcpyAsync(D + plan[j].tables, jobs[j]->host, jobs[j]->bytes, cudaMemcpyHostToDevice, s), "upload job tables");
     check(cudaMemcpyAsync(b.d_jobs, b.hj.data(), sizeof(wcdev::JobDev) * nj, cudaMemcpyHostToDevice, s), "upload descriptors");
@@ -536,8 +543,37 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
         for (size_t j = 0; j < nj; ++j)
             check(cudaMemsetAsync(D + o_f16[j], 0, f16_bytes[j], s), "clear readout images");
     }
-    check(cudaStreamSynchronize(s), "batch upload");
+    if (!copy_stream) check(cudaStreamSynchronize(s), "batch upload");
     return bp;
+}
+
+// The device bytes a job takes in a batch plan: its tables, state and
+// outputs (as upload_batch lays them out), its share of the batch-wide
+// tensor-core images (per 128-row tile and per network row) and of the work
+// items, rounded up. Used to size waves before the exact plan is made.
+size_t job_device_bytes(const DeviceCtx& dev, const JobBlob& jb) {
+    const JobImage& J = *jb.img;
+    auto r = [](size_t x) { return (x + 255) & ~(size_t)255; };
+    size_t b = r(jb.bytes) + 4 * r(4ull * J.ncells) + r(4ull * J.reach_len) * (J.cfg.snapshots ? 2 : 1) +
+               r(4ull * J.val_len[0]) + r(4ull * J.val_len[1]) + r(4ull * J.ncells) +
+               r(4ull * J.ncarried * (J.root_nc[0] + J.root_nc[1])) + r(8ull * (J.root_nc[0] + J.root_nc[1]));
+    if (J.cfg.snapshots) b += r(2ull * (jb.nsnaps_kept - 1) * jb.carry_width);
+    const bool net = dev.have_net, exact = net && dev.precise;
+    if (net) {
+        b += r(4ull * 2 * 10 * NET_TYPE) + r(4ull * 2 * 10 * 3 * NET_POOL) + r(4ull * J.ncfg * NET_D) +
+             r(4ull * J.ncfg * NET_POOL);
+        if (exact) {
+            b += r(4ull * J.nrows_net * NET_D) + r(4ull * J.nrows_net * NET_JW) + r(4ull * J.nrows_net * 2 * NET_POOL);
+        } else {
+            const size_t tiles = (J.nrows_net + 127) / 128;
+            const size_t npass = (J.ncfg_player[0] + 127) / 128 + (J.ncfg_player[1] + 127) / 128;
+            b += r(4ull * 10 * NET_C) + r((65536ull + 16384ull) * npass) + tiles * (32768ull + 65536ull + 32768ull + 16) +
+                 J.nrows_net * (2ull * NET_JW + 8);
+        }
+    }
+    // descriptors, work items (one per <= 256 tasks of a level range) and row / config indices
+    b += sizeof(wcdev::JobDev) + 16ull * (J.ncells / 128 + 4 * J.nlevels + 8) + 8ull * (J.nrows_net + J.ncfg);
+    return b + b / 64 + 4096;
 }
 
 // ---------------------------------------------------------- the schedule
@@ -864,20 +900,21 @@ void download_conv(Batch& b, size_t job, float* out) {
     check(cudaStreamSynchronize(s), "download conv");
 }
 
-void check_batch_error(Batch& b) {
+void check_batch_error(Batch& b, cudaStream_t stream) {
     if (!b.d_err) return;
+    cudaStream_t s = stream ? stream : b.dev->stream;
     int e[4] = {0, 0, 0, 0};
-    check(cudaMemcpyAsync(e, b.d_err, 16, cudaMemcpyDeviceToHost, b.dev->stream), "read error flag");
-    check(cudaStreamSynchronize(b.dev->stream), "read error flag");
+    check(cudaMemcpyAsync(e, b.d_err, 16, cudaMemcpyDeviceToHost, s), "read error flag");
+    check(cudaStreamSynchronize(s), "read error flag");
     if (e[0])
         throw std::runtime_error("a tensor-core wait exceeded its time limit (code " + std::to_string(e[0]) +
                                  (e[0] > 10 ? ", in-flight work did not drain: reset the device context" : "") + ")");
 }
 
-void download(Batch& b, size_t job, float* strategy, float* roots, uint16_t* carries) {
+void download(Batch& b, size_t job, float* strategy, float* roots, uint16_t* carries, cudaStream_t stream) {
     const JobBlob& jb = *b.jobs[job];
     const JobImage& J = *jb.img;
-    cudaStream_t s = b.dev->stream;
+    cudaStream_t s = stream ? stream : b.dev->stream;
     if (strategy)
         check(cudaMemcpyAsync(strategy, b.dmem + b.out_off[4 * job], 4ull * J.ncells, cudaMemcpyDeviceToHost, s), "download strategy");
     if (roots)

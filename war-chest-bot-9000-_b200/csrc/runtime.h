@@ -32,6 +32,14 @@ struct DeviceCtx {
     uint8_t* fast_mem = nullptr;
     wcdev::FastNetDev fast{};
     std::mutex mu;  // one batch at a time per device
+    // Waves (solve_waves): two device arenas reused across calls, so a wave's
+    // tables upload on copy_stream while the previous wave solves on
+    // `stream`; wave_budget bounds a wave's device bytes (0: set from the
+    // free memory on first use, or from WC_WAVE_BYTES).
+    uint8_t* arena[2] = {nullptr, nullptr};
+    size_t arena_bytes[2] = {0, 0};
+    cudaStream_t copy_stream = nullptr;
+    size_t wave_budget = 0;
 };
 
 // Build the fast-path weight pack from the fp32 blob (host arrays) and upload it.
@@ -68,6 +76,7 @@ struct Batch {
     std::vector<const JobBlob*> jobs;
     uint8_t* dmem = nullptr;
     size_t dbytes = 0;
+    bool owns_dmem = true;  // false when placed in a device arena of the context
     std::vector<wcdev::JobDev> hj;
     wcdev::JobDev* d_jobs = nullptr;
     struct Range { uint32_t off = 0, n = 0; };
@@ -121,7 +130,14 @@ enum TimeClass {
 // After a profiled solve has finished: summed milliseconds per class.
 void read_profile(Batch& b, double* ms /* N_TC */);
 
-std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobBlob*>& jobs);
+// Plan a batch and copy its tables to the device. Without `mem` the batch
+// allocates its own device memory and the copies finish before the return;
+// with `mem` (mem_bytes long, e.g. a wave arena) it is placed there, and with
+// `copy_stream` the copies are only enqueued on that stream.
+std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobBlob*>& jobs, uint8_t* mem = nullptr,
+                                    size_t mem_bytes = 0, cudaStream_t copy_stream = nullptr);
+// An upper bound of the device bytes a job takes in a batch (wave sizing).
+size_t job_device_bytes(const DeviceCtx& dev, const JobBlob& jb);
 // Run the whole solve on the device (asynchronous on dev.stream).
 void enqueue_solve(Batch& b);
 // Leaf evaluation alone: the per-solve network, the initial (uniform)
@@ -135,7 +151,7 @@ void download_leaf_values(Batch& b, size_t job, int p, float* out);
 // their row means).
 void download_board_rows(Batch& b, size_t job, float* pb, float* jp);
 // Copy one job's results to host buffers (synchronous). Any pointer may be null.
-void download(Batch& b, size_t job, float* strategy, float* roots, uint16_t* carries);
+void download(Batch& b, size_t job, float* strategy, float* roots, uint16_t* carries, cudaStream_t stream = nullptr);
 
 // After a solve: exploitability passes of every job's live root under its
 // average strategy (Solver::nash_conv, search.rs:1884-1907); download_conv
@@ -146,6 +162,6 @@ void download_conv(Batch& b, size_t job, float* out);
 
 void check(cudaError_t e, const char* what);
 // Throw if a kernel recorded a bounded-wait timeout during the last solve.
-void check_batch_error(Batch& b);
+void check_batch_error(Batch& b, cudaStream_t stream = nullptr);
 
 }  // namespace wc

@@ -53,7 +53,7 @@ class _Result(C.Structure):
     _fields_ = [("strategy", C.POINTER(C.c_float)), ("ncells", C.c_uint64),
                 ("root_values", C.POINTER(C.c_float)), ("nroots", C.c_uint64), ("root_width", C.c_uint64),
                 ("carries", C.POINTER(C.c_uint16)), ("carry_snapshots", C.c_uint64), ("carry_width", C.c_uint64),
-                ("weight_version", C.c_uint64)]
+                ("weight_version", C.c_uint64), ("oversize_route", C.c_int32), ("card_exclusive_route", C.c_int32)]
 
 
 def _load() -> C.CDLL:
@@ -357,6 +357,8 @@ class SolveResult:
     root_values: List[List[np.ndarray]]
     carries: Optional[np.ndarray]
     weight_version: int
+    oversize_route: bool = False
+    card_exclusive_route: bool = False
 
 
 def _take_result(r: _Result, job: PackedJob) -> SolveResult:
@@ -368,7 +370,7 @@ def _take_result(r: _Result, job: PackedJob) -> SolveResult:
     if r.carry_snapshots:
         carries = np.ctypeslib.as_array(r.carries, (r.carry_snapshots * r.carry_width,)).copy().view(np.float16)
         carries = carries.reshape(r.carry_snapshots, r.carry_width)
-    out = SolveResult(strat, rv, carries, r.weight_version)
+    out = SolveResult(strat, rv, carries, r.weight_version, bool(r.oversize_route), bool(r.card_exclusive_route))
     lib().wc_result_free(C.byref(r))
     return out
 
