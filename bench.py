@@ -52,6 +52,9 @@ def parse():
                     help="value network: tcgen05 with f16 / bf16 operands, fp32 exact, or none")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg (profiling runs)")
     ap.add_argument("--build-threads", type=int, default=0)
+    ap.add_argument("--workload", default="solve", choices=["solve", "leaf"],
+                    help="solve: the configs[2] batched solve (the bench line); leaf: configs[1], value-net leaf "
+                         "inference alone at 1K / 16K / 256K rows (one JSON line per batch size, not a bench line)")
     return ap.parse_args()
 
 
@@ -258,10 +261,87 @@ def cpu_baseline(oracle, cfg, weights, seeds):
                       f"extrapolated; {wall:.1f} s wall"}
 
 
+def leaf_workload(args):
+    """the value network alone on rows from seeded random
+    playouts of 10-60 plies. Positions: the roots of seeds 0.. with a seeded
+    ply count in [10, 60] (wc_root_generate: seeded draft, uniform decisions,
+    on to the next MainPlay); rows: the network rows of their depth-1
+    subgames (each a position one coin play later, with both players' belief
+    supports as the configs), taken until the batch size is reached. A leaf
+    inference of a row is the trunk once plus both seat queries (join and
+    readout over the row's configs), as the reference evaluates it
+    (search.rs:1464-1636); the per-config encoder runs once per subgame.
+    Times are CUDA events of wc_batch_leaf_values (per-solve network once,
+    then the two seat queries). Accuracy: leaf values of the 16-bit paths
+    against the fp32 path, norm-wise relative, over the whole batch."""
+    import warchest_b200 as wc
+
+    wc.set_cap_marker_value(0.0)
+    weights = wc.seeded_weights("he", 0)
+    cfg = wc.Cfg(depth=1, iters=0, snapshots=False, cfr=wc.Cfr.PLUS)
+    rng = np.random.default_rng(2024)
+    hbm, tflops, src = peaks()
+    threads = os.cpu_count() or 1
+    pool, seed = [], 0  # depth-1 jobs of seeds 0, 1, ... in seed order (built natively, in chunks)
+    for target in (1024, 16384, 262144):
+        while sum(j.info["net_rows"] for j in pool) < target:
+            roots = []
+            for s in range(seed, seed + 2048):
+                try:
+                    roots.append(wc.generate_root(s, int(rng.integers(10, 61))))
+                except wc.SolveError:  # the game ended before the root
+                    pass
+            seed += 2048
+            pool += [j for j in wc.PackedJob.build_many(roots, cfg, threads=threads)
+                     if j is not None and j.info["net_rows"] > 0]
+        jobs, rows = [], 0
+        for j in pool:
+            if rows >= target:
+                break
+            jobs.append(j)
+            rows += j.info["net_rows"]
+        counts = np.sum([j.counts() for j in jobs], axis=0)
+        configs = sum(j.info["configs"] for j in jobs)
+        flops = 17.0e6 * rows + 2 * 197.6e3 * rows + 512 * (counts[14] + counts[15]) + 170e3 * configs
+        line = {"workload": f"configs[1]: leaf inference alone, {rows} rows (target {target}) from {len(jobs)} "
+                            f"positions of 10-60 seeded playout plies", "rows": rows, "configs": int(configs)}
+        vals = {}
+        for net in ("exact", "bf16", "f16"):
+            c = wc.spawn(0, *weights, net=net)
+            try:
+                b = c.upload(jobs)
+                for _ in range(3):  # warm-up
+                    b.leaf_values(0)
+                t = []
+                for _ in range(5):
+                    a = b.leaf_values(0, profile=True)
+                    z = b.leaf_values(1, profile=True)
+                    t.append(a["net_solve"] + a["leaf"] + z["leaf"])
+                ms = float(np.median(t))
+                parts = []
+                for p in (0, 1):
+                    b.leaf_values(p)
+                    parts.append(np.concatenate([b.leaf_values_of(j, p) for j in range(len(jobs))]))
+                vals[net] = np.concatenate(parts)
+                b.free()
+            finally:
+                c.close()
+            line[net] = {"ms": ms, "rows_per_s": rows / (ms / 1e3), "tflops": flops / (ms / 1e3) / 1e12,
+                         "frac_of_bf16_peak": flops / (ms / 1e3) / 1e12 / tflops}
+        for net in ("bf16", "f16"):
+            line[net]["rel_err_vs_fp32"] = float(np.linalg.norm(vals[net] - vals["exact"]) /
+                                                 np.linalg.norm(vals["exact"]))
+        line["peak_source"] = src
+        print(json.dumps(line), flush=True)
+
+
 def main():
     global PLIES
     args = parse()
     PLIES = args.plies
+    if args.workload == "leaf":
+        leaf_workload(args)
+        return
     if args.impl == "reference":
         # the CPU reference runs on rank 0 alone; other ranks exit without work
         world = int(os.environ.get("WORLD_SIZE", "1"))

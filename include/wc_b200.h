@@ -280,6 +280,42 @@ int wc_debug_umma_gemm(const uint16_t* a, const uint16_t* b, int k, int n, float
  * serialised by the caller. */
 int wc_debug_umma_gemm_static(const uint16_t* a, const uint16_t* b, int k, int n, float* d);
 
+/* ---- continual re-solving ------------------------------------------------- */
+/* A game whose seats both play by solving: at a decision it builds the
+ * depth-limited subgame (Solver::new), the caller solves it, and the game
+ * then walks the solved tree with the real play (each decision sampled from
+ * the CFR average of the true config, both beliefs Bayes-filtered on the
+ * public observations and the draws), until the walk leaves the tree at a
+ * leaf. The next decision re-solves, and its Phase 2 values the carried
+ * beliefs: the exit's beliefs under the solve's per-iterate averages (from
+ * the carry store, f16) and the live belief. Replaces the reference's game
+ * actor (engine/src/selfplay.rs:466-905: finish_walk, Game::advance,
+ * Game::resume; engine/src/gpu/client.rs:20-92 CarryStore::select); as
+ * there, a subgame over the node cap falls back to one uniform decision and
+ * drops the carried beliefs. Snapshots are always kept. */
+typedef struct wc_game wc_game;
+enum { WC_GAME_SOLVE = 1, WC_GAME_ENDED = 2 };
+/* From a seeded game (make_game, selfplay.rs:59-81) or from a root (root
+ * encoding above: the state and both beliefs, e.g. wc_root_generate_wide's
+ * belief-heavy roots). `seed` drives the game's own draws and sampling. */
+int wc_game_new(uint64_t seed, int random_draft, const wc_solve_cfg* cfg, wc_game** out);
+int wc_game_from_root(const uint8_t* root, size_t len, uint64_t seed, const wc_solve_cfg* cfg, wc_game** out);
+/* Stop (WC_GAME_ENDED) once n subgames have been solved and the walk of the
+ * last has left its tree (0: play to the end of the game). */
+int wc_game_set_max_solves(wc_game* g, uint32_t n);
+/* Play until the next solve: *step = WC_GAME_SOLVE with *job a new job (the
+ * subgame with its carried roots, owned by the caller: solve it, pass its
+ * result to wc_game_resume, then free it), or WC_GAME_ENDED with *job NULL. */
+int wc_game_advance(wc_game* g, wc_job** job, int* step);
+/* Start the walk of the pending subgame with its solve's result. */
+int wc_game_resume(wc_game* g, const wc_job* job, const wc_result* res);
+/* decisions, solves, capped solves, walk decisions, walk draws, ended,
+ * winner (-1: none), walking. */
+int wc_game_counters(const wc_game* g, int64_t* out8);
+/* The game's current state and beliefs in the root encoding. */
+int wc_game_root(const wc_game* g, uint8_t* buf, size_t cap, size_t* len);
+void wc_game_free(wc_game* g);
+
 /* ---- streaming submit / wait ---------------------------------------------- */
 /* The job stays owned by the caller and must outlive the wc_wait of its
  * ticket; free it (wc_job_free) after that wait returns. */

@@ -12,6 +12,7 @@
 #include <vector>
 
 #include "../war-chest-bot-9000-_b200/csrc/host/roots.h"
+#include "../war-chest-bot-9000-_b200/csrc/host/walk.h"
 #include "cfr_cpu.h"
 
 using namespace oracle;
@@ -330,6 +331,54 @@ int oracle_leaf_parts(void* h, int p, float* hout, float* opp_reach, uint32_t* c
         for (size_t c = 0; c < t.nc(i, p); ++c) cidx[at++] = idx[c];
     }
     return 0;
+}
+
+// The continual re-solving walk (the host Game, selfplay.rs:466-905) with
+// every subgame solved here by the CPU solver, which carries its exit beliefs
+// in f32 as the reference's CPU walk does. Writes the game's counters and
+// its final state and beliefs in the root encoding.
+int oracle_walk(uint64_t seed, int random_draft, const OracleCfg* cfg, const float* w, const float* b,
+                const float* ln, uint32_t max_solves, int64_t* counters8, uint8_t* root_out, size_t cap,
+                size_t* len) {
+    try {
+        auto net = std::make_shared<Net>();
+        if (w) {
+            net->w.assign(w, w + net->L.w_len);
+            net->b.assign(b, b + net->L.b_len);
+            net->ln.assign(ln, ln + net->L.ln_len);
+            net->empty = false;
+        }
+        wc::Game g(seed, random_draft != 0, to_cfg(cfg));
+        g.set_max_solves(max_solves);
+        while (g.advance() == wc::Game::NEED_SOLVE) {
+            std::shared_ptr<wc::Tree> tree(g.take_pending_tree().release());
+            auto sv = std::make_shared<Solver>(*tree, net.get());
+            sv->multistep(tree->cfg.iters);
+            std::vector<std::vector<float>> roots;
+            const size_t w0 = tree->nc(0, 0) + tree->nc(0, 1);
+            for (uint32_t r = 0; r < g.pending_nroots(); ++r)
+                roots.emplace_back(g.pending_roots().begin() + r * w0, g.pending_roots().begin() + (r + 1) * w0);
+            sv->value_under(roots);  // Phase 2, as the solve would run it
+            wc::WalkResult res;
+            res.strategy = sv->average();
+            res.cpu_carried = [tree, sv, net](uint32_t node) { return sv->carried_beliefs(node); };
+            g.resume(res);
+        }
+        g.counters(counters8);
+        wc::Root r;
+        r.s = g.state();
+        r.ctx = g.ctx();
+        r.bel[0] = g.belief(0);
+        r.bel[1] = g.belief(1);
+        std::vector<uint8_t> bytes = wc::root_to_bytes(r);
+        if (len) *len = bytes.size();
+        if (!root_out || bytes.size() > cap) { g_err = "root buffer too small"; return 2; }
+        std::memcpy(root_out, bytes.data(), bytes.size());
+        return 0;
+    } catch (const std::exception& e) {
+        g_err = e.what();
+        return 1;
+    }
 }
 
 // Per network row, the number of player-p configs it carries (the row

@@ -153,6 +153,25 @@ class Oracle:
             self.h = C.c_void_p()
 
 
+def walk(seed: int, cfg, weights=None, max_solves: int = 0, random_draft: bool = True):
+    """The continual re-solving game with every subgame solved by the CPU
+    solver (oracle_walk): (counters dict, final root bytes)."""
+    if weights is None:
+        w = b = ln = None
+    else:
+        _, wa, ba, la = weights
+        w, b, ln = wa.ctypes.data, ba.ctypes.data, la.ctypes.data
+    ctr = (C.c_int64 * 8)()
+    buf = C.create_string_buffer(1 << 22)
+    n = C.c_size_t()
+    rc = lib().oracle_walk(C.c_uint64(seed), int(random_draft), C.byref(ocfg(cfg)), w, b, ln, C.c_uint32(max_solves),
+                           ctr, buf, C.c_size_t(1 << 22), C.byref(n))
+    if rc:
+        raise RuntimeError(lib().oracle_last_error().decode())
+    names = ["decisions", "solves", "capped", "walk_decisions", "walk_draws", "ended", "winner", "walking"]
+    return dict(zip(names, list(ctr))), buf.raw[: n.value]
+
+
 def micro_root(seed: int, warmup: int, plies: int):
     buf = C.create_string_buffer(1 << 20)
     n = C.c_size_t()

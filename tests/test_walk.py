@@ -1,0 +1,34 @@
+"""Continual re-solving (engine/src/selfplay.rs:466-905): a game of two
+solving seats that walks each solved subgame with the real play and
+re-solves where the walk leaves the tree, carrying the exit beliefs into
+the next solve's Phase 2.
+
+CPU: the walk driven by the CPU solver (oracle_walk) plays whole games with
+every lockstep check of the reference walk holding (the tree's supports
+equal the Bayes-filtered beliefs at every decision and after every draw run,
+the true config never leaves the belief). GPU (test_gpu_walk.py): the same
+games solved on the device give the same trajectory.
+"""
+import pytest
+
+
+@pytest.mark.parametrize("seed,depth", [(1, 1), (2, 2)])
+def test_cpu_walk_plays_whole_games(wc, oracle, seed, depth):
+    cfg = wc.Cfg(depth=depth, iters=8, snapshots=True, cfr=wc.Cfr.PLUS, node_cap=20000)
+    ctr, root = oracle.walk(seed, cfg, None, max_solves=0)
+    print(ctr)
+    assert ctr["ended"] == 1 and ctr["solves"] >= 2
+    # every solved tree is walked from its root; deeper trees hold several decisions
+    assert ctr["walk_decisions"] >= ctr["solves"] + ctr["capped"] * 0
+    if depth > 1:
+        assert ctr["walk_decisions"] > ctr["solves"]
+    assert ctr["winner"] in (-1, 0, 1)
+
+
+def test_cpu_walk_with_network_stops_after_max_solves(wc, oracle):
+    weights = wc.seeded_weights("test", 0xD15EA5E)
+    cfg = wc.Cfg(depth=2, iters=8, snapshots=True, cfr=wc.Cfr.PLUS, node_cap=20000)
+    ctr, root = oracle.walk(3, cfg, weights, max_solves=3)
+    print(ctr)
+    assert ctr["solves"] == 3 and ctr["ended"] == 1 and ctr["walking"] == 0
+    assert len(root) > 0

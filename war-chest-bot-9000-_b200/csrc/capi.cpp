@@ -14,12 +14,17 @@
 #include "../../include/wc_b200.h"
 #include "cuda/kernels.h"
 #include "host/job.h"
+#include "host/walk.h"
 #include "runtime.h"
 
 using namespace wc;
 
 struct wc_job {
     std::unique_ptr<JobBlob> blob;
+};
+
+struct wc_game {
+    std::unique_ptr<Game> g;
 };
 
 struct wc_batch {
@@ -536,6 +541,93 @@ bool parse_state(const uint8_t* st, size_t len, State* s) {
     return st && read_state(st, len, &at, s) && at == len;
 }
 }  // namespace
+
+// ---- continual re-solving (selfplay.rs:466-905)
+
+int wc_game_new(uint64_t seed, int random_draft, const wc_solve_cfg* cfg, wc_game** out) {
+    if (!cfg || !out) return fail(WC_E_ARG, "null argument");
+    return guarded([&] {
+        auto g = std::make_unique<wc_game>();
+        g->g = std::make_unique<Game>(seed, random_draft != 0, solve_cfg(cfg));
+        *out = g.release();
+        return (int)WC_OK;
+    });
+}
+
+int wc_game_from_root(const uint8_t* root, size_t len, uint64_t seed, const wc_solve_cfg* cfg, wc_game** out) {
+    if (!root || !cfg || !out) return fail(WC_E_ARG, "null argument");
+    return guarded([&] {
+        Root r;
+        if (!root_from_bytes(root, len, &r)) return fail(WC_E_ARG, "malformed root bytes");
+        auto g = std::make_unique<wc_game>();
+        g->g = std::make_unique<Game>(r, seed, solve_cfg(cfg));
+        *out = g.release();
+        return (int)WC_OK;
+    });
+}
+
+int wc_game_set_max_solves(wc_game* g, uint32_t n) {
+    if (!g) return fail(WC_E_ARG, "null game");
+    g->g->set_max_solves(n);
+    return WC_OK;
+}
+
+int wc_game_advance(wc_game* g, wc_job** job, int* step) {
+    if (!g || !job || !step) return fail(WC_E_ARG, "null argument");
+    *job = nullptr;
+    return guarded([&] {
+        const Game::Step st = g->g->advance();
+        *step = st == Game::NEED_SOLVE ? WC_GAME_SOLVE : WC_GAME_ENDED;
+        if (st == Game::NEED_SOLVE) {
+            std::unique_ptr<Tree> tree = g->g->take_pending_tree();
+            auto j = std::make_unique<wc_job>();
+            j->blob = make_blob(flatten(*tree, g->g->pending_roots(), g->g->pending_nroots()));
+            *job = j.release();
+        }
+        return (int)WC_OK;
+    });
+}
+
+int wc_game_resume(wc_game* g, const wc_job* job, const wc_result* res) {
+    if (!g || !job || !res) return fail(WC_E_ARG, "null argument");
+    return guarded([&] {
+        const JobBlob& jb = *job->blob;
+        const JobImage& J = *jb.img;
+        if (res->ncells != J.ncells) return fail(WC_E_ARG, "the result is not this job's");
+        WalkResult w;
+        w.strategy.assign(res->strategy, res->strategy + res->ncells);
+        w.carry_snapshots = (uint32_t)res->carry_snapshots;
+        w.carry_width = (uint32_t)res->carry_width;
+        if (res->carries) w.carries.assign(res->carries, res->carries + res->carry_snapshots * res->carry_width);
+        const uint32_t* co = jb.arr<uint32_t>(JobBlob::CARRY_OFF);
+        w.carry_off.assign(co, co + jb.nexit + 1);
+        w.exit_nodes = J.exit_nodes;
+        g->g->resume(w);
+        return (int)WC_OK;
+    });
+}
+
+int wc_game_counters(const wc_game* g, int64_t* out) {
+    if (!g || !out) return fail(WC_E_ARG, "null argument");
+    g->g->counters(out);
+    return WC_OK;
+}
+
+int wc_game_root(const wc_game* g, uint8_t* buf, size_t cap, size_t* len) {
+    if (!g) return fail(WC_E_ARG, "null game");
+    Root r;
+    r.s = g->g->state();
+    r.ctx = g->g->ctx();
+    r.bel[0] = g->g->belief(0);
+    r.bel[1] = g->g->belief(1);
+    std::vector<uint8_t> b = root_to_bytes(r);
+    if (len) *len = b.size();
+    if (!buf || b.size() > cap) return fail(WC_E_ARG, "root buffer too small");
+    std::memcpy(buf, b.data(), b.size());
+    return WC_OK;
+}
+
+void wc_game_free(wc_game* g) { delete g; }
 
 int wc_state_legal_actions(const uint8_t* state, size_t len, uint32_t* codes, size_t cap, size_t* n) {
     return guarded([&] {

@@ -103,6 +103,14 @@ def _load() -> C.CDLL:
         "wc_state_apply": (I, [C.c_char_p, C.c_size_t, C.c_uint32, I, C.c_char_p, C.c_size_t, P(C.c_size_t)]),
         "wc_state_query": (I, [C.c_char_p, C.c_size_t, P(C.c_int32)]),
         "wc_roots_file_split": (I, [C.c_char_p, C.c_size_t, P(U64), P(U64), C.c_size_t, P(C.c_size_t)]),
+        "wc_game_new": (I, [U64, I, P(_SolveCfg), P(VP)]),
+        "wc_game_from_root": (I, [C.c_char_p, C.c_size_t, U64, P(_SolveCfg), P(VP)]),
+        "wc_game_set_max_solves": (I, [VP, C.c_uint32]),
+        "wc_game_advance": (I, [VP, P(VP), P(C.c_int)]),
+        "wc_game_resume": (I, [VP, VP, P(_Result)]),
+        "wc_game_counters": (I, [VP, P(C.c_int64)]),
+        "wc_game_root": (I, [VP, C.c_char_p, C.c_size_t, P(C.c_size_t)]),
+        "wc_game_free": (None, [VP]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -419,6 +427,35 @@ class GpuClient:
         _check(lib().wc_solve_batch(self._ctx, arr, n, res))
         return [_take_result(res[i], jobs[i]) for i in range(n)]
 
+    def play(self, games: Sequence["Game"]) -> int:
+        """Drive games to their end (the reference's GPU game stream,
+        selfplay.rs:1224, in lockstep rounds): each round every live game
+        advances to its next solve, the pending subgames are solved together
+        in one wc_solve_batch, and each game resumes its walk with its own
+        result. Returns the subgames solved."""
+        live, solved = list(games), 0
+        while live:
+            pend = []
+            for g in live:
+                job = g.advance()
+                if job is not None:
+                    pend.append((g, job))
+            if not pend:
+                break
+            n = len(pend)
+            arr = (C.c_void_p * n)(*[j._h.value for _, j in pend])
+            res = (_Result * n)()
+            _check(lib().wc_solve_batch(self._ctx, arr, n, res))
+            try:
+                for i, (g, j) in enumerate(pend):
+                    _check(lib().wc_game_resume(g._h, j._h, C.byref(res[i])))
+            finally:
+                for i in range(n):
+                    lib().wc_result_free(C.byref(res[i]))
+            solved += n
+            live = [g for g, _ in pend]
+        return solved
+
     def upload(self, jobs: Sequence[PackedJob], dev_index: int = 0) -> "DeviceBatch":
         n = len(jobs)
         arr = (C.c_void_p * n)(*[j._h.value for j in jobs])
@@ -516,6 +553,50 @@ class DeviceBatch:
     def __del__(self):
         if getattr(self, "_h", None) is not None and self._h.value and _lib is not None:
             self.free()
+
+
+class Game:
+    """A game of two solving seats with continual re-solving (selfplay.rs:
+    466-905 Game::advance / resume): advance() plays to the next subgame
+    solve and returns its job (or None when the game is over); the caller
+    solves it and calls resume(job, result) (GpuClient.play drives many games
+    this way)."""
+
+    COUNTERS = ["decisions", "solves", "capped", "walk_decisions", "walk_draws", "ended", "winner", "walking"]
+
+    def __init__(self, cfg: Cfg, seed: int = 0, random_draft: bool = True, root: Optional[bytes] = None,
+                 max_solves: int = 0):
+        self.cfg = cfg
+        h = C.c_void_p()
+        if root is None:
+            _check(lib().wc_game_new(seed, int(random_draft), C.byref(cfg._c()), C.byref(h)))
+        else:
+            _check(lib().wc_game_from_root(root, len(root), seed, C.byref(cfg._c()), C.byref(h)))
+        self._h = h
+        if max_solves:
+            _check(lib().wc_game_set_max_solves(self._h, max_solves))
+
+    def advance(self) -> Optional[PackedJob]:
+        job, step = C.c_void_p(), C.c_int()
+        _check(lib().wc_game_advance(self._h, C.byref(job), C.byref(step)))
+        return PackedJob(job.value, b"", self.cfg) if step.value == 1 else None
+
+    def counters(self) -> dict:
+        out = (C.c_int64 * 8)()
+        _check(lib().wc_game_counters(self._h, out))
+        return dict(zip(self.COUNTERS, list(out)))
+
+    def root(self) -> bytes:
+        """The current state and beliefs in the root encoding."""
+        n = C.c_size_t()
+        buf = C.create_string_buffer(1 << 22)
+        _check(lib().wc_game_root(self._h, buf, 1 << 22, C.byref(n)))
+        return buf.raw[: n.value]
+
+    def __del__(self):
+        if getattr(self, "_h", None) is not None and self._h.value and _lib is not None:
+            lib().wc_game_free(self._h)
+            self._h = C.c_void_p()
 
 
 NET_MODES = {"bf16": 0, "exact": 1, "f16": 2}
