@@ -152,8 +152,7 @@ def algorithmic_work(jobs):
     tensor FLOPs for the network kernels. Per unit:
       rows     24 B per legal cell (regret R/W, current W, child value, index) + 8 B per row
       vgather  12 B per entry (index, weight, source value) + 8 B per output
-      reach    16 B per cell entry (source, weight, parent reach, strategy), 16 B per draw entry, 8 B per
-               output; then the average pass: 12 B per decision cell (current, sum R/W), 12 B per row
+      reach    24 B per cell entry, 16 B per draw entry, 8 B per output
       pool     8 B per leaf-config entry (reach, column) + 128 B per row (the f16 pooled atom)
       join     4 x 2*128*128 FLOP per network row
       head     2*128*256 FLOP per network row + 2*256 per leaf-config entry of the traverser
@@ -171,8 +170,7 @@ def algorithmic_work(jobs):
     return {
         "rows": ("hbm", (24 * (c[0] + c[1]) + 8 * (c[2] + c[3])) * pairs),
         "vgather": ("hbm", (12 * (c[4] + c[5]) + 8 * (c[6] + c[7])) * pairs),
-        "reach": ("hbm", (16 * (c[8] + c[9]) + 16 * (c[10] + c[11]) + 8 * (c[12] + c[13]) +
-                          12 * (c[0] + c[1]) + 12 * (c[2] + c[3])) * pairs),
+        "reach": ("hbm", (24 * (c[8] + c[9]) + 16 * (c[10] + c[11]) + 8 * (c[12] + c[13])) * pairs),
         "pool": ("hbm", (8 * entries + 128 * rows) * calls),
         "join": ("tensor", 4 * 2 * 128 * 128 * rows * calls),
         "head": ("tensor", (2 * 128 * 256 * rows + 2 * 256 * entries) * calls),

@@ -148,8 +148,10 @@ __global__ void k_vgather(const JobDev* __restrict__ jobs, const WorkItem* __res
 }
 
 // Reach into one child config: sum over (parent config, weight) entries.
+// With sum_update, every decision entry also folds the fresh reach-weighted
+// strategy into the running sum: sum = sum * dg + reach * cur.
 __global__ void k_rgather(const JobDev* __restrict__ jobs, const WorkItem* __restrict__ items, int strat_sel,
-                          int which_reach) {
+                          int which_reach, int sum_update, float dg) {
     const WorkItem wi = items[blockIdx.x];
     if (threadIdx.x >= wi.count) return;
     const JobDev& J = jobs[wi.job];
@@ -163,39 +165,13 @@ __global__ void k_rgather(const JobDev* __restrict__ jobs, const WorkItem* __res
         float prod;
         if (w < J.ncells) {
             prod = reach[J.rge_src[e]] * strat[w];
+            if (sum_update) J.sum[w] = J.sum[w] * dg + prod;
         } else {
             prod = reach[J.rge_src[e]] * J.drawp[w - J.ncells];
         }
         acc += prod;
     }
     reach[wi.out_first + threadIdx.x] = acc;
-}
-
-// The average update of one work item of decision rows (search.rs:1818-1835
-// with backprop's discount): sum = sum * dg + reach(row) * cur, cell by cell
-// in coalesced order. Each row's reach is read once into shared memory, and
-// each cell finds its row through a shared-memory map (an item holds at most
-// WI_TASKS rows and ROW_CELL_CAP cells, or a single longer row). The two
-// products and the sum are separately rounded, as in the reference.
-__global__ void k_avg(const JobDev* __restrict__ jobs, const WorkItem* __restrict__ items, float dg) {
-    __shared__ float s_reach[WI_TASKS];
-    __shared__ uint8_t s_row[ROW_CELL_CAP];
-    const WorkItem wi = items[blockIdx.x];
-    const JobDev& J = jobs[wi.job];
-    const uint32_t c0 = J.row_off[wi.first], nc = J.row_off[wi.first + wi.count] - c0;
-    const bool staged = nc <= (uint32_t)ROW_CELL_CAP;
-    if (threadIdx.x < wi.count) {
-        const uint32_t row = wi.first + threadIdx.x;
-        s_reach[threadIdx.x] = J.reach[J.row_ridx[row]];
-        if (staged)
-            for (uint32_t c = J.row_off[row] - c0; c < J.row_off[row + 1] - c0; ++c) s_row[c] = (uint8_t)threadIdx.x;
-    }
-    __syncthreads();
-    for (uint32_t i = threadIdx.x; i < nc; i += blockDim.x) {
-        const uint32_t c = c0 + i;
-        const float r = s_reach[staged ? s_row[i] : 0];
-        J.sum[c] = J.sum[c] * dg + r * J.cur[c];
-    }
 }
 
 // Terminal leaves: utility times the opponent's reach mass (search.rs:1591-1604).
@@ -342,11 +318,8 @@ void launch_vgather(const JobDev* jobs, const WorkItem* items, uint32_t n, int p
     if (n) k_vgather<<<n, WI_TASKS, 0, s>>>(jobs, items, p);
 }
 void launch_rgather(const JobDev* jobs, const WorkItem* items, uint32_t n, int strat_sel, int which_reach,
-                    cudaStream_t s) {
-    if (n) k_rgather<<<n, WI_TASKS, 0, s>>>(jobs, items, strat_sel, which_reach);
-}
-void launch_avg(const JobDev* jobs, const WorkItem* items, uint32_t n, float dg, cudaStream_t s) {
-    if (n) k_avg<<<n, WI_TASKS, 0, s>>>(jobs, items, dg);
+                    int sum_update, float dg, cudaStream_t s) {
+    if (n) k_rgather<<<n, WI_TASKS, 0, s>>>(jobs, items, strat_sel, which_reach, sum_update, dg);
 }
 void launch_terminal(const JobDev* jobs, const WorkItem* items, uint32_t n, int p, cudaStream_t s) {
     if (n) k_terminal<<<n, WI_TASKS, 0, s>>>(jobs, items, p);

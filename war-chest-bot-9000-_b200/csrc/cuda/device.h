@@ -18,7 +18,6 @@ struct JobDev {
     const uint32_t* cell_vidx;
     const uint32_t* row_off;
     const uint8_t* row_player;
-    const uint32_t* row_ridx;   // per decision row: reach slot of its node and config
     const uint32_t* vg_start;
     const uint32_t* vge_idx;
     const uint32_t* vge_w;

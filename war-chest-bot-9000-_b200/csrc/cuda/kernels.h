@@ -18,8 +18,7 @@ void launch_rows(const JobDev* jobs, const WorkItem* items, uint32_t n, int p, i
                  float db, float predict, cudaStream_t s);
 void launch_vgather(const JobDev* jobs, const WorkItem* items, uint32_t n, int p, cudaStream_t s);
 void launch_rgather(const JobDev* jobs, const WorkItem* items, uint32_t n, int strat_sel, int which_reach,
-                    cudaStream_t s);
-void launch_avg(const JobDev* jobs, const WorkItem* items, uint32_t n, float dg, cudaStream_t s);
+                    int sum_update, float dg, cudaStream_t s);
 void launch_terminal(const JobDev* jobs, const WorkItem* items, uint32_t n, int p, cudaStream_t s);
 void launch_netrows_zero(const JobDev* jobs, const WorkItem* items, uint32_t n, int p, cudaStream_t s);
 void launch_seed_root(const JobDev* jobs, uint32_t njobs, int which_reach, int carried_index, cudaStream_t s);

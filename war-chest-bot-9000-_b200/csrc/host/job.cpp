@@ -13,7 +13,7 @@ size_t JobImage::table_bytes() const {
               lr_nc.size() + lr_vidx.size() + leaf_coff.size() + leaf_cidx.size() + tl_ridx.size() +
               tl_nc.size() + tl_vidx.size() + tl_util0.size() + cphi.size() + card_feat.size() + cfg_col.size() +
               leaf_col.size() + root_belief.size() + carried.size());
-    b += row_player.size() + gpu_rows.size() + cplayer.size() + 4 * row_ridx.size();
+    b += row_player.size() + gpu_rows.size() + cplayer.size();
     return b;
 }
 
@@ -81,12 +81,6 @@ std::unique_ptr<JobImage> flatten(const Tree& t, const std::vector<float>& carri
         }
     J.ndec_rows = (uint32_t)J.row_player.size();
     if (J.cell_ref.size() != J.ncells) throw std::logic_error("cell sort lost cells");
-    std::vector<std::pair<uint32_t, uint32_t>> row_node;  // (node, config) of each sorted row
-    row_node.reserve(J.ndec_rows);
-    for (uint32_t lv = 0; lv < L; ++lv)
-        for (int p = 0; p < 2; ++p)
-            for (uint32_t i : dec[p][lv])
-                for (uint32_t c = 0; c < nc(i, p); ++c) row_node.emplace_back(i, c);
 
     // ---- value arenas per traverser
     std::vector<uint32_t> vblk[2];
@@ -129,9 +123,6 @@ std::unique_ptr<JobImage> flatten(const Tree& t, const std::vector<float>& carri
             }
         }
     J.reach_len = rcur;
-    J.row_ridx.resize(J.ndec_rows);
-    for (uint32_t r = 0; r < J.ndec_rows; ++r)
-        J.row_ridx[r] = rblk[J.row_player[r]][row_node[r].first] + row_node[r].second;
 
     const uint32_t ONE = J.ncells + J.ndraw;
 

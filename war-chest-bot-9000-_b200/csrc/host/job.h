@@ -45,7 +45,6 @@ struct JobImage {
     std::vector<uint32_t> cell_vidx;  // successor value index in the acting player's value arena
     std::vector<uint32_t> row_off;    // ndec_rows + 1, over sorted cells
     std::vector<uint8_t> row_player;  // acting player of each row
-    std::vector<uint32_t> row_ridx;   // each row's reach slot: its node and config of the acting player
     // per (level, player): ranges in row / vgather / rgather task spaces
     std::vector<LevelRange> rows_rng, vg_rng, rg_rng;  // index: level * 2 + player
     std::vector<uint32_t> vg_start, vge_idx, vge_w;

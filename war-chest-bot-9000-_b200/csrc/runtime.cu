@@ -51,7 +51,7 @@ std::unique_ptr<JobBlob> make_blob(std::unique_ptr<JobImage> img) {
         v(J.rge_src), v(J.rge_w), v(J.drawp), v(J.cell_ref), v(J.lr_ridx), v(J.lr_nc), v(J.lr_vidx),
         v(J.leaf_coff), v(J.leaf_cidx), v(J.tl_ridx), v(J.tl_nc), v(J.tl_vidx), v(J.tl_util0), v(J.gpu_rows),
         v(J.cphi), v(J.cplayer), v(J.card_feat), v(J.root_belief), v(J.carried), v(carry_off), v(J.cfg_col),
-        v(J.leaf_col), v(J.row_ridx)};
+        v(J.leaf_col)};
     size_t at = 0;
     for (int i = 0; i < JobBlob::N_ARR; ++i) {
         b->off[i] = at;
@@ -82,7 +82,7 @@ std::unique_ptr<JobBlob> make_blob(std::unique_ptr<JobImage> img) {
     drop(J.rg_start), drop(J.rge_src), drop(J.rge_w), drop(J.drawp), drop(J.cell_ref), drop(J.lr_ridx);
     drop(J.lr_nc), drop(J.lr_vidx), drop(J.leaf_coff), drop(J.leaf_cidx), drop(J.tl_ridx), drop(J.tl_nc);
     drop(J.tl_vidx), drop(J.tl_util0), drop(J.gpu_rows), drop(J.cphi), drop(J.cplayer), drop(J.card_feat);
-    drop(J.root_belief), drop(J.carried), drop(J.cfg_col), drop(J.leaf_col), drop(J.row_ridx);
+    drop(J.root_belief), drop(J.carried), drop(J.cfg_col), drop(J.leaf_col);
     b->img = std::move(img);
     return b;
 }
@@ -350,16 +350,6 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
             });
         }
     b.rows_all = range_of([&] { for (uint32_t j = 0; j < nj; ++j) add_items(items, j, 0, jobs[j]->img->ndec_rows, 0); });
-    for (int p = 0; p < 2; ++p)
-        b.rows_of[p] = range_of([&] {
-            for (uint32_t lv = 0; lv < L; ++lv)
-                for (uint32_t j = 0; j < nj; ++j) {
-                    const JobImage& J = *jobs[j]->img;
-                    if (lv >= J.nlevels) continue;
-                    const LevelRange& r = J.rows_rng[lv * 2 + p];
-                    add_row_items(items, j, r.first, r.count, r.out_first, jobs[j]->arr<uint32_t>(JobBlob::ROW_OFF));
-                }
-        });
     b.cells_all = range_of([&] { for (uint32_t j = 0; j < nj; ++j) add_items(items, j, 0, jobs[j]->img->ncells, 0); });
     b.term_all = range_of([&] { for (uint32_t j = 0; j < nj; ++j) add_items(items, j, 0, jobs[j]->img->nterm, 0); });
     b.netrows_all = range_of([&] { for (uint32_t j = 0; j < nj; ++j) add_items(items, j, 0, jobs[j]->img->nrows_net, 0); });
@@ -439,7 +429,6 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
         d.cell_vidx = t32(JobBlob::CELL_VIDX);
         d.row_off = t32(JobBlob::ROW_OFF);
         d.row_player = t8(JobBlob::ROW_PLAYER);
-        d.row_ridx = t32(JobBlob::ROW_RIDX);
         d.vg_start = t32(JobBlob::VG_START);
         d.vge_idx = t32(JobBlob::VGE_IDX);
         d.vge_w = t32(JobBlob::VGE_W);
@@ -651,23 +640,14 @@ struct Sched {
     }
     const wcdev::WorkItem* it(const Batch::Range& r) const { return I + r.off; }
 
-    // Full or single-mover reach propagation below the seeded root; with
-    // sum_update, then the average update of the movers' decision cells
-    // (search.rs:1818-1835, with backprop's discount): sum = sum * dg +
-    // reach * cur, over the final reaches of this pass.
+    // Full or single-mover reach propagation below the seeded root.
     void propagate(int strat_sel, int which_reach, int mover_mask, int sum_update, float dg) {
         for (uint32_t lv = 1; lv < b.nlevels; ++lv)
             for (int q = 0; q < 2; ++q) {
                 if (!(mover_mask & (1 << q))) continue;
                 const Batch::Range& r = b.rg[lv * 2 + q];
-                timed(TC_REACH, [&] { b.count_launch(r.n), wcdev::launch_rgather(J, it(r), r.n, strat_sel, which_reach, s); });
+                timed(TC_REACH, [&] { b.count_launch(r.n), wcdev::launch_rgather(J, it(r), r.n, strat_sel, which_reach, sum_update, dg, s); });
             }
-        if (!sum_update) return;
-        for (int q = 0; q < 2; ++q) {
-            if (!(mover_mask & (1 << q))) continue;
-            const Batch::Range& r = b.rows_of[q];
-            timed(TC_REACH, [&] { b.count_launch(r.n), wcdev::launch_avg(J, it(r), r.n, dg, s); });
-        }
     }
 
     void leaf_values(int p, int pool_mask) {

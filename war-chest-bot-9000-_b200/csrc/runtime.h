@@ -55,7 +55,7 @@ struct JobBlob {
     enum Arr {
         CELL_VIDX, ROW_OFF, ROW_PLAYER, VG_START, VGE_IDX, VGE_W, RG_START, RGE_SRC, RGE_W, DRAWP, CELL_REF,
         LR_RIDX, LR_NC, LR_VIDX, LEAF_COFF, LEAF_CIDX, TL_RIDX, TL_NC, TL_VIDX, TL_UTIL0, GPU_ROWS, CPHI,
-        CPLAYER, CARD_FEAT, ROOT_BELIEF, CARRIED, CARRY_OFF, CFG_COL, LEAF_COL, ROW_RIDX, N_ARR
+        CPLAYER, CARD_FEAT, ROOT_BELIEF, CARRIED, CARRY_OFF, CFG_COL, LEAF_COL, N_ARR
     };
     size_t off[N_ARR] = {};
     // A packed array. The blob is the only copy: make_blob releases the
@@ -85,7 +85,6 @@ struct Batch {
     uint32_t nlevels = 0;
     std::vector<Range> rows, vg, rg;  // [level * 2 + player]
     Range rows_all, cells_all, term_all, netrows_all, exits_all;
-    Range rows_of[2];  // each player's decision rows over all levels (the average pass)
     uint32_t* d_row_job = nullptr;
     uint32_t* d_row_local = nullptr;
     uint32_t* d_cfg_job = nullptr;
