@@ -45,16 +45,21 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--subgames", type=int, default=4096, help="subgames per GPU")
+    ap.add_argument("--subgames-total", type=int, default=0,
+                    help="configs[3]: this many subgames split over the ranks (strong scaling), each rank's shard "
+                         "solved through wc_solve_batch's memory-bounded waves; a separate line, not the bench line")
     ap.add_argument("--depth", type=int, default=3)
     ap.add_argument("--iters", type=int, default=512)
     ap.add_argument("--plies", type=int, default=20)
-    ap.add_argument("--net", default="f16", choices=["f16", "bf16", "exact", "none"],
-                    help="value network: tcgen05 with f16 / bf16 operands, fp32 exact, or none")
+    ap.add_argument("--net", default="bf16", choices=["bf16", "f16", "exact", "none"],
+                    help="value network: tcgen05 with bf16 operands for the per-iteration chain (trunk and "
+                         "readout f16), f16 operands throughout, fp32 exact, or none")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg (profiling runs)")
     ap.add_argument("--build-threads", type=int, default=0)
-    ap.add_argument("--workload", default="solve", choices=["solve", "leaf"],
+    ap.add_argument("--workload", default="solve", choices=["solve", "leaf", "batch"],
                     help="solve: the configs[2] batched solve (the bench line); leaf: configs[1], value-net leaf "
-                         "inference alone at 1K / 16K / 256K rows (one JSON line per batch size, not a bench line)")
+                         "inference alone at 1K / 16K / 256K rows; batch: the training-batch expansion of replay "
+                         "rows at 1K / 256K rows (one JSON line per batch size, not bench lines)")
     return ap.parse_args()
 
 
@@ -156,7 +161,9 @@ def algorithmic_work(jobs):
       pool     8 B per leaf-config entry (reach, column) + 128 B per row (the f16 pooled atom)
       join     4 x 2*128*128 FLOP per network row
       head     2*128*256 FLOP per network row + 2*256 per leaf-config entry of the traverser
-      trunk    17.0 MFLOP per network row (once per solve)
+      trunk    17.0 MFLOP per distinct public row of a job (once per solve; rows
+               that repeat a public row share its board pieces, so the work
+               the solve must do is per distinct row)
     CFR classes run once per iteration for one player, so a solve does each
     player's share iters/2 times; the leaf classes run once per iteration and
     twice per carried root in Phase 2."""
@@ -174,7 +181,7 @@ def algorithmic_work(jobs):
         "pool": ("hbm", (8 * entries + 128 * rows) * calls),
         "join": ("tensor", 4 * 2 * 128 * 128 * rows * calls),
         "head": ("tensor", (2 * 128 * 256 * rows + 2 * 256 * entries) * calls),
-        "trunk": ("tensor", 17.0e6 * rows),
+        "trunk": ("tensor", 17.0e6 * c[20]),
     }
 
 
@@ -261,6 +268,90 @@ def cpu_baseline(oracle, cfg, weights, seeds):
                       f"extrapolated; {wall:.1f} s wall"}
 
 
+def batch_workload(args):
+    """The training batch (train/gpu_batch.py make_batch): replay rows packed
+    from seeded positions (0-60 plies, the distinct rows repeated to the batch
+    size), 1-4 configs per (row, seat) with seeded counts. Device: CUDA events
+    around wc_replay_expand on torch's stream, inputs already on the device,
+    L2 flushed (a 256 MB write) before each timed call; e2e adds the host to
+    device copies of the compact arrays (make_batch as a trainer calls it).
+    Algorithmic bytes: the row (215 B) and both views' features (2 x 897 x
+    4 B) per row, 15 B of counts in and 60 B of phi out per config, each
+    config's span id (8 B). CPU: the oracle's restatement of the CPU batch
+    (train/train.py:249-270) on one thread, on the 1K batch."""
+    import ctypes as Cc
+
+    import torch
+
+    import oracle_lib
+    import warchest_b200 as wc
+    from warchest_b200 import gpu_batch
+
+    hbm, _, src = peaks()
+    dev = torch.device("cuda:0")
+    distinct = []
+    for s in range(512):
+        try:
+            distinct.append(np.frombuffer(wc.pack_row(wc.generate_root(s, plies=int(s % 61))), np.uint8))
+        except wc.SolveError:
+            pass
+    distinct = np.stack(distinct)
+    gpu_batch.warmup(dev)
+    flush = torch.empty(64 << 20, dtype=torch.float32, device=dev)
+    for n in (1024, 262144):
+        rng = np.random.default_rng(n)
+        rows = distinct[rng.integers(0, len(distinct), n)]
+        seg = np.repeat(np.arange(2 * n, dtype=np.int64), rng.integers(1, 5, 2 * n))
+        m = len(seg)
+        cc = rng.integers(0, 4, (m, 15)).astype(np.uint8)
+        parts = (rows, np.zeros((n, 10), np.uint8), cc, (seg % 2).astype(np.uint8), np.ones(m, np.float32),
+                 np.zeros(m, np.float32), seg)
+        rows_t = torch.as_tensor(rows, device=dev)
+        cc_t = torch.as_tensor(cc, device=dev)
+        seg_t = torch.as_tensor(seg, device=dev)
+        x = torch.empty((2 * n, wc.PUBFEAT), dtype=torch.float32, device=dev)
+        phi = torch.empty((m, 15), dtype=torch.float32, device=dev)
+        stream = torch.cuda.current_stream(dev)
+        times, e2e = [], []
+        for it in range(8):
+            flush.fill_(float(it))
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            wc._check(wc.lib().wc_replay_expand(rows_t.data_ptr(), n, cc_t.data_ptr(), seg_t.data_ptr(), m,
+                                                x.data_ptr(), phi.data_ptr(), stream.cuda_stream))
+            b.record(stream)
+            torch.cuda.synchronize(dev)
+            if it >= 3:
+                times.append(a.elapsed_time(b))
+            t0 = time.perf_counter()
+            out = gpu_batch.make_batch(parts, None, dev)
+            torch.cuda.synchronize(dev)
+            if it >= 3:
+                e2e.append((time.perf_counter() - t0) * 1e3)
+            del out
+        ms = float(np.median(times))
+        nbytes = 215.0 * n + 2 * 897 * 4.0 * n + (15 + 60 + 8) * float(m)
+        line = {"workload": f"training batch: {n} replay rows, {m} configs", "rows": n, "configs": m,
+                "ms": ms, "rows_per_s": n / (ms / 1e3),
+                "roofline": {"bound": "hbm", "achieved": nbytes / (ms / 1e3) / 1e9, "peak": hbm, "unit": "GB/s",
+                             "frac": nbytes / (ms / 1e3) / 1e9 / hbm, "peak_source": src},
+                "e2e_ms": float(np.median(e2e)), "e2e_rows_per_s": n / (float(np.median(e2e)) / 1e3)}
+        if n == 1024:
+            L = oracle_lib.lib()
+            xo = np.zeros((2 * n, wc.PUBFEAT), np.float32)
+            po = np.zeros((m, 15), np.float32)
+            t0 = time.perf_counter()
+            L.oracle_replay_make_batch(rows.ctypes.data_as(Cc.c_void_p), Cc.c_size_t(n), cc.ctypes.data_as(Cc.c_void_p),
+                                       seg.ctypes.data_as(Cc.c_void_p), Cc.c_size_t(m), xo.ctypes.data_as(Cc.c_void_p),
+                                       po.ctypes.data_as(Cc.c_void_p))
+            cpu_ms = (time.perf_counter() - t0) * 1e3
+            line["cpu_baseline"] = {"value": n / (cpu_ms / 1e3), "unit": "rows/s", "cores": 1, "kind": "port",
+                                    "sample": f"the {n}-row batch, once"}
+            line["equal_to_cpu_batch"] = bool(np.array_equal(x.cpu().numpy(), xo) and
+                                              np.array_equal(phi.cpu().numpy(), po))
+        print(json.dumps(line), flush=True)
+
+
 def leaf_workload(args):
     """the value network alone on rows from seeded random
     playouts of 10-60 plies. Positions: the roots of seeds 0.. with a seeded
@@ -302,7 +393,7 @@ def leaf_workload(args):
             rows += j.info["net_rows"]
         counts = np.sum([j.counts() for j in jobs], axis=0)
         configs = sum(j.info["configs"] for j in jobs)
-        flops = 17.0e6 * rows + 2 * 197.6e3 * rows + 512 * (counts[14] + counts[15]) + 170e3 * configs
+        flops = 17.0e6 * counts[20] + 2 * 197.6e3 * rows + 512 * (counts[14] + counts[15]) + 170e3 * configs
         line = {"workload": f"configs[1]: leaf inference alone, {rows} rows (target {target}) from {len(jobs)} "
                             f"positions of 10-60 seeded playout plies", "rows": rows, "configs": int(configs)}
         vals = {}
@@ -341,6 +432,12 @@ def main():
     PLIES = args.plies
     if args.workload == "leaf":
         leaf_workload(args)
+        return
+    if args.workload == "batch":
+        batch_workload(args)
+        return
+    if args.subgames_total:
+        total_workload(args)
         return
     if args.impl == "reference":
         # the CPU reference runs on rank 0 alone; other ranks exit without work
@@ -470,6 +567,69 @@ def main():
         dist.destroy_process_group()
 
 
+def total_workload(args):
+    """--subgames-total subgames (seeds 0 ..) split
+    evenly over the ranks (strong scaling), depth 3, 512 CFR+ iterations,
+    the net every iteration. A shard larger than one device batch is solved
+    in memory-bounded waves by wc_solve_batch (each wave's host tables
+    uploaded while the previous wave solves), so a step is one
+    wc_solve_batch call timed on the host clock (uploads and the result
+    download inside), max over ranks; one untimed call first sizes the wave
+    arenas."""
+    world, rank, local = dist_setup(args)
+    import warchest_b200 as wc
+
+    wc.set_cap_marker_value(0.0)
+    cfg = wc.Cfg(depth=args.depth, iters=args.iters, snapshots=False, cfr=cfr_plus(wc), node_cap=200000)
+    per = args.subgames_total // world
+    seeds = list(range(rank * per, (rank + 1) * per if rank + 1 < world else args.subgames_total))
+    local_world = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
+    threads = args.build_threads or max(1, (os.cpu_count() or 1) // max(1, local_world))
+    t0 = time.perf_counter()
+    _, jobs = build_jobs(wc, seeds, cfg, threads)
+    build_s = time.perf_counter() - t0
+    weights = wc.seeded_weights("he", 0)
+    if world > 1:
+        import torch
+
+        tw = broadcast_weights(weights, torch.device("cuda", local))
+        torch.cuda.synchronize()
+        client = wc.spawn(local, net=args.net)
+        client.set_weights_device(0, tw[0].data_ptr(), tw[1].data_ptr(), tw[2].data_ptr())
+    else:
+        client = wc.spawn(local, *weights, net=args.net)
+    nu = sum(j.info["nodes"] for j in jobs) * float(args.iters)
+    for _ in range(max(1, args.warmup)):
+        client.solve_batch(jobs)
+    times = []
+    for _ in range(args.steps):
+        barrier(world)
+        t0 = time.perf_counter()
+        res = client.solve_batch(jobs)
+        times.append(time.perf_counter() - t0)
+        del res
+    step_s = max_over_ranks(world, float(np.mean(times)))
+    total_nu = allsum(world, nu)
+    solved = allsum(world, float(len(jobs)))
+    if rank == 0:
+        line = {"metric": METRIC, "value": total_nu / step_s, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": max(1, args.warmup), "ms_per_step": step_s * 1e3, "higher_is_better": True,
+                "scaling": "strong", "dtype": DTYPES[args.net], "data": "synthetic (seeded roots, seeded He-normal weights)",
+                "config": {"workload": f"configs[3]: {args.subgames_total} subgames over {world} GPU(s), depth "
+                                       f"{args.depth}, {args.iters} CFR+ iters, v5 net every iteration",
+                           "subgames_total": args.subgames_total, "subgames_solved": int(solved),
+                           "parallelism": f"shards{world}", "timing": "host clock around wc_solve_batch "
+                           "(memory-bounded waves, tables uploaded inside the step), max over ranks"},
+                "host_build_s": build_s}
+        print(json.dumps(line), flush=True)
+    client.close()
+    if world > 1:
+        import torch.distributed as dist
+
+        barrier(world)
+        dist.destroy_process_group()
+
+
 def batch_levels(jobs):
     return max(j.info["levels"] for j in jobs)
 
@@ -537,7 +697,8 @@ KERNELS = {"rows": "k_rows", "vgather": "k_vgather", "reach": "k_rgather", "pool
 # The pooling figure is of a launch that pooled both players.
 TRAFFIC_PER_ROW = {"head": 1025.4, "join": 796.9, "pool": 349.2, "trunk": 880.5}
 DTYPES = {"f16": "f32 CFR state, f16 tensor-core value net (fp32 accumulate)",
-          "bf16": "f32 CFR state, bf16 tensor-core value net (fp32 accumulate)",
+          "bf16": "f32 CFR state, tensor-core value net (fp32 accumulate): bf16 operands for the per-iteration "
+                  "pooling / join / join-output chain, f16 for the once-per-solve trunk and the readout",
           "exact": "f32", "none": "f32"}
 
 if __name__ == "__main__":

@@ -100,7 +100,12 @@ typedef struct wc_result {
  *   WC_NET_F16    tcgen05 tensor cores, f16 operands, fp32 accumulation: the
  *                 precision class of the reference GPU service's fast mode
  *                 (cuBLAS COMPUTE_32F_FAST_16F, engine/src/gpu/device.rs:2306-2330);
- *   WC_NET_BF16   the same kernels with bf16 operands.
+ *   WC_NET_BF16   the same kernels with bf16 operands for the per-iteration
+ *                 chain (the pooling product, the four join layers and the
+ *                 join output product: nearly all of a solve's network
+ *                 work); the once-per-solve board trunk, its stored rows and
+ *                 the readout <f(c), h> keep f16 operands, since the
+ *                 readout amplifies operand rounding several times.
  * The values 0 / 1 keep the meaning of a `precise` flag (0 = tensor cores in
  * bf16, 1 = exact). */
 enum { WC_NET_BF16 = 0, WC_NET_EXACT = 1, WC_NET_F16 = 2 };
@@ -165,12 +170,28 @@ void wc_job_free(wc_job* job);
 /* A 64-bit digest (FNV-1a) of the job's flattened tables, for checking that
  * two builds are identical and as a cache key. */
 int wc_job_digest(const wc_job* job, uint64_t* out);
+/* The reference's job bytes, WCJ8 (engine/src/serialize.rs:1051-1262 to_bytes
+ * / from_bytes, the tables of serialize.rs:689-955 from_solver; docs/TREE.md),
+ * for interop with tapes and services that speak it.
+ * wc_wcj8_from_root: the subgame of a root (root encoding above) built and
+ * written as PackedJob::from_solver(...).to_bytes() would write it, with
+ * `net_dims` as the meta's network shape; *len is set to the byte count,
+ * and WC_E_ARG returned when cap is smaller (call with cap 0 to size).
+ * wc_job_from_wcj8: a solvable job from WCJ8 bytes (the reference's count
+ * checks; a snapshot list other than snapshot_iters(iters) is refused). The
+ * job equals the one wc_job_build makes from the same root (wc_job_digest). */
+int wc_wcj8_from_root(const uint8_t* root, size_t len, const wc_solve_cfg* cfg, const float* carried,
+                      uint32_t ncarried, const uint32_t* net_dims, uint32_t ndims, uint8_t* buf, size_t cap,
+                      size_t* out_len);
+int wc_job_from_wcj8(const uint8_t* bytes, size_t len, wc_job** out);
 /* Work counts for roofline accounting, 20 slots, [p] = player 0 / 1:
  * [0+p] regret-matching cells of p's nodes, [2+p] their rows, [4+p] value-
  * gather entries for traverser p, [6+p] value-gather outputs, [8+p] reach
  * entries through p's decision cells, [10+p] reach entries through p's draws,
  * [12+p] reach outputs of mover p, [14+p] network-row configs of p, [16+p]
- * terminal-leaf configs of p, [18] reach slots, [19] value slots. */
+ * terminal-leaf configs of p, [18] reach slots, [19] value slots; with n > 20
+ * also [20] the distinct public rows among the network rows (the rows the
+ * tensor-core board trunk runs on; the others share a row's board pieces). */
 int wc_job_counts(const wc_job* job, uint64_t* out, int n);
 /* The job's root belief: player 0's then player 1's weights over the root
  * supports (root_nc0 + root_nc1 floats). */
@@ -315,6 +336,37 @@ int wc_game_counters(const wc_game* g, int64_t* out8);
 /* The game's current state and beliefs in the root encoding. */
 int wc_game_root(const wc_game* g, uint8_t* buf, size_t cap, size_t* len);
 void wc_game_free(wc_game* g);
+
+/* ---- training batch ------------------------------------------------------- */
+/* The step after solving in the training loop: compact replay rows expanded
+ * on the training device into the value network's input for both canonical
+ * seat views. Replaces train/gpu_batch.py:119-163 (make_batch's Triton
+ * expansion, train/gpu_batch.py:22-117) with the same outputs as the CPU
+ * batch (train/train.py:249-270: engine/src/rebel.rs:1353 expand_row of each
+ * row and of its mirror, train/mirror.py:60-85).
+ *
+ * wc_replay_pack_row: the replay row (WC_ROW_BYTES bytes, rebel.rs:935-964)
+ * of a state given in the reference's state encoding (write_state), or of
+ * the state that starts a root in the root encoding (bytes after the state
+ * are not read); the row's rules-table hash is rebel.rs:996's.
+ *
+ * wc_replay_expand: every pointer is device memory of the current device,
+ * and the call only enqueues work on `stream` (a cudaStream_t; NULL is the
+ * legacy default stream):
+ *   rows  nrows x WC_ROW_BYTES replay rows;
+ *   cc    m x 15 config counts (hand[5], face-down[5], bag[5]) of the rows'
+ *         belief supports, and seg their span ids 2 row + seat,
+ *         non-decreasing, every span non-empty (train/train.py:70-79);
+ *   x     out, 2 nrows x WC_PUBFEAT floats: view 2r is row r, view 2r + 1
+ *         its mirror, each with its seats' hand / face-down / bag sizes
+ *         (the mirror's exchanged);
+ *   phi   out, m x 15 floats, cc / 5 (CNORM).
+ * The caller checks seg (train.py's np.searchsorted would raise on a span
+ * past the end); unit ids past the table expand to zero facts. */
+enum { WC_ROW_BYTES = 215, WC_PUBFEAT = 897 };
+int wc_replay_pack_row(const uint8_t* state, size_t len, uint8_t* out);
+int wc_replay_expand(const uint8_t* rows, size_t nrows, const uint8_t* cc, const int64_t* seg, size_t m, float* x,
+                     float* phi, void* stream);
 
 /* ---- streaming submit / wait ---------------------------------------------- */
 /* The job stays owned by the caller and must outlive the wc_wait of its

@@ -27,7 +27,7 @@ def test_algorithmic_work_follows_the_counts(jobs):
     calls = jobs[0].cfg.iters + 2  # one carried root (the live belief)
     assert w["rows"] == ("hbm", (24 * (c[0] + c[1]) + 8 * (c[2] + c[3])) * pairs)
     assert w["join"] == ("tensor", 4 * 2 * 128 * 128 * rows * calls)
-    assert w["trunk"] == ("tensor", 17.0e6 * rows)
+    assert w["trunk"] == ("tensor", 17.0e6 * c[20])
     # the regret-matching cells are every legal cell of the trees
     assert c[0] + c[1] == sum(j.info["cells"] for j in jobs)
     for bound, amount in w.values():

@@ -4,8 +4,10 @@ Same trees, same CFR schedule; only the network arithmetic differs (16-bit
 operands with fp32 accumulation on tcgen05, fast GELU). Two operand types:
   * f16, the default: the precision class of the reference GPU service's
     fast mode (cuBLAS COMPUTE_32F_FAST_16F, engine/src/gpu/device.rs:2306-2330);
-  * bf16: 3 fewer significant bits (unit roundoff 2^-9 against 2^-12), so its
-    bars are wider; the numbers it reaches are printed.
+  * bf16: the per-iteration chain (pooling, join layers, join output) on
+    bf16 operands, the once-per-solve board trunk and the readout
+    <f(c), h> on f16 operands (the readout multiplies operand error several
+    times). Held to the same bars; the numbers it reaches are printed.
 
 Checks (the bf16 value-net bar is "within 1e-2 relative, with the
 exploitability of the small config reported"):
@@ -30,7 +32,7 @@ pytestmark = pytest.mark.gpu
 
 # per operand type: (relative root-value bar, absolute root-value bar,
 # relative NashConv excess bar)
-BARS = {"f16": (1e-2, 1e-2, 0.05), "bf16": (4e-2, 8e-2, 0.15)}
+BARS = {"f16": (1e-2, 1e-2, 0.05), "bf16": (1e-2, 1e-2, 0.05)}
 
 
 @pytest.fixture(scope="module")

@@ -136,3 +136,24 @@ def test_wide_roots(wc, oracle):
             o = oracle.Oracle(r, cfg)
             for k in ("nodes", "cells", "net_rows", "configs"):
                 assert job.info[k] == o.shape[k]
+
+
+def test_distinct_public_rows_are_the_distinct_boards(wc, oracle):
+    """The tensor-core trunk runs once per distinct public row of a job
+    (wc_job_counts slot 20) and copies the board pieces to the other rows.
+    That is sound only if the grouping is the one the board network itself
+    makes: the number of distinct rows must equal the number of distinct P
+    rows the CPU oracle's fp32 network computes (engine/src/net.rs:558-731)
+    for the job's network rows."""
+    weights = wc.seeded_weights("he", 0)
+    cfg = wc.Cfg(depth=2, iters=4, snapshots=False, cfr=wc.Cfr.PLUS)
+    shared = 0
+    for seed in range(6):
+        root = wc.generate_root(seed)
+        job = wc.PackedJob.from_root(root, cfg)
+        c = job.counts()
+        pb, _, _, _ = oracle.Oracle(root, cfg, weights).net_pieces()
+        distinct = np.unique(pb.view(np.uint32), axis=0).shape[0]
+        assert c[20] == distinct, (seed, c[20], distinct, job.info["net_rows"])
+        shared += c[20] < job.info["net_rows"]
+    assert shared >= 2  # the same public position, reached along different public paths

@@ -15,6 +15,7 @@
 #include "cuda/kernels.h"
 #include "host/job.h"
 #include "host/walk.h"
+#include "host/wcj8.h"
 #include "runtime.h"
 
 using namespace wc;
@@ -629,6 +630,33 @@ int wc_game_root(const wc_game* g, uint8_t* buf, size_t cap, size_t* len) {
 
 void wc_game_free(wc_game* g) { delete g; }
 
+int wc_replay_pack_row(const uint8_t* state, size_t len, uint8_t* out) {
+    return guarded([&] {
+        static_assert(WC_ROW_BYTES == ROW_BYTES && WC_PUBFEAT == PUBFEAT, "replay layout");
+        State s;
+        size_t at = 0;
+        if (!out) return fail(WC_E_ARG, "no output row");
+        if (!state || !read_state(state, len, &at, &s)) return fail(WC_E_ARG, "malformed state bytes");
+        pack_row(s, Ctx::make(s), out);
+        return (int)WC_OK;
+    });
+}
+
+int wc_replay_expand(const uint8_t* rows, size_t nrows, const uint8_t* cc, const int64_t* seg, size_t m, float* x,
+                     float* phi, void* stream) {
+    return guarded([&] {
+        if (nrows > (1u << 30)) return fail(WC_E_ARG, "too many replay rows");
+        if ((nrows && (!rows || !x)) || (m && (!cc || !seg || !phi)))
+            return fail(WC_E_ARG, "null device pointer");
+        if (nrows && !m) return fail(WC_E_ARG, "rows without configs");
+        if (!wcdev::replay_tables_ready()) return fail(WC_E_CUDA, "replay tables: " + std::string(cudaGetErrorString(cudaGetLastError())));
+        wcdev::launch_replay_expand(rows, (uint32_t)nrows, cc, seg, m, x, phi, static_cast<cudaStream_t>(stream));
+        const cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return fail(WC_E_CUDA, std::string("replay expand: ") + cudaGetErrorString(e));
+        return (int)WC_OK;
+    });
+}
+
 int wc_state_legal_actions(const uint8_t* state, size_t len, uint32_t* codes, size_t cap, size_t* n) {
     return guarded([&] {
         State s;
@@ -717,6 +745,46 @@ int wc_job_build(const uint8_t* root, size_t len, const wc_solve_cfg* cfg, const
     std::string msg;
     const int rc = build_one(root, len, sc, carried, ncarried, out, &msg);
     return rc == WC_OK ? rc : fail(rc, msg);
+}
+
+int wc_wcj8_from_root(const uint8_t* root, size_t len, const wc_solve_cfg* cfg, const float* carried,
+                      uint32_t ncarried, const uint32_t* net_dims, uint32_t ndims, uint8_t* buf, size_t cap,
+                      size_t* out_len) {
+    if (!root || !cfg || !out_len || (ndims && !net_dims) || (ncarried && !carried)) return fail(WC_E_ARG, "null argument");
+    const SolveCfg sc = solve_cfg(cfg);
+    if (sc.depth < 1 || sc.iters < 0) return fail(WC_E_ARG, "depth must be >= 1 and iters >= 0");
+    return guarded([&] {
+        Root r;
+        if (!root_from_bytes(root, len, &r)) return fail(WC_E_ARG, "malformed root bytes");
+        auto tree = build_tree(r.s, r.ctx, sc, r.bel);
+        if (tree->capped) return fail(WC_E_CAPPED, "the tree hit the node cap");
+        const size_t w = tree->nc(0, 0) + tree->nc(0, 1);
+        std::vector<float> car(carried, carried + (size_t)ncarried * w);
+        const std::vector<uint8_t> bytes =
+            wcj8_write(wcj8_from_tree(*tree, car, ncarried, std::vector<uint32_t>(net_dims, net_dims + ndims)));
+        *out_len = bytes.size();
+        if (bytes.size() > cap || !buf) return fail(WC_E_ARG, "buffer too small for the job bytes");
+        std::memcpy(buf, bytes.data(), bytes.size());
+        return (int)WC_OK;
+    });
+}
+
+int wc_job_from_wcj8(const uint8_t* bytes, size_t len, wc_job** out) {
+    if (!bytes || !out) return fail(WC_E_ARG, "null argument");
+    *out = nullptr;
+    return guarded([&] {
+        Wcj8Job j;
+        std::string msg;
+        if (!wcj8_read(bytes, len, &j, &msg)) return fail(WC_E_ARG, msg);
+        std::vector<float> car;
+        uint32_t ncar = 0;
+        auto tree = wcj8_tree(j, &car, &ncar, &msg);
+        if (!tree) return fail(WC_E_ARG, msg);
+        auto job = std::make_unique<wc_job>();
+        job->blob = make_blob(flatten(*tree, car, ncar));
+        *out = job.release();
+        return (int)WC_OK;
+    });
 }
 
 int wc_job_build_batch(const uint8_t* const* roots, const size_t* lens, size_t n, const wc_solve_cfg* cfg,
@@ -848,6 +916,11 @@ int wc_job_counts(const wc_job* job, uint64_t* out, int n) {
     for (uint32_t k = 0; k < J.nterm; ++k) { out[16] += tl_nc[2 * k]; out[17] += tl_nc[2 * k + 1]; }
     out[18] = J.reach_len;
     out[19] = (uint64_t)J.val_len[0] + J.val_len[1];
+    if (n > 20) {
+        const uint32_t* rep = B.arr<uint32_t>(JobBlob::ROW_REP);
+        out[20] = 0;
+        for (uint32_t r = 0; r < J.nrows_net; ++r) out[20] += rep[r] == r;
+    }
     return WC_OK;
 }
 

@@ -100,7 +100,8 @@ struct FastNetDev {
     const float* trunk_ob;      // per trunk block [96]: the out bias
     const float* stem_w;        // [6][96] the hex stem weights (16-byte aligned copy)
     const float* stem_pb;       // [37][96] the hex's position embedding plus the hex stem bias
-    int half;                   // operand type of every tile and stored row: 1 = f16, 0 = bf16
+    int half;                   // the per-iteration chain's operands (pooling, join, join output): 1 = f16,
+                                // 0 = bf16; the trunk, P / jp and the readout are f16 in both
     uint64_t wait_ns;           // limit of each mbarrier wait, ns of %globaltimer (umma::WAIT_NS)
 };
 

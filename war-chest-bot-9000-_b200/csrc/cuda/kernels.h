@@ -63,8 +63,23 @@ void launch_pack_f16(const JobDev* jobs, const uint32_t* cfg_job, const uint32_t
 void trunk_set_constants(const wc::NetLayout& L, const uint8_t* neighbors, const uint8_t* is_location);
 size_t trunk_tiles_bytes();
 void launch_tokproj(const JobDev* jobs, uint32_t njobs, const float* W, cudaStream_t s);
+// The rows (row_job[i], row_local[i]) may be any subset of the batch's
+// network rows: each writes its own P tile-image row and jp row.
 void launch_trunk_fast(const JobDev* jobs, const uint32_t* row_job, const uint32_t* row_local, uint32_t total_rows,
                        const uint8_t* tiles, const float* W, const float* B, const float* LN, const FastNetDev& fn,
                        uint16_t* g_pb, uint16_t* g_jp, int* err, cudaStream_t s);
+// dup: n triples (job, row, representative row): P and jp of the row copied
+// from the representative's, after launch_trunk_fast computed it.
+void launch_board_dup(const JobDev* jobs, const uint32_t* dup, uint32_t n, uint16_t* g_pb, uint16_t* g_jp,
+                      cudaStream_t s);
+
+// replay.cu: the training batch (all pointers device memory). Uploads the
+// card-fact, location and mirror tables to the current device once; false if
+// that fails.
+bool replay_tables_ready();
+// rows: nrows x ROW_BYTES; cc: m x CCOUNTS config counts; seg: m span ids
+// (2 row + seat, non-decreasing); x: 2 nrows x PUBFEAT; phi: m x CCOUNTS.
+void launch_replay_expand(const uint8_t* rows, uint32_t nrows, const uint8_t* cc, const int64_t* seg, uint64_t m,
+                          float* x, float* phi, cudaStream_t s);
 
 }  // namespace wcdev

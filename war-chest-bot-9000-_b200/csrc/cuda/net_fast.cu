@@ -1,6 +1,17 @@
 // The tensor-core ("fast") value network: tcgen05 MMAs with operands in
 // 128-byte-swizzled shared memory and fp32 accumulators in TMEM, epilogues on
 // the CUDA cores (bias, residual, LayerNorm, tanh-GELU).
+//
+// Operand types. The kernels' template flag H is the type of the
+// per-iteration chain, which carries nearly all of a solve's network work:
+// the pooling product, the four join layers and the join output product
+// (H = true: f16, false: bf16). The readout product V = H * F^T always
+// takes f16 operands (the LayerNorm output h and f(c); both well inside
+// f16's range), and so do the stored board rows P and jp that the chain adds
+// in: the readout <f(c), h> is nearly orthogonal for these networks, so it
+// multiplies the relative error of its operands several times, and bf16's
+// 8-bit mantissa there alone costs about 1e-2 relative error in the leaf
+// values, where f16's 11 bits cost about 1e-3.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -141,7 +152,7 @@ struct HeadTile {
 // and the epilogue adds the running sum of the block biases. The four weight
 // tiles stream through one 32 KB slot by bulk copy (the next layer's weight
 // lands during this layer's epilogue) and the next tile's pooled images
-// land during the last layer, so a CTA needs ~73 KB of shared memory and
+// land during the last layer, so a CTA needs ~69 KB of shared memory and
 // three run per SM, each one's MMAs and copies overlapping the others'
 // epilogues. The epilogue takes the row's 128 values in two halves (read
 // twice from TMEM: once for the statistics, once for LayerNorm and GELU).
@@ -162,27 +173,20 @@ __global__ void __launch_bounds__(128, 3)
     uint8_t* smem = align1024(smem_raw);
     uint8_t* sWt = smem;               // the current layer's weight tile
     uint8_t* sA = smem + TILE_J;
-    // [0] b with the seat folded in, [1..3] running sums of the block biases,
-    // [4..7] LayerNorm gammas, [8..11] betas; then per layer the (gamma, beta)
-    // column pairs packed for ln_gelu2
+    // [0] b with the seat folded in, [1..3] running sums of the block biases;
+    // then per layer the LayerNorm's (gamma, beta) column pairs packed for
+    // ln_gelu2
     float (*vec)[JW] = reinterpret_cast<float (*)[JW]>(sA + TILE_J);
-    uint32_t (*gb2)[JW] = reinterpret_cast<uint32_t (*)[JW]>(sA + TILE_J + 12 * JW * 4);
+    uint32_t (*gb2)[JW] = reinterpret_cast<uint32_t (*)[JW]>(sA + TILE_J + 4 * JW * 4);
     const int tid = threadIdx.x, warp = tid >> 5;
     for (int i = tid; i < 4 * (JW / 2); i += blockDim.x) {
         const int L = i / (JW / 2), c = 2 * (i % (JW / 2));
         umma::pack_gb2(fn.ln_g[L], fn.ln_b[L], c, &gb2[L][c]);
     }
-    for (int i = tid; i < 12 * JW; i += blockDim.x) {
+    for (int i = tid; i < 4 * JW; i += blockDim.x) {
         const int v = i / JW, c = i % JW;
-        float x;
-        if (v == 0) {
-            x = fn.beff[p][c];
-        } else if (v < 4) {
-            x = 0.0f;
-            for (int u = 0; u < v; ++u) x += fn.bj[u][c];
-        } else {
-            x = v < 8 ? fn.ln_g[v - 4][c] : fn.ln_b[v - 8][c];
-        }
+        float x = v == 0 ? fn.beff[p][c] : 0.0f;
+        for (int u = 0; u < v; ++u) x += fn.bj[u][c];
         vec[v][c] = x;
     }
     if (tid == 0) {
@@ -251,8 +255,8 @@ __global__ void __launch_bounds__(128, 3)
                     const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
-                        v[8 * i + 2 * e] = umma::Op16<H>::lo(w4[e]) + vec[0][32 * c4 + 8 * i + 2 * e];
-                        v[8 * i + 2 * e + 1] = umma::Op16<H>::hi(w4[e]) + vec[0][32 * c4 + 8 * i + 2 * e + 1];
+                        v[8 * i + 2 * e] = umma::Op16<true>::lo(w4[e]) + vec[0][32 * c4 + 8 * i + 2 * e];
+                        v[8 * i + 2 * e + 1] = umma::Op16<true>::hi(w4[e]) + vec[0][32 * c4 + 8 * i + 2 * e + 1];
                     }
                 }
                 umma::tmem_st32(tmem + lane_off + 32 * c4, v);
@@ -325,8 +329,6 @@ __global__ void __launch_bounds__(128, 3)
             const float mean = s * (1.0f / JW);
             const float inv = rsqrtf(fmaxf(sq * (1.0f / JW) - mean * mean, 0.0f) + 1e-5f);
             const float nm = -mean * inv;
-            const float* gam = vec[4 + L];
-            const float* bet = vec[8 + L];
 #pragma unroll
             for (int hf = 0; hf < 2; ++hf) {
                 uint32_t zr[64];
@@ -343,7 +345,7 @@ __global__ void __launch_bounds__(128, 3)
                         const int c = 8 * c8 + 2 * j, cc = 64 * hf + c;
                         const float x0 = L ? __uint_as_float(zr[c]) + cb[cc] : __uint_as_float(zr[c]);
                         const float x1 = L ? __uint_as_float(zr[c + 1]) + cb[cc + 1] : __uint_as_float(zr[c + 1]);
-                        w4[j] = umma::ln_gelu2<H>(x0 * inv + nm, x1 * inv + nm, cc, gam, bet, gb2[L]);
+                        w4[j] = umma::ln_gelu2<H>(x0 * inv + nm, x1 * inv + nm, cc, gb2[L]);
                     }
                     const uint4 o = make_uint4(w4[0], w4[1], w4[2], w4[3]);
                     const uint32_t off = umma::sw128_offset(128, tid, 64 * hf + 8 * c8);
@@ -560,7 +562,8 @@ __global__ void __launch_bounds__(128, 4)
 // Two tensor-core products per 128-row tile: Y = out * Wout (A = the join
 // output image in shared memory) and the readout V = H * F_p^T against the
 // job's player-p f table (128 configs per pass), with H = LN(y) written by
-// the epilogue into tensor memory as that product's A operand. The P rows
+// the epilogue into tensor memory as that product's A operand (f16: the
+// readout is the product most sensitive to operand rounding). The P rows
 // (which already include bout) arrive per tile by bulk copy, stored by the
 // trunk as 64 KB tile images: row r at r * 512 bytes, its 16-byte chunk k at
 // chunk k ^ (r & 7), so the epilogue's row-per-lane reads are conflict-free.
@@ -704,7 +707,7 @@ __global__ void __launch_bounds__(544, 1)
                 pend_f = false;
                 umma::fence_after_sync();
                 const uint32_t fa = umma::smem_u32(sF);
-                const uint32_t idesc = umma::idesc16(128, 128, umma::Op16<H>::fmt);
+                const uint32_t idesc = umma::idesc16(128, 128, umma::Op16<true>::fmt);  // H, f(c): f16
 #pragma unroll
                 for (int k0 = 0; k0 < D; k0 += 16)
                     umma::mma16_ts(tmem + TV, tmem + TH + k0 / 2, umma::desc_at(fa, 128, k0), idesc, k0 > 0);
@@ -792,8 +795,6 @@ __global__ void __launch_bounds__(544, 1)
                 : "memory");
             return r != 0;
         };
-        const float4* gam4 = reinterpret_cast<const float4*>(fn.ln_g[4] + 64 * cg);
-        const float4* bet4 = reinterpret_cast<const float4*>(fn.ln_b[4] + 64 * cg);
         for (uint32_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
             const HeadTile ht = tiles[t];
             const JobDev& J = jobs[ht.job];
@@ -817,8 +818,8 @@ __global__ void __launch_bounds__(544, 1)
                     const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
-                        v[8 * c + 2 * i] += umma::Op16<H>::lo(w4[i]);
-                        v[8 * c + 2 * i + 1] += umma::Op16<H>::hi(w4[i]);
+                        v[8 * c + 2 * i] += umma::Op16<true>::lo(w4[i]);
+                        v[8 * c + 2 * i + 1] += umma::Op16<true>::hi(w4[i]);
                     }
                 }
                 float s = 0.0f;
@@ -861,15 +862,15 @@ __global__ void __launch_bounds__(544, 1)
                 for (int c = 0; c < 4; ++c) m2 += __uint_as_float(r8[2 * c + 1]) + 64.0f * (mc[c] - mean) * (mc[c] - mean);
                 inv = rsqrtf(m2 * (1.0f / D) + 1e-5f);
             }
-            // h = LN(y) as 16-bit pairs into H's TMEM columns (K = 64 cg ..)
+            // h = LN(y) as f16 pairs into H's TMEM columns (K = 64 cg ..)
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 float v[32];
                 umma::tmem_ld32(tmem + lane_off + TY + 64 * cg + 32 * h, v);
                 uint32_t hw[16];
-                if constexpr (H) {
-                    // f16: the affine in f16x2 on the normalised pair (the
-                    // result is an f16 operand either way)
+                {
+                    // the affine in f16x2 on the normalised pair (the result
+                    // is an f16 operand either way)
                     const float nm = -mean * inv;
 #pragma unroll
                     for (int c = 0; c < 16; ++c) {
@@ -878,15 +879,6 @@ __global__ void __launch_bounds__(544, 1)
                         const __half2 x = __hfma2(n, *reinterpret_cast<const __half2*>(&gb.x),
                                                   *reinterpret_cast<const __half2*>(&gb.y));
                         hw[c] = *reinterpret_cast<const uint32_t*>(&x);
-                    }
-                } else {
-#pragma unroll
-                    for (int c = 0; c < 8; ++c) {
-                        const float4 g = ldg4_inplace(gam4 + 8 * h + c), b = ldg4_inplace(bet4 + 8 * h + c);
-                        hw[2 * c] = umma::Op16<H>::pack((v[4 * c] - mean) * inv * g.x + b.x,
-                                                        (v[4 * c + 1] - mean) * inv * g.y + b.y);
-                        hw[2 * c + 1] = umma::Op16<H>::pack((v[4 * c + 2] - mean) * inv * g.z + b.z,
-                                                            (v[4 * c + 3] - mean) * inv * g.w + b.w);
                     }
                 }
                 asm volatile(
@@ -972,8 +964,9 @@ __global__ void __launch_bounds__(544, 1)
 
 // f(c) of every config as the readout's B-operand images: for each player,
 // passes of 128 configs (by index among the player's configs) x 256, K-major
-// and 128-byte swizzled; player 0's passes first. Likewise g(c) as the
-// pooling's B images (64 features x 128 configs).
+// and 128-byte swizzled; player 0's passes first, always f16 (the readout's
+// operand type). Likewise g(c) as the pooling's B images (64 features x 128
+// configs) in the chain's type H.
 template <bool H>
 __global__ void k_pack_f16(const JobDev* __restrict__ jobs, const uint32_t* __restrict__ cfg_job,
                            const uint32_t* __restrict__ cfg_local, uint32_t total_cfgs) {
@@ -985,7 +978,7 @@ __global__ void k_pack_f16(const JobDev* __restrict__ jobs, const uint32_t* __re
     uint8_t* img = reinterpret_cast<uint8_t*>(J.f16) +
                    ((J.cplayer[c] == 1 ? (J.ncfg_player[0] + 127) / 128 : 0) + (col >> 7)) * (size_t)(2 * TILE_J);
     for (int j = threadIdx.x; j < D; j += blockDim.x)
-        *reinterpret_cast<uint16_t*>(img + umma::sw128_offset(128, i, j)) = umma::Op16<H>::one(J.cf[(size_t)c * D + j]);
+        *reinterpret_cast<uint16_t*>(img + umma::sw128_offset(128, i, j)) = umma::Op16<true>::one(J.cf[(size_t)c * D + j]);
     // g(c) into the pooling B image: row = feature, K = config index
     uint8_t* gimg = reinterpret_cast<uint8_t*>(J.g16) +
                     ((J.cplayer[c] == 1 ? (J.ncfg_player[0] + 127) / 128 : 0) + (col >> 7)) * (size_t)ATOM;
@@ -1026,7 +1019,7 @@ bool raise_smem_limit(const void* fn, size_t smem) {
 void launch_join_fast(const JobDev* jobs, const void* tiles, uint32_t ntiles, const FastNetDev& fn, int p,
                       const uint16_t* pool_img, const uint16_t* jp, uint16_t* zout_img, int* err, cudaStream_t s) {
     if (!ntiles) return;
-    const size_t smem = 2 * TILE_J + 16 * JW * 4 + 1024;  // the weight slot, the A operand, the vectors
+    const size_t smem = 2 * TILE_J + 8 * JW * 4 + 1024;  // the weight slot, the A operand, the vectors
     auto kern = fn.half ? k_join_fast<true> : k_join_fast<false>;
     if (!raise_smem_limit((const void*)kern, smem)) return;
     uint32_t grid = std::min<uint32_t>(ntiles, 3u * (uint32_t)num_sms());

@@ -1,0 +1,170 @@
+// The training batch's device expansion: compact replay rows in, the value
+// network's public input for both canonical seat views out
+// (train/gpu_batch.py:22-117 _expand_rows and make_batch, train/train.py:
+// 70-79 public_sizes and 249-270 make_batch, engine/src/rebel.rs:1144-1234
+// write_public_features_raw and 1353-1393 expand_row, train/mirror.py:60-85
+// mirror_rows).
+//
+// View 2r is replay row r; view 2r + 1 is its mirror (the board rotated by
+// 180 degrees and the seats exchanged), applied while the row is read rather
+// than materialised. The per-seat hand / face-down / bag sizes come from the
+// first config of each (row, seat) span of the config arrays, exchanged for
+// the mirrored view. Every feature is one IEEE division of a small integer
+// (or a table entry), so the floats equal the CPU encoder's bit for bit.
+//
+// Byte work bound by HBM writes (PUBFEAT floats per view against 215 bytes
+// read): one warp per view, the row staged in shared memory, the features
+// written lane-strided (coalesced).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+#include <mutex>
+#include <set>
+
+#include "../host/pbs.h"
+#include "kernels.h"
+
+namespace wcdev {
+
+namespace {
+
+using namespace wc;
+
+__constant__ float c_card_feat[N_UNITS * CARD_FEATS];
+__constant__ uint8_t c_is_loc[N_HEXES];
+__constant__ uint8_t c_hex_mirror[N_HEXES];
+
+constexpr int VIEWS_PER_CTA = 8;
+constexpr int ROW_STRIDE = (ROW_BYTES + 15) / 16 * 16;
+
+__device__ __forceinline__ uint32_t flip_seat(uint32_t v) { return v == 0 ? 1u : (v == 1 ? 0u : v); }
+
+__global__ void __launch_bounds__(32 * VIEWS_PER_CTA)
+    k_replay_expand(const uint8_t* __restrict__ rows, uint32_t nviews, const uint8_t* __restrict__ cc,
+                    const int64_t* __restrict__ seg, uint64_t m, float* __restrict__ x) {
+    __shared__ uint8_t s_row[VIEWS_PER_CTA][ROW_STRIDE];
+    __shared__ uint32_t s_size[VIEWS_PER_CTA][6];  // hand[2], fd[2], bag[2] of the view's seats
+    const uint32_t w = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const uint32_t v = blockIdx.x * VIEWS_PER_CTA + w;
+    if (v >= nviews) return;  // whole warps leave: no block-wide barrier follows
+    const uint32_t r = v >> 1;
+    const bool mir = v & 1u;
+    const uint8_t* row = rows + (size_t)r * ROW_BYTES;
+    for (uint32_t k = lane; k < ROW_BYTES; k += 32) s_row[w][k] = row[k];
+    if (lane < 2) {
+        // public_sizes: the first config whose span id is >= 2 r + seat
+        // (np.searchsorted 'left'); the mirrored view reads the other seat
+        const int64_t key = 2 * (int64_t)r + (mir ? 1 - (int)lane : (int)lane);
+        uint64_t lo = 0, hi = m;
+        while (lo < hi) {
+            const uint64_t mid = (lo + hi) / 2;
+            if (seg[mid] < key) lo = mid + 1;
+            else hi = mid;
+        }
+        uint32_t hand = 0, fd = 0, bag = 0;
+        if (lo < m) {
+            const uint8_t* c = cc + lo * CCOUNTS;
+            for (int k = 0; k < NSLOT; ++k) {
+                hand += c[k];
+                fd += c[NSLOT + k];
+                bag += c[2 * NSLOT + k];
+            }
+        }
+        s_size[w][lane] = hand & 0xffu;  // the sums are cast to u8 (.astype(np.uint8))
+        s_size[w][2 + lane] = fd & 0xffu;
+        s_size[w][4 + lane] = bag & 0xffu;
+    }
+    __syncwarp();
+    const uint8_t* R = s_row[w];
+    uint32_t on_board[2] = {0, 0};
+    for (int h = 0; h < N_HEXES; ++h) {
+        const uint32_t mk = mir ? flip_seat(R[ROW_HEX_MARKER + c_hex_mirror[h]]) : R[ROW_HEX_MARKER + h];
+        if (mk < 2) ++on_board[mk];
+    }
+    uint32_t init = mir ? flip_seat(R[ROW_INITIATIVE]) : R[ROW_INITIATIVE];
+    if (init > 1) init = 0;  // expand_row's guard (rebel.rs:1377)
+    const uint32_t to_act = mir ? flip_seat(R[ROW_TO_ACT]) : R[ROW_TO_ACT];
+    const uint32_t plies = R[ROW_PLIES] | ((uint32_t)R[ROW_PLIES + 1] << 8);
+    float* out = x + (size_t)v * PUBFEAT;
+    for (int j = lane; j < PUBFEAT; j += 32) {
+        float val = 0.0f;
+        if (j < HEX_BLOCK) {
+            const int h = j / HEX_CH, ch = j % HEX_CH;
+            const int src = mir ? c_hex_mirror[h] : h;
+            const uint32_t owner = mir ? flip_seat(R[ROW_HEX_OWNER + src]) : R[ROW_HEX_OWNER + src];
+            const uint32_t marker = mir ? flip_seat(R[ROW_HEX_MARKER + src]) : R[ROW_HEX_MARKER + src];
+            const uint32_t slot = R[ROW_HEX_SLOT + src];
+            if (ch < 2) val = owner == (uint32_t)ch ? 1.0f : 0.0f;
+            else if (ch == 2) val = owner != NONE ? (float)R[ROW_HEX_HEIGHT + src] / 5.0f : 0.0f;
+            else if (ch < 5) val = marker == (uint32_t)(ch - 3) ? 1.0f : 0.0f;
+            else if (ch == 5) val = c_is_loc[h] ? 1.0f : 0.0f;
+            else val = (owner < 2 && slot < NSLOT && (uint32_t)(ch - HEX_FACTS) == owner * NSLOT + slot) ? 1.0f : 0.0f;
+        } else if (j < OFF_CARDS) {
+            const int q = j - OFF_PILES, t = q / PILE_COUNTS, k = q % PILE_COUNTS;
+            const int st = mir ? (t + NSLOT) % NTYPE : t;
+            val = (float)R[ROW_PILES + st * PILE_COUNTS + k] / 5.0f;
+        } else if (j < OFF_LOOSE) {
+            const int q = j - OFF_CARDS, t = q / CARD_FEATS, f = q % CARD_FEATS;
+            const int st = mir ? (t + NSLOT) % NTYPE : t;
+            const uint32_t id = R[ROW_IDS + st];
+            val = id < (uint32_t)N_UNITS ? c_card_feat[id * CARD_FEATS + f] : 0.0f;
+        } else if (j < OFF_LOOSE + 2 * PLAYER_SCALARS) {
+            const int q = j - OFF_LOOSE, p = q / PLAYER_SCALARS, f = q % PLAYER_SCALARS;
+            const uint32_t in_hand = (uint32_t)MARKERS_TOTAL - on_board[p];
+            if (f == 0) val = (float)in_hand / 6.0f;
+            else if (f == 1) val = (float)(MARKERS_TOTAL - in_hand) / 6.0f;
+            else if (f == 2) val = (float)s_size[w][p] / 3.0f;
+            else if (f == 3) val = (float)s_size[w][2 + p] / MAX_COINS;
+            else if (f == 4) val = (float)s_size[w][4 + p] / MAX_COINS;
+            else val = init == (uint32_t)p ? 1.0f : 0.0f;
+        } else {
+            const int g = j - OFF_LOOSE - 2 * PLAYER_SCALARS;
+            if (g == 0) val = (float)plies / (float)MAX_MAIN_PLAYS;
+            else if (g == 1) val = R[ROW_INIT_MOVED] != 0 ? 1.0f : 0.0f;
+            else val = to_act == 0 ? 1.0f : 0.0f;
+        }
+        out[j] = val;
+    }
+}
+
+// phi = config counts / CNORM (train/train.py:267)
+__global__ void k_replay_phi(const uint8_t* __restrict__ cc, uint64_t total, float* __restrict__ phi) {
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x)
+        phi[i] = (float)cc[i] / CNORM;
+}
+
+std::mutex g_tables_mu;
+std::set<int> g_tables_ready;
+
+}  // namespace
+
+bool replay_tables_ready() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return false;
+    std::lock_guard<std::mutex> lk(g_tables_mu);
+    if (g_tables_ready.count(dev)) return true;
+    float card[N_UNITS * CARD_FEATS];
+    for (int u = 0; u < N_UNITS; ++u) write_card_features((uint8_t)u, card + u * CARD_FEATS);
+    uint8_t loc[N_HEXES], mirror[N_HEXES];
+    for (int h = 0; h < N_HEXES; ++h) {
+        loc[h] = board().is_location[h] ? 1 : 0;
+        mirror[h] = (uint8_t)mirror_hex(h);
+    }
+    if (cudaMemcpyToSymbol(c_card_feat, card, sizeof card) != cudaSuccess ||
+        cudaMemcpyToSymbol(c_is_loc, loc, sizeof loc) != cudaSuccess ||
+        cudaMemcpyToSymbol(c_hex_mirror, mirror, sizeof mirror) != cudaSuccess)
+        return false;
+    g_tables_ready.insert(dev);
+    return true;
+}
+
+void launch_replay_expand(const uint8_t* rows, uint32_t nrows, const uint8_t* cc, const int64_t* seg, uint64_t m,
+                          float* x, float* phi, cudaStream_t s) {
+    const uint32_t nviews = 2 * nrows;
+    if (nviews) k_replay_expand<<<(nviews + VIEWS_PER_CTA - 1) / VIEWS_PER_CTA, 32 * VIEWS_PER_CTA, 0, s>>>(rows, nviews, cc, seg, m, x);
+    const uint64_t total = m * (uint64_t)CCOUNTS;
+    if (total) k_replay_phi<<<(unsigned)std::min<uint64_t>((total + 255) / 256, 148ull * 16), 256, 0, s>>>(cc, total, phi);
+}
+
+}  // namespace wcdev

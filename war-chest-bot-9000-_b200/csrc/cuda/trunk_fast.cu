@@ -7,10 +7,18 @@
 // 32 (w / 4) .. + 31. Per block the two GEMMs run on tcgen05:
 //   mix: [a | sum of the six neighbours' a] (K = 192) x W_mix (N = 96)
 //   out: LNGELU(y) (K = 96) x W_out (N = 96)
-// with the block's bf16 weight tiles streamed from global memory by bulk
+// with the block's weight tiles streamed from global memory by bulk
 // asynchronous copies into two shared-memory buffers (the next block's
 // weights land while this block computes). The per-board pooling GEMM,
-// the stem and the board readout are small and run on the CUDA cores.
+// the stem and the board readout are small and run on the CUDA cores with
+// fp32 weights.
+//
+// The operands of both products, and the stored rows P and jp, are f16 in
+// either tensor-core network mode: the trunk runs once per solve (its cost
+// does not scale with the iterations), and its error reaches every leaf
+// value through the near-orthogonal readout <f(c), h>, which amplifies it
+// several times; bf16 operands here alone put the leaf values near 1e-2
+// relative error, f16 (three more mantissa bits) keeps them near 1e-3.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -41,18 +49,13 @@ constexpr uint32_t OUT_BYTES = 96 * 2 * 128;   // [96][96]: 2 atoms (second half
 constexpr uint32_t BLOCK_BYTES = MIX_BYTES + OUT_BYTES;  // 61440
 constexpr uint32_t A1_BYTES = 128 * 3 * 128;   // [128][192]
 constexpr uint32_t A2_BYTES = 128 * 2 * 128;   // [128][96]
+using F16 = umma::Op16<true>;
 
 // One elected thread: fetch a block's weight tiles into `dst`.
 __device__ __forceinline__ void fetch_block(uint8_t* dst, const uint8_t* tiles, int blk, uint64_t* bar) {
     umma::expect_tx(bar, BLOCK_BYTES);
     const uint8_t* src = tiles + (size_t)blk * BLOCK_BYTES;
     for (uint32_t o = 0; o < BLOCK_BYTES; o += 15360) umma::bulk_g2s(dst + o, src + o, 15360, bar);
-}
-
-template <bool H>
-__device__ __forceinline__ void put_x32(uint8_t* tile, uint32_t R, uint32_t r, uint32_t k0, const float* v) {
-#pragma unroll
-    for (int c = 0; c < 4; ++c) umma::st_chunk<H>(tile, R, r, k0 + 8 * c, v + 8 * c);
 }
 
 // out[i][n] = bias[n] + sum_k in[i][k] * W[k][n] for the NB rows of a tile, on
@@ -104,15 +107,14 @@ __device__ __forceinline__ void rows_gemm(const float* in, int ldi, const float*
     }
 }
 
-// Eight consecutive 16-bit operands of row r, columns [k, k + 8), as floats.
-template <bool H>
+// Eight consecutive f16 operands of row r, columns [k, k + 8), as floats.
 __device__ __forceinline__ void ld_chunk(const uint8_t* tile, uint32_t R, uint32_t r, uint32_t k, float* v) {
     const uint4 q = *reinterpret_cast<const uint4*>(tile + umma::sw128_offset(R, r, k));
     const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        v[2 * i] = umma::Op16<H>::lo(w4[i]);
-        v[2 * i + 1] = umma::Op16<H>::hi(w4[i]);
+        v[2 * i] = F16::lo(w4[i]);
+        v[2 * i + 1] = F16::hi(w4[i]);
     }
 }
 
@@ -153,7 +155,6 @@ struct HeadSmem {
     float part[3 * BOARDS * D];  // K-slice partial sums of the readout GEMMs
 };
 
-template <bool H>
 __global__ void __launch_bounds__(384, 1)
     k_trunk_fast(const JobDev* __restrict__ jobs, const uint32_t* __restrict__ row_job,
                  const uint32_t* __restrict__ row_local, uint32_t total_rows, const uint8_t* __restrict__ tiles,
@@ -361,8 +362,7 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
                         const int k = 8 * c + 2 * j;
-                        w4[j] = real_row ? umma::ln_gelu2<H>(x[k] * inv + nm, x[k + 1] * inv + nm, col0 + k, gam, bet,
-                                                             S.gb2[blk][0])
+                        w4[j] = real_row ? umma::ln_gelu2<true>(x[k] * inv + nm, x[k + 1] * inv + nm, col0 + k, S.gb2[blk][0])
                                          : 0u;
                     }
                     *reinterpret_cast<uint4*>(sA1 + umma::sw128_offset(128, row, col0 + 8 * c)) =
@@ -372,11 +372,8 @@ __global__ void __launch_bounds__(384, 1)
             __syncthreads();
             // neighbour sums -> columns 96..191; board pooling (mean | max) of a
             {
-                float nsum[32];
-#pragma unroll
-                for (int j = 0; j < 32; ++j) nsum[j] = 0.0f;
-                if (H) {
-                    // f16: packed adds (the sum is stored as f16 anyway)
+                {
+                    // packed f16 adds (the sum is stored as an f16 operand anyway)
                     __half2 acc[16];
 #pragma unroll
                     for (int j = 0; j < 16; ++j) acc[j] = __float2half2_rn(0.0f);
@@ -404,22 +401,6 @@ __global__ void __launch_bounds__(384, 1)
                         o.w = *reinterpret_cast<const uint32_t*>(&acc[4 * c + 3]);
                         *reinterpret_cast<uint4*>(sA1 + umma::sw128_offset(128, row, C + col0 + 8 * c)) = o;
                     }
-                } else {
-                    {
-#pragma unroll
-                        for (int d = 0; d < 6; ++d) {
-                            const int nr = nbr[d];
-                            if (nr < 0) continue;
-#pragma unroll
-                            for (int c = 0; c < 4; ++c) {
-                                float v[8];
-                                ld_chunk<H>(sA1, 128, nr, col0 + 8 * c, v);
-#pragma unroll
-                                for (int j = 0; j < 8; ++j) nsum[8 * c + j] += v[j];
-                            }
-                        }
-                    }
-                    put_x32<H>(sA1, 128, row, C + col0, nsum);
                 }
             }
             // mean | max over each board's hexes: (board, 8-column chunk, hex group)
@@ -435,7 +416,7 @@ __global__ void __launch_bounds__(384, 1)
                     for (int j = 0; j < 8; ++j) { sum[j] = 0.0f; mx[j] = -INFINITY; }
                     for (int h = gidx; h < NH; h += HG) {
                         float v[8];
-                        ld_chunk<H>(sA1, 128, i * NH + h, c0, v);
+                        ld_chunk(sA1, 128, i * NH + h, c0, v);
 #pragma unroll
                         for (int j = 0; j < 8; ++j) { sum[j] += v[j]; mx[j] = fmaxf(mx[j], v[j]); }
                     }
@@ -474,7 +455,7 @@ __global__ void __launch_bounds__(384, 1)
             }
             if (tid == 0) {
                 const uint32_t aa = umma::smem_u32(sA1), wb = umma::smem_u32(sW[buf]);
-                const uint32_t idesc = umma::idesc16(128, 96, umma::Op16<H>::fmt);
+                const uint32_t idesc = umma::idesc16(128, 96, F16::fmt);
 #pragma unroll
                 for (int k0 = 0; k0 < 2 * C; k0 += 16)
                     umma::mma16(tmem, umma::desc_at(aa, 128, k0), umma::desc_at(wb, 96, k0), idesc, k0 > 0);
@@ -519,8 +500,7 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
                         const int k = 8 * c + 2 * j;
-                        w4[j] = real_row ? umma::ln_gelu2<H>(y[k] * inv + nm, y[k + 1] * inv + nm, col0 + k, gam, bet,
-                                                             S.gb2[blk][1])
+                        w4[j] = real_row ? umma::ln_gelu2<true>(y[k] * inv + nm, y[k + 1] * inv + nm, col0 + k, S.gb2[blk][1])
                                          : 0u;
                     }
                     *reinterpret_cast<uint4*>(sA2 + umma::sw128_offset(128, row, col0 + 8 * c)) =
@@ -533,7 +513,7 @@ __global__ void __launch_bounds__(384, 1)
             umma::fence_after_sync();
             if (tid == 0) {
                 const uint32_t aa = umma::smem_u32(sA2), wb = umma::smem_u32(sW[buf] + MIX_BYTES);
-                const uint32_t idesc = umma::idesc16(128, 96, umma::Op16<H>::fmt);
+                const uint32_t idesc = umma::idesc16(128, 96, F16::fmt);
 #pragma unroll
                 for (int k0 = 0; k0 < C; k0 += 16)
                     umma::mma16(tmem + 128, umma::desc_at(aa, 128, k0), umma::desc_at(wb, 96, k0), idesc, k0 > 0);
@@ -659,7 +639,7 @@ __global__ void __launch_bounds__(384, 1)
                 const size_t slot = jobs[row_job[gb_[i]]].tile_base + lr / 128;
                 const uint32_t rt = lr % 128;
                 g_pb[slot * 32768 + rt * 256 + ((uint32_t)(c >> 3) ^ (rt & 7)) * 8 + (c & 7)] =
-                    umma::Op16<H>::one(Hd.P[i][c] + bout[c] - S.gb[i][0]);
+                    F16::one(Hd.P[i][c] + bout[c] - S.gb[i][0]);
             }
         }
         rows_gemm<BOARDS, D, JW, 3, 1, 22>(&Hd.P[0][0], D, W + L.join_p.w, nullptr, &Hd.jp[0][0], JW, Hd.part);
@@ -676,7 +656,8 @@ __global__ void __launch_bounds__(384, 1)
         for (int q = tid; q < BOARDS * JW; q += blockDim.x) {
             int i = q / JW, c = q % JW;
             if (i < nb)
-                g_jp[(size_t)gb_[i] * JW + c] = umma::Op16<H>::one(Hd.jp[i][c] - S.gb[i][1]);
+                g_jp[((size_t)jobs[row_job[gb_[i]]].row_base + row_local[gb_[i]]) * JW + c] =
+                    F16::one(Hd.jp[i][c] - S.gb[i][1]);
         }
         __syncthreads();
     }
@@ -727,13 +708,38 @@ void launch_tokproj(const JobDev* jobs, uint32_t njobs, const float* W, cudaStre
     if (njobs) k_tokproj<<<njobs, 256, 0, s>>>(jobs, W);
 }
 
+// P and jp of every duplicate row from its representative (the first row of
+// its job with the same public row bytes, which the trunk computed): one
+// warp per row, 16-byte chunks; a P row's chunk k sits at k ^ (row & 7) of
+// its 512-byte row in the tile image, so the chunk is read at the
+// representative's position and written at the duplicate's.
+__global__ void __launch_bounds__(256) k_board_dup(const JobDev* __restrict__ jobs, const uint32_t* __restrict__ dup,
+                                                   uint32_t n, uint16_t* __restrict__ g_pb, uint16_t* __restrict__ g_jp) {
+    const uint32_t w = blockIdx.x * 8 + threadIdx.x / 32, lane = threadIdx.x % 32;
+    if (w >= n) return;
+    const JobDev& J = jobs[dup[3 * w]];
+    const uint32_t d = dup[3 * w + 1], r = dup[3 * w + 2];
+    const size_t td = (size_t)J.tile_base + d / 128, tr = (size_t)J.tile_base + r / 128;
+    const uint32_t rd = d % 128, rr = r % 128;
+    const uint4* src = reinterpret_cast<const uint4*>(g_pb + tr * 32768 + rr * 256);
+    uint4* dst = reinterpret_cast<uint4*>(g_pb + td * 32768 + rd * 256);
+    dst[lane ^ (rd & 7)] = src[lane ^ (rr & 7)];
+    if (lane < JW / 8)
+        reinterpret_cast<uint4*>(g_jp + ((size_t)J.row_base + d) * JW)[lane] =
+            reinterpret_cast<const uint4*>(g_jp + ((size_t)J.row_base + r) * JW)[lane];
+}
+
+void launch_board_dup(const JobDev* jobs, const uint32_t* dup, uint32_t n, uint16_t* g_pb, uint16_t* g_jp,
+                      cudaStream_t s) {
+    if (n) k_board_dup<<<(n + 7) / 8, 256, 0, s>>>(jobs, dup, n, g_pb, g_jp);
+}
+
 void launch_trunk_fast(const JobDev* jobs, const uint32_t* row_job, const uint32_t* row_local, uint32_t total_rows,
                        const uint8_t* tiles, const float* W, const float* B, const float* LN, const FastNetDev& fn,
                        uint16_t* g_pb, uint16_t* g_jp, int* err, cudaStream_t s) {
-    const bool half = fn.half != 0;
     if (!total_rows) return;
     const size_t smem = 2 * BLOCK_BYTES + A1_BYTES + A2_BYTES + sizeof(TrunkSmem) + 1024;
-    auto kern = half ? k_trunk_fast<true> : k_trunk_fast<false>;
+    auto kern = k_trunk_fast;
     if (!raise_smem_limit((const void*)kern, smem)) return;
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);

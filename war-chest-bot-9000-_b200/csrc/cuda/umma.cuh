@@ -277,16 +277,6 @@ __device__ __forceinline__ uint4 pack_chunk(const float* x) {
                       Op16<HALF>::pack(x[6], x[7]));
 }
 
-// Store 8 consecutive operands (one 16-byte chunk) of row r, columns [k, k+8).
-template <bool HALF = false>
-__device__ __forceinline__ void st_chunk(uint8_t* tile, uint32_t R, uint32_t r, uint32_t k, const float* x) {
-    *reinterpret_cast<uint4*>(tile + sw128_offset(R, r, k)) = pack_chunk<HALF>(x);
-}
-
-__device__ __forceinline__ void st_zero_chunk(uint8_t* tile, uint32_t R, uint32_t r, uint32_t k) {
-    *reinterpret_cast<uint4*>(tile + sw128_offset(R, r, k)) = make_uint4(0, 0, 0, 0);
-}
-
 // GELU (tanh form) for the tensor-core path, through the identity
 // 0.5 x (1 + tanh(u)) = x / (1 + exp(-2u)), u = sqrt(2/pi) (x + 0.044715 x^3),
 // with the hardware base-2 exponential (relative error about 2^-22) and a fast
@@ -304,43 +294,18 @@ __device__ __forceinline__ float gelu_fast(float x) {
     return __fdividef(x, 1.0f + e);
 }
 
-// GELU (tanh form) of two floats, returned as a packed pair of 16-bit
-// operands. f16: computed in f16x2 arithmetic with the hardware f16x2 tanh
-// (two elements per instruction; its error is of the order of the f16
-// rounding the result gets anyway), as x (1 + tanh(u)) / 2 with x^2 capped at
-// 1024 inside u (|x| >= 32: tanh has long saturated, and u stays finite).
-// bf16: the fp32 gelu_fast, then rounded.
-template <bool HALF>
-__device__ __forceinline__ uint32_t gelu_pack2(float a, float b);
-template <>
-__device__ __forceinline__ uint32_t gelu_pack2<true>(float a, float b) {
-    const __half2 x = __floats2half2_rn(a, b);
-    const __half2 x2 = __hmin2(__hmul2(x, x), __float2half2_rn(1024.0f));
-    const __half2 u = __hmul2(x, __hfma2(x2, __float2half2_rn(0.035677408f), __float2half2_rn(0.79788456f)));
-    uint32_t ub = *reinterpret_cast<const uint32_t*>(&u), tb;
-    asm("tanh.approx.f16x2 %0, %1;" : "=r"(tb) : "r"(ub));
-    const __half2 t = *reinterpret_cast<const __half2*>(&tb);
-    const __half2 g = __hmul2(x, __hfma2(t, __float2half2_rn(0.5f), __float2half2_rn(0.5f)));
-    return *reinterpret_cast<const uint32_t*>(&g);
-}
-template <>
-__device__ __forceinline__ uint32_t gelu_pack2<false>(float a, float b) {
-    return Op16<false>::pack(gelu_fast(a), gelu_fast(b));
-}
-
-// LayerNorm affine + GELU of two already-normalised values n = (x - mean) / sd
-// at columns c, c + 1, packed as two 16-bit operands. gb2 holds the
-// (gamma, beta) pairs of the columns as packed f16x2 words: [2 * (c / 2)] the
-// gammas, [2 * (c / 2) + 1] the betas. f16: affine and GELU in f16x2 (one
-// conversion, one FMA for gamma / beta, the tanh form with x^2 capped at
-// 1024, where tanh has long saturated; 7 packed ops and one tanh per pair).
-// bf16: fp32 affine and gelu_fast.
-template <bool HALF>
-__device__ __forceinline__ uint32_t ln_gelu2(float n0, float n1, int c, const float* gam, const float* bet,
-                                             const uint32_t* gb2);
-template <>
-__device__ __forceinline__ uint32_t ln_gelu2<true>(float n0, float n1, int c, const float*, const float*,
-                                                   const uint32_t* gb2) {
+// LayerNorm affine + GELU (tanh form) of two already-normalised values
+// n = (x - mean) / sd at columns c, c + 1, packed as two 16-bit operands.
+// gb2 holds the (gamma, beta) pairs of the columns as packed f16x2 words:
+// [2 * (c / 2)] the gammas, [2 * (c / 2) + 1] the betas. Computed in f16x2
+// arithmetic with the hardware f16x2 tanh (one conversion, one FMA for gamma /
+// beta, the tanh form x (1 + tanh(u)) / 2 with x^2 capped at 1024 inside u,
+// where tanh has long saturated; 7 packed ops and one tanh per pair): its
+// error is of the order of the f16 rounding of the result. For bf16 operands
+// the f16 pair is then rounded to bf16 (3 fewer mantissa bits, so the f16
+// steps add little), which keeps the epilogue at the f16 path's instruction
+// count.
+__device__ __forceinline__ __half2 ln_gelu2_h(float n0, float n1, int c, const uint32_t* gb2) {
     const uint2 gb = *reinterpret_cast<const uint2*>(gb2 + 2 * (c >> 1));
     const __half2 n = __floats2half2_rn(n0, n1);
     const __half2 x = __hfma2(n, *reinterpret_cast<const __half2*>(&gb.x), *reinterpret_cast<const __half2*>(&gb.y));
@@ -349,13 +314,17 @@ __device__ __forceinline__ uint32_t ln_gelu2<true>(float n0, float n1, int c, co
     uint32_t ub = *reinterpret_cast<const uint32_t*>(&u), tb;
     asm("tanh.approx.f16x2 %0, %1;" : "=r"(tb) : "r"(ub));
     const __half2 t = *reinterpret_cast<const __half2*>(&tb);
-    const __half2 g = __hmul2(x, __hfma2(t, __float2half2_rn(0.5f), __float2half2_rn(0.5f)));
-    return *reinterpret_cast<const uint32_t*>(&g);
+    return __hmul2(x, __hfma2(t, __float2half2_rn(0.5f), __float2half2_rn(0.5f)));
 }
-template <>
-__device__ __forceinline__ uint32_t ln_gelu2<false>(float n0, float n1, int c, const float* gam, const float* bet,
-                                                    const uint32_t*) {
-    return Op16<false>::pack(gelu_fast(n0 * gam[c] + bet[c]), gelu_fast(n1 * gam[c + 1] + bet[c + 1]));
+template <bool HALF>
+__device__ __forceinline__ uint32_t ln_gelu2(float n0, float n1, int c, const uint32_t* gb2) {
+    const __half2 g = ln_gelu2_h(n0, n1, c, gb2);
+    if constexpr (HALF) {
+        return *reinterpret_cast<const uint32_t*>(&g);
+    } else {
+        const float2 f = __half22float2(g);
+        return Op16<false>::pack(f.x, f.y);
+    }
 }
 
 // (gamma, beta) of columns c, c + 1 as the packed words ln_gelu2 reads.
@@ -363,13 +332,6 @@ __device__ __forceinline__ void pack_gb2(const float* gam, const float* bet, int
     const __half2 g = __floats2half2_rn(gam[c], gam[c + 1]), b = __floats2half2_rn(bet[c], bet[c + 1]);
     out2[0] = *reinterpret_cast<const uint32_t*>(&g);
     out2[1] = *reinterpret_cast<const uint32_t*>(&b);
-}
-
-// GELU of 8 consecutive floats as one 16-byte chunk of 16-bit operands.
-template <bool HALF>
-__device__ __forceinline__ uint4 gelu_chunk(const float* x) {
-    return make_uint4(gelu_pack2<HALF>(x[0], x[1]), gelu_pack2<HALF>(x[2], x[3]), gelu_pack2<HALF>(x[4], x[5]),
-                      gelu_pack2<HALF>(x[6], x[7]));
 }
 
 }  // namespace umma

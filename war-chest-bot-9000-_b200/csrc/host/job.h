@@ -58,6 +58,7 @@ struct JobImage {
     std::vector<uint32_t> tl_ridx, tl_nc, tl_vidx;  // [2 * nterm]
     std::vector<float> tl_util0;                    // utility for player 0
     std::vector<uint8_t> gpu_rows;                  // nrows_net * GPU_ROW_BYTES
+    std::vector<uint32_t> row_rep;                  // per network row: the first row with the same public row bytes
     std::vector<float> cphi;                        // ncfg * CFEAT
     std::vector<uint8_t> cplayer;
     std::vector<uint32_t> cfg_col;                  // index of each config among its player's configs

@@ -2,6 +2,7 @@
 #include "pbs.h"
 
 #include <algorithm>
+#include <cstring>
 #include <stdexcept>
 
 namespace wc {
@@ -431,6 +432,59 @@ void normalize_weights(const float* w, size_t n, float* out) {
 }
 
 // rebel.rs:1274-1306.
+// rebel.rs:996-1030: FNV-1a over the tables the expansion depends on (the
+// location map, every unit's card facts as f32 bits, the layout constants),
+// each mixed in as one u64.
+uint64_t rules_table_hash() {
+    uint64_t h = 0xcbf29ce484222325ull;
+    auto mix = [&](uint64_t x) { h = (h ^ x) * 0x100000001b3ull; };
+    const Board& bd = board();
+    for (int k = 0; k < N_HEXES; ++k) mix(bd.is_location[k] ? 1u : 0u);
+    for (int u = 0; u < N_UNITS; ++u) {
+        float f[CARD_FEATS];
+        write_card_features((uint8_t)u, f);
+        for (float x : f) {
+            uint32_t bits;
+            std::memcpy(&bits, &x, 4);
+            mix(bits);
+        }
+    }
+    for (int c : {PUBFEAT, HEX_FACTS, HEX_CH, CARD_FEATS, NSLOT, NTYPE, N_HEXES, PILE_COUNTS, LOOSE}) mix((uint64_t)c);
+    return h;
+}
+
+// rebel.rs:1236-1268: the replay row of a live state.
+void pack_row(const State& s, const Ctx& ctx, uint8_t* out) {
+    const uint32_t version = ROW_FORMAT_VERSION;
+    const uint64_t hash = rules_table_hash();
+    for (int k = 0; k < 4; ++k) out[ROW_VERSION + k] = (uint8_t)(version >> (8 * k));
+    for (int k = 0; k < 8; ++k) out[ROW_HASH + k] = (uint8_t)(hash >> (8 * k));
+    for (int t = 0; t < 2 * NSLOT; ++t) out[ROW_IDS + t] = ctx.slots[t / NSLOT][t % NSLOT];
+    for (int h = 0; h < N_HEXES; ++h) {
+        out[ROW_HEX_OWNER + h] = s.hex_owner[h];
+        out[ROW_HEX_SLOT + h] = s.hex_owner[h] == NONE ? NONE : (uint8_t)ctx.slot_of[s.hex_owner[h]][s.hex_type[h]];
+        out[ROW_HEX_HEIGHT + h] = s.hex_height[h];
+        out[ROW_HEX_MARKER + h] = s.loc_marker[h];
+    }
+    for (int p = 0; p < 2; ++p) {
+        uint8_t res[NSLOT];
+        reserve(s, (uint8_t)p, ctx, res);
+        for (int k = 0; k < NSLOT; ++k) {
+            const int u = ctx.slots[p][k], at = ROW_PILES + (p * NSLOT + k) * PILE_COUNTS;
+            out[at] = res[k];
+            out[at + 1] = s.zones[p][Z_FACEUP][u];
+            out[at + 2] = s.zones[p][Z_SUPPLY][u];
+            out[at + 3] = s.zones[p][Z_ELIM][u];
+        }
+    }
+    out[ROW_INITIATIVE] = s.initiative;
+    out[ROW_INIT_MOVED] = s.initiative_moved ? 1 : 0;
+    out[ROW_TO_ACT] = s.to_act();
+    const uint16_t plies = (uint16_t)(MAX_MAIN_PLAYS - std::min<uint16_t>(s.main_plays, MAX_MAIN_PLAYS));
+    out[ROW_PLIES] = (uint8_t)(plies & 0xff);
+    out[ROW_PLIES + 1] = (uint8_t)(plies >> 8);
+}
+
 void pack_gpu_row(const State& s, const Ctx& ctx, uint8_t* out) {
     for (int h = 0; h < N_HEXES; ++h) {
         out[GPU_ROW_HEX_OWNER + h] = s.hex_owner[h];

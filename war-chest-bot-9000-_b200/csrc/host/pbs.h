@@ -129,6 +129,26 @@ constexpr int GPU_ROW_TO_ACT = GPU_ROW_INIT_MOVED + 1;
 constexpr int GPU_ROW_PLIES = GPU_ROW_TO_ACT + 1;
 constexpr int GPU_ROW_BYTES = GPU_ROW_PLIES + 2;
 
+// Replay row (rebel.rs:935-964), 215 bytes: the training buffer's compact
+// record of a position; the training batch expands it on the device.
+constexpr int ROW_VERSION = 0;
+constexpr int ROW_HASH = 4;
+constexpr int ROW_IDS = 12;
+constexpr int ROW_HEX_OWNER = 22;
+constexpr int ROW_HEX_SLOT = ROW_HEX_OWNER + N_HEXES;
+constexpr int ROW_HEX_HEIGHT = ROW_HEX_SLOT + N_HEXES;
+constexpr int ROW_HEX_MARKER = ROW_HEX_HEIGHT + N_HEXES;
+constexpr int ROW_PILES = ROW_HEX_MARKER + N_HEXES;
+constexpr int ROW_INITIATIVE = ROW_PILES + 2 * NSLOT * PILE_COUNTS;
+constexpr int ROW_INIT_MOVED = ROW_INITIATIVE + 1;
+constexpr int ROW_TO_ACT = ROW_INIT_MOVED + 1;
+constexpr int ROW_PLIES = ROW_TO_ACT + 1;
+constexpr int ROW_BYTES = ROW_PLIES + 2;
+constexpr uint32_t ROW_FORMAT_VERSION = 1;  // rebel.rs:990
+
+uint64_t rules_table_hash();                                   // rebel.rs:996-1030
+void pack_row(const State& s, const Ctx& ctx, uint8_t* out);  // rebel.rs:1236-1268
+
 void pack_gpu_row(const State& s, const Ctx& ctx, uint8_t* out);
 void expand_gpu_row(const uint8_t* row, const uint8_t* ids /*NTYPE*/, float* out /*PUBFEAT*/);
 void write_public_features(const State& s, const Ctx& ctx, float* out);

@@ -51,7 +51,7 @@ std::unique_ptr<JobBlob> make_blob(std::unique_ptr<JobImage> img) {
         v(J.rge_src), v(J.rge_w), v(J.drawp), v(J.cell_ref), v(J.lr_ridx), v(J.lr_nc), v(J.lr_vidx),
         v(J.leaf_coff), v(J.leaf_cidx), v(J.tl_ridx), v(J.tl_nc), v(J.tl_vidx), v(J.tl_util0), v(J.gpu_rows),
         v(J.cphi), v(J.cplayer), v(J.card_feat), v(J.root_belief), v(J.carried), v(carry_off), v(J.cfg_col),
-        v(J.leaf_col)};
+        v(J.leaf_col), v(J.row_rep)};
     size_t at = 0;
     for (int i = 0; i < JobBlob::N_ARR; ++i) {
         b->off[i] = at;
@@ -82,7 +82,7 @@ std::unique_ptr<JobBlob> make_blob(std::unique_ptr<JobImage> img) {
     drop(J.rg_start), drop(J.rge_src), drop(J.rge_w), drop(J.drawp), drop(J.cell_ref), drop(J.lr_ridx);
     drop(J.lr_nc), drop(J.lr_vidx), drop(J.leaf_coff), drop(J.leaf_cidx), drop(J.tl_ridx), drop(J.tl_nc);
     drop(J.tl_vidx), drop(J.tl_util0), drop(J.gpu_rows), drop(J.cphi), drop(J.cplayer), drop(J.card_feat);
-    drop(J.root_belief), drop(J.carried), drop(J.cfg_col), drop(J.leaf_col);
+    drop(J.root_belief), drop(J.carried), drop(J.cfg_col), drop(J.leaf_col), drop(J.row_rep);
     b->img = std::move(img);
     return b;
 }
@@ -172,9 +172,9 @@ void build_fast_pack(DeviceCtx& d, const float* W, const float* B, const float* 
     put_tile(blob.data(), W + L.join_b.w, 128, NET_JW, h);
     for (int i = 0; i < 3; ++i) put_tile(blob.data() + (1 + i) * TJ, W + L.join_w[i].w, NET_JW, NET_JW, h);
     put_tile(blob.data() + off_out, W + L.join_out.w, NET_JW, NET_D, h);
-    for (int i = 0; i < NET_BLOCKS; ++i) {
-        put_tile(blob.data() + off_trunk + i * BLK, W + L.mix[i].w, 2 * NET_C, NET_C, h);
-        put_tile(blob.data() + off_trunk + i * BLK + MIX, W + L.out[i].w, NET_C, NET_C, h);
+    for (int i = 0; i < NET_BLOCKS; ++i) {  // the trunk's tiles are f16 in both modes
+        put_tile(blob.data() + off_trunk + i * BLK, W + L.mix[i].w, 2 * NET_C, NET_C, true);
+        put_tile(blob.data() + off_trunk + i * BLK + MIX, W + L.out[i].w, NET_C, NET_C, true);
     }
     std::memcpy(blob.data() + off_f, vec.data(), 4 * vec.size());
     check(cudaSetDevice(d.device), "set device");
@@ -354,18 +354,29 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
     b.term_all = range_of([&] { for (uint32_t j = 0; j < nj; ++j) add_items(items, j, 0, jobs[j]->img->nterm, 0); });
     b.netrows_all = range_of([&] { for (uint32_t j = 0; j < nj; ++j) add_items(items, j, 0, jobs[j]->img->nrows_net, 0); });
     b.exits_all = range_of([&] { for (uint32_t j = 0; j < nj; ++j) add_items(items, j, 0, jobs[j]->nexit, 0); });
-    std::vector<uint32_t> row_job, row_local, cfg_job, cfg_local;
+    std::vector<uint32_t> row_job, row_local, cfg_job, cfg_local, dup;
+    const bool fast = dev.have_net && !dev.precise;
     for (uint32_t j = 0; j < nj; ++j) {
         const JobImage& J = *jobs[j]->img;
-        for (uint32_t r = 0; r < J.nrows_net; ++r) { row_job.push_back(j); row_local.push_back(r); }
+        // the tensor-core trunk runs on each distinct public row once; the
+        // other rows take their representative's P and jp (k_board_dup)
+        const uint32_t* rep = jobs[j]->arr<uint32_t>(JobBlob::ROW_REP);
+        for (uint32_t r = 0; r < J.nrows_net; ++r) {
+            if (fast && rep[r] != r) {
+                dup.insert(dup.end(), {j, r, rep[r]});
+                continue;
+            }
+            row_job.push_back(j);
+            row_local.push_back(r);
+        }
         for (uint32_t c = 0; c < J.ncfg; ++c) { cfg_job.push_back(j); cfg_local.push_back(c); }
         b.max_carried = std::max(b.max_carried, J.ncarried);
         b.node_updates += (double)J.nodes * (double)J.cfg.iters;
         b.leaf_evals += (double)J.nrows_net * (double)J.cfg.iters;
     }
     b.total_rows = (uint32_t)row_job.size();
+    b.n_dup = (uint32_t)(dup.size() / 3);
     b.total_cfgs = (uint32_t)cfg_job.size();
-    const bool fast = dev.have_net && !dev.precise;
     std::vector<size_t> o_f16(nj, 0);
     size_t o_gpool = 0, o_gjp = 0, o_gmass = 0, o_gpb = 0, o_gz = 0, o_tiles = 0, o_err = 0;
     struct HeadTile { uint32_t job, first, count, pad; };
@@ -389,7 +400,7 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
             f16_bytes[j] = (65536ull + 16384ull) * npass;
             o_f16[j] = A.take(f16_bytes[j]);
         }
-        size_t R = row_job.size();
+        size_t R = row_job.size() + b.n_dup;
         o_gpool = A.take(32768ull * NT);  // [tile][player 0 | player 1] 128 x 64 images
         o_gjp = A.take(2ull * R * NET_JW);
         o_gmass = A.take(8ull * R);
@@ -402,6 +413,7 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
     size_t o_items = A.take(sizeof(wcdev::WorkItem) * items.size());
     size_t o_rj = A.take(4ull * row_job.size()), o_rl = A.take(4ull * row_local.size());
     size_t o_cj = A.take(4ull * cfg_job.size()), o_cl = A.take(4ull * cfg_local.size());
+    size_t o_dup = A.take(4ull * dup.size());
     b.dbytes = A.at;
     if (mem) {
         if (b.dbytes > mem_bytes) throw std::runtime_error("batch plan exceeds its arena");
@@ -510,6 +522,7 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
     b.d_row_local = reinterpret_cast<uint32_t*>(D + o_rl);
     b.d_cfg_job = reinterpret_cast<uint32_t*>(D + o_cj);
     b.d_cfg_local = reinterpret_cast<uint32_t*>(D + o_cl);
+    b.d_dup = reinterpret_cast<uint32_t*>(D + o_dup);
     if (fast) {
         b.g_pool_img = reinterpret_cast<uint16_t*>(D + o_gpool);
         b.g_jp = reinterpret_cast<uint16_t*>(D + o_gjp);
@@ -529,6 +542,8 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
         check(cudaMemcpyAsync(b.d_row_job, row_job.data(), 4 * row_job.size(), cudaMemcpyHostToDevice, s), "upload rows");
         check(cudaMemcpyAsync(b.d_row_local, row_local.data(), 4 * row_local.size(), cudaMemcpyHostToDevice, s), "upload rows");
     }
+    if (!dup.empty())
+        check(cudaMemcpyAsync(b.d_dup, dup.data(), 4 * dup.size(), cudaMemcpyHostToDevice, s), "upload duplicate rows");
     if (!cfg_job.empty()) {
         check(cudaMemcpyAsync(b.d_cfg_job, cfg_job.data(), 4 * cfg_job.size(), cudaMemcpyHostToDevice, s), "upload cfgs");
         check(cudaMemcpyAsync(b.d_cfg_local, cfg_local.data(), 4 * cfg_local.size(), cudaMemcpyHostToDevice, s), "upload cfgs");
@@ -572,7 +587,8 @@ size_t job_device_bytes(const DeviceCtx& dev, const JobBlob& jb) {
         }
     }
     // descriptors, work items (one per <= 256 tasks of a level range) and row / config indices
-    b += sizeof(wcdev::JobDev) + 16ull * (J.ncells / 128 + 4 * J.nlevels + 8) + 8ull * (J.nrows_net + J.ncfg);
+    b += sizeof(wcdev::JobDev) + 16ull * (J.ncells / 128 + 4 * J.nlevels + 8) + 8ull * (J.nrows_net + J.ncfg) +
+         12ull * J.nrows_net;
     return b + b / 64 + 4096;
 }
 
@@ -718,6 +734,7 @@ void enqueue_leaf_values(Batch& b, int p) {
                     b.count_launch(nj), wcdev::launch_tokproj(S.J, nj, dv.W, S.s);
                     b.count_launch(b.total_rows), wcdev::launch_trunk_fast(S.J, b.d_row_job, b.d_row_local, b.total_rows, dv.fast.trunk_tiles, dv.W,
                                              dv.B, dv.LN, dv.fast, b.g_pb, b.g_jp, b.d_err, S.s);
+                    b.count_launch(b.n_dup ? 1 : 0), wcdev::launch_board_dup(S.J, b.d_dup, b.n_dup, b.g_pb, b.g_jp, S.s);
                 });
             }
             b.count_launch(b.total_cfgs), wcdev::launch_configs(S.J, b.d_cfg_job, b.d_cfg_local, b.total_cfgs, dv.W, dv.B, dv.LN, S.s);
@@ -772,14 +789,7 @@ void download_board_rows(Batch& b, size_t job, float* pb, float* jp) {
         const size_t rt = r % 128, base = (r / 128) * 32768 + rt * 256;
         for (size_t c = 0; c < NET_D; ++c) hp[r * NET_D + c] = hpt[base + (((c >> 3) ^ (rt & 7)) << 3) + (c & 7)];
     }
-    const bool half = b.dev->half;
-    auto f = [half](uint16_t v) {
-        if (half) return __half2float(__ushort_as_half(v));
-        uint32_t u = (uint32_t)v << 16;
-        float x;
-        std::memcpy(&x, &u, 4);
-        return x;
-    };
+    auto f = [](uint16_t v) { return __half2float(__ushort_as_half(v)); };  // P and jp are f16 in both modes
     if (pb) for (size_t i = 0; i < hp.size(); ++i) pb[i] = f(hp[i]);
     if (jp) for (size_t i = 0; i < hj.size(); ++i) jp[i] = f(hj[i]);
 }
@@ -812,6 +822,7 @@ void enqueue_solve(Batch& b) {
                     b.count_launch(nj), wcdev::launch_tokproj(S.J, nj, dv.W, S.s);
                     b.count_launch(b.total_rows), wcdev::launch_trunk_fast(S.J, b.d_row_job, b.d_row_local, b.total_rows, dv.fast.trunk_tiles, dv.W,
                                              dv.B, dv.LN, dv.fast, b.g_pb, b.g_jp, b.d_err, S.s);
+                    b.count_launch(b.n_dup ? 1 : 0), wcdev::launch_board_dup(S.J, b.d_dup, b.n_dup, b.g_pb, b.g_jp, S.s);
                 });
             }
             b.count_launch(b.total_cfgs), wcdev::launch_configs(S.J, b.d_cfg_job, b.d_cfg_local, b.total_cfgs, dv.W, dv.B, dv.LN, S.s);

@@ -24,7 +24,7 @@ struct DeviceCtx {
     float* LN = nullptr;
     bool have_net = false;
     bool precise = true;  // fp32 network in the reference's operation order
-    bool half = true;     // tensor-core network operands: f16 (true) or bf16
+    bool half = true;     // the tensor-core net's per-iteration chain operands: f16 (true) or bf16
     uint64_t wait_ns = 2000000000ull;  // limit of each tensor-core mbarrier wait (ns)
     uint64_t version = 0;
     NetLayout L;
@@ -55,7 +55,7 @@ struct JobBlob {
     enum Arr {
         CELL_VIDX, ROW_OFF, ROW_PLAYER, VG_START, VGE_IDX, VGE_W, RG_START, RGE_SRC, RGE_W, DRAWP, CELL_REF,
         LR_RIDX, LR_NC, LR_VIDX, LEAF_COFF, LEAF_CIDX, TL_RIDX, TL_NC, TL_VIDX, TL_UTIL0, GPU_ROWS, CPHI,
-        CPLAYER, CARD_FEAT, ROOT_BELIEF, CARRIED, CARRY_OFF, CFG_COL, LEAF_COL, N_ARR
+        CPLAYER, CARD_FEAT, ROOT_BELIEF, CARRIED, CARRY_OFF, CFG_COL, LEAF_COL, ROW_REP, N_ARR
     };
     size_t off[N_ARR] = {};
     // A packed array. The blob is the only copy: make_blob releases the
@@ -90,6 +90,10 @@ struct Batch {
     uint32_t* d_cfg_job = nullptr;
     uint32_t* d_cfg_local = nullptr;
     uint32_t total_rows = 0, total_cfgs = 0, max_carried = 0;
+    // tensor-core path: the row lists above hold each job's distinct public
+    // rows only; d_dup holds (job, row, representative row) of the others
+    uint32_t* d_dup = nullptr;
+    uint32_t n_dup = 0;
     // fast network path: global per-row bf16 activations and per-job tiles
     uint16_t* g_pool_img = nullptr; // [tile][player][128 x POOL operand image]
     uint16_t* g_jp = nullptr;     // [rows][JW]

@@ -111,6 +111,11 @@ def _load() -> C.CDLL:
         "wc_game_counters": (I, [VP, P(C.c_int64)]),
         "wc_game_root": (I, [VP, C.c_char_p, C.c_size_t, P(C.c_size_t)]),
         "wc_game_free": (None, [VP]),
+        "wc_replay_pack_row": (I, [C.c_char_p, C.c_size_t, C.c_char_p]),
+        "wc_wcj8_from_root": (I, [C.c_char_p, C.c_size_t, P(_SolveCfg), VP, C.c_uint32, P(C.c_uint32), C.c_uint32,
+                                  C.c_char_p, C.c_size_t, P(C.c_size_t)]),
+        "wc_job_from_wcj8": (I, [C.c_char_p, C.c_size_t, P(VP)]),
+        "wc_replay_expand": (I, [VP, C.c_size_t, VP, VP, C.c_size_t, VP, VP, VP]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -204,6 +209,39 @@ def apply_action(state: bytes, code: int, unchecked: bool = False) -> bytes:
     n = C.c_size_t()
     _check(lib().wc_state_apply(state, len(state), code, int(unchecked), buf, 4096, C.byref(n)))
     return buf.raw[: n.value]
+
+
+ROW_BYTES = 215   # replay row (engine/src/rebel.rs:935-964)
+PUBFEAT = 897     # the public encoding's width (engine/src/rebel.rs:1044)
+CCOUNTS = 15      # config counts per config (engine/src/rebel.rs:68)
+
+
+def pack_row(state: bytes) -> bytes:
+    """pack_row (engine/src/rebel.rs:1236): the replay row of a state in the
+    write_state encoding, or of the state a root starts with."""
+    buf = C.create_string_buffer(ROW_BYTES)
+    _check(lib().wc_replay_pack_row(state, len(state), buf))
+    return buf.raw
+
+
+def wcj8_bytes(root: bytes, cfg: "Cfg", carried: Optional[np.ndarray] = None, net_dims=(5,)) -> bytes:
+    """PackedJob::from_solver(root's subgame, carried).to_bytes() (engine/src/
+    serialize.rs:340-357, 1051-1125): the reference's WCJ8 job bytes."""
+    if carried is not None:
+        carried = np.ascontiguousarray(carried, np.float32)
+        n, ptr = carried.shape[0], carried.ctypes.data
+    else:
+        n, ptr = 0, None
+    dims = (C.c_uint32 * max(1, len(net_dims)))(*net_dims)
+    need = C.c_size_t()
+    rc = lib().wc_wcj8_from_root(root, len(root), C.byref(cfg._c()), ptr, n, dims, len(net_dims), None, 0,
+                                 C.byref(need))
+    if rc != 1 or need.value == 0:
+        _check(rc)
+    buf = C.create_string_buffer(need.value)
+    _check(lib().wc_wcj8_from_root(root, len(root), C.byref(cfg._c()), ptr, n, dims, len(net_dims), buf,
+                                   need.value, C.byref(need)))
+    return buf.raw[: need.value]
 
 
 def state_query(state: bytes) -> dict:
@@ -300,6 +338,15 @@ class PackedJob:
         return cls(h.value, root, cfg)
 
     @classmethod
+    def from_wcj8(cls, data: bytes, cfg: Cfg) -> "PackedJob":
+        """A job from the reference's WCJ8 job bytes (PackedJob::from_bytes,
+        engine/src/serialize.rs:1127); `cfg` records the solve configuration
+        the bytes carry."""
+        h = C.c_void_p()
+        _check(lib().wc_job_from_wcj8(data, len(data), C.byref(h)))
+        return cls(h.value, b"", cfg)
+
+    @classmethod
     def build_many(cls, roots: Sequence[bytes], cfg: Cfg, threads: int = 0,
                    carried: Optional[Sequence[Optional[np.ndarray]]] = None) -> List[Optional["PackedJob"]]:
         """Jobs for many roots on native host threads (wc_job_build_batch): the
@@ -334,8 +381,8 @@ class PackedJob:
 
     def counts(self) -> np.ndarray:
         """Per-player work counts (see wc_job_counts)."""
-        out = (C.c_uint64 * 20)()
-        _check(lib().wc_job_counts(self._h, out, 20))
+        out = (C.c_uint64 * 21)()
+        _check(lib().wc_job_counts(self._h, out, 21))
         return np.array(list(out), np.int64)
 
     def root_belief(self) -> np.ndarray:
