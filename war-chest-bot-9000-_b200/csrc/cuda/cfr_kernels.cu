@@ -10,6 +10,7 @@
 // Memory layout: see host/job.h. One CTA per work item, one thread per task.
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <cfloat>
 #include <cstdint>
 
@@ -28,6 +29,16 @@ __device__ __forceinline__ const float* pick_strat(const JobDev& J, int strat_se
 }
 
 // Uniform initial strategy, zero regrets and sums (search.rs:820-836).
+// The readout column of every leaf-config entry (leaf_col[e] =
+// cfg_col[leaf_cidx[e]]), derived on the device after a job's tables land:
+// one grid row of blocks per job, grid-stride over its entries.
+__global__ void k_leaf_col(const JobDev* __restrict__ jobs, uint32_t first) {
+    const JobDev& J = jobs[first + blockIdx.y];
+    const uint32_t n = J.leaf_coff[2 * J.nrows_net];
+    for (uint32_t e = blockIdx.x * blockDim.x + threadIdx.x; e < n; e += gridDim.x * blockDim.x)
+        J.leaf_col[e] = J.cfg_col[J.leaf_cidx[e]];
+}
+
 __global__ void k_init_rows(const JobDev* __restrict__ jobs, const WorkItem* __restrict__ items) {
     const WorkItem wi = items[blockIdx.x];
     if (threadIdx.x >= wi.count) return;
@@ -306,6 +317,11 @@ __global__ void k_carry(const JobDev* __restrict__ jobs, const WorkItem* __restr
 }
 
 // ------------------------------------------------------------- launchers
+
+void launch_leaf_col(const JobDev* jobs, uint32_t njobs, cudaStream_t s) {
+    for (uint32_t first = 0; first < njobs; first += 65535u)
+        k_leaf_col<<<dim3(16, std::min(65535u, njobs - first)), 256, 0, s>>>(jobs, first);
+}
 
 void launch_init_rows(const JobDev* jobs, const WorkItem* items, uint32_t n, cudaStream_t s) {
     if (n) k_init_rows<<<n, WI_TASKS, 0, s>>>(jobs, items);

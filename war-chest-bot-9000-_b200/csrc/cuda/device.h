@@ -35,7 +35,8 @@ struct JobDev {
     const uint32_t* tl_nc;
     const uint32_t* tl_vidx;
     const float* tl_util0;
-    const uint8_t* gpu_rows;
+    const uint8_t* gpu_rows;   // the distinct public rows (201 bytes each)
+    const uint32_t* row_gpu;   // per network row: its public row's index in gpu_rows
     const float* cphi;
     const uint8_t* cplayer;
     const float* card_feat;
@@ -47,7 +48,8 @@ struct JobDev {
     const float* weights_ln;
     float* cardm;      // [2][NTYPE][3 * POOL]: cfg_m applied to the card tokens
     const uint32_t* cfg_col;  // config -> index among its player's configs
-    const uint32_t* leaf_col; // per leaf_cidx entry: its config's cfg_col (the readout column)
+    uint32_t* leaf_col;       // per leaf_cidx entry: its config's cfg_col (the readout column), derived on
+                              // the device at upload (k_leaf_col), so host tables do not carry it
     uint16_t* f16;     // fast path: f(c) as readout operand images, 128 configs x D each (64 KB),
                        // player 0's ceil(n0 / 128) passes then player 1's
     uint16_t* g16;     // fast path: g(c) as pooling operand images, 64 x 128 configs each (16 KB), same order

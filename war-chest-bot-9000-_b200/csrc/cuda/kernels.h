@@ -14,6 +14,8 @@ enum BackMode { BACK_REGRET = 0, BACK_VALUE = 1, BACK_BEST = 2 };
 
 // cfr_kernels.cu
 void launch_init_rows(const JobDev* jobs, const WorkItem* items, uint32_t n, cudaStream_t s);
+// leaf_col of every job from its uploaded leaf_cidx and cfg_col (at upload)
+void launch_leaf_col(const JobDev* jobs, uint32_t njobs, cudaStream_t s);
 void launch_rows(const JobDev* jobs, const WorkItem* items, uint32_t n, int p, int mode, int strat_sel, float da,
                  float db, float predict, cudaStream_t s);
 void launch_vgather(const JobDev* jobs, const WorkItem* items, uint32_t n, int p, cudaStream_t s);

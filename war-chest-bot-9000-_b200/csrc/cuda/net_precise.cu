@@ -117,7 +117,7 @@ __global__ void k_trunk(const JobDev* __restrict__ jobs, const uint32_t* __restr
     TrunkSmem& S = *reinterpret_cast<TrunkSmem*>(smem_raw);
     const JobDev& J = jobs[row_job[blockIdx.x]];
     const uint32_t r = row_local[blockIdx.x];
-    const uint8_t* row = J.gpu_rows + (size_t)r * ROW_BYTES;
+    const uint8_t* row = J.gpu_rows + (size_t)J.row_gpu[r] * ROW_BYTES;
     const int tid = threadIdx.x, nt = blockDim.x;
 
     // expand the compact public row (rebel.rs:1144-1233)

@@ -14,7 +14,8 @@
 //
 // Byte work bound by HBM writes (PUBFEAT floats per view against 215 bytes
 // read): one warp per view, the row staged in shared memory, the features
-// written lane-strided (coalesced).
+// written lane-strided (coalesced), each section's features computed with
+// selects and table reads (no divergent branches, no divisions).
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -34,18 +35,34 @@ using namespace wc;
 __constant__ float c_card_feat[N_UNITS * CARD_FEATS];
 __constant__ uint8_t c_is_loc[N_HEXES];
 __constant__ uint8_t c_hex_mirror[N_HEXES];
+// k / d for every byte k and the divisors the encoding uses, each the IEEE
+// quotient (computed on the host): a table read equals the division the CPU
+// encoder does, without the division's instruction sequence per feature
+constexpr int Q5 = 0, Q3 = 1, Q21 = 2, Q6 = 3;
+__constant__ float c_quot[4][256];
 
 constexpr int VIEWS_PER_CTA = 8;
 constexpr int ROW_STRIDE = (ROW_BYTES + 15) / 16 * 16;
+static_assert(HEX_CH == 16 && PILE_COUNTS == 4, "the index arithmetic below");
 
 __device__ __forceinline__ uint32_t flip_seat(uint32_t v) { return v == 0 ? 1u : (v == 1 ? 0u : v); }
 
 __global__ void __launch_bounds__(32 * VIEWS_PER_CTA)
     k_replay_expand(const uint8_t* __restrict__ rows, uint32_t nviews, const uint8_t* __restrict__ cc,
                     const int64_t* __restrict__ seg, uint64_t m, float* __restrict__ x) {
+    __shared__ float s_quot[4][256];
+    __shared__ float s_card[N_UNITS * CARD_FEATS];
+    __shared__ uint8_t s_loc[N_HEXES], s_mir[N_HEXES];
     __shared__ uint8_t s_row[VIEWS_PER_CTA][ROW_STRIDE];
     __shared__ uint32_t s_size[VIEWS_PER_CTA][6];  // hand[2], fd[2], bag[2] of the view's seats
-    const uint32_t w = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const uint32_t tid = threadIdx.x, w = tid / 32, lane = tid % 32;
+    for (uint32_t i = tid; i < 4 * 256; i += blockDim.x) s_quot[i / 256][i % 256] = c_quot[i / 256][i % 256];
+    for (uint32_t i = tid; i < N_UNITS * CARD_FEATS; i += blockDim.x) s_card[i] = c_card_feat[i];
+    if (tid < N_HEXES) {
+        s_loc[tid] = c_is_loc[tid];
+        s_mir[tid] = c_hex_mirror[tid];
+    }
+    __syncthreads();
     const uint32_t v = blockIdx.x * VIEWS_PER_CTA + w;
     if (v >= nviews) return;  // whole warps leave: no block-wide barrier follows
     const uint32_t r = v >> 1;
@@ -77,54 +94,70 @@ __global__ void __launch_bounds__(32 * VIEWS_PER_CTA)
     }
     __syncwarp();
     const uint8_t* R = s_row[w];
-    uint32_t on_board[2] = {0, 0};
-    for (int h = 0; h < N_HEXES; ++h) {
-        const uint32_t mk = mir ? flip_seat(R[ROW_HEX_MARKER + c_hex_mirror[h]]) : R[ROW_HEX_MARKER + h];
-        if (mk < 2) ++on_board[mk];
-    }
-    uint32_t init = mir ? flip_seat(R[ROW_INITIATIVE]) : R[ROW_INITIATIVE];
-    if (init > 1) init = 0;  // expand_row's guard (rebel.rs:1377)
-    const uint32_t to_act = mir ? flip_seat(R[ROW_TO_ACT]) : R[ROW_TO_ACT];
-    const uint32_t plies = R[ROW_PLIES] | ((uint32_t)R[ROW_PLIES + 1] << 8);
     float* out = x + (size_t)v * PUBFEAT;
-    for (int j = lane; j < PUBFEAT; j += 32) {
-        float val = 0.0f;
-        if (j < HEX_BLOCK) {
-            const int h = j / HEX_CH, ch = j % HEX_CH;
-            const int src = mir ? c_hex_mirror[h] : h;
-            const uint32_t owner = mir ? flip_seat(R[ROW_HEX_OWNER + src]) : R[ROW_HEX_OWNER + src];
-            const uint32_t marker = mir ? flip_seat(R[ROW_HEX_MARKER + src]) : R[ROW_HEX_MARKER + src];
-            const uint32_t slot = R[ROW_HEX_SLOT + src];
-            if (ch < 2) val = owner == (uint32_t)ch ? 1.0f : 0.0f;
-            else if (ch == 2) val = owner != NONE ? (float)R[ROW_HEX_HEIGHT + src] / 5.0f : 0.0f;
-            else if (ch < 5) val = marker == (uint32_t)(ch - 3) ? 1.0f : 0.0f;
-            else if (ch == 5) val = c_is_loc[h] ? 1.0f : 0.0f;
-            else val = (owner < 2 && slot < NSLOT && (uint32_t)(ch - HEX_FACTS) == owner * NSLOT + slot) ? 1.0f : 0.0f;
-        } else if (j < OFF_CARDS) {
-            const int q = j - OFF_PILES, t = q / PILE_COUNTS, k = q % PILE_COUNTS;
-            const int st = mir ? (t + NSLOT) % NTYPE : t;
-            val = (float)R[ROW_PILES + st * PILE_COUNTS + k] / 5.0f;
-        } else if (j < OFF_LOOSE) {
-            const int q = j - OFF_CARDS, t = q / CARD_FEATS, f = q % CARD_FEATS;
-            const int st = mir ? (t + NSLOT) % NTYPE : t;
-            const uint32_t id = R[ROW_IDS + st];
-            val = id < (uint32_t)N_UNITS ? c_card_feat[id * CARD_FEATS + f] : 0.0f;
-        } else if (j < OFF_LOOSE + 2 * PLAYER_SCALARS) {
-            const int q = j - OFF_LOOSE, p = q / PLAYER_SCALARS, f = q % PLAYER_SCALARS;
-            const uint32_t in_hand = (uint32_t)MARKERS_TOTAL - on_board[p];
-            if (f == 0) val = (float)in_hand / 6.0f;
-            else if (f == 1) val = (float)(MARKERS_TOTAL - in_hand) / 6.0f;
-            else if (f == 2) val = (float)s_size[w][p] / 3.0f;
-            else if (f == 3) val = (float)s_size[w][2 + p] / MAX_COINS;
-            else if (f == 4) val = (float)s_size[w][4 + p] / MAX_COINS;
-            else val = init == (uint32_t)p ? 1.0f : 0.0f;
-        } else {
-            const int g = j - OFF_LOOSE - 2 * PLAYER_SCALARS;
-            if (g == 0) val = (float)plies / (float)MAX_MAIN_PLAYS;
-            else if (g == 1) val = R[ROW_INIT_MOVED] != 0 ? 1.0f : 0.0f;
-            else val = to_act == 0 ? 1.0f : 0.0f;
+    // per hex: owner one-hot, height / 5, marker one-hot, location, the
+    // owner's slot one-hot (selects, no divergent branches)
+    for (int j = lane; j < HEX_BLOCK; j += 32) {
+        const int h = j >> 4, ch = j & 15;
+        const int src = mir ? s_mir[h] : h;
+        uint32_t owner = R[ROW_HEX_OWNER + src], marker = R[ROW_HEX_MARKER + src];
+        if (mir) {
+            owner = flip_seat(owner);
+            marker = flip_seat(marker);
         }
+        const uint32_t slot = R[ROW_HEX_SLOT + src];
+        const float hq = s_quot[Q5][R[ROW_HEX_HEIGHT + src]];
+        float val = 0.0f;
+        val = (ch < 2 && owner == (uint32_t)ch) ? 1.0f : val;
+        val = (ch == 2 && owner != NONE) ? hq : val;
+        val = (ch >= 3 && ch < 5 && marker == (uint32_t)(ch - 3)) ? 1.0f : val;
+        val = (ch == 5 && s_loc[h]) ? 1.0f : val;
+        val = (ch >= HEX_FACTS && owner < 2 && slot < NSLOT && (uint32_t)(ch - HEX_FACTS) == owner * NSLOT + slot)
+                  ? 1.0f : val;
         out[j] = val;
+    }
+    // the piles of each coin type / 5 (the mirror exchanges the seats' halves)
+    for (int q = lane; q < NTYPE * PILE_COUNTS; q += 32) {
+        const int t = q >> 2, st = mir ? (t + NSLOT) % NTYPE : t;
+        out[OFF_PILES + q] = s_quot[Q5][R[ROW_PILES + st * PILE_COUNTS + (q & 3)]];
+    }
+    // the printed card facts of each coin type's unit
+    for (int q = lane; q < NTYPE * CARD_FEATS; q += 32) {
+        const int t = q / CARD_FEATS, f = q - t * CARD_FEATS, st = mir ? (t + NSLOT) % NTYPE : t;
+        const uint32_t id = R[ROW_IDS + st];
+        out[OFF_CARDS + q] = id < (uint32_t)N_UNITS ? s_card[id * CARD_FEATS + f] : 0.0f;
+    }
+    // per seat: markers in hand and on the board / 6, hand / 3, face-down and
+    // bag / 21, initiative; then plies remaining / 256, initiative moved, to act
+    if (lane < LOOSE) {
+        uint32_t on_board = 0;
+        const uint32_t seat = lane < 2 * PLAYER_SCALARS ? lane / PLAYER_SCALARS : 0;
+        for (int h = 0; h < N_HEXES; ++h) {
+            const uint32_t mk = mir ? flip_seat(R[ROW_HEX_MARKER + s_mir[h]]) : R[ROW_HEX_MARKER + h];
+            on_board += mk == seat;
+        }
+        uint32_t init = mir ? flip_seat(R[ROW_INITIATIVE]) : R[ROW_INITIATIVE];
+        if (init > 1) init = 0;  // expand_row's guard (rebel.rs:1377)
+        const uint32_t to_act = mir ? flip_seat(R[ROW_TO_ACT]) : R[ROW_TO_ACT];
+        const uint32_t plies = R[ROW_PLIES] | ((uint32_t)R[ROW_PLIES + 1] << 8);
+        const uint32_t in_hand = ((uint32_t)MARKERS_TOTAL - on_board) & 0xffu;  // u8 arithmetic, as the encoder's
+        float val;
+        if (lane < 2 * PLAYER_SCALARS) {
+            const uint32_t f = lane % PLAYER_SCALARS;
+            val = f == 0   ? s_quot[Q6][in_hand]
+                  : f == 1 ? s_quot[Q6][((uint32_t)MARKERS_TOTAL - in_hand) & 0xffu]
+                  : f == 2 ? s_quot[Q3][s_size[w][seat]]
+                  : f == 3 ? s_quot[Q21][s_size[w][2 + seat]]
+                  : f == 4 ? s_quot[Q21][s_size[w][4 + seat]]
+                           : (init == seat ? 1.0f : 0.0f);
+        } else {
+            const uint32_t g = lane - 2 * PLAYER_SCALARS;
+            // MAX_MAIN_PLAYS is 2^8: the quotient is exact, a product by 2^-8
+            val = g == 0 ? (float)plies * (1.0f / (float)MAX_MAIN_PLAYS)
+                  : g == 1 ? (R[ROW_INIT_MOVED] != 0 ? 1.0f : 0.0f)
+                           : (to_act == 0 ? 1.0f : 0.0f);
+        }
+        out[OFF_LOOSE + lane] = val;
     }
 }
 
@@ -146,6 +179,10 @@ bool replay_tables_ready() {
     if (g_tables_ready.count(dev)) return true;
     float card[N_UNITS * CARD_FEATS];
     for (int u = 0; u < N_UNITS; ++u) write_card_features((uint8_t)u, card + u * CARD_FEATS);
+    float quot[4][256];
+    const float div[4] = {5.0f, 3.0f, MAX_COINS, 6.0f};
+    for (int d = 0; d < 4; ++d)
+        for (int k = 0; k < 256; ++k) quot[d][k] = (float)k / div[d];
     uint8_t loc[N_HEXES], mirror[N_HEXES];
     for (int h = 0; h < N_HEXES; ++h) {
         loc[h] = board().is_location[h] ? 1 : 0;
@@ -153,7 +190,8 @@ bool replay_tables_ready() {
     }
     if (cudaMemcpyToSymbol(c_card_feat, card, sizeof card) != cudaSuccess ||
         cudaMemcpyToSymbol(c_is_loc, loc, sizeof loc) != cudaSuccess ||
-        cudaMemcpyToSymbol(c_hex_mirror, mirror, sizeof mirror) != cudaSuccess)
+        cudaMemcpyToSymbol(c_hex_mirror, mirror, sizeof mirror) != cudaSuccess ||
+        cudaMemcpyToSymbol(c_quot, quot, sizeof quot) != cudaSuccess)
         return false;
     g_tables_ready.insert(dev);
     return true;

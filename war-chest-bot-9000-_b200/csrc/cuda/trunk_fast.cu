@@ -238,7 +238,7 @@ __global__ void __launch_bounds__(384, 1)
             St.occ[q] = -1;
             if (i >= nb) continue;
             const JobDev& J = jobs[row_job[gb_[i]]];
-            const uint8_t* rw = J.gpu_rows + (size_t)row_local[gb_[i]] * 201;
+            const uint8_t* rw = J.gpu_rows + (size_t)J.row_gpu[row_local[gb_[i]]] * 201;
             uint8_t owner = rw[h], slot = rw[37 + h], marker = rw[111 + h];
             if (owner != 255) {
                 f[owner] = 1.0f;
@@ -256,7 +256,7 @@ __global__ void __launch_bounds__(384, 1)
                 continue;
             }
             const JobDev& J = jobs[row_job[gb_[i]]];
-            const uint8_t* rw = J.gpu_rows + (size_t)row_local[gb_[i]] * 201;
+            const uint8_t* rw = J.gpu_rows + (size_t)J.row_gpu[row_local[gb_[i]]] * 201;
             if (k < NTYPE * PILE) {
                 St.piles[i][k] = (float)rw[148 + k] / 5.0f;
             } else {
@@ -591,7 +591,7 @@ __global__ void __launch_bounds__(384, 1)
             float v = 0.0f;
             if (i < nb) {
                 const JobDev& J = jobs[row_job[gb_[i]]];
-                const uint8_t* rw = J.gpu_rows + (size_t)row_local[gb_[i]] * 201;
+                const uint8_t* rw = J.gpu_rows + (size_t)J.row_gpu[row_local[gb_[i]]] * 201;
                 if (j < 12) {
                     int p = j / 6, f = j % 6;
                     uint8_t mh = rw[188 + p];

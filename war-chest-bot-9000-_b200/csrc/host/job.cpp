@@ -14,7 +14,7 @@ size_t JobImage::table_bytes() const {
               vge_w.size() + rg_start.size() + rge_src.size() + rge_w.size() + drawp.size() + lr_ridx.size() +
               lr_nc.size() + lr_vidx.size() + leaf_coff.size() + leaf_cidx.size() + tl_ridx.size() +
               tl_nc.size() + tl_vidx.size() + tl_util0.size() + cphi.size() + card_feat.size() + cfg_col.size() +
-              leaf_col.size() + root_belief.size() + carried.size() + row_rep.size());
+              root_belief.size() + carried.size() + row_rep.size() + row_gpu.size());
     b += row_player.size() + gpu_rows.size() + cplayer.size();
     return b;
 }
@@ -230,31 +230,37 @@ std::unique_ptr<JobImage> flatten(const Tree& t, const std::vector<float>& carri
     }
     J.leaf_coff = t.leaf_coff;
     J.leaf_cidx = t.leaf_cidx;
-    J.gpu_rows = t.gpu_rows;
     // Network rows whose public rows are byte-identical (the same public
     // position reached along different public paths) get the same board
     // pieces P and jp: the board trunk reads nothing else of a row. Each
-    // row names the first row with its bytes; FNV-1a buckets, confirmed by
-    // comparing the bytes (a bucket shared by different rows keeps the
-    // later ones as their own representatives).
+    // row names the first row with its bytes (FNV-1a buckets, confirmed by
+    // comparing the bytes; a bucket shared by different rows keeps the later
+    // ones as their own representatives), and the job keeps each distinct
+    // row's bytes once (row_gpu: the row's index among them).
     J.row_rep.resize(J.nrows_net);
+    J.row_gpu.resize(J.nrows_net);
     {
         std::unordered_map<uint64_t, uint32_t> first;
         first.reserve(2 * J.nrows_net);
         for (uint32_t r = 0; r < J.nrows_net; ++r) {
-            const uint8_t* row = J.gpu_rows.data() + (size_t)r * GPU_ROW_BYTES;
+            const uint8_t* row = t.gpu_rows.data() + (size_t)r * GPU_ROW_BYTES;
             uint64_t h = 1469598103934665603ull;
             for (size_t k = 0; k < GPU_ROW_BYTES; ++k) h = (h ^ row[k]) * 1099511628211ull;
             auto ins = first.emplace(h, r);
             const uint32_t q = ins.first->second;
-            J.row_rep[r] = (!ins.second && std::memcmp(J.gpu_rows.data() + (size_t)q * GPU_ROW_BYTES, row, GPU_ROW_BYTES) == 0) ? q : r;
+            const bool same = !ins.second && std::memcmp(t.gpu_rows.data() + (size_t)q * GPU_ROW_BYTES, row, GPU_ROW_BYTES) == 0;
+            J.row_rep[r] = same ? q : r;
+            if (same) {
+                J.row_gpu[r] = J.row_gpu[q];
+            } else {
+                J.row_gpu[r] = (uint32_t)(J.gpu_rows.size() / GPU_ROW_BYTES);
+                J.gpu_rows.insert(J.gpu_rows.end(), row, row + GPU_ROW_BYTES);
+            }
         }
     }
     J.cphi = t.cphi;
     J.cplayer = t.cplayer;
     for (uint8_t q : J.cplayer) J.cfg_col.push_back(J.ncfg_player[q]++);
-    J.leaf_col.reserve(J.leaf_cidx.size());
-    for (uint32_t c : J.leaf_cidx) J.leaf_col.push_back(J.cfg_col[c]);
     J.nterm = (uint32_t)t.term_leaves.size();
     for (uint32_t i : t.term_leaves) {
         for (int q = 0; q < 2; ++q) {

@@ -57,12 +57,12 @@ struct JobImage {
     std::vector<uint32_t> leaf_coff, leaf_cidx;
     std::vector<uint32_t> tl_ridx, tl_nc, tl_vidx;  // [2 * nterm]
     std::vector<float> tl_util0;                    // utility for player 0
-    std::vector<uint8_t> gpu_rows;                  // nrows_net * GPU_ROW_BYTES
+    std::vector<uint8_t> gpu_rows;                  // the distinct public rows, GPU_ROW_BYTES each
     std::vector<uint32_t> row_rep;                  // per network row: the first row with the same public row bytes
+    std::vector<uint32_t> row_gpu;                  // per network row: its public row's index in gpu_rows
     std::vector<float> cphi;                        // ncfg * CFEAT
     std::vector<uint8_t> cplayer;
     std::vector<uint32_t> cfg_col;                  // index of each config among its player's configs
-    std::vector<uint32_t> leaf_col;                 // cfg_col of every leaf_cidx entry (readout column)
     uint32_t ncfg_player[2] = {0, 0};
     std::vector<float> card_feat;                   // 2 views * NTYPE * CARD_FEATS
     // root beliefs and the carried roots Phase 2 values

@@ -51,7 +51,7 @@ std::unique_ptr<JobBlob> make_blob(std::unique_ptr<JobImage> img) {
         v(J.rge_src), v(J.rge_w), v(J.drawp), v(J.cell_ref), v(J.lr_ridx), v(J.lr_nc), v(J.lr_vidx),
         v(J.leaf_coff), v(J.leaf_cidx), v(J.tl_ridx), v(J.tl_nc), v(J.tl_vidx), v(J.tl_util0), v(J.gpu_rows),
         v(J.cphi), v(J.cplayer), v(J.card_feat), v(J.root_belief), v(J.carried), v(carry_off), v(J.cfg_col),
-        v(J.leaf_col), v(J.row_rep)};
+        v(J.row_rep), v(J.row_gpu)};
     size_t at = 0;
     for (int i = 0; i < JobBlob::N_ARR; ++i) {
         b->off[i] = at;
@@ -82,7 +82,7 @@ std::unique_ptr<JobBlob> make_blob(std::unique_ptr<JobImage> img) {
     drop(J.rg_start), drop(J.rge_src), drop(J.rge_w), drop(J.drawp), drop(J.cell_ref), drop(J.lr_ridx);
     drop(J.lr_nc), drop(J.lr_vidx), drop(J.leaf_coff), drop(J.leaf_cidx), drop(J.tl_ridx), drop(J.tl_nc);
     drop(J.tl_vidx), drop(J.tl_util0), drop(J.gpu_rows), drop(J.cphi), drop(J.cplayer), drop(J.card_feat);
-    drop(J.root_belief), drop(J.carried), drop(J.cfg_col), drop(J.leaf_col), drop(J.row_rep);
+    drop(J.root_belief), drop(J.carried), drop(J.cfg_col), drop(J.row_rep), drop(J.row_gpu);
     b->img = std::move(img);
     return b;
 }
@@ -275,8 +275,8 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
     // ---- device memory plan: per job, table blob then state then outputs
     Alloc A;
     struct Plan {
-        size_t tables, cur, regret, sum, snap, reach, reach2, vals0, vals1, cards, cardm, tokproj, pb, jp, cf, cg, pooled,
-            out_strategy, out_roots, out_carry, out_conv;
+        size_t tables, lcol, cur, regret, sum, snap, reach, reach2, vals0, vals1, cards, cardm, tokproj, pb, jp, cf, cg,
+            pooled, out_strategy, out_roots, out_carry, out_conv;
     };
     std::vector<Plan> plan(nj);
     for (size_t j = 0; j < nj; ++j) {
@@ -284,6 +284,7 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
         const JobImage& J = *jb.img;
         Plan& P = plan[j];
         P.tables = A.take(jb.bytes);
+        P.lcol = A.take(4ull * jb.arr<uint32_t>(JobBlob::LEAF_COFF)[2 * J.nrows_net]);
         P.cur = A.take(4ull * J.ncells);
         P.regret = A.take(4ull * J.ncells);
         P.sum = A.take(4ull * J.ncells);
@@ -459,6 +460,7 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
         d.tl_vidx = t32(JobBlob::TL_VIDX);
         d.tl_util0 = tf(JobBlob::TL_UTIL0);
         d.gpu_rows = t8(JobBlob::GPU_ROWS);
+        d.row_gpu = t32(JobBlob::ROW_GPU);
         d.cphi = tf(JobBlob::CPHI);
         d.cplayer = t8(JobBlob::CPLAYER);
         d.card_feat = tf(JobBlob::CARD_FEAT);
@@ -466,7 +468,7 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
         d.carried = tf(JobBlob::CARRIED);
         d.carry_off = t32(JobBlob::CARRY_OFF);
         d.cfg_col = t32(JobBlob::CFG_COL);
-        d.leaf_col = t32(JobBlob::LEAF_COL);
+        d.leaf_col = reinterpret_cast<uint32_t*>(D + P.lcol);
         d.ncfg_player[0] = J.ncfg_player[0];
         d.ncfg_player[1] = J.ncfg_player[1];
         d.row_base = row_base[j];
@@ -544,6 +546,9 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
     }
     if (!dup.empty())
         check(cudaMemcpyAsync(b.d_dup, dup.data(), 4 * dup.size(), cudaMemcpyHostToDevice, s), "upload duplicate rows");
+    // the readout column of every leaf-config entry, from the uploaded tables
+    wcdev::launch_leaf_col(b.d_jobs, (uint32_t)nj, s);
+    check(cudaGetLastError(), "leaf columns");
     if (!cfg_job.empty()) {
         check(cudaMemcpyAsync(b.d_cfg_job, cfg_job.data(), 4 * cfg_job.size(), cudaMemcpyHostToDevice, s), "upload cfgs");
         check(cudaMemcpyAsync(b.d_cfg_local, cfg_local.data(), 4 * cfg_local.size(), cudaMemcpyHostToDevice, s), "upload cfgs");
@@ -569,7 +574,8 @@ std::unique_ptr<Batch> upload_batch(DeviceCtx& dev, const std::vector<const JobB
 size_t job_device_bytes(const DeviceCtx& dev, const JobBlob& jb) {
     const JobImage& J = *jb.img;
     auto r = [](size_t x) { return (x + 255) & ~(size_t)255; };
-    size_t b = r(jb.bytes) + 4 * r(4ull * J.ncells) + r(4ull * J.reach_len) * (J.cfg.snapshots ? 2 : 1) +
+    size_t b = r(jb.bytes) + r(4ull * jb.arr<uint32_t>(JobBlob::LEAF_COFF)[2 * J.nrows_net]) + 4 * r(4ull * J.ncells) +
+               r(4ull * J.reach_len) * (J.cfg.snapshots ? 2 : 1) +
                r(4ull * J.val_len[0]) + r(4ull * J.val_len[1]) + r(4ull * J.ncells) +
                r(4ull * J.ncarried * (J.root_nc[0] + J.root_nc[1])) + r(8ull * (J.root_nc[0] + J.root_nc[1]));
     if (J.cfg.snapshots) b += r(2ull * (jb.nsnaps_kept - 1) * jb.carry_width);

@@ -55,7 +55,7 @@ struct JobBlob {
     enum Arr {
         CELL_VIDX, ROW_OFF, ROW_PLAYER, VG_START, VGE_IDX, VGE_W, RG_START, RGE_SRC, RGE_W, DRAWP, CELL_REF,
         LR_RIDX, LR_NC, LR_VIDX, LEAF_COFF, LEAF_CIDX, TL_RIDX, TL_NC, TL_VIDX, TL_UTIL0, GPU_ROWS, CPHI,
-        CPLAYER, CARD_FEAT, ROOT_BELIEF, CARRIED, CARRY_OFF, CFG_COL, LEAF_COL, ROW_REP, N_ARR
+        CPLAYER, CARD_FEAT, ROOT_BELIEF, CARRIED, CARRY_OFF, CFG_COL, ROW_REP, ROW_GPU, N_ARR
     };
     size_t off[N_ARR] = {};
     // A packed array. The blob is the only copy: make_blob releases the
