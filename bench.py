@@ -56,10 +56,12 @@ def parse():
                          "readout f16), f16 operands throughout, fp32 exact, or none")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg (profiling runs)")
     ap.add_argument("--build-threads", type=int, default=0)
-    ap.add_argument("--workload", default="solve", choices=["solve", "leaf", "batch"],
+    ap.add_argument("--games", type=int, default=64, help="--workload resolve: games (belief-heavy roots)")
+    ap.add_argument("--workload", default="solve", choices=["solve", "leaf", "batch", "resolve"],
                     help="solve: the configs[2] batched solve (the bench line); leaf: configs[1], value-net leaf "
                          "inference alone at 1K / 16K / 256K rows; batch: the training-batch expansion of replay "
-                         "rows at 1K / 256K rows (one JSON line per batch size, not bench lines)")
+                         "rows at 1K / 256K rows (one JSON line per batch size, not bench lines); resolve: "
+                         "configs[4]'s continual re-solving loop (8 solves per game) at --depth / --iters")
     return ap.parse_args()
 
 
@@ -436,6 +438,9 @@ def main():
     if args.workload == "batch":
         batch_workload(args)
         return
+    if args.workload == "resolve":
+        resolve_workload(args)
+        return
     if args.subgames_total:
         total_workload(args)
         return
@@ -565,6 +570,64 @@ def main():
 
         barrier(world)  # the other ranks wait here while rank 0 timed the CPU baseline
         dist.destroy_process_group()
+
+
+def resolve_workload(args):
+    """BASELINE configs[4]'s loop: --games games from belief-heavy roots
+    (each player's belief over up to 256 consistent configs, Dirichlet(1)
+    weights), each solving a subgame, walking it with the real play and
+    re-solving with the carried beliefs, 8 solves per game, CFR+ at --iters
+    (configs[4]: 1024) and --depth (configs[4]: 4). Rounds run in lockstep as
+    GpuClient.play does: every live game advances to its next solve on host
+    threads (tree build and flattening), the round's subgames are solved in
+    one wc_solve_batch (memory-bounded waves), and each game resumes its walk.
+    Host and GPU time per round are reported apart; node-updates/s is over
+    the solve calls' wall clock."""
+    import ctypes as Cc
+    from concurrent.futures import ThreadPoolExecutor
+
+    import warchest_b200 as wc
+
+    wc.set_cap_marker_value(0.0)
+    cfg = wc.Cfg(depth=args.depth, iters=args.iters, snapshots=True, cfr=cfr_plus(wc), node_cap=200000)
+    weights = wc.seeded_weights("he", 0)
+    client = wc.spawn(0, *weights, net=args.net)
+    games = [wc.Game(cfg, seed=s, root=wc.generate_wide_root(s, 256), max_solves=8) for s in range(args.games)]
+    threads = args.build_threads or (os.cpu_count() or 1)
+    pool = ThreadPoolExecutor(threads)
+    live, rounds, solved, nodes, host_s, gpu_s = list(games), 0, 0, 0.0, 0.0, 0.0
+    while live:
+        t0 = time.perf_counter()
+        jobs = list(pool.map(lambda g: g.advance(), live))
+        host_s += time.perf_counter() - t0
+        pend = [(g, j) for g, j in zip(live, jobs) if j is not None]
+        if not pend:
+            break
+        n = len(pend)
+        arr = (Cc.c_void_p * n)(*[j._h.value for _, j in pend])
+        res = (wc._Result * n)()
+        t0 = time.perf_counter()
+        wc._check(wc.lib().wc_solve_batch(client._ctx, arr, n, res))
+        gpu_s += time.perf_counter() - t0
+        t0 = time.perf_counter()
+        for i, (g, j) in enumerate(pend):
+            wc._check(wc.lib().wc_game_resume(g._h, j._h, Cc.byref(res[i])))
+            wc.lib().wc_result_free(Cc.byref(res[i]))
+        host_s += time.perf_counter() - t0
+        nodes += sum(j.info["nodes"] for _, j in pend) * float(args.iters)
+        solved += n
+        rounds += 1
+        live = [g for g, _ in pend]
+    counters = [g.counters() for g in games]
+    line = {"workload": f"configs[4] loop: {args.games} belief-heavy games (256 configs per player), depth "
+                        f"{args.depth}, {args.iters} CFR+ iters, 8 solves per game, one GPU",
+            "games": args.games, "rounds": rounds, "solves": solved,
+            "walk_decisions": sum(c["walk_decisions"] for c in counters),
+            "capped": sum(c["capped"] for c in counters),
+            "gpu_s": gpu_s, "host_s": host_s, "solves_per_s": solved / (gpu_s + host_s),
+            "node_updates_per_s_gpu": nodes / gpu_s if gpu_s else None, "host_threads": threads}
+    print(json.dumps(line), flush=True)
+    client.close()
 
 
 def total_workload(args):

@@ -307,9 +307,11 @@ __global__ void __launch_bounds__(128, 3)
                 if (L == 3 && t + gridDim.x < ntiles) load_pooled(t + gridDim.x);
             }
             // epilogue: the row's statistics over two 64-column halves, then
-            // LayerNorm and GELU over the halves read again
-            const float* cb = vec[L];  // running bias sum (unused at L = 0)
-            float s4[4] = {0.0f, 0.0f, 0.0f, 0.0f}, q4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            // LayerNorm and GELU over the halves read again; the fp32 steps
+            // run on column pairs (add / fma .f32x2), partial sums kept by
+            // column mod 4 as four scalar chains would be
+            const unsigned long long* cb2 = reinterpret_cast<const unsigned long long*>(vec[L]);  // bias sum pairs
+            unsigned long long s2[2] = {0ull, 0ull}, q2[2] = {0ull, 0ull};
 #pragma unroll
             for (int hf = 0; hf < 2; ++hf) {
                 uint32_t zr[64];
@@ -319,16 +321,19 @@ __global__ void __launch_bounds__(128, 3)
 #pragma unroll
                 for (int c = 0; c < 64; ++c) asm volatile("" : "+r"(zr[c]));  // the values exist after the wait
 #pragma unroll
-                for (int c = 0; c < 64; ++c) {
-                    const float x = L ? __uint_as_float(zr[c]) + cb[64 * hf + c] : __uint_as_float(zr[c]);
-                    s4[c & 3] += x;
-                    q4[c & 3] += x * x;
+                for (int c = 0; c < 64; c += 2) {
+                    unsigned long long x = umma::f2(zr[c], zr[c + 1]);
+                    if (L) x = umma::f2_add(x, cb2[(64 * hf + c) / 2]);
+                    s2[(c >> 1) & 1] = umma::f2_add(s2[(c >> 1) & 1], x);
+                    q2[(c >> 1) & 1] = umma::f2_fma(x, x, q2[(c >> 1) & 1]);
                 }
             }
-            const float s = (s4[0] + s4[1]) + (s4[2] + s4[3]), sq = (q4[0] + q4[1]) + (q4[2] + q4[3]);
+            const float s = (umma::f2_lo(s2[0]) + umma::f2_hi(s2[0])) + (umma::f2_lo(s2[1]) + umma::f2_hi(s2[1]));
+            const float sq = (umma::f2_lo(q2[0]) + umma::f2_hi(q2[0])) + (umma::f2_lo(q2[1]) + umma::f2_hi(q2[1]));
             const float mean = s * (1.0f / JW);
             const float inv = rsqrtf(fmaxf(sq * (1.0f / JW) - mean * mean, 0.0f) + 1e-5f);
             const float nm = -mean * inv;
+            const unsigned long long inv2 = umma::f2(inv, inv), nm2 = umma::f2(nm, nm);
 #pragma unroll
             for (int hf = 0; hf < 2; ++hf) {
                 uint32_t zr[64];
@@ -343,9 +348,10 @@ __global__ void __launch_bounds__(128, 3)
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
                         const int c = 8 * c8 + 2 * j, cc = 64 * hf + c;
-                        const float x0 = L ? __uint_as_float(zr[c]) + cb[cc] : __uint_as_float(zr[c]);
-                        const float x1 = L ? __uint_as_float(zr[c + 1]) + cb[cc + 1] : __uint_as_float(zr[c + 1]);
-                        w4[j] = umma::ln_gelu2<H>(x0 * inv + nm, x1 * inv + nm, cc, gb2[L]);
+                        unsigned long long x = umma::f2(zr[c], zr[c + 1]);
+                        if (L) x = umma::f2_add(x, cb2[cc / 2]);
+                        const unsigned long long n = umma::f2_fma(x, inv2, nm2);
+                        w4[j] = umma::ln_gelu2<H>(umma::f2_lo(n), umma::f2_hi(n), cc, gb2[L]);
                     }
                     const uint4 o = make_uint4(w4[0], w4[1], w4[2], w4[3]);
                     const uint32_t off = umma::sw128_offset(128, tid, 64 * hf + 8 * c8);
@@ -805,12 +811,14 @@ __global__ void __launch_bounds__(544, 1)
             ph_p ^= 1u;
             umma::fence_after_sync();
             // y = Y + P, in two 32-column halves: each half's mean and sum
-            // of squared deviations, and y written back over Y
+            // of squared deviations, and y written back over Y (the fp32
+            // steps on column pairs, add / fma .f32x2)
             float m2h[2], mh[2];
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 float v[32];
                 umma::tmem_ld32(tmem + lane_off + TY + 64 * cg + 32 * h, v);
+                unsigned long long s2[2] = {0ull, 0ull};
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     const uint32_t k = (uint32_t)(8 * cg + 4 * h + c);
@@ -818,19 +826,24 @@ __global__ void __launch_bounds__(544, 1)
                     const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
-                        v[8 * c + 2 * i] += umma::Op16<true>::lo(w4[i]);
-                        v[8 * c + 2 * i + 1] += umma::Op16<true>::hi(w4[i]);
+                        const unsigned long long y = umma::f2_add(umma::f2(v[8 * c + 2 * i], v[8 * c + 2 * i + 1]),
+                                                                  umma::f2(umma::Op16<true>::lo(w4[i]), umma::Op16<true>::hi(w4[i])));
+                        v[8 * c + 2 * i] = umma::f2_lo(y);
+                        v[8 * c + 2 * i + 1] = umma::f2_hi(y);
+                        s2[i & 1] = umma::f2_add(s2[i & 1], y);
                     }
                 }
-                float s = 0.0f;
-#pragma unroll
-                for (int j = 0; j < 32; ++j) s += v[j];
+                const float s = (umma::f2_lo(s2[0]) + umma::f2_hi(s2[0])) + (umma::f2_lo(s2[1]) + umma::f2_hi(s2[1]));
                 const float m = s * (1.0f / 32);
-                float q2 = 0.0f;
+                const unsigned long long nm2 = umma::f2(-m, -m);
+                unsigned long long d2[2] = {0ull, 0ull};
 #pragma unroll
-                for (int j = 0; j < 32; ++j) q2 += (v[j] - m) * (v[j] - m);
+                for (int j = 0; j < 32; j += 2) {
+                    const unsigned long long d = umma::f2_add(umma::f2(v[j], v[j + 1]), nm2);
+                    d2[(j >> 1) & 1] = umma::f2_fma(d, d, d2[(j >> 1) & 1]);
+                }
                 mh[h] = m;
-                m2h[h] = q2;
+                m2h[h] = (umma::f2_lo(d2[0]) + umma::f2_hi(d2[0])) + (umma::f2_lo(d2[1]) + umma::f2_hi(d2[1]));
                 umma::tmem_st32(tmem + lane_off + TY + 64 * cg + 32 * h, v);
             }
             // the row's four column groups meet through V's first columns
@@ -872,10 +885,12 @@ __global__ void __launch_bounds__(544, 1)
                     // the affine in f16x2 on the normalised pair (the result
                     // is an f16 operand either way)
                     const float nm = -mean * inv;
+                    const unsigned long long inv2 = umma::f2(inv, inv), nmp = umma::f2(nm, nm);
 #pragma unroll
                     for (int c = 0; c < 16; ++c) {
                         const uint2 gb = *reinterpret_cast<const uint2*>(&gb2[64 * cg + 32 * h + 2 * c]);
-                        const __half2 n = __floats2half2_rn(fmaf(v[2 * c], inv, nm), fmaf(v[2 * c + 1], inv, nm));
+                        const unsigned long long y = umma::f2_fma(umma::f2(v[2 * c], v[2 * c + 1]), inv2, nmp);
+                        const __half2 n = __floats2half2_rn(umma::f2_lo(y), umma::f2_hi(y));
                         const __half2 x = __hfma2(n, *reinterpret_cast<const __half2*>(&gb.x),
                                                   *reinterpret_cast<const __half2*>(&gb.y));
                         hw[c] = *reinterpret_cast<const uint32_t*>(&x);

@@ -47,6 +47,29 @@ static_assert(HEX_CH == 16 && PILE_COUNTS == 4, "the index arithmetic below");
 
 __device__ __forceinline__ uint32_t flip_seat(uint32_t v) { return v == 0 ? 1u : (v == 1 ? 0u : v); }
 
+// np.searchsorted(seg, key, 'left') by the whole warp: each round probes 32
+// points that split the remaining range into 33 parts and keeps the part the
+// ballot names (seg is sorted, so the probes below `key` are a prefix), about
+// four dependent loads for a million configs; the last <= 32 candidates are
+// counted directly.
+__device__ __forceinline__ uint64_t span_start(const int64_t* __restrict__ seg, uint64_t m, int64_t key,
+                                              uint32_t lane) {
+    uint64_t lo = 0, hi = m;  // the answer lies in [lo, hi]
+    while (hi - lo > 32) {
+        const uint64_t len = hi - lo;
+        const bool less = seg[lo + len * (lane + 1) / 33] < key;
+        const uint32_t cnt = __popc(__ballot_sync(0xffffffffu, less));
+        const uint64_t nlo = cnt ? lo + len * cnt / 33 + 1 : lo;
+        const uint64_t nhi = cnt < 32 ? lo + len * (cnt + 1) / 33 : hi;
+        lo = nlo;
+        hi = nhi;
+    }
+    const bool less = lo + lane < hi && seg[lo + lane] < key;
+    return lo + __popc(__ballot_sync(0xffffffffu, less));
+}
+
+// A grid of persistent CTAs: the tables are staged once per CTA, and each
+// warp expands views v, v + 8 G, ... (G CTAs).
 __global__ void __launch_bounds__(32 * VIEWS_PER_CTA)
     k_replay_expand(const uint8_t* __restrict__ rows, uint32_t nviews, const uint8_t* __restrict__ cc,
                     const int64_t* __restrict__ seg, uint64_t m, float* __restrict__ x) {
@@ -63,101 +86,94 @@ __global__ void __launch_bounds__(32 * VIEWS_PER_CTA)
         s_mir[tid] = c_hex_mirror[tid];
     }
     __syncthreads();
-    const uint32_t v = blockIdx.x * VIEWS_PER_CTA + w;
-    if (v >= nviews) return;  // whole warps leave: no block-wide barrier follows
-    const uint32_t r = v >> 1;
-    const bool mir = v & 1u;
-    const uint8_t* row = rows + (size_t)r * ROW_BYTES;
-    for (uint32_t k = lane; k < ROW_BYTES; k += 32) s_row[w][k] = row[k];
-    if (lane < 2) {
-        // public_sizes: the first config whose span id is >= 2 r + seat
-        // (np.searchsorted 'left'); the mirrored view reads the other seat
-        const int64_t key = 2 * (int64_t)r + (mir ? 1 - (int)lane : (int)lane);
-        uint64_t lo = 0, hi = m;
-        while (lo < hi) {
-            const uint64_t mid = (lo + hi) / 2;
-            if (seg[mid] < key) lo = mid + 1;
-            else hi = mid;
-        }
-        uint32_t hand = 0, fd = 0, bag = 0;
-        if (lo < m) {
-            const uint8_t* c = cc + lo * CCOUNTS;
-            for (int k = 0; k < NSLOT; ++k) {
-                hand += c[k];
-                fd += c[NSLOT + k];
-                bag += c[2 * NSLOT + k];
+    for (uint32_t v = blockIdx.x * VIEWS_PER_CTA + w; v < nviews; v += gridDim.x * VIEWS_PER_CTA) {
+        __syncwarp();  // the previous view's reads of s_row and s_size are done
+        const uint32_t r = v >> 1;
+        const bool mir = v & 1u;
+        const uint8_t* row = rows + (size_t)r * ROW_BYTES;
+        for (uint32_t k = lane; k < ROW_BYTES; k += 32) s_row[w][k] = row[k];
+        {
+            // public_sizes: each seat's first config (the mirrored view reads
+            // the other seat's span); lane 2 z + q sums zone z of seat q
+            uint64_t st[2];
+#pragma unroll
+            for (int q = 0; q < 2; ++q) st[q] = span_start(seg, m, 2 * (int64_t)r + (mir ? 1 - q : q), lane);
+            if (lane < 6) {
+                const uint32_t q = lane & 1u, z = lane >> 1;
+                const uint64_t at = q ? st[1] : st[0];
+                uint32_t sum = 0;
+                if (at < m)
+                    for (int k = 0; k < NSLOT; ++k) sum += cc[at * CCOUNTS + z * NSLOT + k];
+                s_size[w][2 * z + q] = sum & 0xffu;  // the sums are cast to u8 (.astype(np.uint8))
             }
         }
-        s_size[w][lane] = hand & 0xffu;  // the sums are cast to u8 (.astype(np.uint8))
-        s_size[w][2 + lane] = fd & 0xffu;
-        s_size[w][4 + lane] = bag & 0xffu;
-    }
-    __syncwarp();
-    const uint8_t* R = s_row[w];
-    float* out = x + (size_t)v * PUBFEAT;
-    // per hex: owner one-hot, height / 5, marker one-hot, location, the
-    // owner's slot one-hot (selects, no divergent branches)
-    for (int j = lane; j < HEX_BLOCK; j += 32) {
-        const int h = j >> 4, ch = j & 15;
-        const int src = mir ? s_mir[h] : h;
-        uint32_t owner = R[ROW_HEX_OWNER + src], marker = R[ROW_HEX_MARKER + src];
-        if (mir) {
-            owner = flip_seat(owner);
-            marker = flip_seat(marker);
+        __syncwarp();
+        const uint8_t* R = s_row[w];
+        float* out = x + (size_t)v * PUBFEAT;
+        // per hex: owner one-hot, height / 5, marker one-hot, location, the
+        // owner's slot one-hot (selects, no divergent branches)
+        for (int j = lane; j < HEX_BLOCK; j += 32) {
+            const int h = j >> 4, ch = j & 15;
+            const int src = mir ? s_mir[h] : h;
+            uint32_t owner = R[ROW_HEX_OWNER + src], marker = R[ROW_HEX_MARKER + src];
+            if (mir) {
+                owner = flip_seat(owner);
+                marker = flip_seat(marker);
+            }
+            const uint32_t slot = R[ROW_HEX_SLOT + src];
+            const float hq = s_quot[Q5][R[ROW_HEX_HEIGHT + src]];
+            float val = 0.0f;
+            val = (ch < 2 && owner == (uint32_t)ch) ? 1.0f : val;
+            val = (ch == 2 && owner != NONE) ? hq : val;
+            val = (ch >= 3 && ch < 5 && marker == (uint32_t)(ch - 3)) ? 1.0f : val;
+            val = (ch == 5 && s_loc[h]) ? 1.0f : val;
+            val = (ch >= HEX_FACTS && owner < 2 && slot < NSLOT && (uint32_t)(ch - HEX_FACTS) == owner * NSLOT + slot)
+                      ? 1.0f : val;
+            out[j] = val;
         }
-        const uint32_t slot = R[ROW_HEX_SLOT + src];
-        const float hq = s_quot[Q5][R[ROW_HEX_HEIGHT + src]];
-        float val = 0.0f;
-        val = (ch < 2 && owner == (uint32_t)ch) ? 1.0f : val;
-        val = (ch == 2 && owner != NONE) ? hq : val;
-        val = (ch >= 3 && ch < 5 && marker == (uint32_t)(ch - 3)) ? 1.0f : val;
-        val = (ch == 5 && s_loc[h]) ? 1.0f : val;
-        val = (ch >= HEX_FACTS && owner < 2 && slot < NSLOT && (uint32_t)(ch - HEX_FACTS) == owner * NSLOT + slot)
-                  ? 1.0f : val;
-        out[j] = val;
-    }
-    // the piles of each coin type / 5 (the mirror exchanges the seats' halves)
-    for (int q = lane; q < NTYPE * PILE_COUNTS; q += 32) {
-        const int t = q >> 2, st = mir ? (t + NSLOT) % NTYPE : t;
-        out[OFF_PILES + q] = s_quot[Q5][R[ROW_PILES + st * PILE_COUNTS + (q & 3)]];
-    }
-    // the printed card facts of each coin type's unit
-    for (int q = lane; q < NTYPE * CARD_FEATS; q += 32) {
-        const int t = q / CARD_FEATS, f = q - t * CARD_FEATS, st = mir ? (t + NSLOT) % NTYPE : t;
-        const uint32_t id = R[ROW_IDS + st];
-        out[OFF_CARDS + q] = id < (uint32_t)N_UNITS ? s_card[id * CARD_FEATS + f] : 0.0f;
-    }
-    // per seat: markers in hand and on the board / 6, hand / 3, face-down and
-    // bag / 21, initiative; then plies remaining / 256, initiative moved, to act
-    if (lane < LOOSE) {
-        uint32_t on_board = 0;
-        const uint32_t seat = lane < 2 * PLAYER_SCALARS ? lane / PLAYER_SCALARS : 0;
-        for (int h = 0; h < N_HEXES; ++h) {
-            const uint32_t mk = mir ? flip_seat(R[ROW_HEX_MARKER + s_mir[h]]) : R[ROW_HEX_MARKER + h];
-            on_board += mk == seat;
+        // the piles of each coin type / 5 (the mirror exchanges the seats' halves)
+        for (int q = lane; q < NTYPE * PILE_COUNTS; q += 32) {
+            const int t = q >> 2, st = mir ? (t + NSLOT) % NTYPE : t;
+            out[OFF_PILES + q] = s_quot[Q5][R[ROW_PILES + st * PILE_COUNTS + (q & 3)]];
         }
-        uint32_t init = mir ? flip_seat(R[ROW_INITIATIVE]) : R[ROW_INITIATIVE];
-        if (init > 1) init = 0;  // expand_row's guard (rebel.rs:1377)
-        const uint32_t to_act = mir ? flip_seat(R[ROW_TO_ACT]) : R[ROW_TO_ACT];
-        const uint32_t plies = R[ROW_PLIES] | ((uint32_t)R[ROW_PLIES + 1] << 8);
-        const uint32_t in_hand = ((uint32_t)MARKERS_TOTAL - on_board) & 0xffu;  // u8 arithmetic, as the encoder's
-        float val;
-        if (lane < 2 * PLAYER_SCALARS) {
-            const uint32_t f = lane % PLAYER_SCALARS;
-            val = f == 0   ? s_quot[Q6][in_hand]
-                  : f == 1 ? s_quot[Q6][((uint32_t)MARKERS_TOTAL - in_hand) & 0xffu]
-                  : f == 2 ? s_quot[Q3][s_size[w][seat]]
-                  : f == 3 ? s_quot[Q21][s_size[w][2 + seat]]
-                  : f == 4 ? s_quot[Q21][s_size[w][4 + seat]]
-                           : (init == seat ? 1.0f : 0.0f);
-        } else {
-            const uint32_t g = lane - 2 * PLAYER_SCALARS;
-            // MAX_MAIN_PLAYS is 2^8: the quotient is exact, a product by 2^-8
-            val = g == 0 ? (float)plies * (1.0f / (float)MAX_MAIN_PLAYS)
-                  : g == 1 ? (R[ROW_INIT_MOVED] != 0 ? 1.0f : 0.0f)
-                           : (to_act == 0 ? 1.0f : 0.0f);
+        // the printed card facts of each coin type's unit
+        for (int q = lane; q < NTYPE * CARD_FEATS; q += 32) {
+            const int t = q / CARD_FEATS, f = q - t * CARD_FEATS, st = mir ? (t + NSLOT) % NTYPE : t;
+            const uint32_t id = R[ROW_IDS + st];
+            out[OFF_CARDS + q] = id < (uint32_t)N_UNITS ? s_card[id * CARD_FEATS + f] : 0.0f;
         }
-        out[OFF_LOOSE + lane] = val;
+        // per seat: markers in hand and on the board / 6, hand / 3, face-down and
+        // bag / 21, initiative; then plies remaining / 256, initiative moved, to act
+        if (lane < LOOSE) {
+            uint32_t on_board = 0;
+            const uint32_t seat = lane < 2 * PLAYER_SCALARS ? lane / PLAYER_SCALARS : 0;
+            for (int h = 0; h < N_HEXES; ++h) {
+                const uint32_t mk = mir ? flip_seat(R[ROW_HEX_MARKER + s_mir[h]]) : R[ROW_HEX_MARKER + h];
+                on_board += mk == seat;
+            }
+            uint32_t init = mir ? flip_seat(R[ROW_INITIATIVE]) : R[ROW_INITIATIVE];
+            if (init > 1) init = 0;  // expand_row's guard (rebel.rs:1377)
+            const uint32_t to_act = mir ? flip_seat(R[ROW_TO_ACT]) : R[ROW_TO_ACT];
+            const uint32_t plies = R[ROW_PLIES] | ((uint32_t)R[ROW_PLIES + 1] << 8);
+            const uint32_t in_hand = ((uint32_t)MARKERS_TOTAL - on_board) & 0xffu;  // u8 arithmetic, as the encoder's
+            float val;
+            if (lane < 2 * PLAYER_SCALARS) {
+                const uint32_t f = lane % PLAYER_SCALARS;
+                val = f == 0   ? s_quot[Q6][in_hand]
+                      : f == 1 ? s_quot[Q6][((uint32_t)MARKERS_TOTAL - in_hand) & 0xffu]
+                      : f == 2 ? s_quot[Q3][s_size[w][seat]]
+                      : f == 3 ? s_quot[Q21][s_size[w][2 + seat]]
+                      : f == 4 ? s_quot[Q21][s_size[w][4 + seat]]
+                               : (init == seat ? 1.0f : 0.0f);
+            } else {
+                const uint32_t g = lane - 2 * PLAYER_SCALARS;
+                // MAX_MAIN_PLAYS is 2^8: the quotient is exact, a product by 2^-8
+                val = g == 0 ? (float)plies * (1.0f / (float)MAX_MAIN_PLAYS)
+                      : g == 1 ? (R[ROW_INIT_MOVED] != 0 ? 1.0f : 0.0f)
+                               : (to_act == 0 ? 1.0f : 0.0f);
+            }
+            out[OFF_LOOSE + lane] = val;
+        }
     }
 }
 
@@ -200,7 +216,13 @@ bool replay_tables_ready() {
 void launch_replay_expand(const uint8_t* rows, uint32_t nrows, const uint8_t* cc, const int64_t* seg, uint64_t m,
                           float* x, float* phi, cudaStream_t s) {
     const uint32_t nviews = 2 * nrows;
-    if (nviews) k_replay_expand<<<(nviews + VIEWS_PER_CTA - 1) / VIEWS_PER_CTA, 32 * VIEWS_PER_CTA, 0, s>>>(rows, nviews, cc, seg, m, x);
+    if (nviews) {
+        int dev = 0, sms = 148;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        const uint32_t want = (nviews + VIEWS_PER_CTA - 1) / VIEWS_PER_CTA;
+        k_replay_expand<<<std::min<uint32_t>(want, (uint32_t)sms * 8), 32 * VIEWS_PER_CTA, 0, s>>>(rows, nviews, cc, seg, m, x);
+    }
     const uint64_t total = m * (uint64_t)CCOUNTS;
     if (total) k_replay_phi<<<(unsigned)std::min<uint64_t>((total + 255) / 256, 148ull * 16), 256, 0, s>>>(cc, total, phi);
 }

@@ -327,6 +327,28 @@ __device__ __forceinline__ uint32_t ln_gelu2(float n0, float n1, int c, const ui
     }
 }
 
+// Pairs of fp32 values in one 64-bit register for the sm_100 packed fp32
+// forms (add / fma .f32x2: two IEEE fp32 operations per instruction, each
+// rounded as the scalar one): low word the first value.
+__device__ __forceinline__ unsigned long long f2(uint32_t lo, uint32_t hi) {
+    unsigned long long d;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "r"(lo), "r"(hi));
+    return d;
+}
+__device__ __forceinline__ unsigned long long f2(float lo, float hi) { return f2(__float_as_uint(lo), __float_as_uint(hi)); }
+__device__ __forceinline__ float f2_lo(unsigned long long v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float f2_hi(unsigned long long v) { return __uint_as_float((uint32_t)(v >> 32)); }
+__device__ __forceinline__ unsigned long long f2_add(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ unsigned long long f2_fma(unsigned long long a, unsigned long long b, unsigned long long c) {
+    unsigned long long d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+
 // (gamma, beta) of columns c, c + 1 as the packed words ln_gelu2 reads.
 __device__ __forceinline__ void pack_gb2(const float* gam, const float* bet, int c, uint32_t* out2) {
     const __half2 g = __floats2half2_rn(gam[c], gam[c + 1]), b = __floats2half2_rn(bet[c], bet[c + 1]);
