@@ -284,6 +284,15 @@ uint64_t wc_batch_launches(const wc_batch* b);
  * self-test of the tensor-core kernels. k % 64 == 0, n % 16 == 0, n <= 256. */
 int wc_debug_umma_gemm(const uint16_t* a, const uint16_t* b, int k, int n, float* d);
 
+/* The time limit of every mbarrier wait in the tensor-core kernels (ns of
+ * %globaltimer; 0 restores the default, 2 s). A debug control with no
+ * counterpart in the reference: with a limit shorter than the work waited on,
+ * the kernels give up, drain what they issued, release their tensor memory
+ * and report the failure through the solve's status (WC_E_CUDA, "a
+ * tensor-core wait exceeded its time limit (code c)"), and the context stays
+ * usable; codes above 10 mean in-flight work did not drain. */
+int wc_debug_set_wait_limit(wc_ctx* ctx, uint64_t ns);
+
 /* wc_debug_umma_gemm without any device allocation; it has no counterpart in
  * the reference. For callers that cannot call cudaMalloc: a host engine whose
  * device memory is owned by another allocator (a caching allocator holding

@@ -867,6 +867,18 @@ void wc_job_free(wc_job* job) { delete job; }
 
 uint64_t wc_batch_launches(const wc_batch* b) { return b ? b->b->launches : 0; }
 
+int wc_debug_set_wait_limit(wc_ctx* ctx, uint64_t ns) {
+    if (!ctx) return fail(WC_E_ARG, "null context");
+    return guarded([&] {
+        for (auto& d : ctx->devs) {
+            std::lock_guard<std::mutex> lk(d->mu);
+            d->wait_ns = ns ? ns : DEFAULT_WAIT_NS;
+            d->fast.wait_ns = d->wait_ns;
+        }
+        return (int)WC_OK;
+    });
+}
+
 int wc_debug_umma_gemm(const uint16_t* a, const uint16_t* b, int k, int n, float* d) {
     int rc = wcdev::umma_selftest(a, b, k, n, d);
     if (rc) return fail(WC_E_CUDA, "tcgen05 self-test failed with code " + std::to_string(rc));

@@ -805,6 +805,8 @@ void enqueue_solve(Batch& b) {
     b.launches = 0;
     DeviceCtx& dv = *b.dev;
     check(cudaSetDevice(dv.device), "set device");
+    // each solve reports its own tensor-core wait failures
+    if (b.d_err) check(cudaMemsetAsync(b.d_err, 0, 16, dv.stream), "clear error flag");
     Sched S(b);
     auto mark = [&](int i) {
         if (!b.profile) return;

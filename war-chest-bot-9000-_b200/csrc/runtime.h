@@ -16,6 +16,10 @@
 
 namespace wc {
 
+// The tensor-core kernels' limit on each mbarrier wait (%globaltimer ns);
+// the work waited on takes microseconds.
+constexpr uint64_t DEFAULT_WAIT_NS = 2000000000ull;
+
 struct DeviceCtx {
     int device = 0;
     cudaStream_t stream = nullptr;
@@ -25,7 +29,7 @@ struct DeviceCtx {
     bool have_net = false;
     bool precise = true;  // fp32 network in the reference's operation order
     bool half = true;     // the tensor-core net's per-iteration chain operands: f16 (true) or bf16
-    uint64_t wait_ns = 2000000000ull;  // limit of each tensor-core mbarrier wait (ns)
+    uint64_t wait_ns = DEFAULT_WAIT_NS;  // limit of each tensor-core mbarrier wait (ns)
     uint64_t version = 0;
     NetLayout L;
     // 16-bit tensor-core copy of the network (fast path)

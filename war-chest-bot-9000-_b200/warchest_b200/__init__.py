@@ -115,6 +115,7 @@ def _load() -> C.CDLL:
         "wc_wcj8_from_root": (I, [C.c_char_p, C.c_size_t, P(_SolveCfg), VP, C.c_uint32, P(C.c_uint32), C.c_uint32,
                                   C.c_char_p, C.c_size_t, P(C.c_size_t)]),
         "wc_job_from_wcj8": (I, [C.c_char_p, C.c_size_t, P(VP)]),
+        "wc_debug_set_wait_limit": (I, [VP, U64]),
         "wc_replay_expand": (I, [VP, C.c_size_t, VP, VP, C.c_size_t, VP, VP, VP]),
     }
     for name, (res, args) in sig.items():
