@@ -78,6 +78,7 @@ __global__ void __launch_bounds__(32 * VIEWS_PER_CTA)
     __shared__ uint8_t s_loc[N_HEXES], s_mir[N_HEXES];
     __shared__ uint8_t s_row[VIEWS_PER_CTA][ROW_STRIDE];
     __shared__ uint32_t s_size[VIEWS_PER_CTA][6];  // hand[2], fd[2], bag[2] of the view's seats
+    __shared__ float s_hex[VIEWS_PER_CTA][HEX_BLOCK];  // a view's hex block as [channel][hex]
     const uint32_t tid = threadIdx.x, w = tid / 32, lane = tid % 32;
     for (uint32_t i = tid; i < 4 * 256; i += blockDim.x) s_quot[i / 256][i % 256] = c_quot[i / 256][i % 256];
     for (uint32_t i = tid; i < N_UNITS * CARD_FEATS; i += blockDim.x) s_card[i] = c_card_feat[i];
@@ -87,7 +88,7 @@ __global__ void __launch_bounds__(32 * VIEWS_PER_CTA)
     }
     __syncthreads();
     for (uint32_t v = blockIdx.x * VIEWS_PER_CTA + w; v < nviews; v += gridDim.x * VIEWS_PER_CTA) {
-        __syncwarp();  // the previous view's reads of s_row and s_size are done
+        __syncwarp();  // the previous view's reads of s_row, s_size and s_hex are done
         const uint32_t r = v >> 1;
         const bool mir = v & 1u;
         const uint8_t* row = rows + (size_t)r * ROW_BYTES;
@@ -110,27 +111,40 @@ __global__ void __launch_bounds__(32 * VIEWS_PER_CTA)
         __syncwarp();
         const uint8_t* R = s_row[w];
         float* out = x + (size_t)v * PUBFEAT;
-        // per hex: owner one-hot, height / 5, marker one-hot, location, the
-        // owner's slot one-hot (selects, no divergent branches)
-        for (int j = lane; j < HEX_BLOCK; j += 32) {
-            const int h = j >> 4, ch = j & 15;
-            const int src = mir ? s_mir[h] : h;
+        // per hex (one lane each, in two rounds): owner one-hot, height / 5,
+        // marker one-hot, location, the owner's slot one-hot, decoded once
+        // into the warp's staging as [channel][hex]; each seat's markers on
+        // the board counted by ballot
+        float* sv = s_hex[w];
+        uint32_t on_board[2] = {0, 0};
+#pragma unroll
+        for (int base = 0; base < N_HEXES; base += 32) {
+            const int h = base + (int)lane;
+            const bool live = h < N_HEXES;
+            const int hh = live ? h : 0;
+            const int src = mir ? s_mir[hh] : hh;
             uint32_t owner = R[ROW_HEX_OWNER + src], marker = R[ROW_HEX_MARKER + src];
             if (mir) {
                 owner = flip_seat(owner);
                 marker = flip_seat(marker);
             }
             const uint32_t slot = R[ROW_HEX_SLOT + src];
-            const float hq = s_quot[Q5][R[ROW_HEX_HEIGHT + src]];
-            float val = 0.0f;
-            val = (ch < 2 && owner == (uint32_t)ch) ? 1.0f : val;
-            val = (ch == 2 && owner != NONE) ? hq : val;
-            val = (ch >= 3 && ch < 5 && marker == (uint32_t)(ch - 3)) ? 1.0f : val;
-            val = (ch == 5 && s_loc[h]) ? 1.0f : val;
-            val = (ch >= HEX_FACTS && owner < 2 && slot < NSLOT && (uint32_t)(ch - HEX_FACTS) == owner * NSLOT + slot)
-                      ? 1.0f : val;
-            out[j] = val;
+            on_board[0] += __popc(__ballot_sync(0xffffffffu, live && marker == 0));
+            on_board[1] += __popc(__ballot_sync(0xffffffffu, live && marker == 1));
+            if (live) {
+                const uint32_t hot = owner < 2 && slot < NSLOT ? owner * NSLOT + slot : 0xffu;
+                sv[0 * N_HEXES + h] = owner == 0 ? 1.0f : 0.0f;
+                sv[1 * N_HEXES + h] = owner == 1 ? 1.0f : 0.0f;
+                sv[2 * N_HEXES + h] = owner != NONE ? s_quot[Q5][R[ROW_HEX_HEIGHT + src]] : 0.0f;
+                sv[3 * N_HEXES + h] = marker == 0 ? 1.0f : 0.0f;
+                sv[4 * N_HEXES + h] = marker == 1 ? 1.0f : 0.0f;
+                sv[5 * N_HEXES + h] = s_loc[h] ? 1.0f : 0.0f;
+#pragma unroll
+                for (int k = 0; k < NTYPE; ++k) sv[(HEX_FACTS + k) * N_HEXES + h] = hot == (uint32_t)k ? 1.0f : 0.0f;
+            }
         }
+        __syncwarp();
+        for (int j = lane; j < HEX_BLOCK; j += 32) out[j] = sv[(j & 15) * N_HEXES + (j >> 4)];
         // the piles of each coin type / 5 (the mirror exchanges the seats' halves)
         for (int q = lane; q < NTYPE * PILE_COUNTS; q += 32) {
             const int t = q >> 2, st = mir ? (t + NSLOT) % NTYPE : t;
@@ -145,17 +159,13 @@ __global__ void __launch_bounds__(32 * VIEWS_PER_CTA)
         // per seat: markers in hand and on the board / 6, hand / 3, face-down and
         // bag / 21, initiative; then plies remaining / 256, initiative moved, to act
         if (lane < LOOSE) {
-            uint32_t on_board = 0;
             const uint32_t seat = lane < 2 * PLAYER_SCALARS ? lane / PLAYER_SCALARS : 0;
-            for (int h = 0; h < N_HEXES; ++h) {
-                const uint32_t mk = mir ? flip_seat(R[ROW_HEX_MARKER + s_mir[h]]) : R[ROW_HEX_MARKER + h];
-                on_board += mk == seat;
-            }
+            const uint32_t seat_board = seat ? on_board[1] : on_board[0];
             uint32_t init = mir ? flip_seat(R[ROW_INITIATIVE]) : R[ROW_INITIATIVE];
             if (init > 1) init = 0;  // expand_row's guard (rebel.rs:1377)
             const uint32_t to_act = mir ? flip_seat(R[ROW_TO_ACT]) : R[ROW_TO_ACT];
             const uint32_t plies = R[ROW_PLIES] | ((uint32_t)R[ROW_PLIES + 1] << 8);
-            const uint32_t in_hand = ((uint32_t)MARKERS_TOTAL - on_board) & 0xffu;  // u8 arithmetic, as the encoder's
+            const uint32_t in_hand = ((uint32_t)MARKERS_TOTAL - seat_board) & 0xffu;  // u8 arithmetic, as the encoder's
             float val;
             if (lane < 2 * PLAYER_SCALARS) {
                 const uint32_t f = lane % PLAYER_SCALARS;
