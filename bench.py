@@ -550,7 +550,8 @@ def main():
     net_rows = sum(j.info["net_rows"] for j in jobs)
     traffic = TRAFFIC_PER_ROW[dom] * net_rows if dom in TRAFFIC_PER_ROW else None
     roofline.update({"kernel": KERNELS.get(dom, dom), "traffic": traffic, "peak_source": src,
-                     "traffic_basis": "ncu DRAM bytes per network row (64-subgame capture) x this workload's rows",
+                     "traffic_basis": "ncu DRAM bytes per network row (256-subgame capture, images above the L2) "
+                                      "x this workload's rows",
                      "per_class": per_class, "per_class_ms": prof})
 
     if rank == 0:
@@ -754,11 +755,12 @@ PLIES = 20
 KERNELS = {"rows": "k_rows", "vgather": "k_vgather", "reach": "k_rgather", "pool": "k_pool_fast",
            "join": "k_join_fast", "head": "k_head_fast", "trunk": "k_trunk_fast"}
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per network row
-# per launch, from one ncu capture of the kernel on 64 subgames (372,818
-# rows, seeds 0..63, depth 3); a launch's traffic grows with
-# its rows, so the full launch's traffic is this times the workload's rows.
-# The pooling figure is of a launch that pooled both players.
-TRAFFIC_PER_ROW = {"head": 1025.4, "join": 796.9, "pool": 349.2, "trunk": 880.5}
+# per launch, from one ncu capture of each kernel on 256 subgames (1,441,491
+# rows, seeds 0..255, depth 3, 4 GB on the device, its images far above the
+# L2); a launch's traffic grows with its rows, so the full launch's traffic
+# is this times the workload's rows. The pooling figure is of a launch that
+# pooled both players.
+TRAFFIC_PER_ROW = {"head": 1015.6, "join": 915.5, "pool": 451.6, "trunk": 438.4}
 DTYPES = {"f16": "f32 CFR state, f16 tensor-core value net (fp32 accumulate)",
           "bf16": "f32 CFR state, tensor-core value net (fp32 accumulate): bf16 operands for the per-iteration "
                   "pooling / join / join-output chain, f16 for the once-per-solve trunk and the readout",

@@ -391,11 +391,10 @@ __global__ void __launch_bounds__(128, 3)
 // Pooled belief embeddings (search.rs:1512-1547) of one 128-row tile on the
 // tensor cores: pooled_q = beta_q G_q, where beta_q[row][c] is the row's
 // normalised reach on config c (player q's configs, by index; about 20 of
-// ~110 nonzero per row) and G_q[c] = g(c). Each warp loads its 32 rows'
-// entries with one coalesced load per row, reduces each row's reach mass
-// (kept: it is the opponent mass of the other player's readout) and scatters
-// the normalised weights into a zeroed 128 x 128 A tile in shared memory;
-// the job's g table arrives as a 64 x 128 B image by bulk
+// ~110 nonzero per row) and G_q[c] = g(c). One thread per row computes its
+// reach mass (kept: it is the opponent mass of the other player's readout)
+// and scatters its normalised weights into a zeroed 128 x 128 A tile in
+// shared memory; the job's g table arrives as a 64 x 128 B image by bulk
 // copy; one MMA per 128 configs accumulates D = beta G (64 columns of TMEM),
 // which becomes the player's 64-column atom of the tile's pooled image.
 template <bool H>
@@ -440,62 +439,37 @@ __global__ void __launch_bounds__(128, 4)
         for (int q = 0; q < 2; ++q) {
             if (!(mask & (1 << q))) continue;
             const uint32_t ncq = J.ncfg_player[q], nchunk = (ncq + 127) / 128;
-            // The rows' entries, loaded by the warp: lane k holds entry k of
-            // each of the warp's 32 rows (ew / ec, one coalesced load of the
-            // reach and one of the columns per row; entries past 32 are
-            // rare and taken in a second loop). Each row's reach mass is
-            // reduced across the lanes by a transpose-reduce (31 shuffles
-            // for the 32 rows: lane l ends with row l's sum), kept (it is
-            // the opponent mass of the other player's readout) and turned
-            // into the row's normaliser.
-            const uint32_t lane = tid & 31;
-            uint32_t my_ridx = 0, my_n = 0, my_coff = 0;
-            if (valid) {
-                my_ridx = J.lr_ridx[2 * r + q];
-                my_n = J.lr_nc[2 * r + q];
-                my_coff = J.leaf_coff[2 * r + q];
-            }
-            float ew[32];
-            uint32_t ec[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                const uint32_t ri = __shfl_sync(0xffffffffu, my_ridx, i), ni = __shfl_sync(0xffffffffu, my_n, i);
-                const uint32_t ci = __shfl_sync(0xffffffffu, my_coff, i);
-                ew[i] = lane < ni ? J.reach[ri + lane] : 0.0f;
-                ec[i] = lane < ni ? J.leaf_col[ci + lane] : 0xffffffffu;
-            }
-            float tot;
-            {
-                float p[32];
-#pragma unroll
-                for (int i = 0; i < 32; ++i) p[i] = ew[i];
-#pragma unroll
-                for (int off = 16; off >= 1; off >>= 1) {
-                    const bool upper = (lane & (uint32_t)off) != 0;
-#pragma unroll
-                    for (int i = 0; i < off; ++i) {
-                        const float send = upper ? p[i] : p[i + off];
-                        const float keep = upper ? p[i + off] : p[i];
-                        p[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
-                    }
-                }
-                tot = p[0];
-            }
-            // entries past the first 32 (a row with more than 32 configs)
-            for (uint32_t big = __ballot_sync(0xffffffffu, my_n > 32); big; big &= big - 1) {
-                const int i = __ffs(big) - 1;
-                const uint32_t ri = __shfl_sync(0xffffffffu, my_ridx, i), ni = __shfl_sync(0xffffffffu, my_n, i);
-                float x = 0.0f;
-                for (uint32_t e = 32 + lane; e < ni; e += 32) x += J.reach[ri + e];
-#pragma unroll
-                for (int off = 16; off >= 1; off >>= 1) x += __shfl_xor_sync(0xffffffffu, x, off);
-                if (lane == (uint32_t)i) tot += x;
-            }
+            const float* w = nullptr;
+            const uint32_t* lc = nullptr;
+            uint32_t n = 0;
             float scale = 0.0f, flat = 0.0f;
-            if (valid) {
+            // the row's first EC entries, all loads issued at once (a typical
+            // row has ~20), kept in registers for the scatter
+            constexpr int EC = 24;
+            float wr[EC];
+            uint32_t cr[EC];
+#pragma unroll
+            for (int k = 0; k < EC; ++k) {
+                wr[k] = 0.0f;
+                cr[k] = 0xffffffffu;
+            }
+            if (valid) {  // one thread per row: its reach mass and normaliser
+                w = J.reach + J.lr_ridx[2 * r + q];
+                n = J.lr_nc[2 * r + q];
+                lc = J.leaf_col + J.leaf_coff[2 * r + q];
+#pragma unroll
+                for (int k = 0; k < EC; ++k)
+                    if ((uint32_t)k < n) {
+                        wr[k] = w[k];
+                        cr[k] = lc[k];
+                    }
+                float tot = 0.0f;
+#pragma unroll
+                for (int k = 0; k < EC; ++k) tot += wr[k];
+                for (uint32_t e = EC; e < n; ++e) tot += w[e];
                 mass[(size_t)(J.row_base + r) * 2 + q] = tot;
                 if (tot > 1e-30f) scale = 1.0f / tot;
-                else flat = 1.0f / (float)(my_n > 0 ? my_n : 1);
+                else flat = 1.0f / (float)(n > 0 ? n : 1);
             }
             const uint8_t* gsrc = reinterpret_cast<const uint8_t*>(J.g16) +
                                   (q == 1 ? (J.ncfg_player[0] + 127) / 128 : 0) * (size_t)ATOM;
@@ -508,27 +482,18 @@ __global__ void __launch_bounds__(128, 4)
 #pragma unroll
                 for (int k = 0; k < 128; k += 8)
                     *reinterpret_cast<uint4*>(sBeta + umma::sw128_offset(128, tid, k)) = make_uint4(0, 0, 0, 0);
-                __syncwarp();  // the warp's rows are zero before its lanes scatter into them
-                // row 32 w + i's entry `lane`, with that row's normaliser
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const float sc = __shfl_sync(0xffffffffu, scale, i), fl = __shfl_sync(0xffffffffu, flat, i);
-                    const uint32_t col = ec[i] - 128 * c;
+                for (int k = 0; k < EC; ++k) {
+                    const uint32_t col = cr[k] - 128 * c;
                     if (col < 128)
-                        *reinterpret_cast<uint16_t*>(sBeta + umma::sw128_offset(128, 32 * warp + i, col)) =
-                            umma::Op16<H>::one(ew[i] * sc + fl);
+                        *reinterpret_cast<uint16_t*>(sBeta + umma::sw128_offset(128, tid, col)) =
+                            umma::Op16<H>::one(wr[k] * scale + flat);
                 }
-                for (uint32_t big = __ballot_sync(0xffffffffu, my_n > 32); big; big &= big - 1) {
-                    const int i = __ffs(big) - 1;
-                    const uint32_t ri = __shfl_sync(0xffffffffu, my_ridx, i), ni = __shfl_sync(0xffffffffu, my_n, i);
-                    const uint32_t ci = __shfl_sync(0xffffffffu, my_coff, i);
-                    const float sc = __shfl_sync(0xffffffffu, scale, i), fl = __shfl_sync(0xffffffffu, flat, i);
-                    for (uint32_t e = 32 + lane; e < ni; e += 32) {
-                        const uint32_t col = J.leaf_col[ci + e] - 128 * c;
-                        if (col < 128)
-                            *reinterpret_cast<uint16_t*>(sBeta + umma::sw128_offset(128, 32 * warp + i, col)) =
-                                umma::Op16<H>::one(J.reach[ri + e] * sc + fl);
-                    }
+                for (uint32_t e = EC; e < n; ++e) {
+                    const uint32_t col = lc[e] - 128 * c;
+                    if (col < 128)
+                        *reinterpret_cast<uint16_t*>(sBeta + umma::sw128_offset(128, tid, col)) =
+                            umma::Op16<H>::one(w[e] * scale + flat);
                 }
                 {  // the scatter is done and (thread 0) the g chunk has landed
                     bool ok = true;
@@ -840,28 +805,6 @@ __global__ void __launch_bounds__(544, 1)
             const HeadTile ht = tiles[t];
             const JobDev& J = jobs[ht.job];
             const uint32_t npass = (J.ncfg_player[p] + 127) / 128;
-            // The scatter's row metadata, loaded now so the loads land during
-            // the LayerNorm: lane i < 8 holds row 8 w + i's opponent reach
-            // mass (kept by the pooling kernel), entry count, readout columns
-            // and value slots (prefetched into L2); colv[i] is entry `lane` of
-            // row 8 w + i, all eight loaded at once.
-            float s_mass = 0.0f;
-            uint32_t s_nc = 0;
-            unsigned long long s_lcol = 0, s_out = 0;
-            if (lane < 8 && (uint32_t)(8 * warp + lane) < ht.count) {
-                const uint32_t r = ht.first + 8 * warp + lane;      // job-local network row
-                s_mass = mass[(size_t)(J.row_base + r) * 2 + 1 - p];
-                s_nc = J.lr_nc[2 * r + p];
-                s_lcol = reinterpret_cast<unsigned long long>(J.leaf_col + J.leaf_coff[2 * r + p]);
-                s_out = reinterpret_cast<unsigned long long>(J.vals[p] + J.lr_vidx[2 * r + p]);
-            }
-            uint32_t colv[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const uint32_t nc = __shfl_sync(0xffffffffu, s_nc, i);
-                const uint32_t* lc = reinterpret_cast<const uint32_t*>(__shfl_sync(0xffffffffu, s_lcol, i));
-                colv[i] = (uint32_t)lane < nc ? lc[lane] : 0xffffffffu;
-            }
             if (!wait(&bar_y, ph_y)) bad = true;
             ph_y ^= 1u;
             if (!wait(&bar_p, ph_p)) bad = true;
@@ -967,7 +910,27 @@ __global__ void __launch_bounds__(544, 1)
             if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(umma::smem_u32(&h_ready)) : "memory");
             // the scatter: warp w writes the values of rows 8 w .. 8 w + 7, a
             // row's entries across the lanes (coalesced column reads and value
-            // writes), from the row metadata loaded at the tile's start
+            // writes). Lane i < 8 holds row 8 w + i's opponent reach mass (kept
+            // by the pooling kernel), entry count, readout columns and value
+            // slots (prefetched into L2); colv[i] is entry `lane` of row
+            // 8 w + i, all eight loaded at once, during the readout product.
+            float s_mass = 0.0f;
+            uint32_t s_nc = 0;
+            unsigned long long s_lcol = 0, s_out = 0;
+            if (lane < 8 && (uint32_t)(8 * warp + lane) < ht.count) {
+                const uint32_t r = ht.first + 8 * warp + lane;      // job-local network row
+                s_mass = mass[(size_t)(J.row_base + r) * 2 + 1 - p];
+                s_nc = J.lr_nc[2 * r + p];
+                s_lcol = reinterpret_cast<unsigned long long>(J.leaf_col + J.leaf_coff[2 * r + p]);
+                s_out = reinterpret_cast<unsigned long long>(J.vals[p] + J.lr_vidx[2 * r + p]);
+            }
+            uint32_t colv[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const uint32_t nc = __shfl_sync(0xffffffffu, s_nc, i);
+                const uint32_t* lc = reinterpret_cast<const uint32_t*>(__shfl_sync(0xffffffffu, s_lcol, i));
+                colv[i] = (uint32_t)lane < nc ? lc[lane] : 0xffffffffu;
+            }
             for (uint32_t k = 0; k < npass; ++k) {
                 const uint32_t nb = 128 * k;
                 if (!wait(&bar_v, ph_v)) bad = true;
