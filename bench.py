@@ -596,36 +596,63 @@ def resolve_workload(args):
     games = [wc.Game(cfg, seed=s, root=wc.generate_wide_root(s, 256), max_solves=8) for s in range(args.games)]
     threads = args.build_threads or (os.cpu_count() or 1)
     pool = ThreadPoolExecutor(threads)
-    live, rounds, solved, nodes, host_s, gpu_s = list(games), 0, 0, 0.0, 0.0, 0.0
-    while live:
-        t0 = time.perf_counter()
+    # Two halves of the games alternate: while one half's round solves on the
+    # device (a host thread in wc_solve_batch), the other half builds its
+    # next subgames on the host threads, as the reference's game actors keep
+    # building while its GPU service solves.
+    halves = [list(games[0::2]), list(games[1::2])]
+    rounds, solved, nodes, gpu_s = 0, 0, 0.0, 0.0
+
+    def advance(live):
         jobs = list(pool.map(lambda g: g.advance(), live))
-        host_s += time.perf_counter() - t0
-        pend = [(g, j) for g, j in zip(live, jobs) if j is not None]
-        if not pend:
-            break
+        return [(g, j) for g, j in zip(live, jobs) if j is not None]
+
+    def solve(pend):
         n = len(pend)
         arr = (Cc.c_void_p * n)(*[j._h.value for _, j in pend])
         res = (wc._Result * n)()
         t0 = time.perf_counter()
         wc._check(wc.lib().wc_solve_batch(client._ctx, arr, n, res))
-        gpu_s += time.perf_counter() - t0
-        t0 = time.perf_counter()
+        return res, time.perf_counter() - t0
+
+    def resume(pend, res):
         for i, (g, j) in enumerate(pend):
             wc._check(wc.lib().wc_game_resume(g._h, j._h, Cc.byref(res[i])))
             wc.lib().wc_result_free(Cc.byref(res[i]))
-        host_s += time.perf_counter() - t0
-        nodes += sum(j.info["nodes"] for _, j in pend) * float(args.iters)
-        solved += n
+        return [g for g, _ in pend]
+
+    solver = ThreadPoolExecutor(1)
+    wall0 = time.perf_counter()
+    built = [advance(halves[0]), None]
+    k = 0
+    while True:
+        o = 1 - k
+        if not built[k]:  # half k has nothing to solve: go on with the other alone
+            if built[o] is None:
+                built[o] = advance(halves[o])
+            if not built[o]:
+                break
+            built[k], k = None, o
+            continue
+        fut = solver.submit(solve, built[k])  # half k on the device ...
+        if built[o] is None:
+            built[o] = advance(halves[o])     # ... while half o builds on the host
+        res, dt = fut.result()
+        gpu_s += dt
+        nodes += sum(j.info["nodes"] for _, j in built[k]) * float(args.iters)
+        solved += len(built[k])
         rounds += 1
-        live = [g for g, _ in pend]
+        halves[k] = resume(built[k], res)
+        built[k] = None                       # rebuilt while half o solves
+        k = o
+    wall_s = time.perf_counter() - wall0
     counters = [g.counters() for g in games]
     line = {"workload": f"configs[4] loop: {args.games} belief-heavy games (256 configs per player), depth "
                         f"{args.depth}, {args.iters} CFR+ iters, 8 solves per game, one GPU",
             "games": args.games, "rounds": rounds, "solves": solved,
             "walk_decisions": sum(c["walk_decisions"] for c in counters),
             "capped": sum(c["capped"] for c in counters),
-            "gpu_s": gpu_s, "host_s": host_s, "solves_per_s": solved / (gpu_s + host_s),
+            "wall_s": wall_s, "gpu_s": gpu_s, "solves_per_s": solved / wall_s,
             "node_updates_per_s_gpu": nodes / gpu_s if gpu_s else None, "host_threads": threads}
     print(json.dumps(line), flush=True)
     client.close()
