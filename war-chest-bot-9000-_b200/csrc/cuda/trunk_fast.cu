@@ -107,25 +107,6 @@ __device__ __forceinline__ void rows_gemm(const float* in, int ldi, const float*
     }
 }
 
-// Sum of 32 values, and sum of their squared deviations from m, on column
-// pairs (add / fma .f32x2), two chains each.
-__device__ __forceinline__ float pair_sum(const float* v) {
-    unsigned long long a[2] = {0ull, 0ull};
-#pragma unroll
-    for (int j = 0; j < 32; j += 2) a[(j >> 1) & 1] = umma::f2_add(a[(j >> 1) & 1], umma::f2(v[j], v[j + 1]));
-    return (umma::f2_lo(a[0]) + umma::f2_hi(a[0])) + (umma::f2_lo(a[1]) + umma::f2_hi(a[1]));
-}
-__device__ __forceinline__ float pair_dev2(const float* v, float m) {
-    const unsigned long long nm = umma::f2(-m, -m);
-    unsigned long long a[2] = {0ull, 0ull};
-#pragma unroll
-    for (int j = 0; j < 32; j += 2) {
-        const unsigned long long d = umma::f2_add(umma::f2(v[j], v[j + 1]), nm);
-        a[(j >> 1) & 1] = umma::f2_fma(d, d, a[(j >> 1) & 1]);
-    }
-    return (umma::f2_lo(a[0]) + umma::f2_hi(a[0])) + (umma::f2_lo(a[1]) + umma::f2_hi(a[1]));
-}
-
 // Eight consecutive f16 operands of row r, columns [k, k + 8), as floats.
 __device__ __forceinline__ void ld_chunk(const uint8_t* tile, uint32_t R, uint32_t r, uint32_t k, float* v) {
     const uint4 q = *reinterpret_cast<const uint4*>(tile + umma::sw128_offset(R, r, k));
@@ -360,24 +341,28 @@ __global__ void __launch_bounds__(384, 1)
             const int buf = blk & 1;
             // LNGELU(x) -> A1 columns 0..95
             {
-                // the fp32 steps on column pairs (add / fma .f32x2)
-                const float s = pair_sum(x);
+                float s = 0.0f;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) s += x[j];
                 S.part_s[row][cg] = s;
                 __syncthreads();
                 const float mean = (S.part_s[row][0] + S.part_s[row][1] + S.part_s[row][2]) * (1.0f / C);
-                const float q = pair_dev2(x, mean);
+                float q = 0.0f;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) q += (x[j] - mean) * (x[j] - mean);
                 S.part_q[row][cg] = q;
                 __syncthreads();
                 const float inv = rsqrtf((S.part_q[row][0] + S.part_q[row][1] + S.part_q[row][2]) * (1.0f / C) + 1e-5f);
-                const unsigned long long inv2 = umma::f2(inv, inv), nm2 = umma::f2(-mean * inv, -mean * inv);
+                const float nm = -mean * inv;
+                const float* gam = LN + L.norm_g[NetLayout::ln_block(blk, 0)];
+                const float* bet = LN + L.norm_b[NetLayout::ln_block(blk, 0)];
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     uint32_t w4[4];
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
                         const int k = 8 * c + 2 * j;
-                        const unsigned long long n = umma::f2_fma(umma::f2(x[k], x[k + 1]), inv2, nm2);
-                        w4[j] = real_row ? umma::ln_gelu2<true>(umma::f2_lo(n), umma::f2_hi(n), col0 + k, S.gb2[blk][0])
+                        w4[j] = real_row ? umma::ln_gelu2<true>(x[k] * inv + nm, x[k + 1] * inv + nm, col0 + k, S.gb2[blk][0])
                                          : 0u;
                     }
                     *reinterpret_cast<uint4*>(sA1 + umma::sw128_offset(128, row, col0 + 8 * c)) =
@@ -494,23 +479,28 @@ __global__ void __launch_bounds__(384, 1)
                 const float* gbr = &S.gb[real_row ? board : 0][col0];
 #pragma unroll
                 for (int j = 0; j < 32; ++j) y[j] = v[j] + gbr[j];
-                const float s = pair_sum(y);
+                float s = 0.0f;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) s += y[j];
                 S.part_s[row][cg] = s;
                 __syncthreads();
                 const float mean = (S.part_s[row][0] + S.part_s[row][1] + S.part_s[row][2]) * (1.0f / C);
-                const float q = pair_dev2(y, mean);
+                float q = 0.0f;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) q += (y[j] - mean) * (y[j] - mean);
                 S.part_q[row][cg] = q;
                 __syncthreads();
                 const float inv = rsqrtf((S.part_q[row][0] + S.part_q[row][1] + S.part_q[row][2]) * (1.0f / C) + 1e-5f);
-                const unsigned long long inv2 = umma::f2(inv, inv), nm2 = umma::f2(-mean * inv, -mean * inv);
+                const float nm = -mean * inv;
+                const float* gam = LN + L.norm_g[NetLayout::ln_block(blk, 1)];
+                const float* bet = LN + L.norm_b[NetLayout::ln_block(blk, 1)];
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     uint32_t w4[4];
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
                         const int k = 8 * c + 2 * j;
-                        const unsigned long long n = umma::f2_fma(umma::f2(y[k], y[k + 1]), inv2, nm2);
-                        w4[j] = real_row ? umma::ln_gelu2<true>(umma::f2_lo(n), umma::f2_hi(n), col0 + k, S.gb2[blk][1])
+                        w4[j] = real_row ? umma::ln_gelu2<true>(y[k] * inv + nm, y[k + 1] * inv + nm, col0 + k, S.gb2[blk][1])
                                          : 0u;
                     }
                     *reinterpret_cast<uint4*>(sA2 + umma::sw128_offset(128, row, col0 + 8 * c)) =
