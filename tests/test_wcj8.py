@@ -231,3 +231,57 @@ def test_reader_refuses_malformed_bytes(wc):
         with pytest.raises(wc.SolveError) as e:
             wc.PackedJob.from_wcj8(x, cfg_of(wc))
         assert e.value.code == 1
+
+
+def _first(mask):
+    idx = np.flatnonzero(mask)
+    assert idx.size, "the tree has no such entry"
+    return int(idx[0])
+
+
+@pytest.mark.parametrize("what", [
+    "node_child", "legal_child", "legal_trans", "cell_row", "obs_act", "obs_child", "draw_to",
+    "leaf_rows", "term_leaves", "leaf_cidx", "cplayer", "soff", "leaf_coff", "legal_off", "draw_row_start",
+])
+def test_reader_refuses_indices_out_of_range(wc, what):
+    """Bytes whose every count agrees but one index points outside its
+    table: the reader returns an argument error (code 1) rather than handing
+    the flattener an index to follow."""
+    cfg = cfg_of(wc)
+    # roots with chance nodes (seed 6) and with game-ending leaves (seed 23,
+    # 260 plies in) for the tables only those hold
+    seed, plies = {"draw_to": (6, 20), "draw_row_start": (6, 20), "term_leaves": (23, 260)}.get(what, (0, 20))
+    b = wc.wcj8_bytes(wc.generate_root(seed, plies), cfg)
+    j = parse(b)
+    n, big = j["nodes"], 1 << 30
+    if what in ("node_child", "leaf_rows", "term_leaves"):
+        j[what][0] = n
+    elif what == "legal_child":
+        j[what][0] = n + 5
+    elif what == "legal_trans":
+        j[what][_first(j[what] != NONE32)] = big
+    elif what == "cell_row":
+        j[what][0] = big
+    elif what in ("obs_act", "obs_child"):
+        j[what][0] = big
+    elif what == "draw_to":
+        j[what][0] = big
+    elif what == "leaf_cidx":
+        j[what][0] = j["ncfg"]
+    elif what == "cplayer":
+        j[what][0] = 2
+    elif what == "soff":  # a decreasing step that keeps both ends
+        k = _first(np.diff(j["soff"].astype(np.int64)) > 0)
+        j[what][k + 1] = j[what][k] - 1 if j[what][k] else j[what][k + 2] + 1
+    elif what == "leaf_coff":  # a row whose config span no longer fits its node
+        k = _first(np.diff(j["leaf_coff"].astype(np.int64)) > 0)
+        j[what][k + 1] += 1
+    elif what == "legal_off":  # a legal row reaching past its node's cells
+        j[what][1] = big
+    elif what == "draw_row_start":
+        j[what][j["draw_row_off"][_first(j["node_kind"] == 1)]] += 1
+    x = write(j)
+    assert x != b
+    with pytest.raises(wc.SolveError) as e:
+        wc.PackedJob.from_wcj8(x, cfg)
+    assert e.value.code == 1

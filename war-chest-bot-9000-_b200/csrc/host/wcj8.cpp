@@ -516,7 +516,7 @@ std::unique_ptr<Tree> wcj8_tree(const Wcj8Job& j, std::vector<float>* carried, u
         if (n.kind == NK_CHANCE) {
             const uint32_t r0 = j.draw_row_off[i], r1 = j.draw_row_off[i + 1], g0 = j.draw_off[i];
             const uint32_t rows = (uint32_t)t->supports[n.sup[n.player]].size();
-            if (r1 < r0 || r1 - r0 != rows + 1 || r1 > j.draw_row_start.size() || n.nch != 1)
+            if (r1 < r0 || r1 - r0 != rows + 1 || r1 > j.draw_row_start.size() || n.nch != 1 || j.draw_row_start[r0] != 0)
                 return fail("job: draw rows out of range");
             const uint32_t base = (uint32_t)t->draw_to.size();
             for (uint32_t k = r0; k < r1; ++k) t->draw_start.push_back(base + j.draw_row_start[k]);
@@ -525,6 +525,61 @@ std::unique_ptr<Tree> wcj8_tree(const Wcj8Job& j, std::vector<float>* carried, u
             append(t->draw_to, j.draw_to, e0, e1);
             append(t->draw_p, j.draw_p, e0, e1);
         }
+    }
+    // every index the flattener follows must be in range: a malformed job is
+    // an error here, never an out-of-range read there
+    {
+        auto nc = [&](uint32_t i, int q) { return (uint32_t)t->supports[t->nodes[i].sup[q]].size(); };
+        if (t->soff[0] != 0) return fail("job: soff does not start at 0");
+        for (uint32_t i = 0; i < N; ++i) {
+            const NodeRec& n = t->nodes[i];
+            if (j.soff[i + 1] < j.soff[i]) return fail("job: soff decreases");
+            for (uint32_t k = 0; k < n.nch; ++k) {
+                const uint32_t c = t->child[n.child_off + k];
+                if (c >= N || c <= i || j.node_parent[c] != i) return fail("job: a child out of range");
+            }
+            if (n.kind == NK_LEAF && n.nch != 0) return fail("job: a leaf with children");
+            if (n.kind == NK_DECISION) {
+                const int me = n.player;
+                const uint32_t so = j.soff[i], ncell = j.soff[i + 1] - so;
+                for (uint32_t c = 0; c <= nc(i, me); ++c)
+                    if (t->legal_off[n.row_off + c] > ncell || (c && t->legal_off[n.row_off + c] < t->legal_off[n.row_off + c - 1]))
+                        return fail("job: legal rows out of range");
+                for (uint32_t x = 0; x <= n.nch; ++x)
+                    if (t->obs_start[n.obs_off + x] > n.na || (x && t->obs_start[n.obs_off + x] < t->obs_start[n.obs_off + x - 1]))
+                        return fail("job: observation groups out of range");
+                for (uint32_t a = 0; a < n.na; ++a)
+                    if (t->obs_act[n.act_off + a] >= n.na || t->obs_child[n.act_off + a] >= n.nch)
+                        return fail("job: an action out of range");
+                for (uint32_t c = so; c < so + ncell; ++c) {
+                    const uint32_t ch = j.legal_child[c], tr = j.legal_trans[c];
+                    if (ch >= N || j.node_parent[ch] != i) return fail("job: a cell's child out of range");
+                    if (tr != NO_TRANS && tr >= nc(ch, me)) return fail("job: a cell's transition out of range");
+                    if (j.cell_row[c] >= nc(i, me)) return fail("job: a cell's row out of range");
+                }
+            } else if (n.kind == NK_CHANCE) {
+                const uint32_t ch = t->child[n.child_off], m = nc(ch, n.player);
+                for (uint32_t r = 0; r < nc(i, n.player); ++r)
+                    if (t->draw_start[n.draw_off + r + 1] < t->draw_start[n.draw_off + r])
+                        return fail("job: draw rows decrease");
+                for (uint32_t k = t->draw_start[n.draw_off]; k < t->draw_start[n.draw_off + nc(i, n.player)]; ++k)
+                    if (t->draw_to[k] >= m) return fail("job: a draw out of range");
+                if (nc(ch, 1 - n.player) != nc(i, 1 - n.player)) return fail("job: a draw changed the idle player's configs");
+            }
+        }
+        if (j.soff[N] != j.ncells) return fail("job: soff does not end at ncells");
+        for (uint32_t i : j.leaf_rows)
+            if (i >= N || t->nodes[i].kind != NK_LEAF || t->nodes[i].terminal) return fail("job: a network row out of range");
+        for (uint32_t i : j.term_leaves)
+            if (i >= N || t->nodes[i].kind != NK_LEAF) return fail("job: a terminal leaf out of range");
+        if (j.leaf_coff.empty() || j.leaf_coff[0] != 0) return fail("job: leaf_coff does not start at 0");
+        for (size_t k = 0; k + 1 < j.leaf_coff.size(); ++k) {
+            if (j.leaf_coff[k + 1] < j.leaf_coff[k]) return fail("job: leaf_coff decreases");
+            const uint32_t r = (uint32_t)(k / 2), q = (uint32_t)(k % 2);
+            if (j.leaf_coff[k + 1] - j.leaf_coff[k] != nc(j.leaf_rows[r], (int)q)) return fail("job: a row's configs do not fit its node");
+        }
+        for (uint32_t c : j.leaf_cidx)
+            if (c >= j.ncfg || j.cplayer[c] > 1) return fail("job: a leaf config out of range");
     }
     // leaves, configs, public rows
     t->leaf_rows = j.leaf_rows;
