@@ -578,15 +578,12 @@ def resolve_workload(args):
     (each player's belief over up to 256 consistent configs, Dirichlet(1)
     weights), each solving a subgame, walking it with the real play and
     re-solving with the carried beliefs, 8 solves per game, CFR+ at --iters
-    (configs[4]: 1024) and --depth (configs[4]: 4). Rounds run in lockstep as
-    GpuClient.play does: every live game advances to its next solve on host
-    threads (tree build and flattening), the round's subgames are solved in
-    one wc_solve_batch (memory-bounded waves), and each game resumes its walk.
-    Host and GPU time per round are reported apart; node-updates/s is over
-    the solve calls' wall clock."""
-    import ctypes as Cc
-    from concurrent.futures import ThreadPoolExecutor
-
+    (configs[4]: 1024) and --depth (configs[4]: 4), through the public
+    GpuClient.play: continuous batching, as the reference's game actors feed
+    its GPU service (every game builds its next subgame on a host thread as
+    soon as its walk resumes; whenever the device is idle the subgames ready
+    then are solved in one wc_solve_batch). Node-updates/s is over the solve
+    calls' wall clock; solves/s over the whole loop's."""
     import warchest_b200 as wc
 
     wc.set_cap_marker_value(0.0)
@@ -595,61 +592,17 @@ def resolve_workload(args):
     client = wc.spawn(0, *weights, net=args.net)
     games = [wc.Game(cfg, seed=s, root=wc.generate_wide_root(s, 256), max_solves=8) for s in range(args.games)]
     threads = args.build_threads or (os.cpu_count() or 1)
-    pool = ThreadPoolExecutor(threads)
-    # Two halves of the games alternate: while one half's round solves on the
-    # device (a host thread in wc_solve_batch), the other half builds its
-    # next subgames on the host threads, as the reference's game actors keep
-    # building while its GPU service solves.
-    halves = [list(games[0::2]), list(games[1::2])]
-    rounds, solved, nodes, gpu_s = 0, 0, 0.0, 0.0
-
-    def advance(live):
-        jobs = list(pool.map(lambda g: g.advance(), live))
-        return [(g, j) for g, j in zip(live, jobs) if j is not None]
-
-    def solve(pend):
-        n = len(pend)
-        arr = (Cc.c_void_p * n)(*[j._h.value for _, j in pend])
-        res = (wc._Result * n)()
-        t0 = time.perf_counter()
-        wc._check(wc.lib().wc_solve_batch(client._ctx, arr, n, res))
-        return res, time.perf_counter() - t0
-
-    def resume(pend, res):
-        for i, (g, j) in enumerate(pend):
-            wc._check(wc.lib().wc_game_resume(g._h, j._h, Cc.byref(res[i])))
-            wc.lib().wc_result_free(Cc.byref(res[i]))
-        return [g for g, _ in pend]
-
-    solver = ThreadPoolExecutor(1)
+    stats = {}
     wall0 = time.perf_counter()
-    built = [advance(halves[0]), None]
-    k = 0
-    while True:
-        o = 1 - k
-        if not built[k]:  # half k has nothing to solve: go on with the other alone
-            if built[o] is None:
-                built[o] = advance(halves[o])
-            if not built[o]:
-                break
-            built[k], k = None, o
-            continue
-        fut = solver.submit(solve, built[k])  # half k on the device ...
-        if built[o] is None:
-            built[o] = advance(halves[o])     # ... while half o builds on the host
-        res, dt = fut.result()
-        gpu_s += dt
-        nodes += sum(j.info["nodes"] for _, j in built[k]) * float(args.iters)
-        solved += len(built[k])
-        rounds += 1
-        halves[k] = resume(built[k], res)
-        built[k] = None                       # rebuilt while half o solves
-        k = o
+    solved = client.play(games, threads=threads, stats=stats)
     wall_s = time.perf_counter() - wall0
     counters = [g.counters() for g in games]
+    nodes = stats["nodes"] * float(args.iters)
+    gpu_s = stats["solve_s"]
     line = {"workload": f"configs[4] loop: {args.games} belief-heavy games (256 configs per player), depth "
-                        f"{args.depth}, {args.iters} CFR+ iters, 8 solves per game, one GPU",
-            "games": args.games, "rounds": rounds, "solves": solved,
+                        f"{args.depth}, {args.iters} CFR+ iters, 8 solves per game, one GPU, continuous batching",
+            "games": args.games, "batches": stats["batches"], "largest_batch": stats["largest_batch"],
+            "solves": solved,
             "walk_decisions": sum(c["walk_decisions"] for c in counters),
             "capped": sum(c["capped"] for c in counters),
             "wall_s": wall_s, "gpu_s": gpu_s, "solves_per_s": solved / wall_s,

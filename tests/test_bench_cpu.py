@@ -68,3 +68,4 @@ def test_workload_builder_skips_capped_roots(wc):
         except wc.SolveError as e:
             assert e.code == 3
     assert roots == kept
+

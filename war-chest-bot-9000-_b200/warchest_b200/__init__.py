@@ -475,33 +475,85 @@ class GpuClient:
         _check(lib().wc_solve_batch(self._ctx, arr, n, res))
         return [_take_result(res[i], jobs[i]) for i in range(n)]
 
-    def play(self, games: Sequence["Game"]) -> int:
+    def play(self, games: Sequence["Game"], threads: Optional[int] = None,
+             stats: Optional[dict] = None) -> int:
         """Drive games to their end (the reference's GPU game stream,
-        selfplay.rs:1224, in lockstep rounds): each round every live game
-        advances to its next solve, the pending subgames are solved together
-        in one wc_solve_batch, and each game resumes its walk with its own
-        result. Returns the subgames solved."""
-        live, solved = list(games), 0
-        while live:
-            pend = []
-            for g in live:
-                job = g.advance()
-                if job is not None:
-                    pend.append((g, job))
-            if not pend:
-                break
-            n = len(pend)
-            arr = (C.c_void_p * n)(*[j._h.value for _, j in pend])
-            res = (_Result * n)()
-            _check(lib().wc_solve_batch(self._ctx, arr, n, res))
+        selfplay.rs:1224: game actors building subgames while the GPU
+        service batches whatever they have submitted).
+
+        Each game advances to its next solve on one of `threads` host
+        threads (default: every core) on its own: tree build and flattening.
+        Whenever the device is idle, every subgame ready at that moment is
+        solved in one wc_solve_batch. Each game then resumes its walk with its
+        own result, on the calling thread between solves, so its job's pinned
+        tables are released while the device is idle, and its next build
+        starts at once. A subgame's solve does not depend on the batch it
+        lands in, so the games play exactly as one at a time would. A build
+        error is raised here once the builds in flight have finished.
+        Returns the subgames solved; `stats`, when given, receives the
+        batches, the largest batch, the solved subgames' nodes and the
+        seconds spent in wc_solve_batch."""
+        import queue
+        import time
+        from concurrent.futures import ThreadPoolExecutor
+
+        games = list(games)
+        ready: "queue.Queue" = queue.Queue()  # (game, job or None when the game is over, error)
+
+        def build(g):
             try:
-                for i, (g, j) in enumerate(pend):
-                    _check(lib().wc_game_resume(g._h, j._h, C.byref(res[i])))
-            finally:
-                for i in range(n):
-                    lib().wc_result_free(C.byref(res[i]))
-            solved += n
-            live = [g for g, _ in pend]
+                ready.put((g, g.advance(), None))
+            except BaseException as e:  # handed to the solving thread, which raises it
+                ready.put((g, None, e))
+
+        solved = batches = biggest = nodes = 0
+        solve_s = 0.0
+        pool = ThreadPoolExecutor(max(1, threads or os.cpu_count() or 1))
+        try:
+            for g in games:
+                pool.submit(build, g)
+            active = len(games)
+            while active:
+                got = [ready.get()]   # block until a subgame (or a finished game) is ready
+                while True:           # then take everything else ready now
+                    try:
+                        got.append(ready.get_nowait())
+                    except queue.Empty:
+                        break
+                pend = []
+                for g, job, err in got:
+                    if err is not None:
+                        raise err
+                    if job is None:
+                        active -= 1
+                    else:
+                        pend.append((g, job))
+                del got
+                if not pend:
+                    continue
+                n = len(pend)
+                arr = (C.c_void_p * n)(*[j._h.value for _, j in pend])
+                res = (_Result * n)()
+                t0 = time.perf_counter()
+                _check(lib().wc_solve_batch(self._ctx, arr, n, res))
+                solve_s += time.perf_counter() - t0
+                try:
+                    for i, (g, j) in enumerate(pend):
+                        _check(lib().wc_game_resume(g._h, j._h, C.byref(res[i])))
+                finally:
+                    for i in range(n):
+                        lib().wc_result_free(C.byref(res[i]))
+                for g, _ in pend:
+                    pool.submit(build, g)
+                solved += n
+                batches += 1
+                biggest = max(biggest, n)
+                nodes += sum(j.info["nodes"] for _, j in pend)
+                del pend, arr, res
+        finally:
+            pool.shutdown(wait=True, cancel_futures=True)
+        if stats is not None:
+            stats.update(batches=batches, largest_batch=biggest, nodes=nodes, solve_s=solve_s)
         return solved
 
     def upload(self, jobs: Sequence[PackedJob], dev_index: int = 0) -> "DeviceBatch":
