@@ -22,6 +22,16 @@ class OCfg(C.Structure):
 _lib = None
 
 
+def _weight_ptrs(weights):
+    """The weight arrays as pointers. Entry points without declared argument
+    types receive a Python int as a 32-bit C int, which cuts an address above
+    4 GB, so every pointer goes through c_void_p."""
+    if weights is None:
+        return None, None, None
+    _, wa, ba, la = weights
+    return C.c_void_p(wa.ctypes.data), C.c_void_p(ba.ctypes.data), C.c_void_p(la.ctypes.data)
+
+
 def lib():
     global _lib
     if _lib is None:
@@ -65,11 +75,7 @@ class Oracle:
     def __init__(self, root: bytes, cfg, weights=None):
         self.cfg = cfg
         self._keep = weights
-        if weights is None:
-            w = b = ln = None
-        else:
-            _, wa, ba, la = weights
-            w, b, ln = wa.ctypes.data, ba.ctypes.data, la.ctypes.data
+        w, b, ln = _weight_ptrs(weights)
         self.h = C.c_void_p(lib().oracle_solver_new(root, len(root), C.byref(ocfg(cfg)), w, b, ln))
         if not self.h.value:
             raise RuntimeError(lib().oracle_last_error().decode())
@@ -156,11 +162,7 @@ class Oracle:
 def walk(seed: int, cfg, weights=None, max_solves: int = 0, random_draft: bool = True):
     """The continual re-solving game with every subgame solved by the CPU
     solver (oracle_walk): (counters dict, final root bytes)."""
-    if weights is None:
-        w = b = ln = None
-    else:
-        _, wa, ba, la = weights
-        w, b, ln = wa.ctypes.data, ba.ctypes.data, la.ctypes.data
+    w, b, ln = _weight_ptrs(weights)
     ctr = (C.c_int64 * 8)()
     buf = C.create_string_buffer(1 << 22)
     n = C.c_size_t()
@@ -189,11 +191,7 @@ def solve_many(roots, cfg, weights, threads: int) -> float:
     arr = (C.c_char_p * n)(*roots)
     lens = (C.c_size_t * n)(*[len(r) for r in roots])
     out = C.c_double()
-    if weights is None:
-        w = b = ln = None
-    else:
-        _, wa, ba, la = weights
-        w, b, ln = wa.ctypes.data, ba.ctypes.data, la.ctypes.data
+    w, b, ln = _weight_ptrs(weights)
     lib().oracle_solve_many(arr, lens, n, C.byref(ocfg(cfg)), w, b, ln, threads, C.byref(out))
     return out.value
 
@@ -204,10 +202,6 @@ def bench(roots, cfg, weights, threads: int, k1: int = 2, k2: int = 4):
     arr = (C.c_char_p * n)(*roots)
     lens = (C.c_size_t * n)(*[len(r) for r in roots])
     out = (C.c_double * 3)()
-    if weights is None:
-        w = b = ln = None
-    else:
-        _, wa, ba, la = weights
-        w, b, ln = wa.ctypes.data, ba.ctypes.data, la.ctypes.data
+    w, b, ln = _weight_ptrs(weights)
     lib().oracle_bench(arr, lens, n, C.byref(ocfg(cfg)), w, b, ln, threads, k1, k2, out)
     return out[0], out[1], int(out[2])

@@ -32,3 +32,19 @@ def test_cpu_walk_with_network_stops_after_max_solves(wc, oracle):
     print(ctr)
     assert ctr["solves"] == 3 and ctr["ended"] == 1 and ctr["walking"] == 0
     assert len(root) > 0
+
+
+def test_oracle_takes_weights_above_4gb(wc, oracle):
+    """The oracle entry points without declared argument types get their
+    weight pointers as c_void_p: weights at addresses above 4 GB (views into
+    a large, mmap-backed buffer) reach the walk intact."""
+    import numpy as np
+
+    dims, w, b, ln = wc.seeded_weights("test", 0xD15EA5E)
+    # above glibc's largest dynamic mmap threshold (32 MB), so always mmap-backed
+    big = np.zeros(w.size + b.size + ln.size + (1 << 24), np.float32)
+    hw, hb, hl = big[: w.size], big[w.size: w.size + b.size], big[w.size + b.size: w.size + b.size + ln.size]
+    hw[:], hb[:], hl[:] = w, b, ln
+    assert hw.ctypes.data >= 1 << 32, "the buffer did not land above 4 GB"
+    cfg = wc.Cfg(depth=2, iters=8, snapshots=True, cfr=wc.Cfr.PLUS, node_cap=20000)
+    assert oracle.walk(3, cfg, (dims, hw, hb, hl), max_solves=1) == oracle.walk(3, cfg, (dims, w, b, ln), max_solves=1)
