@@ -242,6 +242,7 @@ def _first(mask):
 @pytest.mark.parametrize("what", [
     "node_child", "legal_child", "legal_trans", "cell_row", "obs_act", "obs_child", "draw_to",
     "leaf_rows", "term_leaves", "leaf_cidx", "cplayer", "soff", "leaf_coff", "legal_off", "draw_row_start",
+    "cfg_span", "cfg_total", "legal_row_of",
 ])
 def test_reader_refuses_indices_out_of_range(wc, what):
     """Bytes whose every count agrees but one index points outside its
@@ -280,6 +281,11 @@ def test_reader_refuses_indices_out_of_range(wc, what):
         j[what][1] = big
     elif what == "draw_row_start":
         j[what][j["draw_row_off"][_first(j["node_kind"] == 1)]] += 1
+    elif what in ("cfg_span", "cfg_total"):  # spans no solvable job has, refused before anything is sized by them
+        add = (1 << 20) + 1 if what == "cfg_span" else 1 << 28
+        j["cfg_off"][-2:] += np.uint32(add)
+    elif what == "legal_row_of":  # a first legal row whose end would wrap 32 bits
+        j[what][_first(j["node_kind"] == 0)] = NONE32 - 1
     x = write(j)
     assert x != b
     with pytest.raises(wc.SolveError) as e:

@@ -440,11 +440,18 @@ std::unique_ptr<Tree> wcj8_tree(const Wcj8Job& j, std::vector<float>* carried, u
         }
     // supports: one per (node, player), sized by the config spans (a solve
     // reads their counts only)
-    t->supports.reserve(2 * N);
+    // spans bounded before anything is sized by them: 2^20 configs per (node,
+    // player) and 2^28 in all, against about 2^26.6 for the largest job the
+    // builder makes (200,000 nodes x 2 players x 256 configs)
+    constexpr uint32_t SPAN_MAX = 1u << 20, TOTAL_MAX = 1u << 28;
+    if (j.cfg_off.size() != 2 * (size_t)N + 1 || j.cfg_off[0] != 0 || j.cfg_off.back() > TOTAL_MAX)
+        return fail("job: config spans out of range");
     for (size_t k = 0; k + 1 < j.cfg_off.size(); ++k) {
         if (j.cfg_off[k + 1] < j.cfg_off[k]) return fail("job: cfg_off decreases");
-        t->supports.emplace_back(j.cfg_off[k + 1] - j.cfg_off[k]);
+        if (j.cfg_off[k + 1] - j.cfg_off[k] > SPAN_MAX) return fail("job: a config span out of range");
     }
+    t->supports.reserve(2 * N);
+    for (size_t k = 0; k + 1 < j.cfg_off.size(); ++k) t->supports.emplace_back(j.cfg_off[k + 1] - j.cfg_off[k]);
     std::vector<uint8_t> is_term(N, 0);
     std::vector<float> util(N, 0.0f);
     for (size_t k = 0; k < j.term_leaves.size(); ++k) {
@@ -492,7 +499,7 @@ std::unique_ptr<Tree> wcj8_tree(const Wcj8Job& j, std::vector<float>* carried, u
             append(t->obs_child, j.obs_child, act_base, act_base + na);
             const int me = n.player;
             const uint32_t nc = (uint32_t)t->supports[n.sup[me]].size(), row0 = j.legal_row_of[i];
-            if (row0 == NO_ROW || row0 + nc >= j.legal_off.size() || se < so || se > j.ncells)
+            if (row0 == NO_ROW || (uint64_t)row0 + nc >= j.legal_off.size() || se < so || se > j.ncells)
                 return fail("job: legal rows out of range");
             for (uint32_t c = 0; c <= nc; ++c) t->legal_off.push_back(j.legal_off[row0 + c] - so);
             append(t->legal_action, j.legal_action, so, se);
