@@ -335,27 +335,53 @@ static double choose(uint32_t n, uint32_t k) {
     return r;
 }
 
-static void deal_rec(const uint8_t* src, int slot, uint32_t left, double num, const Config& c, double denom,
-                     std::vector<Config>& kid, std::vector<float>& prob) {
+// Slot by slot, x coins from this slot for x ascending; `take` packs the
+// coins taken so far (byte s: slot s). Only the counts that leave no more
+// coins than the later slots hold are visited (suf[s]: coins in slots s..):
+// the other branches deal nothing, so the dealt hands, their order and their
+// products are those of the full enumeration.
+static void deal_rec(const uint8_t* src, const uint32_t* suf, int slot, uint32_t left, double num, uint64_t take,
+                     double denom, std::vector<uint64_t>& out, std::vector<float>& prob) {
     if (slot == NSLOT) {
-        if (left == 0) {
-            kid.push_back(c);
-            prob.push_back((float)(num / denom));
-        }
+        out.push_back(take);
+        prob.push_back((float)(num / denom));
         return;
     }
-    uint32_t lim = std::min<uint32_t>(left, src[slot]);
-    for (uint32_t x = 0; x <= lim; ++x) {
-        Config c2 = c;
-        c2.hand[slot] += (uint8_t)x;
-        deal_rec(src, slot + 1, left - x, num * choose(src[slot], x), c2, denom, kid, prob);
-    }
+    const uint32_t hi = std::min<uint32_t>(left, src[slot]);
+    const uint32_t lo = left > suf[slot + 1] ? left - suf[slot + 1] : 0;
+    for (uint32_t x = lo; x <= hi; ++x)
+        deal_rec(src, suf, slot + 1, left - x, num * choose(src[slot], x), take | ((uint64_t)x << (8 * slot)), denom,
+                 out, prob);
 }
 
+// The hands of a (source, k) pair depend on nothing else: each pair is
+// enumerated once per scratch and its hands are added to every base config
+// that draws from it.
 void DrawScratch::deal(const uint8_t* src, uint32_t k, const Config& base) {
-    uint32_t total = 0;
-    for (int s = 0; s < NSLOT; ++s) total += src[s];
-    deal_rec(src, 0, k, 1.0, base, choose(total, k), kid, prob);
+    uint64_t key = k;
+    for (int s = 0; s < NSLOT; ++s) key = (key << 8) | src[s];
+    uint32_t entry;
+    if (const uint32_t* e = deal_index.find(key)) {
+        entry = *e;
+    } else {
+        uint32_t suf[NSLOT + 1];
+        suf[NSLOT] = 0;
+        for (int s = NSLOT - 1; s >= 0; --s) suf[s] = suf[s + 1] + src[s];
+        const uint32_t first = (uint32_t)deal_take.size();
+        if (k <= suf[0])  // else no hand: more coins than the source holds
+            deal_rec(src, suf, 0, k, 1.0, 0, choose(suf[0], k), deal_take, deal_p);
+        entry = (uint32_t)deal_span.size();
+        deal_span.emplace_back(first, (uint32_t)deal_take.size() - first);
+        deal_index.insert(key, entry);
+    }
+    const auto [first, n] = deal_span[entry];
+    for (uint32_t i = first; i < first + n; ++i) {
+        Config c = base;
+        const uint64_t take = deal_take[i];
+        for (int s = 0; s < NSLOT; ++s) c.hand[s] = (uint8_t)(c.hand[s] + (uint8_t)(take >> (8 * s)));
+        kid.push_back(c);
+        prob.push_back(deal_p[i]);
+    }
 }
 
 // rebel.rs:743-771.

@@ -5,6 +5,7 @@
 #include <cstdint>
 #include <vector>
 
+#include "flatmap.h"
 #include "game.h"
 
 namespace wc {
@@ -86,6 +87,13 @@ struct DrawScratch {
     std::vector<float> acc;
     std::vector<uint8_t> hit;
     std::vector<uint32_t> touched;
+    // the hands dealt from each (source counts, k) met so far: the coins
+    // taken per slot (5 bytes, packed) and the probability, in enumeration
+    // order; deal_span[i] = (first, count) of entry i of deal_index
+    FlatMap deal_index;
+    std::vector<uint64_t> deal_take;
+    std::vector<float> deal_p;
+    std::vector<std::pair<uint32_t, uint32_t>> deal_span;
     void transition(const std::vector<Config>& cfg, const uint8_t* reserve, const uint8_t* faceup,
                     std::vector<Config>& support, DrawMap& map, bool set_pending);
     void run(const std::vector<Config>& cfg, const uint8_t* reserve, const uint8_t* faceup, uint8_t k,

@@ -1,5 +1,6 @@
 // Public subgame tree construction (engine/src/search.rs:724-1462).
 #include "tree.h"
+#include "flatmap.h"
 
 #include <algorithm>
 #include <cmath>
@@ -112,7 +113,8 @@ namespace {
 struct Builder {
     Tree& t;
     DrawScratch draw_scratch;
-    std::unordered_map<uint64_t, uint32_t> cmap;
+    FlatMap cmap;       // (player, config counts) -> interned config id
+    FlatMap leaf_runs;  // (support, player, reserve) -> start of an equal run in leaf_cidx
     std::vector<std::pair<uint64_t, uint32_t>> cell_order;
 
     explicit Builder(Tree& tree) : t(tree) {}
@@ -122,16 +124,18 @@ struct Builder {
         config_counts(c, res, cnt);
         uint64_t key = (uint64_t)p;
         for (int k = 0; k < CCOUNTS; ++k) key = (key << 4) | cnt[k];
-        auto it = cmap.find(key);
-        if (it != cmap.end()) return it->second;
+        if (const uint32_t* v = cmap.find(key)) return *v;
         uint32_t i = (uint32_t)t.ncfg++;
         for (int k = 0; k < CCOUNTS; ++k) t.cphi.push_back((float)cnt[k] / CNORM);
         t.cplayer.push_back((uint8_t)p);
-        cmap.emplace(key, i);
+        cmap.insert(key, i);
         return i;
     }
 
-    // search.rs:1375-1425.
+    // search.rs:1375-1425. A leaf's config ids depend only on its support,
+    // the player and the player's reserve: a leaf whose three match an
+    // earlier leaf's copies that leaf's run (every config in it is interned
+    // already, so no id is assigned out of the first-seen order).
     void push_leaf(uint32_t id, const State& s, const uint32_t sup[2]) {
         if (s.is_terminal()) {
             t.term_leaves.push_back(id);
@@ -143,8 +147,27 @@ struct Builder {
         for (int p = 0; p < 2; ++p) {
             uint8_t res[NSLOT];
             reserve(s, (uint8_t)p, t.ctx, res);
-            t.leaf_coff.push_back((uint32_t)t.leaf_cidx.size());
-            for (const Config& c : t.supports[sup[p]]) t.leaf_cidx.push_back(intern_config(c, res, p));
+            const size_t base = t.leaf_cidx.size();
+            t.leaf_coff.push_back((uint32_t)base);
+            const std::vector<Config>& cfgs = t.supports[sup[p]];
+            // the run key: support (32 bits), player, the reserve in nibbles
+            // (reserves of 16 or more are never cached)
+            uint64_t key = ((uint64_t)sup[p] << 1) | (uint64_t)p;
+            bool keyed = true;
+            for (int k = 0; k < NSLOT; ++k) {
+                keyed = keyed && res[k] < 16;
+                key = (key << 4) | (res[k] & 15u);
+            }
+            if (keyed) {
+                if (const uint32_t* run = leaf_runs.find(key)) {
+                    t.leaf_cidx.resize(base + cfgs.size());
+                    std::copy(t.leaf_cidx.begin() + *run, t.leaf_cidx.begin() + *run + cfgs.size(),
+                              t.leaf_cidx.begin() + base);
+                    continue;
+                }
+            }
+            for (const Config& c : cfgs) t.leaf_cidx.push_back(intern_config(c, res, p));
+            if (keyed) leaf_runs.insert(key, (uint32_t)base);
         }
         t.leaf_rows.push_back(id);
     }
