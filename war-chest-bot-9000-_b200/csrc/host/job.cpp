@@ -128,9 +128,21 @@ std::unique_ptr<JobImage> flatten(const Tree& t, const std::vector<float>& carri
 
     const uint32_t ONE = J.ncells + J.ndraw;
 
-    // ---- reach gathers, per (level, mover), in the oracle's order
+    // ---- reach gathers, per (level, mover), in the oracle's order: a child's
+    // entries are collected in the reference's visiting order, then grouped
+    // by output config with a stable counting sort (each output keeps its
+    // entries in visiting order)
+    // every cell and every draw entry lands in at most one list, and every
+    // non-root (node, mover) config heads one
+    J.rge_src.reserve(J.ncells + J.ndraw);
+    J.rge_w.reserve(J.ncells + J.ndraw);
+    J.rg_start.reserve(J.reach_len + 1);
     J.rg_start.push_back(0);
-    std::vector<std::vector<std::pair<uint32_t, uint32_t>>> lists;
+    struct Ent {
+        uint32_t out, src, w;
+    };
+    std::vector<Ent> ents, sorted;
+    std::vector<uint32_t> at;
     for (uint32_t lv = 1; lv < L; ++lv)
         for (int q = 0; q < 2; ++q) {
             LevelRange& rg = J.rg_rng[lv * 2 + q];
@@ -140,12 +152,12 @@ std::unique_ptr<JobImage> flatten(const Tree& t, const std::vector<float>& carri
                 const NodeRec& pn = t.nodes[pa];
                 if (pn.player != q) continue;
                 uint32_t nout = nc(c, q);
-                lists.assign(nout, {});
+                ents.clear();
                 uint32_t src0 = rblk[q][pa];
                 if (pn.kind == NK_CHANCE) {
                     for (uint32_t ci = 0; ci < nc(pa, q); ++ci)
                         for (uint32_t k = t.draw_start[pn.draw_off + ci]; k < t.draw_start[pn.draw_off + ci + 1]; ++k)
-                            lists[t.draw_to[k]].emplace_back(src0 + ci, J.ncells + k);
+                            ents.push_back({t.draw_to[k], src0 + ci, J.ncells + k});
                 } else {
                     uint32_t ch = child_index[c];
                     uint32_t so = t.soff[pa];
@@ -155,19 +167,48 @@ std::unique_ptr<JobImage> flatten(const Tree& t, const std::vector<float>& carri
                             uint32_t cell = t.action_cell[so + y];
                             uint32_t tr = t.legal_trans[so + cell];
                             if (tr == NO_TRANS) continue;
-                            lists[tr].emplace_back(src0 + t.cell_row[so + cell], sorted_of[so + cell]);
+                            ents.push_back({tr, src0 + t.cell_row[so + cell], sorted_of[so + cell]});
                         }
                     }
                 }
-                for (auto& l : lists) {
-                    for (auto& e : l) { J.rge_src.push_back(e.first); J.rge_w.push_back(e.second); }
-                    J.rg_start.push_back((uint32_t)J.rge_src.size());
+                at.assign(nout + 1, 0);
+                for (const Ent& e : ents) {
+                    if (e.out >= nout) throw std::logic_error("a reach entry outside its child's configs");
+                    ++at[e.out + 1];
+                }
+                for (uint32_t o = 0; o < nout; ++o) at[o + 1] += at[o];
+                const size_t base = J.rge_src.size();
+                for (uint32_t o = 0; o < nout; ++o) J.rg_start.push_back((uint32_t)(base + at[o + 1]));
+                sorted.resize(ents.size());
+                for (const Ent& e : ents) sorted[at[e.out]++] = e;
+                J.rge_src.resize(base + sorted.size());
+                J.rge_w.resize(base + sorted.size());
+                for (size_t i = 0; i < sorted.size(); ++i) {
+                    J.rge_src[base + i] = sorted[i].src;
+                    J.rge_w[base + i] = sorted[i].w;
                 }
             }
             rg.count = (uint32_t)J.rg_start.size() - 1 - rg.first;
         }
 
     // ---- value gathers, per (level, traverser)
+    {
+        size_t entries = 0, outs = 0;  // sized once: the loops below only append
+        for (int p = 0; p < 2; ++p)
+            for (uint32_t i = 0; i < N; ++i) {
+                const NodeRec& n = t.nodes[i];
+                if (n.kind == NK_DECISION && n.player != p) {
+                    entries += (size_t)nc(i, p) * n.nch;
+                    outs += nc(i, p);
+                } else if (n.kind == NK_CHANCE) {
+                    entries += n.player == p ? t.draw_start[n.draw_off + nc(i, p)] - t.draw_start[n.draw_off] : nc(i, p);
+                    outs += nc(i, p);
+                }
+            }
+        J.vge_idx.reserve(entries);
+        J.vge_w.reserve(entries);
+        J.vg_start.reserve(outs + 1);
+    }
     J.vg_start.push_back(0);
     for (uint32_t lv = 0; lv < L; ++lv)
         for (int p = 0; p < 2; ++p) {

@@ -113,8 +113,30 @@ namespace {
 struct Builder {
     Tree& t;
     DrawScratch draw_scratch;
-    FlatMap cmap;       // (player, config counts) -> interned config id
-    FlatMap leaf_runs;  // (support, player, reserve) -> start of an equal run in leaf_cidx
+    FlatMap cmap;  // (player, config counts) -> interned config id
+    // runs of interned ids already in leaf_cidx, by a hash of (configs,
+    // player, reserve); run_index maps the hash to an entry of runs
+    struct LeafRun {
+        uint32_t sup, off;
+        uint8_t p, res[NSLOT];
+    };
+    std::vector<LeafRun> runs;
+    FlatMap run_index;
+    static_assert(sizeof(Config) == 2 * NSLOT + 1, "configs compare bytewise: no padding");
+    // draw transitions already in the tree, by a hash of their inputs (the
+    // drawer's configs, reserve, face-up counts, steps, Warrior Priest draw):
+    // the first node's rows start at t.draw_start[start_at]; its child's
+    // support is out_sup
+    struct DrawRun {
+        uint32_t in_sup, out_sup, start_at;
+        uint8_t res[NSLOT], fu[NSLOT], steps, wp;
+    };
+    std::vector<DrawRun> draw_runs;
+    FlatMap draw_index;
+
+    static bool same_configs(const std::vector<Config>& a, const std::vector<Config>& b) {
+        return a.size() == b.size() && (a.data() == b.data() || std::memcmp(a.data(), b.data(), a.size() * sizeof(Config)) == 0);
+    }
     std::vector<std::pair<uint64_t, uint32_t>> cell_order;
 
     explicit Builder(Tree& tree) : t(tree) {}
@@ -132,10 +154,12 @@ struct Builder {
         return i;
     }
 
-    // search.rs:1375-1425. A leaf's config ids depend only on its support,
-    // the player and the player's reserve: a leaf whose three match an
-    // earlier leaf's copies that leaf's run (every config in it is interned
-    // already, so no id is assigned out of the first-seen order).
+    // search.rs:1375-1425. A leaf's config ids depend only on its configs,
+    // the player and the player's reserve, and nearly every leaf repeats an
+    // earlier leaf's three (the same configs reached along other public
+    // paths): such a leaf copies that leaf's run, found by a hash and
+    // confirmed field by field. Every config of a copied run is interned
+    // already, so no id is assigned out of the first-seen order.
     void push_leaf(uint32_t id, const State& s, const uint32_t sup[2]) {
         if (s.is_terminal()) {
             t.term_leaves.push_back(id);
@@ -150,24 +174,29 @@ struct Builder {
             const size_t base = t.leaf_cidx.size();
             t.leaf_coff.push_back((uint32_t)base);
             const std::vector<Config>& cfgs = t.supports[sup[p]];
-            // the run key: support (32 bits), player, the reserve in nibbles
-            // (reserves of 16 or more are never cached)
-            uint64_t key = ((uint64_t)sup[p] << 1) | (uint64_t)p;
-            bool keyed = true;
-            for (int k = 0; k < NSLOT; ++k) {
-                keyed = keyed && res[k] < 16;
-                key = (key << 4) | (res[k] & 15u);
-            }
-            if (keyed) {
-                if (const uint32_t* run = leaf_runs.find(key)) {
+            uint64_t h = FlatMap::mix(((uint64_t)p << 40) | ((uint64_t)res[0] << 32) | ((uint64_t)res[1] << 24) |
+                                      ((uint64_t)res[2] << 16) | ((uint64_t)res[3] << 8) | res[4]);
+            for (const Config& c : cfgs) h = FlatMap::mix(h ^ c.key());
+            if (h == FlatMap::FREE) h = 0;
+            const uint32_t* e = run_index.find(h);
+            if (e) {
+                const LeafRun& r = runs[*e];
+                const std::vector<Config>& prev = t.supports[r.sup];
+                if (r.p == p && std::memcmp(r.res, res, NSLOT) == 0 && prev.size() == cfgs.size() &&
+                    (r.sup == sup[p] || std::memcmp(prev.data(), cfgs.data(), cfgs.size() * sizeof(Config)) == 0)) {
                     t.leaf_cidx.resize(base + cfgs.size());
-                    std::copy(t.leaf_cidx.begin() + *run, t.leaf_cidx.begin() + *run + cfgs.size(),
+                    std::copy(t.leaf_cidx.begin() + r.off, t.leaf_cidx.begin() + r.off + cfgs.size(),
                               t.leaf_cidx.begin() + base);
                     continue;
                 }
             }
             for (const Config& c : cfgs) t.leaf_cidx.push_back(intern_config(c, res, p));
-            if (keyed) leaf_runs.insert(key, (uint32_t)base);
+            if (!e) {  // (a hash taken by other contents keeps its first run)
+                LeafRun r{sup[p], (uint32_t)base, (uint8_t)p, {}};
+                std::memcpy(r.res, res, NSLOT);
+                run_index.insert(h, (uint32_t)runs.size());
+                runs.push_back(r);
+            }
         }
         t.leaf_rows.push_back(id);
     }
@@ -226,21 +255,60 @@ struct Builder {
                 steps += 1;
                 if (!(cs.pending.kind == C_DRAW && cs.to_act() == player)) break;
             }
-            std::vector<Config> support;
-            DrawMap draw;
-            if (wp) draw_scratch.transition(t.supports[sup_in[me]], res, fu, support, draw, true);
-            else draw_scratch.run(t.supports[sup_in[me]], res, fu, steps, support, draw);
-            // store the map: rows + 1 global offsets
+            // the same inputs give the same transition (rebel.rs:570-771 read
+            // nothing else): a repeat copies the first node's rows and child
+            // support, found by a hash and confirmed field by field
+            const std::vector<Config>& in = t.supports[sup_in[me]];
+            uint64_t h = FlatMap::mix(((uint64_t)steps << 1) | (wp ? 1u : 0u));
+            for (int k = 0; k < NSLOT; ++k) h = FlatMap::mix(h ^ ((uint64_t)res[k] << 8 | fu[k]));
+            for (const Config& c : in) h = FlatMap::mix(h ^ c.key());
+            if (h == FlatMap::FREE) h = 0;
+            const uint32_t* e = draw_index.find(h);
+            const DrawRun* hit = nullptr;
+            if (e) {
+                const DrawRun& r = draw_runs[*e];
+                if (r.steps == steps && r.wp == (wp ? 1 : 0) && std::memcmp(r.res, res, NSLOT) == 0 &&
+                    std::memcmp(r.fu, fu, NSLOT) == 0 && same_configs(t.supports[r.in_sup], in))
+                    hit = &r;
+            }
+            const uint32_t start_at = (uint32_t)t.draw_start.size();
             uint32_t base = (uint32_t)t.draw_to.size();
-            for (uint32_t x : draw.start) t.draw_start.push_back(base + x);
-            t.draw_to.insert(t.draw_to.end(), draw.to.begin(), draw.to.end());
-            t.draw_p.insert(t.draw_p.end(), draw.p.begin(), draw.p.end());
+            std::vector<Config> support;
+            if (hit) {
+                const uint32_t b0 = t.draw_start[hit->start_at], rows = (uint32_t)in.size();
+                for (uint32_t r = 0; r <= rows; ++r) {
+                    const uint32_t x = t.draw_start[hit->start_at + r] - b0;
+                    t.draw_start.push_back(base + x);
+                }
+                const uint32_t n = t.draw_start.back() - base;
+                t.draw_to.resize(base + n);
+                std::copy(t.draw_to.begin() + b0, t.draw_to.begin() + b0 + n, t.draw_to.begin() + base);
+                t.draw_p.resize(base + n);
+                std::copy(t.draw_p.begin() + b0, t.draw_p.begin() + b0 + n, t.draw_p.begin() + base);
+                support = t.supports[hit->out_sup];
+            } else {
+                DrawMap draw;
+                if (wp) draw_scratch.transition(in, res, fu, support, draw, true);
+                else draw_scratch.run(in, res, fu, steps, support, draw);
+                // store the map: rows + 1 global offsets
+                for (uint32_t x : draw.start) t.draw_start.push_back(base + x);
+                t.draw_to.insert(t.draw_to.end(), draw.to.begin(), draw.to.end());
+                t.draw_p.insert(t.draw_p.end(), draw.p.begin(), draw.p.end());
+            }
             t.child.push_back(0);
             t.nodes[id].kind = NK_CHANCE;
             t.nodes[id].nch = 1;
             t.nodes[id].draw_steps = steps;
             uint32_t cc[2] = {sup_in[0], sup_in[1]};
+            const uint32_t in_sup = sup_in[me];
             cc[me] = push_support(std::move(support));
+            if (!hit && !e) {  // (a hash taken by other inputs keeps its first transition)
+                DrawRun r{in_sup, cc[me], start_at, {}, {}, steps, (uint8_t)(wp ? 1 : 0)};
+                std::memcpy(r.res, res, NSLOT);
+                std::memcpy(r.fu, fu, NSLOT);
+                draw_index.insert(h, (uint32_t)draw_runs.size());
+                draw_runs.push_back(r);
+            }
             uint32_t ch = build(cs, depth, cc, level + 1);
             t.child[t.nodes[id].child_off] = ch;
             return id;
