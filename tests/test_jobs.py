@@ -157,3 +157,22 @@ def test_distinct_public_rows_are_the_distinct_boards(wc, oracle):
         assert c[20] == distinct, (seed, c[20], distinct, job.info["net_rows"])
         shared += c[20] < job.info["net_rows"]
     assert shared >= 2  # the same public position, reached along different public paths
+
+
+def test_jobs_match_the_pinned_digests(wc):
+    """The builder's output byte for byte (wc_job_digest) on seeded roots of
+    depths 1-3 and belief-heavy depth-4 roots, against the digests pinned in
+    tests/golden/job_digests.json (written by tests/golden/make_job_digests.py;
+    the builder before its draw-transition and leaf-run reuse wrote the same
+    digests)."""
+    import importlib.util
+    import json
+    import os
+
+    here = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+    spec = importlib.util.spec_from_file_location("make_job_digests", os.path.join(here, "make_job_digests.py"))
+    gen = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(gen)
+    want = json.load(open(os.path.join(here, "job_digests.json")))
+    got = gen.digests(wc)
+    assert [c["digest"] for c in got] == [c["digest"] for c in want]

@@ -36,15 +36,28 @@ def test_cpu_walk_with_network_stops_after_max_solves(wc, oracle):
 
 def test_oracle_takes_weights_above_4gb(wc, oracle):
     """The oracle entry points without declared argument types get their
-    weight pointers as c_void_p: weights at addresses above 4 GB (views into
-    a large, mmap-backed buffer) reach the walk intact."""
+    weight pointers as c_void_p: weights placed above 4 GB (an anonymous
+    mapping at a high hint address) reach the walk intact."""
+    import ctypes as C
+
     import numpy as np
 
     dims, w, b, ln = wc.seeded_weights("test", 0xD15EA5E)
-    # above glibc's largest dynamic mmap threshold (32 MB), so always mmap-backed
-    big = np.zeros(w.size + b.size + ln.size + (1 << 24), np.float32)
-    hw, hb, hl = big[: w.size], big[w.size: w.size + b.size], big[w.size + b.size: w.size + b.size + ln.size]
-    hw[:], hb[:], hl[:] = w, b, ln
-    assert hw.ctypes.data >= 1 << 32, "the buffer did not land above 4 GB"
-    cfg = wc.Cfg(depth=2, iters=8, snapshots=True, cfr=wc.Cfr.PLUS, node_cap=20000)
-    assert oracle.walk(3, cfg, (dims, hw, hb, hl), max_solves=1) == oracle.walk(3, cfg, (dims, w, b, ln), max_solves=1)
+    n = w.size + b.size + ln.size
+    libc = C.CDLL(None)
+    libc.mmap.restype = C.c_void_p
+    libc.mmap.argtypes = [C.c_void_p, C.c_size_t, C.c_int, C.c_int, C.c_int, C.c_long]
+    libc.munmap.argtypes = [C.c_void_p, C.c_size_t]
+    nbytes = 4 * n
+    addr = libc.mmap(C.c_void_p(0x5F0000000000), nbytes, 0x3, 0x22, -1, 0)  # RW, private anonymous
+    assert addr not in (None, C.c_void_p(-1).value)
+    try:
+        assert addr >= 1 << 32, "the mapping did not land above 4 GB"
+        big = np.ctypeslib.as_array((C.c_float * n).from_address(addr))
+        hw, hb, hl = big[: w.size], big[w.size: w.size + b.size], big[w.size + b.size:]
+        hw[:], hb[:], hl[:] = w, b, ln
+        cfg = wc.Cfg(depth=2, iters=8, snapshots=True, cfr=wc.Cfr.PLUS, node_cap=20000)
+        assert oracle.walk(3, cfg, (dims, hw, hb, hl), max_solves=1) == oracle.walk(3, cfg, (dims, w, b, ln),
+                                                                                     max_solves=1)
+    finally:
+        libc.munmap(C.c_void_p(addr), nbytes)  # the views die with this call's frame, unread
