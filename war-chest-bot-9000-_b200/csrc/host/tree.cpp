@@ -154,12 +154,16 @@ struct Builder {
         return i;
     }
 
-    // search.rs:1375-1425. A leaf's config ids depend only on its configs,
-    // the player and the player's reserve, and nearly every leaf repeats an
-    // earlier leaf's three (the same configs reached along other public
-    // paths): such a leaf copies that leaf's run, found by a hash and
-    // confirmed field by field. Every config of a copied run is interned
-    // already, so no id is assigned out of the first-seen order.
+    // search.rs:1375-1425. The public row is packed at the leaf; the configs'
+    // interning waits for the end of the build (finish_leaves, in leaf order,
+    // so the ids are those of interning at each leaf) and is skipped for a
+    // tree that hits the node cap, which is never solved.
+    struct PendingLeaf {
+        uint32_t sup[2];
+        uint8_t res[2][NSLOT];
+    };
+    std::vector<PendingLeaf> pending;
+
     void push_leaf(uint32_t id, const State& s, const uint32_t sup[2]) {
         if (s.is_terminal()) {
             t.term_leaves.push_back(id);
@@ -168,37 +172,54 @@ struct Builder {
         size_t at = t.gpu_rows.size();
         t.gpu_rows.resize(at + GPU_ROW_BYTES);
         pack_gpu_row(s, t.ctx, t.gpu_rows.data() + at);
+        PendingLeaf pl;
         for (int p = 0; p < 2; ++p) {
-            uint8_t res[NSLOT];
-            reserve(s, (uint8_t)p, t.ctx, res);
-            const size_t base = t.leaf_cidx.size();
-            t.leaf_coff.push_back((uint32_t)base);
-            const std::vector<Config>& cfgs = t.supports[sup[p]];
-            uint64_t h = FlatMap::mix(((uint64_t)p << 40) | ((uint64_t)res[0] << 32) | ((uint64_t)res[1] << 24) |
-                                      ((uint64_t)res[2] << 16) | ((uint64_t)res[3] << 8) | res[4]);
-            for (const Config& c : cfgs) h = FlatMap::mix(h ^ c.key());
-            if (h == FlatMap::FREE) h = 0;
-            const uint32_t* e = run_index.find(h);
-            if (e) {
-                const LeafRun& r = runs[*e];
-                const std::vector<Config>& prev = t.supports[r.sup];
-                if (r.p == p && std::memcmp(r.res, res, NSLOT) == 0 && prev.size() == cfgs.size() &&
-                    (r.sup == sup[p] || std::memcmp(prev.data(), cfgs.data(), cfgs.size() * sizeof(Config)) == 0)) {
-                    t.leaf_cidx.resize(base + cfgs.size());
-                    std::copy(t.leaf_cidx.begin() + r.off, t.leaf_cidx.begin() + r.off + cfgs.size(),
-                              t.leaf_cidx.begin() + base);
-                    continue;
-                }
-            }
-            for (const Config& c : cfgs) t.leaf_cidx.push_back(intern_config(c, res, p));
-            if (!e) {  // (a hash taken by other contents keeps its first run)
-                LeafRun r{sup[p], (uint32_t)base, (uint8_t)p, {}};
-                std::memcpy(r.res, res, NSLOT);
-                run_index.insert(h, (uint32_t)runs.size());
-                runs.push_back(r);
+            pl.sup[p] = sup[p];
+            reserve(s, (uint8_t)p, t.ctx, pl.res[p]);
+        }
+        pending.push_back(pl);
+        t.leaf_rows.push_back(id);
+    }
+
+    // A leaf's config ids depend only on its configs, the player and the
+    // player's reserve, and nearly every leaf repeats an earlier leaf's three
+    // (the same configs reached along other public paths): such a leaf copies
+    // that leaf's run, found by a hash and confirmed field by field. Every
+    // config of a copied run is interned already, so no id is assigned out of
+    // the first-seen order.
+    void finish_leaves() {
+        for (const PendingLeaf& pl : pending)
+            for (int p = 0; p < 2; ++p) intern_leaf(pl.sup, pl.res[p], p);
+        pending.clear();
+    }
+
+    void intern_leaf(const uint32_t sup[2], const uint8_t* res, int p) {
+        const size_t base = t.leaf_cidx.size();
+        t.leaf_coff.push_back((uint32_t)base);
+        const std::vector<Config>& cfgs = t.supports[sup[p]];
+        uint64_t h = FlatMap::mix(((uint64_t)p << 40) | ((uint64_t)res[0] << 32) | ((uint64_t)res[1] << 24) |
+                                  ((uint64_t)res[2] << 16) | ((uint64_t)res[3] << 8) | res[4]);
+        for (const Config& c : cfgs) h = FlatMap::mix(h ^ c.key());
+        if (h == FlatMap::FREE) h = 0;
+        const uint32_t* e = run_index.find(h);
+        if (e) {
+            const LeafRun& r = runs[*e];
+            const std::vector<Config>& prev = t.supports[r.sup];
+            if (r.p == p && std::memcmp(r.res, res, NSLOT) == 0 && prev.size() == cfgs.size() &&
+                (r.sup == sup[p] || std::memcmp(prev.data(), cfgs.data(), cfgs.size() * sizeof(Config)) == 0)) {
+                t.leaf_cidx.resize(base + cfgs.size());
+                std::copy(t.leaf_cidx.begin() + r.off, t.leaf_cidx.begin() + r.off + cfgs.size(),
+                          t.leaf_cidx.begin() + base);
+                return;
             }
         }
-        t.leaf_rows.push_back(id);
+        for (const Config& c : cfgs) t.leaf_cidx.push_back(intern_config(c, res, p));
+        if (!e) {  // (a hash taken by other contents keeps its first run)
+            LeafRun r{sup[p], (uint32_t)base, (uint8_t)p, {}};
+            std::memcpy(r.res, res, NSLOT);
+            run_index.insert(h, (uint32_t)runs.size());
+            runs.push_back(r);
+        }
     }
 
     uint32_t push_support(std::vector<Config>&& v) {
@@ -452,6 +473,7 @@ std::unique_ptr<Tree> build_tree(const State& root, const Ctx& ctx, const SolveC
     sup[0] = b.push_support(std::vector<Config>(bel[0].cfg));
     sup[1] = b.push_support(std::vector<Config>(bel[1].cfg));
     b.build(root, std::max(cfg.depth, 1), sup, 0);
+    if (!t->capped) b.finish_leaves();
     t->soff.push_back((uint32_t)t->legal_action.size());
     t->leaf_coff.push_back((uint32_t)t->leaf_cidx.size());
     return t;
