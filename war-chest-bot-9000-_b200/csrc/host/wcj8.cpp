@@ -312,7 +312,7 @@ std::vector<uint8_t> wcj8_write(const Wcj8Job& j) {
 
 // serialize.rs:1127-1240, with its count checks.
 bool wcj8_read(const uint8_t* data, size_t n, Wcj8Job* out, std::string* err) {
-    Reader r{data, n};
+    Reader r{data, n, 0, {}};
     Wcj8Job j;
     auto fail = [&](const std::string& m) {
         if (err) *err = m;
