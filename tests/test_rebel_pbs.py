@@ -11,8 +11,6 @@ a function of the beliefs alone.
 """
 import ctypes as C
 
-import pytest
-
 
 def _run(fn, *args):
     msg = C.create_string_buffer(2048)

@@ -11,7 +11,6 @@ missing.
 from __future__ import annotations
 
 import ctypes as C
-import math
 import os
 from dataclasses import dataclass, field
 from typing import List, Optional, Sequence
