@@ -138,6 +138,7 @@ struct Builder {
         return a.size() == b.size() && (a.data() == b.data() || std::memcmp(a.data(), b.data(), a.size() * sizeof(Config)) == 0);
     }
     std::vector<std::pair<uint64_t, uint32_t>> cell_order;
+    std::vector<Config> adv;  // a decision node's successor config per cell
 
     explicit Builder(Tree& tree) : t(tree) {}
 
@@ -388,8 +389,10 @@ struct Builder {
         std::vector<uint32_t> action_cell(ncell);
         for (uint32_t cell = 0; cell < ncell; ++cell) action_cell[afill[t.legal_action[cell0 + cell]]++] = cell;
 
-        // child supports, by sorted config key (search.rs:1164-1197)
+        // child supports, by sorted config key (search.rs:1164-1197); each
+        // cell's successor config is computed once (adv, by cell)
         std::vector<std::vector<Config>> child_cfgs(nch);
+        adv.resize(ncell);
         for (uint32_t ch = 0; ch < nch; ++ch) {
             cell_order.clear();
             for (uint32_t j = obs_start[ch]; j < obs_start[ch + 1]; ++j) {
@@ -398,8 +401,7 @@ struct Builder {
                     uint32_t cell = action_cell[x];
                     if (t.legal_child[cell0 + cell] != ch) continue;
                     uint32_t ci = t.cell_row[cell0 + cell];
-                    Config n;
-                    if (advance_config(mine[ci], aslot[a], fdown[a], &n)) cell_order.emplace_back(n.key(), cell);
+                    if (advance_config(mine[ci], aslot[a], fdown[a], &adv[cell])) cell_order.emplace_back(adv[cell].key(), cell);
                 }
             }
             std::sort(cell_order.begin(), cell_order.end());
@@ -409,11 +411,7 @@ struct Builder {
                 uint32_t cell = kc.second;
                 if (kc.first != prev) {
                     prev = kc.first;
-                    uint32_t ci = t.cell_row[cell0 + cell];
-                    uint32_t a = t.legal_action[cell0 + cell];
-                    Config n;
-                    advance_config(mine[ci], aslot[a], fdown[a], &n);
-                    sup.push_back(n);
+                    sup.push_back(adv[cell]);
                 }
                 t.legal_trans[cell0 + cell] = (uint32_t)(sup.size() - 1);
             }
