@@ -481,7 +481,9 @@ class GpuClient:
         service batches whatever they have submitted).
 
         Each game advances to its next solve on one of `threads` host
-        threads (default: every core) on its own: tree build and flattening.
+        threads on its own: tree build and flattening. The default is the
+        cores divided among the node's ranks (LOCAL_WORLD_SIZE, as torchrun
+        sets it; 1 without it).
         Whenever the device is idle, every subgame ready at that moment is
         solved in one wc_solve_batch. Each game then resumes its walk with its
         own result, on the calling thread between solves, so its job's pinned
@@ -507,7 +509,9 @@ class GpuClient:
 
         solved = batches = biggest = nodes = 0
         solve_s = 0.0
-        pool = ThreadPoolExecutor(max(1, threads or os.cpu_count() or 1))
+        if not threads:
+            threads = (os.cpu_count() or 1) // max(1, int(os.environ.get("LOCAL_WORLD_SIZE", "1") or 1))
+        pool = ThreadPoolExecutor(max(1, threads))
         try:
             for g in games:
                 pool.submit(build, g)
